@@ -1,0 +1,397 @@
+"""Benchmark: fused NF4 GEMV on the reference's headline configuration.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--m M] [--impl ours|reference]
+
+Workload: W (N=4096, K=14336) with N(0, 0.02^2)
+entries, NF4 blocksize 64, double-quantized (8-bit dynamic map, blocksize 256,
+around the float32 mean); x bf16 (M, 14336) of N(0, 1); y = x @ W.T.
+Synthetic, seeded data (torch Philox on the device). Eight independent weight
+copies (8 x 30.3 MB = 242 MB, more than the 126 MB L2) are rotated so every
+call reads its weight from HBM.
+
+A step is one GEMV call. `value` is the whole job's effective bandwidth
+(algorithmic bytes: weight 30,292,996 B + x M*K*2 + y M*N*2, per call) with
+inputs resident in HBM, timed with CUDA events around the replay of a CUDA
+graph that holds the K timed calls. `e2e` is the same metric through the
+public API (bnb_b200.matmul) with x copied from pinned host memory and y read
+back every step. `m_sweep` repeats the device timing at M = 2..20.
+
+Multi-GPU (torchrun, one process per GPU): every rank runs the same workload
+on its own weights (independent objects, no collective; weak scaling); the
+timed region is bracketed by barriers and the max over ranks is reported.
+
+`--impl reference` times the reference's arithmetic on the host cores: the
+reference has no CPU kernel path of its own (its kernels are GPU-only CuTe DSL)
+and cannot be installed here, so its GEMV is the oracle's C restatement
+(oracle/bnbq_oracle.c, OpenMP on every core), on the same configuration.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT / "bitsandbytes-jax_b200"))
+sys.path.insert(0, str(ROOT))
+
+N_ROWS, K_COLS, BS, BS2, ROTATE = 4096, 14336, 64, 256, 8
+W_BYTES = N_ROWS * K_COLS // 2 + N_ROWS * K_COLS // BS + (N_ROWS * K_COLS // BS // BS2) * 4 + 256 * 4 + 4
+METRIC = "NF4 GEMV effective HBM GB/s & µs at M=1..20 (4096×14336), % of B200 peak"
+WORKLOAD = ("fused NF4 GEMV y = x @ W.T, W 4096x14336 NF4 bs64 double-quantized (bs2 256), "
+            "x bf16 M x 14336, 8 rotated weight copies")
+
+
+def algo_bytes(m: int) -> int:
+    return W_BYTES + m * K_COLS * 2 + m * N_ROWS * 2
+
+
+def measured_peaks() -> tuple[float, str]:
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        try:
+            return float(json.loads(p.read_text())["hbm_gbs"]), "measured"
+        except Exception:
+            pass
+    return 6650.0, "fallback"
+
+
+def profiled_traffic(m: int):
+    """DRAM bytes per launch from the committed ncu summary, if one exists."""
+    p = ROOT / "profiles" / "gemv_nf4_traffic.json"
+    if p.exists():
+        try:
+            return json.loads(p.read_text()).get(f"m{m}")
+        except Exception:
+            return None
+    return None
+
+
+# --------------------------------------------------------------- clocks
+
+class ClockSampler:
+    """nvidia-smi clocks and throttle reasons while the timed region runs."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.gpu = gpu_index
+        self.proc = None
+        self.lines: list[str] = []
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.FIELDS}",
+                 "--format=csv,noheader,nounits", "-lms", "100"],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.thread = threading.Thread(target=self._read, daemon=True)
+            self.thread.start()
+            time.sleep(0.25)
+        except FileNotFoundError:
+            self.proc = None
+        return self
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def __exit__(self, *exc):
+        if self.proc is not None:
+            time.sleep(0.2)
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+
+    def summary(self) -> dict:
+        sms, maxes, reasons = [], [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in self.lines:
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sms.append(float(parts[1]))
+                maxes.append(float(parts[2]))
+            except ValueError:
+                continue
+            for name, v in zip(names, parts[5:9]):
+                if v.lower() == "active":
+                    reasons.add(name)
+        if not sms:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "samples": 0}
+        return {"sm_mhz": statistics.median(sms), "sm_max_mhz": max(maxes),
+                "reasons": sorted(reasons), "samples": len(sms)}
+
+
+# ------------------------------------------------------------------ ours
+
+def make_weights(torch, bnb, device, seed: int):
+    ws = []
+    for i in range(ROTATE):
+        g = torch.Generator(device).manual_seed(seed * 100 + i)
+        w = (torch.randn(N_ROWS, K_COLS, device=device, generator=g) * 0.02).to(torch.bfloat16)
+        ws.append(bnb.quantize(w, "nf4", BS, double_quant=True))
+        del w
+    torch.cuda.synchronize()
+    return ws
+
+
+def gemv_args(w):
+    a = w.absmax
+    return w.data, a.data, (a.absmax, a.code, a.offset, a.blocksize)
+
+
+def time_device(torch, gemv_nf4, ws, x, steps: int, warmup: int, dist=None):
+    """Device time of `steps` GEMV calls replayed from one CUDA graph."""
+    m = x.shape[0]
+    ys = [torch.empty(m, N_ROWS, dtype=torch.bfloat16, device=x.device) for _ in range(ROTATE)]
+    args = [gemv_args(w) for w in ws]
+
+    def call(i):
+        d, aq, nested = args[i % ROTATE]
+        gemv_nf4(x, d, aq, N_ROWS, BS, nested=nested, out=ys[i % ROTATE])
+
+    for i in range(max(warmup, 3)):  # eager warm-up (also primes per-device setup)
+        call(i)
+    torch.cuda.synchronize()
+    stream = torch.cuda.Stream(device=x.device)
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.stream(stream):
+        with torch.cuda.graph(graph, stream=stream):
+            for i in range(steps):
+                call(i)
+    for _ in range(max(warmup // max(steps, 1), 1) + 2):  # graph warm-up replays
+        graph.replay()
+    torch.cuda.synchronize()
+    if dist is not None:
+        dist.barrier()
+    torch.cuda.synchronize()
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    start.record(stream)
+    with torch.cuda.stream(stream):
+        graph.replay()
+    end.record(stream)
+    torch.cuda.synchronize()
+    if dist is not None:
+        dist.barrier()
+    ms = start.elapsed_time(end)
+    del graph
+    return ms, ys[0]
+
+
+def time_e2e(torch, bnb, ws, m: int, steps: int, warmup: int):
+    """The public API with host buffers: pinned x -> device, matmul, y -> host."""
+    dev = ws[0].data.device
+    g = torch.Generator().manual_seed(7)
+    xh = torch.randn(m, K_COLS, generator=g).to(torch.bfloat16).pin_memory()
+    yh = torch.empty(m, N_ROWS, dtype=torch.bfloat16).pin_memory()
+
+    def step(i):
+        xd = xh.to(dev, non_blocking=True)
+        y = bnb.matmul(xd, ws[i % ROTATE])
+        yh.copy_(y, non_blocking=True)
+
+    for i in range(max(warmup, 3)):
+        step(i)
+    torch.cuda.synchronize()
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    start.record()
+    for i in range(steps):
+        step(i)
+    end.record()
+    torch.cuda.synchronize()
+    ms = start.elapsed_time(end)
+    return ms, m * K_COLS * 2, m * N_ROWS * 2
+
+
+def cpu_baseline_gemv(seconds: float = 12.0):
+    """The oracle's C restatement of the reference GEMV (its float32
+    numerics), M=1 on the full 4096x14336 weight, OpenMP on every host core."""
+    import numpy as np
+    from oracle import oracle as O
+    rng = np.random.default_rng(0)
+    w = (rng.standard_normal(N_ROWS * K_COLS) * 0.02).astype(np.float32)
+    q, am = O.quantize_nf4(w, O.F32, BS)
+    off = O.mean_f32(am)
+    code = O.create_dynamic_map()
+    q2, am2 = O.quantize_8bit(am, O.F32, BS2, code, offset=off)
+    scales = O.nested_absmax(q2, am2, code, off, BS2)  # decoded per call below
+    x = O.f32_to_bf16(rng.standard_normal((1, K_COLS)).astype(np.float32)).reshape(1, K_COLS)
+    cores = O.num_threads()
+    O.gemv_ref(x, O.BF16, q, N_ROWS, BS, scales)  # warm-up
+    calls, t0 = 0, time.perf_counter()
+    while True:
+        scales = O.nested_absmax(q2, am2, code, off, BS2)
+        O.gemv_ref(x, O.BF16, q, N_ROWS, BS, scales)
+        calls += 1
+        el = time.perf_counter() - t0
+        if el >= seconds:
+            break
+    gbs = algo_bytes(1) * calls / el / 1e9
+    return {"value": round(gbs, 3), "unit": "GB/s", "cores": cores, "kind": "port",
+            "sample": f"{calls} full M=1 GEMV calls (4096x14336, double-quantized) in {el:.1f} s"}
+
+
+def run_ours(args, dist, rank, world, local_rank):
+    import torch
+    import bnb_b200 as bnb
+    from bnb_b200.kernels import gemv_nf4
+
+    device = torch.device("cuda", local_rank)
+    torch.cuda.set_device(device)
+    ws = make_weights(torch, bnb, device, seed=rank + 1)
+    g = torch.Generator(device).manual_seed(1234)
+    x = torch.randn(args.m, K_COLS, device=device, generator=g).to(torch.bfloat16)
+
+    with ClockSampler(local_rank) as clocks:
+        ms, _ = time_device(torch, gemv_nf4, ws, x, args.steps, args.warmup, dist)
+    ms_t = torch.tensor([ms], device=device, dtype=torch.float64)
+    if dist is not None:
+        dist.all_reduce(ms_t, op=dist.ReduceOp.MAX)
+    ms_max = float(ms_t.item())
+
+    sweep = {}
+    for m in ([2, 4, 8, 16, 20] if args.sweep else []):
+        xm = torch.randn(m, K_COLS, device=device, generator=g).to(torch.bfloat16)
+        t, _ = time_device(torch, gemv_nf4, ws, xm, max(args.steps // 4, 64), args.warmup)
+        per = t / max(args.steps // 4, 64)
+        sweep[f"m{m}"] = {"us": round(per * 1e3, 3), "gbs": round(algo_bytes(m) / (per * 1e-3) / 1e9, 1)}
+
+    e2e_ms, h2d, d2h = time_e2e(torch, bnb, ws, args.m, min(args.steps, 500), args.warmup)
+    e2e_steps = min(args.steps, 500)
+
+    if rank != 0:
+        return None
+    per_call_ms = ms_max / args.steps
+    value = algo_bytes(args.m) * args.steps * world / (ms_max * 1e-3) / 1e9
+    peak, peak_kind = measured_peaks()
+    achieved = algo_bytes(args.m) / (per_call_ms * 1e-3) / 1e9
+    traffic = profiled_traffic(args.m)
+    line = {
+        "metric": METRIC,
+        "value": round(value, 2),
+        "unit": "GB/s",
+        "n_gpus": world,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": round(per_call_ms, 6),
+        "us_per_call": round(per_call_ms * 1e3, 3),
+        "higher_is_better": True,
+        "scaling": "weak",
+        "vs_baseline": None,
+        "dtype": "bf16",
+        "data": "synthetic (seeded torch Philox: W ~ N(0, 0.02^2), x ~ N(0, 1))",
+        "config": {"workload": WORKLOAD, "m": args.m, "n": N_ROWS, "k": K_COLS, "blocksize": BS,
+                   "blocksize2": BS2, "weight_bytes": W_BYTES, "algorithmic_bytes_per_call": algo_bytes(args.m),
+                   "l2": "8 rotated weight copies, 242 MB > 126 MB L2", "timing": "CUDA graph of the K calls",
+                   "parallelism": f"replicas x{world}" if world > 1 else "1 GPU"},
+        "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
+                     "frac": round(achieved / peak, 4), "peak_source": peak_kind,
+                     "traffic": traffic, "kernel": "gemv_kernel"},
+        "e2e": {"value": round(algo_bytes(args.m) * e2e_steps / (e2e_ms * 1e-3) / 1e9, 2), "unit": "GB/s",
+                "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+                "us_per_step": round(e2e_ms / e2e_steps * 1e3, 3)},
+        "gpu_launches": args.steps,
+        "clocks": clocks.summary(),
+        "m_sweep": sweep,
+    }
+    if world == 1 and not args.no_cpu_baseline:
+        line["cpu_baseline"] = cpu_baseline_gemv()
+    return line
+
+
+def run_reference(args, rank):
+    """The reference's arithmetic on the host cores (see module docstring)."""
+    if rank != 0:
+        return None
+    import numpy as np
+    from oracle import oracle as O
+    rng = np.random.default_rng(0)
+    w = (rng.standard_normal(N_ROWS * K_COLS) * 0.02).astype(np.float32)
+    q, am = O.quantize_nf4(w, O.F32, BS)
+    off = O.mean_f32(am)
+    code = O.create_dynamic_map()
+    q2, am2 = O.quantize_8bit(am, O.F32, BS2, code, offset=off)
+    x = O.f32_to_bf16(rng.standard_normal((args.m, K_COLS)).astype(np.float32)).reshape(args.m, K_COLS)
+    cores = O.num_threads()
+
+    def step():
+        scales = O.nested_absmax(q2, am2, code, off, BS2)
+        O.gemv_ref(x, O.BF16, q, N_ROWS, BS, scales)
+
+    for _ in range(args.warmup):
+        step()
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        step()
+    el = time.perf_counter() - t0
+    value = algo_bytes(args.m) * args.steps / el / 1e9
+    return {
+        "impl": "reference",
+        "metric": METRIC, "value": round(value, 3), "unit": "GB/s", "n_gpus": 1,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(el / args.steps * 1e3, 4),
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+        "data": "synthetic (numpy default_rng(0): W ~ N(0, 0.02^2), x ~ N(0, 1))",
+        "config": {"workload": WORKLOAD, "m": args.m, "n": N_ROWS, "k": K_COLS, "blocksize": BS,
+                   "blocksize2": BS2, "algorithmic_bytes_per_call": algo_bytes(args.m)},
+        "cpu_baseline": {"value": round(value, 3), "unit": "GB/s", "cores": cores, "kind": "port",
+                         "sample": f"{args.steps} full GEMV calls at M={args.m} on the host"},
+        "e2e": {"value": round(value, 3), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=2000)
+    ap.add_argument("--warmup", type=int, default=16)
+    ap.add_argument("--m", type=int, default=1)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--no-sweep", dest="sweep", action="store_false")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+
+    if args.impl == "reference":
+        if args.steps > 50:
+            args.steps = 50  # each host step is a full GEMV: keep the run to seconds
+        line = run_reference(args, rank)
+        if line is not None:
+            print(json.dumps(line), flush=True)
+        return
+
+    dist = None
+    if world > 1:
+        import datetime
+        import torch
+        import torch.distributed as td
+        torch.cuda.set_device(local_rank)
+        td.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                              device_id=torch.device("cuda", local_rank))
+        dist = td
+    try:
+        line = run_ours(args, dist, rank, world, local_rank)
+        if line is not None:
+            print(json.dumps(line), flush=True)
+    finally:
+        if dist is not None:
+            dist.barrier()
+            dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

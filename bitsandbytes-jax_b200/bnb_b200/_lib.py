@@ -1,0 +1,115 @@
+"""ctypes binding of libbnbq.so (include/bnbq.h) for torch CUDA tensors.
+
+The library is built in-tree by ``bitsandbytes-jax_b200/build.py`` and loaded
+from this directory; there is no other implementation behind these calls. A
+missing library, a missing GPU or a non-sm_100 device raises -- nothing falls
+back to another code path.
+"""
+from __future__ import annotations
+
+import ctypes as C
+import threading
+from pathlib import Path
+
+import torch
+
+LIB_PATH = Path(__file__).resolve().parent / "libbnbq.so"
+
+F32, F16, BF16 = 0, 1, 2
+OK, ERR_INVALID, ERR_UNSUPPORTED, ERR_MISALIGNED, ERR_CUDA, ERR_DEVICE = 0, -1, -2, -3, -4, -5
+GEMV_MAX_M = 20
+
+DTYPE_CODE = {torch.float32: F32, torch.float16: F16, torch.bfloat16: BF16}
+
+# argument kinds: p = pointer, i = int32, l = int64
+_SIGNATURES = {
+    "bnbq_quantize_nf4": "ipliPPP",
+    "bnbq_quantize_blockwise": "ipliPPPPP",
+    "bnbq_absmax_mean": "PlPP",
+    "bnbq_dequantize_nf4": "iPPliPP",
+    "bnbq_dequantize_blockwise": "iPPPliPPP",
+    "bnbq_dequantize_nf4_nested": "iPPPPPliiPP",
+    "bnbq_dequantize_blockwise_nested": "iPPPPPPliiPP",
+    "bnbq_gemv_nf4": "iPiiPliPPPPPilPlP",
+    "bnbq_matmul_nf4": "iPiiPliPPPPPilPlP",
+    "bnbq_rcp_approx_ftz": "PPlP",
+    "bnbq_version": "",
+}
+_KIND = {"i": C.c_int32, "l": C.c_int64, "P": C.c_void_p, "p": C.c_void_p}
+
+_lock = threading.Lock()
+_lib: C.CDLL | None = None
+
+
+def exported_symbols() -> list[str]:
+    return [*_SIGNATURES, "bnbq_error_string"]
+
+
+def lib() -> C.CDLL:
+    global _lib
+    if _lib is None:
+        with _lock:
+            if _lib is None:
+                if not LIB_PATH.exists():
+                    raise RuntimeError(
+                        f"{LIB_PATH} is missing: build it with `python bitsandbytes-jax_b200/build.py`")
+                L = C.CDLL(str(LIB_PATH))
+                for name, sig in _SIGNATURES.items():
+                    fn = getattr(L, name)
+                    fn.argtypes = [_KIND[c] for c in sig]
+                    fn.restype = C.c_int32
+                L.bnbq_error_string.argtypes = [C.c_int32]
+                L.bnbq_error_string.restype = C.c_char_p
+                _lib = L
+    return _lib
+
+
+class BnbqError(RuntimeError):
+    pass
+
+
+def check(status: int, what: str) -> None:
+    if status == OK:
+        return
+    msg = f"{what}: {lib().bnbq_error_string(status).decode()} (status {status})"
+    if status == ERR_INVALID:
+        raise ValueError(msg)
+    if status == ERR_UNSUPPORTED:
+        raise NotImplementedError(msg)
+    raise BnbqError(msg)
+
+
+def ptr(t: torch.Tensor | None) -> int | None:
+    return None if t is None else t.data_ptr()
+
+
+def stream_of(t: torch.Tensor) -> int:
+    return torch.cuda.current_stream(t.device).cuda_stream
+
+
+def require_cuda(*tensors: torch.Tensor | None) -> torch.device:
+    dev = None
+    for t in tensors:
+        if t is None:
+            continue
+        if not t.is_cuda:
+            raise ValueError(f"expected a CUDA tensor, got one on {t.device}")
+        if dev is None:
+            dev = t.device
+        elif t.device != dev:
+            raise ValueError(f"tensors on different devices: {dev} and {t.device}")
+    if dev is None:
+        raise ValueError("no CUDA tensor given")
+    return dev
+
+
+def aligned(t: torch.Tensor, a: int = 16) -> torch.Tensor:
+    """Contiguous and `a`-byte aligned (slices may start mid-allocation)."""
+    t = t.contiguous()
+    if t.numel() and t.data_ptr() % a:
+        t = t.clone()
+    return t
+
+
+def call(name: str, *args) -> None:
+    check(getattr(lib(), name)(*args), name)

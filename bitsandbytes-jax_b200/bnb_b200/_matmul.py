@@ -1,0 +1,86 @@
+"""``x @ w.T`` for a quantized ``w``, picking the route.
+
+Mirrors the reference's ``bnb_jax._matmul`` (_matmul.py): same ``matmul``
+signature, shape checks and errors, and the same custom backward
+(``g @ w.dequantize(g.dtype)``, no gradient to ``w``, only the quantized weight
+kept for the backward pass).
+
+Routing. An NF4 weight with a bfloat16/float16 x, K % 32 == 0 and blocksize >=
+32 never materializes: up to GEMV_MAX_M rows of x run the fused GEMV (float32
+weights, closer to the exact product than the fallback), more rows run the
+fused tcgen05 dequantize-GEMM (weights decoded to x's dtype in shared memory,
+the fallback's precision). Everything else is ``x @ w.dequantize(x.dtype).T``
+with the dequantize on the sm_100a kernels.
+"""
+from __future__ import annotations
+
+import torch
+
+from .array import QuantizedArray
+from .kernels.gemv import _CHUNK, GEMV_MAX_M, gemv_nf4, matmul_nf4
+
+__all__ = ["matmul"]
+
+# The tcgen05 GEMM is used above GEMV_MAX_M rows when the library provides it.
+USE_FUSED_GEMM = True
+
+
+def matmul(x: torch.Tensor, w: QuantizedArray) -> torch.Tensor:
+    """``x @ w.T`` for a 2-D quantized weight ``w`` (N, K).
+
+    ``x`` is ``(..., K)``; the result is ``(..., N)`` in ``x.dtype``.
+    Differentiable in ``x``: the gradient is ``g @ w.dequantize(g.dtype)``.
+    No gradient flows to ``w``. (reference _matmul.py:19-43)"""
+    if w.ndim != 2:
+        raise ValueError(f"w must be a 2-D weight, got shape {w.shape}")
+    n, k = w.shape
+    if x.shape[-1] != k:
+        raise ValueError(f"contraction mismatch: x {tuple(x.shape)} @ w.T {w.shape[::-1]}")
+    out = _Matmul2d.apply(x.reshape(-1, k), w)
+    return out.reshape(*x.shape[:-1], n)
+
+
+def _fused_args(w: QuantizedArray):
+    absmax = w.absmax
+    if isinstance(absmax, QuantizedArray):
+        assert absmax.code is not None and absmax.offset is not None
+        assert not isinstance(absmax.absmax, QuantizedArray)
+        return absmax.data, (absmax.absmax, absmax.code, absmax.offset, absmax.blocksize)
+    return absmax, None
+
+
+def _forward(xm: torch.Tensor, w: QuantizedArray) -> torch.Tensor:
+    n = w.shape[0]
+    m = xm.shape[0]
+    if _fused_applies(xm, w):
+        absmax, nested = _fused_args(w)
+        if m <= GEMV_MAX_M:
+            return gemv_nf4(xm, w.data, absmax, n, w.blocksize, nested=nested)
+        if USE_FUSED_GEMM:
+            try:
+                return matmul_nf4(xm, w.data, absmax, n, w.blocksize, nested=nested)
+            except NotImplementedError:
+                pass  # this library build has no tcgen05 GEMM: same result via the fallback
+    return xm @ w.dequantize(xm.dtype).T
+
+
+class _Matmul2d(torch.autograd.Function):
+    """custom_vjp of the reference (_matmul.py:46-71)."""
+
+    @staticmethod
+    def forward(ctx, xm: torch.Tensor, w: QuantizedArray) -> torch.Tensor:
+        ctx.w = w
+        return _forward(xm, w)
+
+    @staticmethod
+    def backward(ctx, g: torch.Tensor):
+        return g @ ctx.w.dequantize(g.dtype), None
+
+
+def _fused_applies(xm: torch.Tensor, w: QuantizedArray) -> bool:
+    return (w.qtype == "nf4"
+            and xm.dtype in (torch.bfloat16, torch.float16)
+            and xm.is_cuda
+            and xm.shape[0] > 0
+            and xm.shape[1] % _CHUNK == 0
+            and w.blocksize >= _CHUNK)

@@ -1,0 +1,284 @@
+"""QuantizedArray: a bitsandbytes-quantized tensor on a CUDA device.
+
+Mirrors the reference's ``bnb_jax.array`` (array.py): the same dataclass
+fields, properties, ``dequantize``, ``from_dict`` and ``quantize`` with the
+same arguments and errors. Leaves are torch tensors; the class is registered as
+a torch pytree node (leaves ``data, absmax, code, offset``; static ``qtype,
+blocksize, shape, dtype``), as the reference registers a JAX pytree.
+
+Differences of mechanism, not of result:
+* a double-quantized array decodes in ONE kernel (the nested scale is decoded
+  in-kernel), bitwise equal to the reference's three-step chain (:95-108);
+* double quantization computes the offset with a deterministic on-device mean
+  and centres the absmax inside the 8-bit quantize kernel (:199-202).
+"""
+from __future__ import annotations
+
+import json
+import math
+from dataclasses import dataclass, field, replace
+from typing import Any, Literal
+
+import numpy as np
+import torch
+import torch.utils._pytree as pytree
+
+from .kernels import (
+    absmax_mean,
+    create_dynamic_map,
+    dequantize_blockwise,
+    dequantize_blockwise_nested,
+    dequantize_nf4,
+    dequantize_nf4_nested,
+    quantize_blockwise,
+    quantize_nf4,
+)
+
+__all__ = ["QType", "QuantizedArray", "quantize"]
+
+QType = Literal["nf4", "8bit"]
+"""``"nf4"``: 4-bit NormalFloat, two codes per byte (bitsandbytes'
+``quantize_4bit``). ``"8bit"``: 8-bit blockwise with a 256-entry codebook
+(``quantize_blockwise``)."""
+
+# bitsandbytes' double quantization: absmax is itself 8-bit quantized in
+# blocks of this size, around its mean (reference array.py:30).
+_NESTED_BLOCKSIZE = 256
+
+_DTYPES = {"float16": torch.float16, "bfloat16": torch.bfloat16, "float32": torch.float32}
+
+
+def _dtype_name(dtype: torch.dtype) -> str:
+    return str(dtype).removeprefix("torch.")
+
+
+@dataclass
+class QuantizedArray:
+    """A blockwise-quantized tensor: codes, per-block scales, and the metadata
+    to decode them.
+
+    Element ``i`` decodes as ``table[code_i] * absmax[i // blocksize] + offset``,
+    with ``table`` the NF4 table or the 8-bit codebook ``code``.
+
+    Attributes:
+        data: uint8 codes for the flattened tensor: ``ceil(size / 2)`` bytes
+            for ``"nf4"`` (high nibble first), ``size`` for ``"8bit"``.
+        absmax: float32 scale per block, or itself a ``"8bit"``
+            QuantizedArray when double-quantized.
+        code: the 256-entry float32 codebook (``"8bit"`` only).
+        offset: float32 scalar added after decoding. Only set on the absmax
+            of a double-quantized array, which is quantized around its mean.
+        qtype: ``"nf4"`` or ``"8bit"``.
+        blocksize: elements per absmax block.
+        shape: shape of the decoded tensor.
+        dtype: default dtype :meth:`dequantize` decodes to.
+    (reference array.py:35-68)
+    """
+
+    data: torch.Tensor
+    absmax: torch.Tensor | QuantizedArray
+    code: torch.Tensor | None
+    offset: torch.Tensor | None
+    qtype: QType = field(metadata={"static": True})
+    blocksize: int = field(metadata={"static": True})
+    shape: tuple[int, ...] = field(metadata={"static": True})
+    dtype: torch.dtype = field(default=torch.bfloat16, metadata={"static": True})
+
+    @property
+    def ndim(self) -> int:
+        return len(self.shape)
+
+    @property
+    def size(self) -> int:
+        return math.prod(self.shape)
+
+    @property
+    def nbytes(self) -> int:
+        """Bytes held by all the leaves: codes, scales, codebook."""
+        return sum(t.numel() * t.element_size() for t in pytree.tree_leaves(self)
+                   if isinstance(t, torch.Tensor))
+
+    @property
+    def double_quantized(self) -> bool:
+        return isinstance(self.absmax, QuantizedArray)
+
+    @property
+    def device(self) -> torch.device:
+        return self.data.device
+
+    def astype(self, dtype) -> QuantizedArray:
+        """Return a copy whose default dequantization dtype is ``dtype``."""
+        return replace(self, dtype=dtype)
+
+    def dequantize(self, dtype=None) -> torch.Tensor:
+        """Decode to a dense tensor of ``dtype`` (default: ``self.dtype``),
+        bitwise equal to bitsandbytes' dequantization (reference array.py:91-109)."""
+        dtype = self.dtype if dtype is None else dtype
+        absmax = self.absmax
+        if self.qtype not in ("nf4", "8bit"):
+            raise NotImplementedError(f"dequantization of {self.qtype!r} is not implemented")
+        if self.qtype == "8bit":
+            assert self.code is not None, "8bit QuantizedArray without a codebook"
+        if isinstance(absmax, QuantizedArray) and _fusable(absmax):
+            assert absmax.code is not None and absmax.offset is not None
+            if self.qtype == "nf4":
+                out = dequantize_nf4_nested(self.data, absmax.data, absmax.absmax, absmax.code,
+                                            absmax.offset, self.blocksize, absmax.blocksize,
+                                            dtype, self.size)
+            else:
+                out = dequantize_blockwise_nested(self.data, self.code, absmax.data, absmax.absmax,
+                                                  absmax.code, absmax.offset, self.blocksize,
+                                                  absmax.blocksize, dtype)
+        else:
+            if isinstance(absmax, QuantizedArray):
+                absmax = absmax.dequantize(torch.float32)
+            if self.qtype == "nf4":
+                out = dequantize_nf4(self.data, absmax, blocksize=self.blocksize, dtype=dtype,
+                                     n=self.size)
+            elif self.offset is not None and dtype == torch.float32:
+                # the nested-absmax decode + its offset, in one pass (:103-108)
+                return dequantize_blockwise(self.data, absmax, self.code, blocksize=self.blocksize,
+                                            dtype=dtype, offset=self.offset).reshape(self.shape)
+            else:
+                out = dequantize_blockwise(self.data, absmax, self.code, blocksize=self.blocksize,
+                                           dtype=dtype)
+        if self.offset is not None:
+            out = out + self.offset.to(out.dtype)
+        return out.reshape(self.shape)
+
+    def __repr__(self) -> str:
+        nested = ", double_quantized" if self.double_quantized else ""
+        return (f"QuantizedArray({self.qtype}, shape={self.shape}, "
+                f"dtype={_dtype_name(self.dtype)}, blocksize={self.blocksize}{nested})")
+
+    @classmethod
+    def from_dict(cls, weight: torch.Tensor, qs_dict: dict[str, Any]) -> QuantizedArray:
+        """Wrap a weight from a HuggingFace bnb-4bit state dict.
+
+        ``weight`` is the packed uint8 tensor; ``qs_dict`` its quant state
+        entries with the weight's key prefix stripped (``absmax``,
+        ``quant_map``, ``nested_*``, and either the unpacked metadata or the
+        packed ``quant_state.bitsandbytes__nf4`` JSON tensor).
+        (reference array.py:116-163)
+        """
+        qs_dict = dict(qs_dict)  # make a copy to avoid mutating input
+        packed = [k for k, v in qs_dict.items() if "quant_state" in k and isinstance(v, torch.Tensor)]
+        if "quant_type" not in qs_dict:
+            if len(packed) != 1:
+                raise ValueError(f"expected exactly one packed quant_state item, found {packed}")
+            qs_dict.update(_unpack_tensor_to_dict(qs_dict.pop(packed[0])))
+        qs_dict = {k.split(".")[-1]: v for k, v in qs_dict.items()}  # strip prefixes
+
+        if qs_dict["quant_type"] != "nf4":
+            raise NotImplementedError(f"quant_type {qs_dict['quant_type']!r} is not supported")
+
+        absmax = qs_dict["absmax"]
+        if "nested_absmax" in qs_dict:
+            assert qs_dict["nested_dtype"] == "float32", qs_dict["nested_dtype"]
+            absmax = cls(
+                data=absmax.reshape(-1),
+                absmax=qs_dict["nested_absmax"].reshape(-1),
+                code=qs_dict["nested_quant_map"].reshape(-1),
+                offset=torch.tensor(float(qs_dict["nested_offset"]), dtype=torch.float32,
+                                    device=absmax.device),
+                qtype="8bit",
+                blocksize=int(qs_dict["nested_blocksize"]),
+                shape=tuple(absmax.shape),
+                dtype=torch.float32,
+            )
+        else:
+            absmax = absmax.reshape(-1)
+
+        # quant_map, the NF4 table, is not kept: like bitsandbytes' kernel,
+        # dequantization uses the built-in one
+        return cls(
+            data=weight.reshape(-1),
+            absmax=absmax,
+            code=None,
+            offset=None,
+            qtype="nf4",
+            blocksize=int(qs_dict["blocksize"]),
+            shape=tuple(int(s) for s in qs_dict["shape"]),
+            dtype=_DTYPES[qs_dict["dtype"]],
+        )
+
+
+def _fusable(absmax: QuantizedArray) -> bool:
+    """A nested absmax the one-pass kernels decode: 8-bit, centred, flat scales."""
+    return (absmax.qtype == "8bit" and absmax.offset is not None and absmax.code is not None
+            and isinstance(absmax.absmax, torch.Tensor))
+
+
+def _flatten(qa: QuantizedArray):
+    return [qa.data, qa.absmax, qa.code, qa.offset], (qa.qtype, qa.blocksize, qa.shape, qa.dtype)
+
+
+def _unflatten(leaves, ctx):
+    qtype, blocksize, shape, dtype = ctx
+    data, absmax, code, offset = leaves
+    return QuantizedArray(data, absmax, code, offset, qtype, blocksize, shape, dtype)
+
+
+pytree.register_pytree_node(
+    QuantizedArray, _flatten, _unflatten,
+    serialized_type_name="bnb_b200.array.QuantizedArray",
+)
+
+
+def quantize(
+    array: torch.Tensor,
+    qtype: QType = "nf4",
+    blocksize: int = 64,
+    *,
+    code: torch.Tensor | None = None,
+    double_quant: bool = False,
+    dtype=None,
+) -> QuantizedArray:
+    """Quantize a tensor, bitwise as bitsandbytes does.
+
+    Args:
+        array: float16, bfloat16 or float32 CUDA tensor, any shape.
+        qtype: ``"nf4"`` (``quantize_4bit``) or ``"8bit"`` (``quantize_blockwise``).
+        blocksize: power of two; bitsandbytes supports 32-4096 for nf4 and
+            64-4096 for 8bit.
+        code: the codebook for ``"8bit"`` (default :func:`create_dynamic_map`).
+        double_quant: also quantize the absmax values, as bitsandbytes'
+            ``compress_statistics=True``. The offset is their mean, whose float32
+            rounding can differ from torch's, so this part is close to
+            bitsandbytes but not bitwise.
+        dtype: default dequantization dtype (default: ``array.dtype``).
+    (reference array.py:166-213)
+    """
+    x = array.reshape(-1)
+    if qtype == "nf4":
+        data, absmax = quantize_nf4(x, blocksize=blocksize)
+        code = None
+    elif qtype == "8bit":
+        code = (create_dynamic_map(device=x.device) if code is None
+                else torch.as_tensor(code, dtype=torch.float32).reshape(-1).to(x.device))
+        data, absmax = quantize_blockwise(x, code, blocksize=blocksize)
+    else:
+        raise NotImplementedError(f"quantization to {qtype!r} is not implemented")
+
+    if double_quant:
+        offset = absmax_mean(absmax)
+        code2 = create_dynamic_map(device=x.device)
+        q2, absmax2 = quantize_blockwise(absmax, code2, blocksize=_NESTED_BLOCKSIZE, offset=offset)
+        absmax = QuantizedArray(data=q2, absmax=absmax2, code=code2, offset=offset, qtype="8bit",
+                                blocksize=_NESTED_BLOCKSIZE, shape=tuple(absmax.shape),
+                                dtype=torch.float32)
+
+    return QuantizedArray(
+        data=data,
+        absmax=absmax,
+        code=code,
+        offset=None,
+        qtype=qtype,
+        blocksize=blocksize,
+        shape=tuple(array.shape),
+        dtype=array.dtype if dtype is None else dtype,
+    )
+
+
+def _unpack_tensor_to_dict(tensor: torch.Tensor) -> dict[str, Any]:
+    return json.loads(bytes(np.asarray(tensor.detach().cpu().numpy(), dtype=np.uint8)).decode("utf-8"))

@@ -1,0 +1,125 @@
+"""Fused NF4 dequantize-matmul: ``y = x @ W.T`` with W kept quantized.
+
+Mirrors the reference's bnb_jax.kernels.gemv (kernels/gemv.py): ``gemv_nf4``
+with the same arguments and errors, its ``cutejax.call`` (:195-204) replaced by
+``bnbq_gemv_nf4``. Numerics as the reference: float32 partial sums per
+32-element chunk, each block's scale applied once per chunk, one rounding to
+x's dtype; a one-hot x returns the dequantized weights bitwise.
+
+``matmul_nf4`` (extension) takes any number of rows: the GEMV up to
+``GEMV_MAX_M``, the tcgen05 fused dequantize-GEMM above it.
+"""
+from __future__ import annotations
+
+import torch
+
+from .. import _lib
+from .dequantize import _log2_blocksize
+
+_CHUNK = 32
+GEMV_MAX_M = _lib.GEMV_MAX_M
+
+
+def _rows_per_warp(m: int) -> int:
+    """The reference's tuning knob (kernels/gemv.py:207-215), kept for API
+    compatibility; the sm_100a kernel chooses its own rows per CTA."""
+    return 2 if m <= 2 else 4
+
+
+def _prepare(x, data, absmax, n_rows, blocksize, nested, what):
+    if x.dim() != 2:
+        raise ValueError(f"x must be 2-D (M, K), got shape {tuple(x.shape)}")
+    m, k = x.shape
+    if x.dtype not in (torch.bfloat16, torch.float16):
+        raise NotImplementedError(f"{what} of {x.dtype} x is not implemented")
+    if k % _CHUNK:
+        raise ValueError(f"K must be a multiple of {_CHUNK}, got {k}")
+    _log2_blocksize(blocksize)
+    if blocksize < _CHUNK:
+        raise ValueError(f"blocksize must be >= {_CHUNK}, got {blocksize}")
+    assert data.dtype == torch.uint8 and data.numel() * 2 == n_rows * k, (tuple(data.shape), n_rows, k)
+    _lib.require_cuda(x, data, absmax)
+    xs = _lib.aligned(x)
+    w = _lib.aligned(data.reshape(-1))
+    if nested is None:
+        assert absmax.dtype == torch.float32, absmax.dtype
+        a = _lib.aligned(absmax.reshape(-1), 4)
+        extra = (a, None, None, None, None, 0)
+    else:
+        absmax2, code2, offset, blocksize2 = nested
+        assert absmax.dtype == torch.uint8, absmax.dtype
+        _log2_blocksize(blocksize2)
+        aq = _lib.aligned(absmax.reshape(-1))
+        a2 = _lib.aligned(absmax2.reshape(-1).to(torch.float32), 4)
+        c2 = _lib.aligned(torch.as_tensor(code2, dtype=torch.float32).reshape(-1).to(x.device), 4)
+        off = _lib.aligned(torch.as_tensor(offset, dtype=torch.float32).reshape(1).to(x.device), 4)
+        extra = (None, aq, a2, c2, off, blocksize2)
+    return xs, w, extra
+
+
+def _run(entry, x, data, absmax, n_rows, blocksize, nested, absmax2_block0, out):
+    xs, w, (a, aq, a2, c2, off, bs2) = _prepare(x, data, absmax, n_rows, blocksize, nested, entry)
+    m, k = xs.shape
+    if out is None:
+        out = torch.empty((m, n_rows), dtype=x.dtype, device=x.device)
+    ldy = out.stride(0)
+    assert out.dtype == x.dtype and out.stride(1) == 1 and out.shape == (m, n_rows)
+    with torch.cuda.device(x.device):
+        _lib.call(entry, _lib.DTYPE_CODE[x.dtype], xs.data_ptr(), m, k, w.data_ptr(), n_rows,
+                  blocksize, _lib.ptr(a), _lib.ptr(aq), _lib.ptr(a2), _lib.ptr(c2), _lib.ptr(off),
+                  bs2, absmax2_block0, out.data_ptr(), ldy, _lib.stream_of(xs))
+    return out
+
+
+def gemv_nf4(
+    x: torch.Tensor,
+    data: torch.Tensor,
+    absmax: torch.Tensor,
+    n_rows: int,
+    blocksize: int,
+    *,
+    nested: tuple[torch.Tensor, torch.Tensor, torch.Tensor, int] | None = None,
+    rows_per_warp: int | None = None,
+    absmax2_block0: int = 0,
+    out: torch.Tensor | None = None,
+) -> torch.Tensor:
+    """``x @ W.T`` for an NF4 weight W (n_rows, K), never materialized.
+
+    Args:
+        x: float16 or bfloat16 ``(M, K)``, ``1 <= M <= GEMV_MAX_M``,
+            ``K % 32 == 0``; the result is ``(M, n_rows)`` of the same dtype.
+        data: the packed NF4 codes of the row-major flattened W.
+        absmax: float32 scale per block, or, if ``nested`` is given, the
+            uint8 codes of the double-quantized scales.
+        blocksize: power of two >= 32.
+        nested: ``(absmax2, code2, offset, blocksize2)`` of a double-quantized
+            absmax.
+        rows_per_warp: accepted for compatibility; ignored.
+        absmax2_block0: global index of this weight's first block within
+            ``absmax2``'s indexing (non-zero for a row shard).
+        out: optional ``(M, n_rows)`` output with unit column stride (a row
+            stride larger than n_rows writes into a wider buffer).
+    (reference kernels/gemv.py:148-204)"""
+    del rows_per_warp
+    if not 0 < x.shape[0] <= GEMV_MAX_M:
+        raise ValueError(f"gemv_nf4 takes 1..{GEMV_MAX_M} rows of x, got {x.shape[0]}")
+    return _run("bnbq_gemv_nf4", x, data, absmax, n_rows, blocksize, nested, absmax2_block0, out)
+
+
+def matmul_nf4(
+    x: torch.Tensor,
+    data: torch.Tensor,
+    absmax: torch.Tensor,
+    n_rows: int,
+    blocksize: int,
+    *,
+    nested: tuple[torch.Tensor, torch.Tensor, torch.Tensor, int] | None = None,
+    absmax2_block0: int = 0,
+    out: torch.Tensor | None = None,
+) -> torch.Tensor:
+    """``x @ W.T`` for any M >= 1: the GEMV up to GEMV_MAX_M rows, the fused
+    tcgen05 dequantize-GEMM above (weights decoded to x's dtype in shared
+    memory: the precision of the reference's fallback ``x @ w.dequantize().T``)."""
+    if x.shape[0] < 1:
+        raise ValueError("matmul_nf4 needs at least one row of x")
+    return _run("bnbq_matmul_nf4", x, data, absmax, n_rows, blocksize, nested, absmax2_block0, out)

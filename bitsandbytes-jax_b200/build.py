@@ -1,0 +1,94 @@
+"""Build libbnbq.so, the sm_100a kernels behind include/bnbq.h.
+
+    python bitsandbytes-jax_b200/build.py [--force] [-j N]
+
+Each csrc/*.cu is compiled with nvcc for sm_100a only
+(-gencode arch=compute_100a,code=sm_100a), with the CUDA runtime linked
+statically, then linked into bnb_b200/libbnbq.so next to the Python package
+that loads it. Nothing is built at import time and there is no JIT cache:
+the .so travels with the source tree. Without --force, sources older than the
+library are not rebuilt.
+"""
+from __future__ import annotations
+
+import argparse
+import os
+import shutil
+import subprocess
+from concurrent.futures import ThreadPoolExecutor
+from pathlib import Path
+
+HERE = Path(__file__).resolve().parent
+CSRC = HERE / "csrc"
+INCLUDE = HERE.parent / "include"
+OUT = HERE / "bnb_b200" / "libbnbq.so"
+BUILD = HERE / "_build"
+
+NVCC_FLAGS = [
+    "-gencode", "arch=compute_100a,code=sm_100a",
+    "-O3", "-lineinfo", "-std=c++17",
+    "-Xcompiler", "-fPIC", "-Xcompiler", "-fvisibility=hidden",
+    "--expt-relaxed-constexpr",
+    f"-I{INCLUDE}",
+]
+
+
+def nvcc() -> str:
+    for cand in (os.environ.get("NVCC"), shutil.which("nvcc"), "/usr/local/cuda/bin/nvcc"):
+        if cand and Path(cand).exists():
+            return cand
+    raise RuntimeError("nvcc not found")
+
+
+def _sources() -> list[Path]:
+    return sorted(CSRC.glob("*.cu"))
+
+
+def _deps() -> list[Path]:
+    return _sources() + sorted(CSRC.glob("*.cuh")) + sorted(INCLUDE.glob("*.h"))
+
+
+def up_to_date() -> bool:
+    if not OUT.exists():
+        return False
+    t = OUT.stat().st_mtime
+    return all(p.stat().st_mtime <= t for p in _deps())
+
+
+def build(force: bool = False, jobs: int = 0, verbose_ptxas: bool = False) -> Path:
+    if not force and up_to_date():
+        return OUT
+    BUILD.mkdir(exist_ok=True)
+    cc = nvcc()
+    extra = ["-Xptxas", "-v"] if verbose_ptxas else []
+
+    def compile_one(src: Path) -> Path:
+        obj = BUILD / (src.stem + ".o")
+        cmd = [cc, *NVCC_FLAGS, *extra, "-c", str(src), "-o", str(obj)]
+        r = subprocess.run(cmd, capture_output=True, text=True)
+        if r.returncode != 0:
+            raise RuntimeError(f"nvcc failed on {src.name}:\n{r.stdout}\n{r.stderr}")
+        if verbose_ptxas:
+            print(r.stderr)
+        return obj
+
+    jobs = jobs or min(8, os.cpu_count() or 1)
+    with ThreadPoolExecutor(jobs) as ex:
+        objs = list(ex.map(compile_one, _sources()))
+    tmp = OUT.with_suffix(".so.tmp")
+    cmd = [cc, "-shared", "-gencode", "arch=compute_100a,code=sm_100a", "--cudart", "static",
+           *map(str, objs), "-o", str(tmp)]
+    r = subprocess.run(cmd, capture_output=True, text=True)
+    if r.returncode != 0:
+        raise RuntimeError(f"link failed:\n{r.stdout}\n{r.stderr}")
+    os.replace(tmp, OUT)
+    return OUT
+
+
+if __name__ == "__main__":
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--force", action="store_true")
+    ap.add_argument("-j", type=int, default=0)
+    ap.add_argument("--ptxas-v", action="store_true")
+    args = ap.parse_args()
+    print(build(force=args.force, jobs=args.j, verbose_ptxas=args.ptxas_v))

@@ -1,0 +1,98 @@
+// bnbq_abi.cu -- device checks, status strings, diagnostics and the matmul router.
+#include <mutex>
+
+#include "bnbq_common.cuh"
+
+namespace bnbq {
+
+int gemv_validate(int dtype, const void* x, int32_t m, int32_t k, const uint8_t* w, int64_t n_rows,
+                  int32_t blocksize, const float* absmax, const uint8_t* absmax_q,
+                  const float* absmax2, const float* code2, const float* offset, int32_t blocksize2,
+                  void* y, int64_t ldy);
+int gemv_launch(int dtype, const void* x, int32_t m, int32_t k, const uint8_t* w, int64_t n_rows,
+                int32_t blocksize, const float* absmax, const uint8_t* absmax_q,
+                const float* absmax2, const float* code2, const float* offset, int32_t blocksize2,
+                int64_t absmax2_block0, void* y, int64_t ldy, cudaStream_t s);
+int gemm_launch(int dtype, const void* x, int32_t m, int32_t k, const uint8_t* w, int64_t n_rows,
+                int32_t blocksize, const float* absmax, const uint8_t* absmax_q,
+                const float* absmax2, const float* code2, const float* offset, int32_t blocksize2,
+                int64_t absmax2_block0, void* y, int64_t ldy, cudaStream_t s);
+
+namespace {
+constexpr int kMaxDevices = 64;
+std::once_flag g_once[kMaxDevices];
+DeviceInfo g_info[kMaxDevices];
+int g_status[kMaxDevices];
+
+__global__ void rcp_kernel(const float* in, float* out, int64_t n) {
+  for (int64_t i = int64_t(blockIdx.x) * blockDim.x + threadIdx.x; i < n;
+       i += int64_t(gridDim.x) * blockDim.x)
+    out[i] = rcp_approx_ftz(in[i]);
+}
+}  // namespace
+
+// Queried once per device; the kernels are built for sm_100a only.
+int device_info(DeviceInfo* out) {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return BNBQ_ERR_CUDA;
+  std::call_once(g_once[dev], [dev] {
+    DeviceInfo di;
+    int st = BNBQ_OK;
+    if (cudaDeviceGetAttribute(&di.sm_count, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess ||
+        cudaDeviceGetAttribute(&di.cc_major, cudaDevAttrComputeCapabilityMajor, dev) != cudaSuccess ||
+        cudaDeviceGetAttribute(&di.cc_minor, cudaDevAttrComputeCapabilityMinor, dev) != cudaSuccess)
+      st = BNBQ_ERR_CUDA;
+    else if (di.cc_major != 10 || di.cc_minor != 0)
+      st = BNBQ_ERR_DEVICE;
+    g_info[dev] = di;
+    g_status[dev] = st;
+  });
+  *out = g_info[dev];
+  return g_status[dev];
+}
+
+}  // namespace bnbq
+
+using namespace bnbq;
+
+extern "C" int bnbq_matmul_nf4(int dtype, const void* x, int32_t m, int32_t k, const uint8_t* w,
+                               int64_t n_rows, int32_t blocksize, const float* absmax,
+                               const uint8_t* absmax_q, const float* absmax2, const float* code2,
+                               const float* offset, int32_t blocksize2, int64_t absmax2_block0,
+                               void* y, int64_t ldy, void* stream) {
+  if (int st = gemv_validate(dtype, x, m, k, w, n_rows, blocksize, absmax, absmax_q, absmax2, code2,
+                             offset, blocksize2, y, ldy))
+    return st;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (m <= BNBQ_GEMV_MAX_M)
+    return gemv_launch(dtype, x, m, k, w, n_rows, blocksize, absmax, absmax_q, absmax2, code2,
+                       offset, blocksize2, absmax2_block0, y, ldy, s);
+  return gemm_launch(dtype, x, m, k, w, n_rows, blocksize, absmax, absmax_q, absmax2, code2,
+                     offset, blocksize2, absmax2_block0, y, ldy, s);
+}
+
+extern "C" int bnbq_rcp_approx_ftz(const float* in, float* out, int64_t n, void* stream) {
+  if (n < 0 || (n > 0 && (!in || !out))) return BNBQ_ERR_INVALID;
+  if (!aligned(in, 4) || !aligned(out, 4)) return BNBQ_ERR_MISALIGNED;
+  if (n == 0) return BNBQ_OK;
+  DeviceInfo di;
+  if (int st = device_info(&di)) return st;
+  int64_t grid = (n + 255) / 256;
+  if (grid > int64_t(di.sm_count) * 8) grid = int64_t(di.sm_count) * 8;
+  rcp_kernel<<<dim3(unsigned(grid)), 256, 0, static_cast<cudaStream_t>(stream)>>>(in, out, n);
+  return launch_status();
+}
+
+extern "C" const char* bnbq_error_string(int status) {
+  switch (status) {
+    case BNBQ_OK: return "ok";
+    case BNBQ_ERR_INVALID: return "invalid argument";
+    case BNBQ_ERR_UNSUPPORTED: return "unsupported dtype or shape";
+    case BNBQ_ERR_MISALIGNED: return "misaligned pointer";
+    case BNBQ_ERR_CUDA: return "CUDA error";
+    case BNBQ_ERR_DEVICE: return "device is not sm_100 (B200)";
+    default: return "unknown status";
+  }
+}
+
+extern "C" int bnbq_version(void) { return 100; }

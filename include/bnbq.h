@@ -1,0 +1,169 @@
+/*
+ * bnbq.h -- C ABI of the B200 (sm_100a) blockwise-quantization kernels.
+ *
+ * This is the boundary that replaces the reference's `cutejax.call(...)`
+ * custom calls (bnb_jax 0.2.0, src/bnb_jax/kernels/{quantize,dequantize,gemv}.py).
+ * Every entry point takes raw device pointers, element counts and a CUDA
+ * stream (as `void*`, i.e. a `cudaStream_t`), enqueues its kernels on that
+ * stream and returns immediately: no allocation, no host synchronisation.
+ * The caller owns every buffer. Outputs are written at their exact sizes
+ * (ceil(n/2) NF4 bytes, n 8-bit bytes, ceil(n/bs) absmax values, n decoded
+ * elements): the reference's host-side pad and slice copies do not exist here.
+ *
+ * Numerics follow bitsandbytes' fast-math arithmetic exactly as the reference
+ * restates it (src/bnb_jax/kernels/_ptx.py:15-33): mul.ftz.f32, abs/max.ftz,
+ * rcp.approx.ftz.f32, round-to-nearest conversions. Codes, absmax and decoded
+ * values are bitwise those of the reference.
+ *
+ * Pointer alignment: element buffers (x, out, y) and code buffers must be
+ * 16-byte aligned; absmax / codebook pointers 4-byte aligned. A misaligned
+ * pointer returns BNBQ_ERR_MISALIGNED without launching anything.
+ *
+ * Return value: BNBQ_OK (0) or a negative status; bnbq_error_string() names it.
+ * Nothing here calls exit(), traps on the device, or leaves work half-queued
+ * on an argument error.
+ */
+#ifndef BNBQ_H_
+#define BNBQ_H_
+
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define BNBQ_API __attribute__((visibility("default")))
+#else
+#define BNBQ_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* element types (the reference's _DTYPES, kernels/quantize.py:35) */
+enum bnbq_dtype { BNBQ_F32 = 0, BNBQ_F16 = 1, BNBQ_BF16 = 2 };
+
+enum bnbq_status {
+  BNBQ_OK = 0,
+  BNBQ_ERR_INVALID = -1,     /* bad size / blocksize / null pointer (ValueError in Python) */
+  BNBQ_ERR_UNSUPPORTED = -2, /* dtype or shape outside what the kernel implements (NotImplementedError) */
+  BNBQ_ERR_MISALIGNED = -3,  /* a pointer breaks the alignment rule above */
+  BNBQ_ERR_CUDA = -4,        /* a CUDA runtime call or launch failed */
+  BNBQ_ERR_DEVICE = -5       /* the current device is not sm_100 */
+};
+
+/* Largest batch the CUDA-core GEMV handles; bnbq_matmul_nf4 uses the tcgen05
+ * GEMM above it. Same value as the reference's GEMV_MAX_M (kernels/gemv.py:42). */
+#define BNBQ_GEMV_MAX_M 20
+
+/* ---------------------------------------------------------------- quantize */
+
+/* NF4 blockwise quantize of n elements of `dtype` at `x`.
+ * q: ceil(n/2) bytes, two codes per byte, high nibble first; absmax: ceil(n/bs) floats.
+ * blocksize: power of two, 8 <= bs <= 4096 (the reference accepts any power of
+ * two >= 8, kernels/dequantize.py:87-90; bitsandbytes uses 32..4096).
+ * Replaces: cutejax.call(_quant_launch, ..., nf4=True) at kernels/quantize.py:226-233
+ * behind quantize_nf4 (kernels/quantize.py:238-248). A partial last block reads
+ * as zero-padded, as the reference's jnp.pad does (kernels/quantize.py:221-225). */
+BNBQ_API int bnbq_quantize_nf4(int dtype, const void* x, int64_t n, int32_t blocksize,
+                      uint8_t* q, float* absmax, void* stream);
+
+/* 8-bit blockwise quantize with a 256-entry float32 codebook `code` (device).
+ * q: n bytes; absmax: ceil(n/bs) floats. blocksize: power of two, 8..4096.
+ * `offset` (device, one float, may be NULL): when given, every element is first
+ * replaced by fl32(x - *offset) -- the centring step of double quantization,
+ * array.py:200-201 (`quantize(absmax - offset, "8bit", 256)`), fused here.
+ * Replaces: cutejax.call(_quant_launch, ..., nf4=False) at kernels/quantize.py:226-233
+ * behind quantize_blockwise (kernels/quantize.py:251-262). */
+BNBQ_API int bnbq_quantize_blockwise(int dtype, const void* x, int64_t n, int32_t blocksize,
+                            const float* code, const float* offset,
+                            uint8_t* q, float* absmax, void* stream);
+
+/* offset[0] = mean(absmax[0..nb)) as float32 (double accumulation, one rounding;
+ * deterministic). Replaces the XLA reduction `jnp.mean(absmax)` at array.py:200. */
+BNBQ_API int bnbq_absmax_mean(const float* absmax, int64_t nb, float* offset, void* stream);
+
+/* -------------------------------------------------------------- dequantize */
+
+/* out[i] = dtype(mul.ftz(NF4_TABLE[nibble_i], absmax[i / bs])), i < n.
+ * Replaces: cutejax.call(_dequant_launch, ..., nf4=True) at kernels/dequantize.py:110-116
+ * behind dequantize_nf4 (kernels/dequantize.py:120-134). */
+BNBQ_API int bnbq_dequantize_nf4(int dtype, const uint8_t* q, const float* absmax,
+                        int64_t n, int32_t blocksize, void* out, void* stream);
+
+/* out[i] = dtype(mul.ftz(code[q_i], absmax[i / bs])) (+ *offset, float32 add, when
+ * offset != NULL and dtype is F32: the offset add of a nested absmax, array.py:107-108).
+ * Replaces: cutejax.call(_dequant_launch, ..., nf4=False) at kernels/dequantize.py:110-116
+ * behind dequantize_blockwise (kernels/dequantize.py:137-148). */
+BNBQ_API int bnbq_dequantize_blockwise(int dtype, const uint8_t* q, const float* absmax,
+                              const float* code, int64_t n, int32_t blocksize,
+                              const float* offset, void* out, void* stream);
+
+/* Double-quantized NF4 decode in one pass: the block scale is decoded in-kernel as
+ *   a_b = fl32(mul.ftz(code2[absmax_q[b]], absmax2[b / bs2]) + offset[0])
+ * and out[i] = dtype(mul.ftz(NF4_TABLE[nibble_i], a_{i/bs})).
+ * Bitwise equal to the reference's three-step chain QuantizedArray.dequantize
+ * (array.py:95-104: nested 8-bit dequantize, XLA add of the offset, NF4 dequantize). */
+BNBQ_API int bnbq_dequantize_nf4_nested(int dtype, const uint8_t* q, const uint8_t* absmax_q,
+                               const float* absmax2, const float* code2, const float* offset,
+                               int64_t n, int32_t blocksize, int32_t blocksize2,
+                               void* out, void* stream);
+
+/* Double-quantized 8-bit decode in one pass (same nested scale decode as above, then
+ * the 8-bit codebook `code`). Replaces array.py:95-97 + :103-104 for qtype "8bit". */
+BNBQ_API int bnbq_dequantize_blockwise_nested(int dtype, const uint8_t* q, const float* code,
+                                     const uint8_t* absmax_q, const float* absmax2,
+                                     const float* code2, const float* offset,
+                                     int64_t n, int32_t blocksize, int32_t blocksize2,
+                                     void* out, void* stream);
+
+/* ------------------------------------------------------------------ matmul */
+
+/* y[m, j] = sum_k x[m, k] * W[j, k] for an NF4 weight W of n_rows x k, never
+ * materialised. x: m x k row-major, dtype F16 or BF16; y: m x n_rows of the same
+ * dtype with row stride ldy (>= n_rows) elements.
+ * w: the weight's packed codes, row-major, n_rows*k/2 bytes (high nibble first).
+ * Scales: `absmax` (n_rows*k/bs floats) when absmax_q == NULL; otherwise the
+ * double-quantized triple absmax_q (n_rows*k/bs bytes), absmax2, code2 (256) and
+ * offset (1 float), with absmax2 indexed by the GLOBAL block number
+ * (absmax2_block0 + local block) / blocksize2, so that a row shard of a weight can
+ * pass its own slices of w / absmax_q and the whole absmax2.
+ * Numerics: per block, t = sum table[q]*x in float32; acc += a*t; one rounding
+ * to dtype at the end (kernels/gemv.py:97-123). A one-hot x returns the decoded
+ * weights bitwise.
+ * Requires k % 32 == 0 and 32 <= blocksize (a power of two), like the reference
+ * (kernels/gemv.py:172-181). bnbq_gemv_nf4 handles 1 <= m <= BNBQ_GEMV_MAX_M.
+ * Replaces: cutejax.call(_gemv_launch, ...) at kernels/gemv.py:195-204 (gemv_nf4). */
+BNBQ_API int bnbq_gemv_nf4(int dtype, const void* x, int32_t m, int32_t k,
+                  const uint8_t* w, int64_t n_rows, int32_t blocksize,
+                  const float* absmax, const uint8_t* absmax_q, const float* absmax2,
+                  const float* code2, const float* offset, int32_t blocksize2,
+                  int64_t absmax2_block0, void* y, int64_t ldy, void* stream);
+
+/* Same contract for any m >= 1: the GEMV for m <= BNBQ_GEMV_MAX_M, the tcgen05/TMEM
+ * fused dequantize-GEMM above it (weights decoded to dtype in shared memory, i.e.
+ * the reference fallback's precision `x @ w.dequantize(x.dtype).T`, _matmul.py:58-59,
+ * accumulated in float32 in tensor memory).
+ * Replaces: the router _matmul_2d (_matmul.py:46-60) for NF4 weights. */
+BNBQ_API int bnbq_matmul_nf4(int dtype, const void* x, int32_t m, int32_t k,
+                    const uint8_t* w, int64_t n_rows, int32_t blocksize,
+                    const float* absmax, const uint8_t* absmax_q, const float* absmax2,
+                    const float* code2, const float* offset, int32_t blocksize2,
+                    int64_t absmax2_block0, void* y, int64_t ldy, void* stream);
+
+/* ------------------------------------------------------------ diagnostics */
+
+/* out[i] = rcp.approx.ftz.f32(in[i]): the hardware reciprocal the quantize kernels
+ * use for 1/absmax (kernels/_ptx.py:20-22). Lets a CPU checker take the device's
+ * own reciprocal instead of modelling it. */
+BNBQ_API int bnbq_rcp_approx_ftz(const float* in, float* out, int64_t n, void* stream);
+
+/* Human-readable name of a status code (static storage). */
+BNBQ_API const char* bnbq_error_string(int status);
+
+/* Library version: major*10000 + minor*100 + patch. */
+BNBQ_API int bnbq_version(void);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* BNBQ_H_ */

@@ -1,0 +1,72 @@
+"""The C ABI library loads and exports every entry point include/bnbq.h
+declares; host-only entry points answer without a GPU. No compute is called."""
+from __future__ import annotations
+
+import ctypes
+import re
+from pathlib import Path
+
+import pytest
+
+ROOT = Path(__file__).resolve().parents[1]
+HEADER = ROOT / "include" / "bnbq.h"
+LIB = ROOT / "bitsandbytes-jax_b200" / "bnb_b200" / "libbnbq.so"
+
+
+def declared_symbols() -> list[str]:
+    text = HEADER.read_text()
+    return sorted(set(re.findall(r"BNBQ_API\s+[\w\s\*]*?\b(bnbq_\w+)\s*\(", text)))
+
+
+def test_header_declares_the_boundary():
+    syms = declared_symbols()
+    for s in ["bnbq_quantize_nf4", "bnbq_quantize_blockwise", "bnbq_dequantize_nf4",
+              "bnbq_dequantize_blockwise", "bnbq_dequantize_nf4_nested", "bnbq_gemv_nf4",
+              "bnbq_matmul_nf4", "bnbq_error_string"]:
+        assert s in syms
+
+
+@pytest.fixture(scope="module")
+def lib():
+    if not LIB.exists():
+        pytest.fail(f"{LIB} not built (python bitsandbytes-jax_b200/build.py)")
+    return ctypes.CDLL(str(LIB))
+
+
+def test_library_exports_every_declared_symbol(lib):
+    missing = [s for s in declared_symbols() if not hasattr(lib, s)]
+    assert not missing, missing
+
+
+def test_python_binding_covers_the_header():
+    from bnb_b200 import _lib
+    assert sorted(_lib.exported_symbols()) == declared_symbols()
+
+
+def test_host_only_entry_points(lib):
+    lib.bnbq_error_string.restype = ctypes.c_char_p
+    assert lib.bnbq_error_string(0) == b"ok"
+    assert b"misaligned" in lib.bnbq_error_string(-3)
+    assert lib.bnbq_error_string(12345) == b"unknown status"
+    assert lib.bnbq_version() >= 100
+
+
+def test_argument_errors_need_no_device(lib):
+    """Bad arguments are rejected before any CUDA call (status, no launch)."""
+    P = ctypes.c_void_p
+    f = lib.bnbq_quantize_nf4
+    f.argtypes = [ctypes.c_int, P, ctypes.c_int64, ctypes.c_int32, P, P, P]
+    assert f(7, None, 16, 64, None, None, None) == -2        # unknown dtype
+    assert f(0, None, 16, 48, None, None, None) == -1        # blocksize not a power of two
+    assert f(0, None, 16, 64, None, None, None) == -1        # null pointers
+    assert f(0, P(8), 16, 64, P(16), P(16), None) == -3      # x not 16-byte aligned
+    assert f(0, None, 0, 64, None, None, None) == 0          # empty input: nothing to do
+    g = lib.bnbq_gemv_nf4
+    g.argtypes = [ctypes.c_int, P, ctypes.c_int32, ctypes.c_int32, P, ctypes.c_int64, ctypes.c_int32,
+                  P, P, P, P, P, ctypes.c_int32, ctypes.c_int64, P, ctypes.c_int64, P]
+    args = [2, P(256), 1, 100, P(256), 8, 64, P(256), None, None, None, None, 0, 0, P(256), 8, None]
+    assert g(*args) == -1                                     # K % 32 != 0
+    args[3] = 128; args[0] = 0
+    assert g(*args) == -2                                     # float32 x
+    args[0] = 2; args[2] = 21
+    assert g(*args) == -1                                     # M above the GEMV limit
