@@ -34,6 +34,7 @@ _SIGNATURES = {
     "bnbq_matmul_nf4": "iPiiPliPPPPPilPlP",
     "bnbq_rcp_approx_ftz": "PPlP",
     "bnbq_version": "",
+    "bnbq_wait_timeouts": "P",
 }
 _KIND = {"i": C.c_int32, "l": C.c_int64, "P": C.c_void_p, "p": C.c_void_p}
 
@@ -109,6 +110,13 @@ def aligned(t: torch.Tensor, a: int = 16) -> torch.Tensor:
     if t.numel() and t.data_ptr() % a:
         t = t.clone()
     return t
+
+
+def wait_timeouts() -> int:
+    """Device-side bounded waits that expired so far (0 in normal operation)."""
+    n = C.c_uint32(0)
+    check(lib().bnbq_wait_timeouts(C.byref(n)), "bnbq_wait_timeouts")
+    return int(n.value)
 
 
 def call(name: str, *args) -> None:

@@ -13,6 +13,7 @@ int gemv_launch(int dtype, const void* x, int32_t m, int32_t k, const uint8_t* w
                 int32_t blocksize, const float* absmax, const uint8_t* absmax_q,
                 const float* absmax2, const float* code2, const float* offset, int32_t blocksize2,
                 int64_t absmax2_block0, void* y, int64_t ldy, cudaStream_t s);
+int gemv_wait_timeouts(unsigned int* out);
 int gemm_launch(int dtype, const void* x, int32_t m, int32_t k, const uint8_t* w, int64_t n_rows,
                 int32_t blocksize, const float* absmax, const uint8_t* absmax_q,
                 const float* absmax2, const float* code2, const float* offset, int32_t blocksize2,
@@ -40,7 +41,8 @@ int device_info(DeviceInfo* out) {
     int st = BNBQ_OK;
     if (cudaDeviceGetAttribute(&di.sm_count, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess ||
         cudaDeviceGetAttribute(&di.cc_major, cudaDevAttrComputeCapabilityMajor, dev) != cudaSuccess ||
-        cudaDeviceGetAttribute(&di.cc_minor, cudaDevAttrComputeCapabilityMinor, dev) != cudaSuccess)
+        cudaDeviceGetAttribute(&di.cc_minor, cudaDevAttrComputeCapabilityMinor, dev) != cudaSuccess ||
+        cudaDeviceGetAttribute(&di.smem_optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev) != cudaSuccess)
       st = BNBQ_ERR_CUDA;
     else if (di.cc_major != 10 || di.cc_minor != 0)
       st = BNBQ_ERR_DEVICE;
@@ -81,6 +83,16 @@ extern "C" int bnbq_rcp_approx_ftz(const float* in, float* out, int64_t n, void*
   if (grid > int64_t(di.sm_count) * 8) grid = int64_t(di.sm_count) * 8;
   rcp_kernel<<<dim3(unsigned(grid)), 256, 0, static_cast<cudaStream_t>(stream)>>>(in, out, n);
   return launch_status();
+}
+
+extern "C" int bnbq_wait_timeouts(unsigned int* count) {
+  if (!count) return BNBQ_ERR_INVALID;
+  DeviceInfo di;
+  if (int st = device_info(&di)) return st;
+  unsigned int g = 0;
+  if (gemv_wait_timeouts(&g) != 0) return BNBQ_ERR_CUDA;
+  *count = g;
+  return BNBQ_OK;
 }
 
 extern "C" const char* bnbq_error_string(int status) {

@@ -140,6 +140,7 @@ __device__ __constant__ static const uint32_t kNF4ThresholdBits[15] = {
 
 struct DeviceInfo {
   int sm_count = 0;
+  int smem_optin = 0;  // max dynamic shared memory per block (opt-in), bytes
   int cc_major = 0;
   int cc_minor = 0;
 };

@@ -20,6 +20,7 @@
 // The nested (double-quantized) scale is decoded per chunk and row:
 //   a = fl32(mul.ftz(code2[absmax_q[blk]], absmax2[(block0 + blk) >> log2 bs2]) + offset)
 // bitwise the value QuantizedArray.dequantize produces (array.py:95-108).
+#include "bnbq_async.cuh"
 #include "bnbq_common.cuh"
 
 namespace bnbq {
@@ -54,121 +55,749 @@ __device__ __forceinline__ void store_y(void* y, int64_t i, float v) {
   else static_cast<__half*>(y)[i] = __float2half_rn(v);
 }
 
-constexpr int kMaxWarps = 8;
+constexpr int kMaxWarps = 16;
+
+// Per-thread loads of one 32-element chunk of R rows (the software-pipeline
+// stage). XF: x of every batch row is prefetched with it (small M).
+template <int M, int R, bool NESTED, bool XF>
+struct Stage {
+  uint4 codes[R];
+  float scale_or_a2[R];  // plain: the absmax; nested: absmax2
+  int q2[R];             // nested: absmax code
+  uint4 x[XF ? M : 1][4];
+};
+
+template <typename XT, int M, int R, bool NESTED, bool XF>
+__device__ __forceinline__ void load_stage(Stage<M, R, NESTED, XF>& st, const GemvArgs& a,
+                                           const int64_t (&rows)[R], int c) {
+#pragma unroll
+  for (int r = 0; r < R; ++r) {
+    const int64_t e0 = rows[r] * a.k + int64_t(c) * 32;
+    st.codes[r] = __ldg(reinterpret_cast<const uint4*>(a.w + (e0 >> 1)));
+    const int64_t blk = e0 >> a.log2_bs;
+    if constexpr (NESTED) {
+      st.q2[r] = __ldg(a.absmax_q + blk);
+      st.scale_or_a2[r] = __ldg(a.absmax2 + ((a.block0 + blk) >> a.log2_bs2));
+    } else {
+      st.scale_or_a2[r] = __ldg(a.absmax + blk);
+    }
+  }
+  if constexpr (XF) {
+    const XT* x = static_cast<const XT*>(a.x);
+#pragma unroll
+    for (int m = 0; m < M; ++m)
+#pragma unroll
+      for (int i = 0; i < 4; ++i)
+        st.x[m][i] = __ldg(reinterpret_cast<const uint4*>(x + int64_t(m) * a.k + c * 32 + i * 8));
+  }
+}
+
+// Pair table in dynamic shared memory: entry b (a code byte: high nibble =
+// even element, low nibble = odd element) is (table[b >> 4], table[b & 15]),
+// replicated once per lane at [b][lane] (256 x 32 x 8 B = 64 KB), so that the
+// 32 lanes of a warp read 32 distinct banks whatever their bytes are.
+constexpr int kPairTableBytes = 256 * 32 * 8;
+extern __shared__ float2 s_pair[];
+
+// The same table in global memory, built at compile time, so a CTA can bulk-copy
+// it into shared memory instead of storing 64 KB entry by entry.
+struct PairTable {
+  float2 v[256 * 32];
+  constexpr PairTable() : v() {
+    constexpr float t[16] = {
+        -1.0f, -0.6961928009986877f, -0.5250730514526367f, -0.39491748809814453f,
+        -0.28444138169288635f, -0.18477343022823334f, -0.09105003625154495f, 0.0f,
+        0.07958029955625534f, 0.16093020141124725f, 0.24611230194568634f, 0.33791524171829224f,
+        0.44070982933044434f, 0.5626170039176941f, 0.7229568362236023f, 1.0f};
+    for (int i = 0; i < 256 * 32; ++i) v[i] = float2{t[(i >> 5) >> 4], t[(i >> 5) & 15]};
+  }
+};
+__device__ __align__(128) const PairTable g_pair_table{};
+
+// Byte offset of (byte j of `word`, this lane) in s_pair: one prmt builds
+// (byte << 8) | lane_x8, where lane_x8 = lane * 8 sits in byte 0 of `lane_b`.
+__device__ __forceinline__ float2 pair_at(uint32_t word, uint32_t lane_b, int j) {
+  const uint32_t off = __byte_perm(word, lane_b, 0x5504 | (j << 4));
+  return *reinterpret_cast<const float2*>(reinterpret_cast<const char*>(s_pair) + off);
+}
+
+template <typename XT, int M, int R, bool NESTED, bool XF>
+__device__ __forceinline__ void compute_stage(const Stage<M, R, NESTED, XF>& st, const GemvArgs& a,
+                                              const float* s_code2, float offset, int c,
+                                              uint32_t lane_b, float (&acc)[M][R]) {
+  float scale[R];
+#pragma unroll
+  for (int r = 0; r < R; ++r) {
+    if constexpr (NESTED) scale[r] = add_rn(mul_ftz(s_code2[st.q2[r]], st.scale_or_a2[r]), offset);
+    else scale[r] = st.scale_or_a2[r];
+  }
+  float2 t[M][R];
+#pragma unroll
+  for (int m = 0; m < M; ++m)
+#pragma unroll
+    for (int r = 0; r < R; ++r) t[m][r] = make_float2(0.0f, 0.0f);
+  const XT* x = static_cast<const XT*>(a.x);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {  // 8 elements: one 32-bit code word per row
+    float2 wv[R][4];
+#pragma unroll
+    for (int r = 0; r < R; ++r) {
+      const uint32_t word = i == 0 ? st.codes[r].x : i == 1 ? st.codes[r].y : i == 2 ? st.codes[r].z : st.codes[r].w;
+#pragma unroll
+      for (int j = 0; j < 4; ++j) wv[r][j] = pair_at(word, lane_b, j);
+    }
+#pragma unroll
+    for (int m = 0; m < M; ++m) {
+      uint4 xv;
+      if constexpr (XF) xv = st.x[m][i];
+      else xv = __ldg(reinterpret_cast<const uint4*>(x + int64_t(m) * a.k + c * 32 + i * 8));
+      const uint32_t xs[4] = {xv.x, xv.y, xv.z, xv.w};
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const float2 xf = unpack_x<XT>(xs[j]);
+#pragma unroll
+        for (int r = 0; r < R; ++r) t[m][r] = __ffma2_rn(wv[r][j], xf, t[m][r]);
+      }
+    }
+  }
+#pragma unroll
+  for (int m = 0; m < M; ++m)
+#pragma unroll
+    for (int r = 0; r < R; ++r) acc[m][r] = __fmaf_rn(scale[r], t[m][r].x + t[m][r].y, acc[m][r]);
+}
+
+// Persistent: CTA b takes row groups b, b + gridDim.x, ... of R rows; its
+// threads split each group's K/32 chunks (thread t: t, t + blockDim, ...).
+// The loads of a thread's next chunk (of this group or the next) are issued
+// before the current chunk is computed.
+// Threads per CTA at most: wide CTAs for small M, 256 (255 registers) above.
+constexpr int max_threads_for(int M) { return M == 1 ? kMaxWarps * 32 : 256; }
 
 template <typename XT, int M, int R, bool NESTED>
-__global__ void __launch_bounds__(kMaxWarps * 32)
-gemv_kernel(GemvArgs a) {
-  __shared__ float s_table[16];
+__global__ void __launch_bounds__(max_threads_for(M))
+gemv_kernel(GemvArgs a, int64_t n_groups) {
+  constexpr bool XF = M <= 2;
   __shared__ float s_code2[NESTED ? 256 : 1];
-  __shared__ float s_red[kMaxWarps][M * R];
+  __shared__ float s_red[2][kMaxWarps][M * R];
   const int tid = threadIdx.x;
   const int nthreads = blockDim.x;
   const int lane = tid & 31, warp = tid >> 5;
-  if (tid < 16) s_table[tid] = kNF4Table[tid];
+  for (int i = tid; i < 256 * 32; i += nthreads) {
+    const int b = i >> 5;
+    s_pair[i] = make_float2(kNF4Table[b >> 4], kNF4Table[b & 15]);
+  }
+  const uint32_t lane_b = uint32_t(lane) * 8u;
   if constexpr (NESTED) {
     for (int i = tid; i < 256; i += nthreads) s_code2[i] = __ldg(a.code2 + i);
   }
   __syncthreads();
 
-  const int64_t row0 = int64_t(blockIdx.x) * R;
-  const int cpr = a.k >> 5;  // chunks per row
+  const int cpr = a.k >> 5;
   const float offset = NESTED ? __ldg(a.offset) : 0.0f;
-  const XT* x = static_cast<const XT*>(a.x);
+  const int iters = (cpr + nthreads - 1) / nthreads;
 
-  int64_t rows[R];
+  auto rows_of = [&](int64_t g, int64_t (&rows)[R]) {
 #pragma unroll
-  for (int r = 0; r < R; ++r) rows[r] = min(row0 + r, a.n_rows - 1);  // clamp; results dropped
+    for (int r = 0; r < R; ++r) rows[r] = min(g * R + r, a.n_rows - 1);  // clamp; results dropped
+  };
 
+  Stage<M, R, NESTED, XF> sa, sb;  // ping-pong stages, kept in registers
+  int64_t g = blockIdx.x;
+  if (g >= n_groups) return;
+  int64_t rows[R];
+  rows_of(g, rows);
+  int it = 0;
+  int c = min(tid, cpr - 1);
+  load_stage<XT>(sa, a, rows, c);
+  int parity = 0;
   float acc[M][R];
 #pragma unroll
   for (int m = 0; m < M; ++m)
 #pragma unroll
     for (int r = 0; r < R; ++r) acc[m][r] = 0.0f;
 
-  for (int c = tid; c < cpr; c += nthreads) {
-    uint4 codes[R];
-    float scale[R];
-#pragma unroll
-    for (int r = 0; r < R; ++r) {
-      const int64_t e0 = rows[r] * a.k + int64_t(c) * 32;  // element index in this shard
-      codes[r] = __ldg(reinterpret_cast<const uint4*>(a.w + (e0 >> 1)));
-      const int64_t blk = e0 >> a.log2_bs;
-      if constexpr (NESTED) {
-        const int q2 = __ldg(a.absmax_q + blk);
-        scale[r] = add_rn(mul_ftz(s_code2[q2], __ldg(a.absmax2 + ((a.block0 + blk) >> a.log2_bs2))), offset);
-      } else {
-        scale[r] = __ldg(a.absmax + blk);
-      }
+  // Computes `cur` (this thread's chunk `c` of group `g`) after issuing the
+  // loads of the following stage into `nxt`. Returns true when done.
+  auto step = [&](Stage<M, R, NESTED, XF>& cur, Stage<M, R, NESTED, XF>& nxt) -> bool {
+    int64_t g_next = g;
+    int it_next = it + 1;
+    if (it_next == iters) { g_next = g + gridDim.x; it_next = 0; }
+    int64_t rows_next[R];
+    const int c_next = min(tid + it_next * nthreads, cpr - 1);
+    if (g_next < n_groups) {
+      rows_of(g_next, rows_next);
+      load_stage<XT>(nxt, a, rows_next, c_next);
     }
-    float2 t[M][R];
+    if (tid + it * nthreads < cpr)
+      compute_stage<XT>(cur, a, s_code2, offset, c, lane_b, acc);
+    if (it_next == 0) {
+      // group done: CTA reduction and store
 #pragma unroll
-    for (int m = 0; m < M; ++m)
+      for (int m = 0; m < M; ++m)
 #pragma unroll
-      for (int r = 0; r < R; ++r) t[m][r] = make_float2(0.0f, 0.0f);
-
+        for (int r = 0; r < R; ++r) {
+          float v = acc[m][r];
 #pragma unroll
-    for (int i = 0; i < 4; ++i) {  // 8 elements: one 32-bit code word per row
-      float wv[R][8];
-#pragma unroll
-      for (int r = 0; r < R; ++r) {
-        const uint32_t word = i == 0 ? codes[r].x : i == 1 ? codes[r].y : i == 2 ? codes[r].z : codes[r].w;
-#pragma unroll
-        for (int j = 0; j < 4; ++j) {
-          wv[r][2 * j] = s_table[(word >> (8 * j + 4)) & 15u];  // high nibble first
-          wv[r][2 * j + 1] = s_table[(word >> (8 * j)) & 15u];
+          for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+          if (lane == 0) s_red[parity][warp][m * R + r] = v;
+          acc[m][r] = 0.0f;
         }
+      __syncthreads();
+      const int nw = nthreads >> 5;
+      for (int i = tid; i < M * R; i += nthreads) {
+        float v = 0.0f;
+        for (int w = 0; w < nw; ++w) v += s_red[parity][w][i];
+        const int m = i / R, r = i % R;
+        const int64_t row = g * R + r;
+        if (row < a.n_rows) store_y<XT>(a.y, int64_t(m) * a.ldy + row, v);
       }
-#pragma unroll
-      for (int m = 0; m < M; ++m) {
-        const uint4 xv = __ldg(reinterpret_cast<const uint4*>(x + int64_t(m) * a.k + c * 32 + i * 8));
-        const uint32_t xs[4] = {xv.x, xv.y, xv.z, xv.w};
-#pragma unroll
-        for (int j = 0; j < 4; ++j) {
-          const float2 xf = unpack_x<XT>(xs[j]);
-#pragma unroll
-          for (int r = 0; r < R; ++r) fma2(t[m][r], make_float2(wv[r][2 * j], wv[r][2 * j + 1]), xf);
-        }
-      }
+      parity ^= 1;
+      if (g_next >= n_groups) return true;
     }
+    g = g_next;
+    it = it_next;
+    c = c_next;
 #pragma unroll
-    for (int m = 0; m < M; ++m)
-#pragma unroll
-      for (int r = 0; r < R; ++r) acc[m][r] = __fmaf_rn(scale[r], t[m][r].x + t[m][r].y, acc[m][r]);
-  }
+    for (int r = 0; r < R; ++r) rows[r] = rows_next[r];
+    return false;
+  };
 
-  // CTA reduction: butterfly within each warp, then across warps in smem.
-#pragma unroll
-  for (int m = 0; m < M; ++m)
-#pragma unroll
-    for (int r = 0; r < R; ++r) {
-      float v = acc[m][r];
-#pragma unroll
-      for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
-      if (lane == 0) s_red[warp][m * R + r] = v;
-    }
-  __syncthreads();
-  const int nw = nthreads >> 5;
-  for (int i = tid; i < M * R; i += nthreads) {
-    float v = 0.0f;
-    for (int w = 0; w < nw; ++w) v += s_red[w][i];
-    const int m = i / R, r = i % R;
-    if (row0 + r < a.n_rows) store_y<XT>(a.y, int64_t(m) * a.ldy + row0 + r, v);
+  while (true) {
+    if (step(sa, sb)) break;
+    if (step(sb, sa)) break;
   }
 }
 
-// Rows per CTA: enough to share each x load, few enough to keep registers.
-constexpr int rows_for(int M) { return M <= 4 ? 4 : (M <= 8 ? 2 : 1); }
+// ---------------------------------------------------------------------------
+// Bulk-copy pipelined GEMV for M <= 2 (the decode batch sizes).
+//
+// One CTA per SM walks row groups g = blockIdx.x, blockIdx.x + gridDim.x, ...
+// of R rows. A producer warp streams each group's codes (R rows x K/2 bytes,
+// contiguous in HBM) and, when they are 16-byte aligned, its block scales
+// (R x K/bs bytes of nested codes, or floats) into a ring of shared-memory
+// stages with cp.async.bulk, completion counted on a per-stage "full"
+// mbarrier. More than 100 KB per SM is in flight without using registers.
+// Consumer thread t owns chunks t, t + 32*NC, ... of every row (SLOTS of
+// them); its x never changes, so it is widened to float32 into registers once.
+// Per stage a thread decodes its chunks through the pair table and
+// accumulates with fma.rn.f32x2. Partial sums leave each warp through a
+// transposed butterfly into shared memory; a per-stage counter tells the last
+// warp of the group to add them up and store y. No CTA-wide barrier runs in
+// the loop, so warps drift apart and overlap their load, decode and fma phases.
+// A stage is refilled only after every consumer warp has arrived on its
+// "empty" mbarrier, the last warp after storing, so the partial-sum slot of a
+// stage is never overwritten early.
+// Programmatic dependent launch: weights and scales may be fetched before the
+// preceding kernel in the stream finishes (they are never written by it);
+// x is read and y written only after griddepcontrol.wait.
+// Every wait is bounded; a timeout is recorded (bnbq_wait_timeouts) and the
+// kernel stops early instead of hanging.
 
-// Warps per CTA so that the K/32 chunks split evenly (fewest idle lanes).
-int pick_warps(int cpr) {
-  int best = 8;
-  double best_eff = 0.0;
-  for (int w = 8; w >= 4; --w) {
+// ---------------------------------------------------------------------------
+// Flat GEMV for small M: one CTA per R consecutive rows (the whole K), many
+// CTAs per SM. Each thread owns SLOTS chunks of every row and issues all of
+// its loads -- codes, block scales, then x -- before decoding anything, so the
+// memory system sees ~256 bytes in flight per thread; the hardware CTA
+// scheduler overlaps one CTA's loads with another's arithmetic. Decode uses
+// the 16-entry table in shared memory: per code word, two shift-and-mask ops
+// give 4 high-nibble and 4 low-nibble byte offsets, one prmt extracts each,
+// one LDS reads the value. Partial sums: transposed warp butterfly, then one
+// pass through shared memory. Programmatic dependent launch: weights and
+// scales are requested before griddepcontrol.wait, x after it.
+
+template <int N>
+__device__ __forceinline__ float warp_reduce_many(float (&v)[N], int lane) {
+  // halves the set of values at each of the first log2(N) steps; afterwards
+  // lane l holds the sum of value (l >> (5 - log2 N)) when its low bits are 0
+  int n = N;
+  int o = 16;
+#pragma unroll
+  for (; o > 0 && n > 1; o >>= 1) {
+    const bool upper = (lane & o) != 0;
+#pragma unroll
+    for (int j = 0; j < N / 2; ++j) {
+      if (j < n / 2) {
+        const float send = upper ? v[j] : v[j + n / 2];
+        const float keep = upper ? v[j + n / 2] : v[j];
+        v[j] = keep + __shfl_xor_sync(0xffffffffu, send, o);
+      }
+    }
+    n >>= 1;
+  }
+  float vs = v[0];
+#pragma unroll
+  for (; o > 0; o >>= 1) vs += __shfl_xor_sync(0xffffffffu, vs, o);
+  return vs;
+}
+
+template <typename XT, int M, int R, bool NESTED, int SLOTS>
+__global__ void __launch_bounds__(256)
+gemv_flat_kernel(GemvArgs a) {
+  __shared__ float s_table[16];
+  __shared__ float s_code2[NESTED ? 256 : 1];
+  __shared__ float s_red[8][M * R];
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int nthreads = blockDim.x;
+  const int cpr = a.k >> 5;
+  const int64_t row0 = int64_t(blockIdx.x) * R;
+
+  // ---- weights and scales (never written by the preceding kernel)
+  uint4 codes[SLOTS][R];
+  float sc[SLOTS][R];
+  int q2[SLOTS][R];
+#pragma unroll
+  for (int sl = 0; sl < SLOTS; ++sl) {
+    const int c = min(tid + sl * nthreads, cpr - 1);
+#pragma unroll
+    for (int r = 0; r < R; ++r) {
+      const int64_t row = min(row0 + r, a.n_rows - 1);
+      const int64_t e0 = row * a.k + int64_t(c) * 32;
+      codes[sl][r] = __ldg(reinterpret_cast<const uint4*>(a.w + (e0 >> 1)));
+      const int64_t blk = e0 >> a.log2_bs;
+      if constexpr (NESTED) {
+        q2[sl][r] = __ldg(a.absmax_q + blk);
+        sc[sl][r] = __ldg(a.absmax2 + ((a.block0 + blk) >> a.log2_bs2));
+      } else {
+        q2[sl][r] = 0;
+        sc[sl][r] = __ldg(a.absmax + blk);
+      }
+    }
+  }
+  if (tid < 16) s_table[tid] = kNF4Table[tid];
+  if constexpr (NESTED) {
+    for (int i = tid; i < 256; i += nthreads) s_code2[i] = __ldg(a.code2 + i);
+  }
+  asm volatile("griddepcontrol.launch_dependents;");
+  asm volatile("griddepcontrol.wait;" ::: "memory");  // x may come from the previous kernel
+  const XT* x = static_cast<const XT*>(a.x);
+  uint4 xv[SLOTS][M][4];
+#pragma unroll
+  for (int sl = 0; sl < SLOTS; ++sl) {
+    const int c = min(tid + sl * nthreads, cpr - 1);
+#pragma unroll
+    for (int m = 0; m < M; ++m)
+#pragma unroll
+      for (int i = 0; i < 4; ++i)
+        xv[sl][m][i] = __ldg(reinterpret_cast<const uint4*>(x + int64_t(m) * a.k + c * 32 + i * 8));
+  }
+  const float offset = NESTED ? __ldg(a.offset) : 0.0f;
+  __syncthreads();
+
+  float acc[M * R];
+#pragma unroll
+  for (int i = 0; i < M * R; ++i) acc[i] = 0.0f;
+  const char* tbl = reinterpret_cast<const char*>(s_table);
+#pragma unroll
+  for (int sl = 0; sl < SLOTS; ++sl) {
+    if (tid + sl * nthreads >= cpr) continue;
+#pragma unroll
+    for (int r = 0; r < R; ++r) {
+      const float scale = NESTED ? add_rn(mul_ftz(s_code2[q2[sl][r]], sc[sl][r]), offset) : sc[sl][r];
+      const uint32_t words[4] = {codes[sl][r].x, codes[sl][r].y, codes[sl][r].z, codes[sl][r].w};
+      float2 w2[16];
+#pragma unroll
+      for (int wi = 0; wi < 4; ++wi) {
+        const uint32_t hi4 = (words[wi] >> 2) & 0x3c3c3c3cu;  // even elements' nibble x 4, per byte
+        const uint32_t lo4 = (words[wi] << 2) & 0x3c3c3c3cu;  // odd elements'
+#pragma unroll
+        for (int j = 0; j < 4; ++j)
+          w2[4 * wi + j] = make_float2(*reinterpret_cast<const float*>(tbl + __byte_perm(hi4, 0, 0x4440 + j)),
+                                       *reinterpret_cast<const float*>(tbl + __byte_perm(lo4, 0, 0x4440 + j)));
+      }
+#pragma unroll
+      for (int m = 0; m < M; ++m) {
+        const uint32_t xw[16] = {xv[sl][m][0].x, xv[sl][m][0].y, xv[sl][m][0].z, xv[sl][m][0].w,
+                                 xv[sl][m][1].x, xv[sl][m][1].y, xv[sl][m][1].z, xv[sl][m][1].w,
+                                 xv[sl][m][2].x, xv[sl][m][2].y, xv[sl][m][2].z, xv[sl][m][2].w,
+                                 xv[sl][m][3].x, xv[sl][m][3].y, xv[sl][m][3].z, xv[sl][m][3].w};
+        float2 t[4];
+#pragma unroll
+        for (int q = 0; q < 4; ++q) t[q] = make_float2(0.0f, 0.0f);
+#pragma unroll
+        for (int e = 0; e < 16; ++e) t[e & 3] = __ffma2_rn(w2[e], unpack_x<XT>(xw[e]), t[e & 3]);
+        const float2 u = __fadd2_rn(__fadd2_rn(t[0], t[1]), __fadd2_rn(t[2], t[3]));
+        acc[m * R + r] = __fmaf_rn(scale, u.x + u.y, acc[m * R + r]);
+      }
+    }
+  }
+
+  const float vs = warp_reduce_many<M * R>(acc, lane);
+  constexpr int kBits = (M * R >= 8) ? 3 : (M * R >= 4 ? 2 : (M * R >= 2 ? 1 : 0));
+  if ((lane & ((32 >> kBits) - 1)) == 0) {
+    const int idx = lane >> (5 - kBits);
+    if (idx < M * R) s_red[warp][idx] = vs;
+  }
+  __syncthreads();
+  if (tid < M * R) {
+    float v = 0.0f;
+    const int nw = nthreads >> 5;
+    for (int w = 0; w < nw; ++w) v += s_red[w][tid];
+    const int m = tid / R, r = tid % R;
+    const int64_t row = row0 + r;
+    if (row < a.n_rows) store_y<XT>(a.y, int64_t(m) * a.ldy + row, v);
+  }
+}
+
+// Threads per CTA for the flat kernel: <= 256, a multiple of 32, with the
+// chunks of a row split into the fewest idle slots.
+int flat_threads(int cpr, int max_slots, int* slots) {
+  int best_t = 256, best_s = 1;
+  double best_eff = -1.0;
+  for (int w = 8; w >= 2; --w) {
+    const int t = 32 * w;
+    const int s = (cpr + t - 1) / t;
+    if (s > max_slots) continue;
+    const double eff = double(cpr) / double(s * t);
+    if (eff > best_eff + 1e-9) { best_eff = eff; best_t = t; best_s = s; }
+  }
+  *slots = best_eff < 0 ? 0 : best_s;
+  return best_t;
+}
+
+template <typename XT, int M, int R, bool NESTED, int SLOTS>
+int launch_flat_t(const GemvArgs& a, int threads, cudaStream_t s) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(unsigned((a.n_rows + R - 1) / R));
+  cfg.blockDim = dim3(threads);
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  if (cudaLaunchKernelEx(&cfg, gemv_flat_kernel<XT, M, R, NESTED, SLOTS>, a) != cudaSuccess) return BNBQ_ERR_CUDA;
+  return launch_status();
+}
+
+constexpr int kMaxRows = 4;
+constexpr int kMaxStages = 8;
+constexpr int kMaxGroupsPerFlush = 32;  // partial sums held in shared memory between flushes
+
+template <typename XT, int M, int R, bool NESTED, int SLOTS>
+__global__ void __launch_bounds__(kMaxWarps * 32, 1)
+gemv_bulk_kernel(GemvArgs a, int n_groups, int n_stages, uint32_t stage_bytes, int scales_in_stage) {
+  __shared__ __align__(16) float s_code2[256];
+  __shared__ float s_part[kMaxGroupsPerFlush][kMaxWarps - 1][M * R];
+  __shared__ __align__(8) uint64_t s_tbl_bar;
+  __shared__ __align__(8) uint64_t s_done_bar;
+  __shared__ volatile int s_abort;  // set by any thread whose wait expired
+  char* stages = reinterpret_cast<char*>(s_pair) + kPairTableBytes;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(stages + size_t(n_stages) * stage_bytes);
+  const int tid = threadIdx.x;
+  const int lane = tid & 31, warp = tid >> 5;
+  const int ncw = (blockDim.x >> 5) - 1;  // consumer warps; the last warp produces
+  const int ncons = ncw * 32;
+  const int cpr = a.k >> 5;
+  const uint32_t row_bytes = uint32_t(a.k) >> 1;
+  const int spr = a.k >> a.log2_bs;  // scales per row (when K % bs == 0)
+  const uint32_t scale_row_bytes = uint32_t(spr) * (NESTED ? 1u : 4u);
+  const uint32_t codes_bytes = uint32_t(R) * row_bytes;
+  if (n_stages < 1 || n_stages > kMaxStages) return;  // the host plans <= kMaxStages
+
+  asm volatile("griddepcontrol.launch_dependents;");
+
+  if (warp == ncw) {  // ------------------------------------------- producer
+    if (lane == 0) {
+      s_abort = 0;
+      mbar_init(smem_u32(&s_tbl_bar), 1);
+      mbar_init(smem_u32(&s_done_bar), uint32_t(ncw));
+      for (int st = 0; st < n_stages; ++st) {
+        mbar_init(smem_u32(bars + st), 1);                         // full
+        mbar_init(smem_u32(bars + n_stages + st), uint32_t(ncw));  // empty
+      }
+      fence_mbar_init();
+      // constant tables first: pair table (4 x 16 KB) and code2
+      const uint32_t tb = smem_u32(&s_tbl_bar);
+      mbar_arrive_expect_tx(tb, kPairTableBytes + (NESTED ? 1024u : 0u));
+      for (int off = 0; off < kPairTableBytes; off += 16384)
+        bulk_g2s(smem_u32(s_pair) + off, reinterpret_cast<const char*>(g_pair_table.v) + off, 16384, tb);
+      if constexpr (NESTED) bulk_g2s(smem_u32(s_code2), a.code2, 1024, tb);
+    }
+    __syncthreads();  // barriers ready for everyone
+    if (lane == 0) {
+      int st = 0;
+      uint32_t phase = 0;
+      int i = 0;
+      for (int g = blockIdx.x; g < n_groups && i < kMaxGroupsPerFlush; g += gridDim.x, ++i) {
+        if (s_abort) break;
+        if (i >= n_stages && !mbar_wait(smem_u32(bars + n_stages + st), phase ^ 1u)) {
+          s_abort = 1;
+          break;
+        }
+        const int64_t row0 = int64_t(g) * R;
+        const uint32_t rows_in = uint32_t(min(int64_t(R), a.n_rows - row0));
+        const uint32_t full = smem_u32(bars + st);
+        const uint32_t dst = smem_u32(stages + size_t(st) * stage_bytes);
+        mbar_arrive_expect_tx(full, rows_in * row_bytes + (scales_in_stage ? rows_in * scale_row_bytes : 0u));
+        bulk_g2s(dst, a.w + row0 * int64_t(row_bytes), rows_in * row_bytes, full);
+        if (scales_in_stage) {
+          const void* src = NESTED ? static_cast<const void*>(a.absmax_q + row0 * spr)
+                                   : static_cast<const void*>(a.absmax + row0 * spr);
+          bulk_g2s(dst + codes_bytes, src, rows_in * scale_row_bytes, full);
+        }
+        if (++st == n_stages) { st = 0; phase ^= 1u; }
+      }
+    }
+    return;
+  }
+
+  // ---------------------------------------------------------------- consumers
+  __syncthreads();  // barriers initialised; tables and the first stages are in flight
+  const uint32_t lane_b = uint32_t(lane) * 8u;
+
+  // per (slot, row): the chunk's block within a group, relative to the group's
+  // first block (K % bs == 0), or its global block for group g (otherwise)
+  int cofs[SLOTS];
+#pragma unroll
+  for (int sl = 0; sl < SLOTS; ++sl) cofs[sl] = min(tid + sl * ncons, cpr - 1) * 32;
+  auto block_of = [&](int g, int sl, int r) -> int64_t {
+    const int64_t row = min(int64_t(g) * R + r, a.n_rows - 1);
+    return (row * a.k + cofs[sl]) >> a.log2_bs;
+  };
+  // second-level scales (nested) two groups ahead; whole scales when they do
+  // not travel with the stage
+  float pre0[SLOTS][R], pre1[SLOTS][R];
+  int preq0[SLOTS][R], preq1[SLOTS][R];
+  auto prefetch = [&](int g, float (&p)[SLOTS][R], int (&q)[SLOTS][R]) {
+#pragma unroll
+    for (int sl = 0; sl < SLOTS; ++sl)
+#pragma unroll
+      for (int r = 0; r < R; ++r) {
+        p[sl][r] = 0.0f;
+        q[sl][r] = 0;
+        if (g < n_groups && (NESTED || !scales_in_stage)) {
+          const int64_t blk = block_of(g, sl, r);
+          if constexpr (NESTED) {
+            p[sl][r] = __ldg(a.absmax2 + ((a.block0 + blk) >> a.log2_bs2));
+            if (!scales_in_stage) q[sl][r] = __ldg(a.absmax_q + blk);
+          } else {
+            p[sl][r] = __ldg(a.absmax + blk);
+          }
+        }
+      }
+  };
+  prefetch(blockIdx.x, pre0, preq0);
+  prefetch(blockIdx.x + gridDim.x, pre1, preq1);
+  // within-group scale index of (slot, row) when scales travel with the stage
+  int sidx[SLOTS][R];
+#pragma unroll
+  for (int sl = 0; sl < SLOTS; ++sl)
+#pragma unroll
+    for (int r = 0; r < R; ++r) sidx[sl][r] = (r * a.k + cofs[sl]) >> a.log2_bs;
+
+  asm volatile("griddepcontrol.wait;" ::: "memory");  // x may come from the previous kernel
+  const XT* x = static_cast<const XT*>(a.x);
+  float2 xr[SLOTS][M][16];
+#pragma unroll
+  for (int sl = 0; sl < SLOTS; ++sl) {
+#pragma unroll
+    for (int m = 0; m < M; ++m)
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const uint4 xv = __ldg(reinterpret_cast<const uint4*>(x + int64_t(m) * a.k + cofs[sl] + i * 8));
+        xr[sl][m][4 * i + 0] = unpack_x<XT>(xv.x);
+        xr[sl][m][4 * i + 1] = unpack_x<XT>(xv.y);
+        xr[sl][m][4 * i + 2] = unpack_x<XT>(xv.z);
+        xr[sl][m][4 * i + 3] = unpack_x<XT>(xv.w);
+      }
+  }
+  const float offset = NESTED ? __ldg(a.offset) : 0.0f;
+  bool ok = mbar_wait(smem_u32(&s_tbl_bar), 0);
+  if (!ok) s_abort = 1;
+
+  constexpr int kBits = (M * R >= 8) ? 3 : (M * R >= 4 ? 2 : (M * R >= 2 ? 1 : 0));
+  // lanes whose low bits are zero hold one of the M*R warp sums after warp_reduce_many
+  const bool holder = (lane & ((32 >> kBits) - 1)) == 0;
+  const int hidx = lane >> (5 - kBits);
+
+  int st = 0;
+  uint32_t phase = 0;
+  int gl = 0;
+  for (int g = blockIdx.x; g < n_groups && gl < kMaxGroupsPerFlush; g += gridDim.x, ++gl) {
+    if (!ok || s_abort) { ok = false; break; }
+    ok = mbar_wait(smem_u32(bars + st), phase);
+    if (!ok) { s_abort = 1; break; }
+    const char* stage = stages + size_t(st) * stage_bytes;
+
+    float scale[SLOTS][R];
+#pragma unroll
+    for (int sl = 0; sl < SLOTS; ++sl)
+#pragma unroll
+      for (int r = 0; r < R; ++r) {
+        float s_;
+        if (scales_in_stage) {
+          if constexpr (NESTED) {
+            const int q2 = reinterpret_cast<const uint8_t*>(stage + codes_bytes)[sidx[sl][r]];
+            s_ = add_rn(mul_ftz(s_code2[q2], pre0[sl][r]), offset);
+          } else {
+            s_ = reinterpret_cast<const float*>(stage + codes_bytes)[sidx[sl][r]];
+          }
+        } else {
+          s_ = NESTED ? add_rn(mul_ftz(s_code2[preq0[sl][r]], pre0[sl][r]), offset) : pre0[sl][r];
+        }
+        scale[sl][r] = s_;
+      }
+#pragma unroll
+    for (int sl = 0; sl < SLOTS; ++sl)
+#pragma unroll
+      for (int r = 0; r < R; ++r) { pre0[sl][r] = pre1[sl][r]; preq0[sl][r] = preq1[sl][r]; }
+    prefetch(g + 2 * int(gridDim.x), pre1, preq1);
+
+    float acc[M * R];
+#pragma unroll
+    for (int e = 0; e < M * R; ++e) acc[e] = 0.0f;
+#pragma unroll
+    for (int sl = 0; sl < SLOTS; ++sl) {
+      const int c = tid + sl * ncons;
+      if (c < cpr) {
+#pragma unroll
+        for (int r = 0; r < R; ++r) {
+          const uint4 cw = *reinterpret_cast<const uint4*>(stage + r * row_bytes + c * 16);
+          const uint32_t words[4] = {cw.x, cw.y, cw.z, cw.w};
+          float2 wv[16];  // all 16 lookups first, then 4 independent fma chains
+#pragma unroll
+          for (int wi = 0; wi < 4; ++wi)
+#pragma unroll
+            for (int j = 0; j < 4; ++j) wv[4 * wi + j] = pair_at(words[wi], lane_b, j);
+#pragma unroll
+          for (int m = 0; m < M; ++m) {
+            float2 t[4];
+#pragma unroll
+            for (int q = 0; q < 4; ++q) t[q] = make_float2(0.0f, 0.0f);
+#pragma unroll
+            for (int e = 0; e < 16; ++e) t[e & 3] = __ffma2_rn(wv[e], xr[sl][m][e], t[e & 3]);
+            const float2 u = __fadd2_rn(__fadd2_rn(t[0], t[1]), __fadd2_rn(t[2], t[3]));
+            acc[m * R + r] = __fmaf_rn(scale[sl][r], u.x + u.y, acc[m * R + r]);
+          }
+        }
+      }
+    }
+    __syncwarp();
+    if (lane == 0) mbar_arrive(smem_u32(bars + n_stages + st));  // stage consumed
+    if (++st == n_stages) { st = 0; phase ^= 1u; }
+
+    const float vs = warp_reduce_many<M * R>(acc, lane);
+    if (holder && hidx < M * R) s_part[gl][warp][hidx] = vs;
+  }
+
+  // Final sums: every consumer warp arrives on s_done (aborted or not); warp
+  // 0 waits for all of them (bounded) and stores y.
+  __syncwarp();
+  if (lane == 0) mbar_arrive(smem_u32(&s_done_bar));
+  if (warp != 0) return;
+  if (!mbar_wait(smem_u32(&s_done_bar), 0) || s_abort) return;
+  for (int e = lane; e < gl * M * R; e += 32) {
+    const int gi = e / (M * R), idx = e % (M * R);
+    float v = 0.0f;
+    for (int w = 0; w < ncw; ++w) v += s_part[gi][w][idx];
+    const int m = idx / R, r = idx % R;
+    const int64_t row = (int64_t(blockIdx.x) + int64_t(gi) * gridDim.x) * R + r;
+    if (row < a.n_rows) store_y<XT>(a.y, int64_t(m) * a.ldy + row, v);
+  }
+}
+
+struct BulkPlan {
+  int scales_in_stage = 0;
+  int ncw = 0;      // consumer warps
+  int slots = 0;    // chunks per consumer thread and row
+  int rows = 0;     // R
+  uint32_t stage_bytes = 0;
+};
+
+// Chooses consumer warps (fewest idle lanes), rows per group and whether the
+// scales travel with the codes; stages are sized at launch.
+bool plan_bulk(int m, int k, int log2_bs, bool nested, int smem_optin, BulkPlan* p) {
+  const int cpr = k >> 5;
+  double best_eff = -1.0;
+  for (int w = kMaxWarps - 1; w >= 4; --w) {
+    const int slots = (cpr + 32 * w - 1) / (32 * w);
+    if (slots * m > 2) continue;
+    const double eff = double(cpr) / double(slots * 32 * w);
+    if (eff > best_eff + 1e-9) { best_eff = eff; p->ncw = w; p->slots = slots; }
+  }
+  if (p->ncw == 0 || best_eff < 0.75) return false;
+  const uint32_t row_bytes = uint32_t(k) >> 1;
+  const bool whole_blocks = (k & ((1 << log2_bs) - 1)) == 0;
+  const uint32_t srb = whole_blocks ? uint32_t(k >> log2_bs) * (nested ? 1u : 4u) : 0u;
+  p->scales_in_stage = whole_blocks && (srb % 16 == 0);
+  const size_t room = size_t(smem_optin) - size_t(kPairTableBytes) - 24 * 1024;  // static smem margin
+  for (int R : {4, 2, 1}) {
+    const uint32_t sb = uint32_t(R) * (row_bytes + (p->scales_in_stage ? srb : 0u));
+    if (room / (sb + 16) >= 4) {
+      p->rows = R;
+      p->stage_bytes = sb;
+      return true;
+    }
+  }
+  return false;
+}
+
+template <typename XT, int M, int R, bool NESTED, int SLOTS>
+int launch_bulk_t(const GemvArgs& a, const BulkPlan& p, const DeviceInfo& di, cudaStream_t s) {
+  auto kern = gemv_bulk_kernel<XT, M, R, NESTED, SLOTS>;
+  cudaFuncAttributes fa;
+  if (cudaFuncGetAttributes(&fa, kern) != cudaSuccess) return BNBQ_ERR_CUDA;
+  const size_t room = size_t(di.smem_optin) - size_t(kPairTableBytes) - fa.sharedSizeBytes - 1024;
+  int stages = int(room / (p.stage_bytes + 16));
+  if (stages > kMaxStages) stages = kMaxStages;
+  if (stages < 2) return BNBQ_ERR_UNSUPPORTED;
+  const size_t smem = size_t(kPairTableBytes) + size_t(stages) * p.stage_bytes + size_t(2 * stages) * 8;
+  if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem)) != cudaSuccess)
+    return BNBQ_ERR_CUDA;
+  const int64_t n_groups = (a.n_rows + R - 1) / R;
+  if (n_groups > INT32_MAX / 2) return BNBQ_ERR_UNSUPPORTED;
+  int64_t grid = n_groups < di.sm_count ? n_groups : di.sm_count;
+  const int64_t min_grid = (n_groups + kMaxGroupsPerFlush - 1) / kMaxGroupsPerFlush;  // <= 32 groups per CTA
+  if (grid < min_grid) grid = min_grid;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(unsigned(grid));
+  cfg.blockDim = dim3((p.ncw + 1) * 32);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  if (cudaLaunchKernelEx(&cfg, kern, a, int(n_groups), stages, p.stage_bytes, p.scales_in_stage) != cudaSuccess)
+    return BNBQ_ERR_CUDA;
+  return launch_status();
+}
+
+template <typename XT, int M, bool NESTED>
+int launch_bulk(const GemvArgs& a, const BulkPlan& p, const DeviceInfo& di, cudaStream_t s) {
+  if constexpr (M <= 2) {
+    if (p.slots == 1) {
+      switch (p.rows) {
+        case 4: return launch_bulk_t<XT, M, 4, NESTED, 1>(a, p, di, s);
+        case 2: return launch_bulk_t<XT, M, 2, NESTED, 1>(a, p, di, s);
+        default: return launch_bulk_t<XT, M, 1, NESTED, 1>(a, p, di, s);
+      }
+    }
+    if constexpr (M == 1) {
+      switch (p.rows) {
+        case 4: return launch_bulk_t<XT, 1, 4, NESTED, 2>(a, p, di, s);
+        case 2: return launch_bulk_t<XT, 1, 2, NESTED, 2>(a, p, di, s);
+        default: return launch_bulk_t<XT, 1, 1, NESTED, 2>(a, p, di, s);
+      }
+    }
+  }
+  return BNBQ_ERR_UNSUPPORTED;
+}
+
+// Rows per group: enough to share each x load, few enough to keep registers.
+constexpr int rows_for(int M) { return M <= 2 ? 4 : (M <= 8 ? 2 : 1); }
+
+// Threads per CTA (multiple of 32, <= 512) splitting the K/32 chunks of a
+// row group with the fewest idle lanes.
+int pick_threads(int cpr, int max_threads) {
+  int best = 128;
+  double best_eff = -1.0;
+  for (int w = max_threads / 32; w >= 4; --w) {
     const int slots = 32 * w;
     const int iters = (cpr + slots - 1) / slots;
     const double eff = double(cpr) / double(iters * slots);
-    if (eff > best_eff + 1e-9) { best_eff = eff; best = w; }
+    if (eff > best_eff + 1e-9) { best_eff = eff; best = slots; }
   }
   return best;
 }
@@ -176,9 +805,43 @@ int pick_warps(int cpr) {
 template <typename XT, int M, bool NESTED>
 int launch_m(const GemvArgs& a, cudaStream_t s) {
   constexpr int R = rows_for(M);
-  const int warps = pick_warps(a.k >> 5);
-  const int64_t grid = (a.n_rows + R - 1) / R;
-  gemv_kernel<XT, M, R, NESTED><<<dim3(unsigned(grid)), dim3(warps * 32), 0, s>>>(a);
+  DeviceInfo di;
+  if (int st = device_info(&di)) return st;
+  if constexpr (M <= 2) {
+    BulkPlan p;
+    // bulk copies need 16-byte aligned sources: codes (checked by the caller),
+    // code2, and the scale arrays when they travel with the stage
+    const bool c2_ok = !NESTED || aligned(a.code2, 16);
+    if (c2_ok && plan_bulk(M, a.k, a.log2_bs, NESTED, di.smem_optin, &p)) {
+      if (p.scales_in_stage && !aligned(NESTED ? static_cast<const void*>(a.absmax_q)
+                                              : static_cast<const void*>(a.absmax), 16))
+        p.scales_in_stage = 0;
+      const int st = launch_bulk<XT, M, NESTED>(a, p, di, s);
+      if (st != BNBQ_ERR_UNSUPPORTED) return st;
+    }
+    int slots = 0;
+    const int threads = flat_threads(a.k >> 5, 2, &slots);
+    if (slots == 1) return launch_flat_t<XT, M, 4, NESTED, 1>(a, threads, s);
+    if (slots == 2) return launch_flat_t<XT, M, 4, NESTED, 2>(a, threads, s);
+  }
+  const int threads = pick_threads(a.k >> 5, max_threads_for(M));
+  const int64_t n_groups = (a.n_rows + R - 1) / R;
+  auto kern = gemv_kernel<XT, M, R, NESTED>;
+  if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kPairTableBytes) != cudaSuccess)
+    return BNBQ_ERR_CUDA;
+  int per_sm = 0;
+  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, threads, kPairTableBytes) != cudaSuccess)
+    return BNBQ_ERR_CUDA;
+  per_sm = per_sm < 1 ? 1 : (per_sm > 2 ? 2 : per_sm);
+  // One CTA per SM when that balances the groups to within 2%, else two.
+  int64_t grid = di.sm_count;
+  {
+    const int64_t rounds1 = (n_groups + grid - 1) / grid;
+    const double eff1 = double(n_groups) / double(rounds1 * grid);
+    if (eff1 < 0.98 && per_sm >= 2) grid = int64_t(di.sm_count) * 2;
+  }
+  if (grid > n_groups) grid = n_groups;
+  kern<<<dim3(unsigned(grid)), dim3(threads), kPairTableBytes, s>>>(a, n_groups);
   return launch_status();
 }
 
@@ -193,6 +856,8 @@ int launch_dispatch(int m, const GemvArgs& a, cudaStream_t s) {
 }
 
 }  // namespace
+
+int gemv_wait_timeouts(unsigned int* out) { return read_wait_timeouts(out); }
 
 // Validation shared with the GEMM path (bnbq_gemm.cu).
 int gemv_validate(int dtype, const void* x, int32_t m, int32_t k, const uint8_t* w, int64_t n_rows,

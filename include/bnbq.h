@@ -156,6 +156,12 @@ BNBQ_API int bnbq_matmul_nf4(int dtype, const void* x, int32_t m, int32_t k,
  * own reciprocal instead of modelling it. */
 BNBQ_API int bnbq_rcp_approx_ftz(const float* in, float* out, int64_t n, void* stream);
 
+/* Number of bounded device-side waits that expired on the current device since
+ * the library was loaded (pipelined kernels wait on their own bulk copies;
+ * each wait gives up after a fixed spin count instead of hanging, and the
+ * kernel then stops early). 0 in normal operation. Synchronous. */
+BNBQ_API int bnbq_wait_timeouts(unsigned int* count);
+
 /* Human-readable name of a status code (static storage). */
 BNBQ_API const char* bnbq_error_string(int status);
 

@@ -188,3 +188,10 @@ def test_gemv_writes_into_wider_output(cuda):
     gemv_nf4(x, w.data, a.data, 256, 64, nested=(a.absmax, a.code, a.offset, 256), out=big[:, 256:512])
     assert torch.equal(big[:, 256:512], bnb_b200.matmul(x, w))
     assert torch.all(big[:, :256] == 7.0) and torch.all(big[:, 512:] == 7.0)
+
+
+def test_no_wait_timeouts(cuda):
+    """The pipelined kernels' bounded waits never expired during these tests."""
+    from bnb_b200 import _lib
+    torch.cuda.synchronize()
+    assert _lib.wait_timeouts() == 0
