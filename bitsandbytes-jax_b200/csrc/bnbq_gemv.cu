@@ -845,12 +845,28 @@ int launch_m(const GemvArgs& a, cudaStream_t s) {
   return launch_status();
 }
 
+// M > 2: the M = 2 (and M = 1) kernels over consecutive pairs of x rows. Each
+// row's arithmetic is that of a single-row call; the weight, read from HBM by
+// the first pass, is served from L2 (126 MB) to the following ones.
+template <typename XT, bool NESTED>
+int launch_pairs(int m, const GemvArgs& a, cudaStream_t s) {
+  for (int m0 = 0; m0 < m; m0 += 2) {
+    GemvArgs b = a;
+    b.x = static_cast<const char*>(a.x) + size_t(m0) * size_t(a.k) * sizeof(XT);
+    b.y = static_cast<char*>(a.y) + size_t(m0) * size_t(a.ldy) * sizeof(XT);
+    const int st = (m - m0 >= 2) ? launch_m<XT, 2, NESTED>(b, s) : launch_m<XT, 1, NESTED>(b, s);
+    if (st != BNBQ_OK) return st;
+  }
+  return BNBQ_OK;
+}
+
 template <typename XT, bool NESTED, int M = 1>
 int launch_dispatch(int m, const GemvArgs& a, cudaStream_t s) {
   if constexpr (M > BNBQ_GEMV_MAX_M) {
     return BNBQ_ERR_INVALID;
   } else {
     if (m == M) return launch_m<XT, M, NESTED>(a, s);
+    if (M == 2) return launch_pairs<XT, NESTED>(m, a, s);
     return launch_dispatch<XT, NESTED, M + 1>(m, a, s);
   }
 }
