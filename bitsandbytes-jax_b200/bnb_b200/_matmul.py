@@ -8,8 +8,8 @@ kept for the backward pass).
 Routing. An NF4 weight with a bfloat16/float16 x, K % 32 == 0 and blocksize >=
 32 never materializes: up to GEMV_MAX_M rows of x run the fused GEMV (float32
 weights, closer to the exact product than the fallback), more rows run the
-fused tcgen05 dequantize-GEMM (weights decoded to x's dtype in shared memory,
-the fallback's precision). Everything else is ``x @ w.dequantize(x.dtype).T``
+fused tcgen05 dequantize-GEMM (weights decoded to x's dtype in tensor memory,
+the fallback's precision, float32 accumulation). Everything else is ``x @ w.dequantize(x.dtype).T``
 with the dequantize on the sm_100a kernels.
 """
 from __future__ import annotations
@@ -20,10 +20,6 @@ from .array import QuantizedArray
 from .kernels.gemv import _CHUNK, GEMV_MAX_M, gemv_nf4, matmul_nf4
 
 __all__ = ["matmul"]
-
-# The tcgen05 GEMM is used above GEMV_MAX_M rows when the library provides it.
-USE_FUSED_GEMM = True
-
 
 def matmul(x: torch.Tensor, w: QuantizedArray) -> torch.Tensor:
     """``x @ w.T`` for a 2-D quantized weight ``w`` (N, K).
@@ -56,11 +52,7 @@ def _forward(xm: torch.Tensor, w: QuantizedArray) -> torch.Tensor:
         absmax, nested = _fused_args(w)
         if m <= GEMV_MAX_M:
             return gemv_nf4(xm, w.data, absmax, n, w.blocksize, nested=nested)
-        if USE_FUSED_GEMM:
-            try:
-                return matmul_nf4(xm, w.data, absmax, n, w.blocksize, nested=nested)
-            except NotImplementedError:
-                pass  # this library build has no tcgen05 GEMM: same result via the fallback
+        return matmul_nf4(xm, w.data, absmax, n, w.blocksize, nested=nested)
     return xm @ w.dequantize(xm.dtype).T
 
 

@@ -118,8 +118,9 @@ def matmul_nf4(
     out: torch.Tensor | None = None,
 ) -> torch.Tensor:
     """``x @ W.T`` for any M >= 1: the GEMV up to GEMV_MAX_M rows, the fused
-    tcgen05 dequantize-GEMM above (weights decoded to x's dtype in shared
-    memory: the precision of the reference's fallback ``x @ w.dequantize().T``)."""
+    tcgen05 dequantize-GEMM above (weights decoded to x's dtype in tensor
+    memory, float32 accumulation: the precision of the reference's fallback
+    ``x @ w.dequantize().T``). K not a multiple of 64 runs as GEMV passes."""
     if x.shape[0] < 1:
         raise ValueError("matmul_nf4 needs at least one row of x")
     return _run("bnbq_matmul_nf4", x, data, absmax, n_rows, blocksize, nested, absmax2_block0, out)

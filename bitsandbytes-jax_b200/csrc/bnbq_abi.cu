@@ -14,6 +14,7 @@ int gemv_launch(int dtype, const void* x, int32_t m, int32_t k, const uint8_t* w
                 const float* absmax2, const float* code2, const float* offset, int32_t blocksize2,
                 int64_t absmax2_block0, void* y, int64_t ldy, cudaStream_t s);
 int gemv_wait_timeouts(unsigned int* out);
+int gemm_wait_timeouts(unsigned int* out);
 int gemm_launch(int dtype, const void* x, int32_t m, int32_t k, const uint8_t* w, int64_t n_rows,
                 int32_t blocksize, const float* absmax, const uint8_t* absmax_q,
                 const float* absmax2, const float* code2, const float* offset, int32_t blocksize2,
@@ -89,9 +90,9 @@ extern "C" int bnbq_wait_timeouts(unsigned int* count) {
   if (!count) return BNBQ_ERR_INVALID;
   DeviceInfo di;
   if (int st = device_info(&di)) return st;
-  unsigned int g = 0;
-  if (gemv_wait_timeouts(&g) != 0) return BNBQ_ERR_CUDA;
-  *count = g;
+  unsigned int g = 0, h = 0;
+  if (gemv_wait_timeouts(&g) != 0 || gemm_wait_timeouts(&h) != 0) return BNBQ_ERR_CUDA;
+  *count = g + h;
   return BNBQ_OK;
 }
 
