@@ -298,7 +298,7 @@ def run_ours(args, dist, rank, world, local_rank):
                    "parallelism": f"replicas x{world}" if world > 1 else "1 GPU"},
         "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
                      "frac": round(achieved / peak, 4), "peak_source": peak_kind,
-                     "traffic": traffic, "kernel": "gemv_kernel"},
+                     "traffic": traffic, "kernel": "gemv_bulk_kernel"},
         "e2e": {"value": round(algo_bytes(args.m) * e2e_steps / (e2e_ms * 1e-3) / 1e9, 2), "unit": "GB/s",
                 "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
                 "us_per_step": round(e2e_ms / e2e_steps * 1e3, 3)},
