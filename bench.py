@@ -20,6 +20,17 @@ Multi-GPU (torchrun, one process per GPU): every rank runs the same workload
 on its own weights (independent objects, no collective; weak scaling); the
 timed region is bracketed by barriers and the max over ranks is reported.
 
+`--workload quant` and `--workload gemm` (not read by the driver) measure the
+other configurations the same way: config 1 (NF4 quantize + dequantize round
+trip of a 4096x4096 bf16 tensor, 8 rotated copies), config 3 (8-bit blockwise
+quantize and dequantize of 2^28+37 elements, f32/f16/bf16, blocksizes 256 and
+4096, 90% N(0,1) + 10% Laplace(0,8)) and config 5 (the fused tcgen05 GEMM on
+the Llama-3-70B MLP shapes at M = 64, 512, 2048, beside dequantize + matmul).
+`--workload llama` is config 4: a Llama-3-8B decode stack (32 layers x q, k,
+v, o, gate, up, down; NF4 bs 64 double-quantized) with every GEMV sharded by
+output rows across the torchrun ranks and its y all-gathered (NCCL); one
+step is one pass over the 224 matrices, captured in a CUDA graph.
+
 `--impl reference` times the reference's arithmetic on the host cores: the
 reference has no CPU kernel path of its own (its kernels are GPU-only CuTe DSL)
 and cannot be installed here, so its GEMV is the oracle's C restatement
@@ -311,6 +322,214 @@ def run_ours(args, dist, rank, world, local_rank):
     return line
 
 
+def time_graph(torch, call, steps: int, warmup: int, device):
+    """Device time of `steps` calls call(i) replayed from one CUDA graph (ms)."""
+    for i in range(max(warmup, 3)):
+        call(i)
+    torch.cuda.synchronize()
+    stream = torch.cuda.Stream(device=device)
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.stream(stream):
+        with torch.cuda.graph(graph, stream=stream):
+            for i in range(steps):
+                call(i)
+    graph.replay()
+    torch.cuda.synchronize()
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    start.record(stream)
+    with torch.cuda.stream(stream):
+        graph.replay()
+    end.record(stream)
+    torch.cuda.synchronize()
+    ms = start.elapsed_time(end)
+    del graph
+    return ms
+
+
+def run_quant_workload(args, local_rank):
+    """Configs 1 and 3: blockwise quantize / dequantize bandwidth."""
+    import torch
+    from bnb_b200.kernels import (create_dynamic_map, dequantize_blockwise, dequantize_nf4,
+                                  quantize_blockwise, quantize_nf4)
+    device = torch.device("cuda", local_rank)
+    torch.cuda.set_device(device)
+    peak, peak_kind = measured_peaks()
+    steps = max(args.steps // 100, 8)
+    out = {}
+    with ClockSampler(local_rank) as clocks:
+        # config 1: 4096 x 4096 bf16, NF4 bs 64, 8 rotated copies (256 MiB)
+        n1 = 4096 * 4096
+        g = torch.Generator(device).manual_seed(0)
+        xs = [(torch.randn(n1, device=device, generator=g) * 0.02).to(torch.bfloat16) for _ in range(8)]
+        qs = [quantize_nf4(x, 64) for x in xs]
+        b1 = n1 * 2 + n1 // 2 + 4 * (n1 // 64)
+        tq = time_graph(torch, lambda i: quantize_nf4(xs[i % 8], 64), steps, args.warmup, device) / steps
+        td = time_graph(torch, lambda i: dequantize_nf4(qs[i % 8][0], qs[i % 8][1], 64, torch.bfloat16),
+                        steps, args.warmup, device) / steps
+        out["config1_nf4_bf16_bs64"] = {
+            "quantize_us": round(tq * 1e3, 2), "quantize_gbs": round(b1 / (tq * 1e-3) / 1e9, 1),
+            "dequantize_us": round(td * 1e3, 2), "dequantize_gbs": round(b1 / (td * 1e-3) / 1e9, 1),
+            "bytes_per_call": b1}
+        del xs, qs
+        # config 3: 2^28 + 37 elements, 90% N(0,1) + 10% Laplace(0,8), 8-bit dynamic map
+        n3 = (1 << 28) + 37
+        code = create_dynamic_map().to(device)
+        base = torch.randn(n3, device=device, generator=g)
+        mask = torch.rand(n3, device=device, generator=g) < 0.1
+        u = torch.rand(n3, device=device, generator=g) - 0.5  # Laplace(0, 8) by inverse CDF
+        lap = -8.0 * torch.sign(u) * torch.log1p(-2.0 * u.abs())
+        del u
+        base = torch.where(mask, lap, base)
+        del mask, lap
+        for dt, name in [(torch.float32, "f32"), (torch.float16, "f16"), (torch.bfloat16, "bf16")]:
+            x = base.to(dt)
+            for bs in (256, 4096):
+                q, a = quantize_blockwise(x, code, bs)
+                b3 = n3 * x.element_size() + n3 + 4 * (-(-n3 // bs))
+                s3 = max(steps // 4, 3)
+                tq = time_graph(torch, lambda i: quantize_blockwise(x, code, bs), s3, 1, device) / s3
+                td = time_graph(torch, lambda i: dequantize_blockwise(q, a, code, bs, dt), s3, 1, device) / s3
+                out[f"config3_8bit_{name}_bs{bs}"] = {
+                    "quantize_us": round(tq * 1e3, 1), "quantize_gbs": round(b3 / (tq * 1e-3) / 1e9, 1),
+                    "dequantize_us": round(td * 1e3, 1), "dequantize_gbs": round(b3 / (td * 1e-3) / 1e9, 1),
+                    "bytes_per_call": b3}
+                del q, a
+            del x
+    c1 = out["config1_nf4_bf16_bs64"]
+    rt_us = c1["quantize_us"] + c1["dequantize_us"]
+    value = 2 * c1["bytes_per_call"] / (rt_us * 1e-6) / 1e9
+    return {
+        "metric": "blockwise quantize/dequantize effective HBM GB/s (configs 1 and 3)",
+        "value": round(value, 1), "unit": "GB/s", "n_gpus": 1, "steps": steps, "warmup": args.warmup,
+        "ms_per_step": round(rt_us * 1e-3, 5), "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "bf16/f16/f32", "data": "synthetic (seeded torch Philox)",
+        "config": {"workload": "config 1 NF4 round trip (value) + config 3 8-bit blockwise (details)",
+                   "l2": "config 1: 8 rotated 32 MiB inputs; config 3: inputs of 0.5-1 GB"},
+        "roofline": {"bound": "hbm", "peak": peak, "unit": "GB/s", "peak_source": peak_kind,
+                     "frac_by_case": {k: {"quantize": round(v["quantize_gbs"] / peak, 3),
+                                          "dequantize": round(v["dequantize_gbs"] / peak, 3)}
+                                      for k, v in out.items()}},
+        "cases": out, "clocks": clocks.summary(),
+    }
+
+
+def run_gemm_workload(args, local_rank):
+    """Config 5: fused NF4 dequantize-GEMM on the Llama-3-70B MLP shapes."""
+    import torch
+    import bnb_b200 as bnb
+    from bnb_b200.kernels.gemv import matmul_nf4
+    device = torch.device("cuda", local_rank)
+    torch.cuda.set_device(device)
+    out = {}
+    peak_tf = 1669.8
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        peak_tf = float(json.loads(p.read_text()).get("bf16_tflops", peak_tf))
+    with ClockSampler(local_rank) as clocks:
+        for (n, k) in [(28672, 8192), (8192, 28672)]:
+            g = torch.Generator(device).manual_seed(n)
+            w = bnb.quantize((torch.randn(n, k, device=device, generator=g) * 0.015).to(torch.bfloat16),
+                             "nf4", 64, double_quant=True)
+            a = w.absmax
+            nested = (a.absmax, a.code, a.offset, a.blocksize)
+            for m in (64, 512, 2048):
+                x = torch.randn(m, k, device=device, generator=g).to(torch.bfloat16)
+                s5 = 5 if m == 2048 else 10
+                tf = time_graph(torch, lambda i: matmul_nf4(x, w.data, a.data, n, 64, nested=nested),
+                                s5, 2, device) / s5
+                tr = time_graph(torch, lambda i: x @ w.dequantize(torch.bfloat16).T, s5, 2, device) / s5
+                fl = 2.0 * m * n * k
+                out[f"{n}x{k}_m{m}"] = {"fused_us": round(tf * 1e3, 1), "fused_tflops": round(fl / (tf * 1e-3) / 1e12, 1),
+                                        "dequant_matmul_us": round(tr * 1e3, 1),
+                                        "speedup_vs_dequant_matmul": round(tr / tf, 2),
+                                        "frac_of_bf16_peak": round(fl / (tf * 1e-3) / 1e12 / peak_tf, 3)}
+            del w, a
+    return {"metric": "fused NF4 dequantize-GEMM TFLOP/s (config 5)", "value": out["28672x8192_m2048"]["fused_tflops"],
+            "unit": "TFLOP/s", "n_gpus": 1, "higher_is_better": True, "dtype": "bf16",
+            "data": "synthetic (seeded torch Philox)",
+            "config": {"workload": "config 5: Llama-3-70B MLP gate/up 28672x8192 and down 8192x28672, NF4 bs64 nested"},
+            "roofline": {"bound": "tensor", "peak": peak_tf, "unit": "TFLOP/s"},
+            "cases": out, "clocks": clocks.summary()}
+
+
+LLAMA8B = [(4096, 4096), (1024, 4096), (1024, 4096), (4096, 4096), (14336, 4096), (14336, 4096), (4096, 14336)]
+
+
+def run_llama_workload(args, dist, rank, world, local_rank):
+    """Config 4: row-sharded GEMV + all-gather over a Llama-3-8B layer stack."""
+    import torch
+    from bnb_b200.parallel import all_gather_rows, matmul_rows, quantize_shard, row_partition, shard_rows
+    device = torch.device("cuda", local_rank)
+    torch.cuda.set_device(device)
+    layers = 32
+    shards, plans = [], []
+    weight_bytes = 0
+    for i in range(layers * len(LLAMA8B)):
+        n, k = LLAMA8B[i % len(LLAMA8B)]
+        ranges = row_partition(n, k, BS * BS2, world)  # whole nested blocks per rank
+        a, b = ranges[rank]
+        g = torch.Generator(device).manual_seed(1000 + i)  # the same full weight on every rank
+        w_rows = (torch.randn(n, k, device=device, generator=g)[a:b] * 0.02).to(torch.bfloat16)
+        qa = quantize_shard(w_rows, "nf4", BS, double_quant=True, group=None if dist is None else dist.group.WORLD)
+        qa = type(qa)(qa.data, qa.absmax, qa.code, qa.offset, qa.qtype, qa.blocksize, (b - a, k), qa.dtype)
+        shards.append(shard_rows(qa, 0, b - a))
+        plans.append(ranges)
+        weight_bytes += n * k // 2 + n * k // BS + 4 * (n * k // BS // BS2)
+        del w_rows
+    torch.cuda.synchronize()
+    g = torch.Generator(device).manual_seed(5)
+    xs = {k: torch.randn(args.m, k, device=device, generator=g).to(torch.bfloat16) for k in (4096, 14336)}
+
+    def step():
+        for sh, ranges in zip(shards, plans):
+            y = matmul_rows(xs[sh.k], sh)
+            if world > 1:
+                all_gather_rows(y, ranges)
+
+    for _ in range(max(args.warmup, 3)):
+        step()
+    torch.cuda.synchronize()
+    stream = torch.cuda.Stream(device=device)
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.stream(stream):
+        with torch.cuda.graph(graph, stream=stream):
+            step()
+    graph.replay()
+    torch.cuda.synchronize()
+    steps = max(args.steps // 200, 5)
+    with ClockSampler(local_rank) as clocks:
+        if dist is not None:
+            dist.barrier()
+        torch.cuda.synchronize()
+        start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        start.record(stream)
+        with torch.cuda.stream(stream):
+            for _ in range(steps):
+                graph.replay()
+        end.record(stream)
+        torch.cuda.synchronize()
+        if dist is not None:
+            dist.barrier()
+    ms = start.elapsed_time(end)
+    del graph
+    torch.cuda.synchronize()
+    ms_t = torch.tensor([ms], device=device, dtype=torch.float64)
+    if dist is not None:
+        dist.all_reduce(ms_t, op=dist.ReduceOp.MAX)
+    ms = float(ms_t.item())
+    if rank != 0:
+        return None
+    per = ms / steps
+    return {"metric": "Llama-3-8B NF4 decode stack: effective weight GB/s, every GEMV row-sharded + all-gathered (config 4)",
+            "value": round(weight_bytes / (per * 1e-3) / 1e9, 1), "unit": "GB/s", "n_gpus": world, "steps": steps,
+            "warmup": args.warmup, "ms_per_step": round(per, 4), "higher_is_better": True, "scaling": "strong",
+            "vs_baseline": None, "dtype": "bf16", "data": "synthetic (seeded torch Philox)",
+            "config": {"workload": "config 4: 32 layers x 7 NF4 matrices, M=%d, row-sharded over %d GPUs, all-gather of y" % (args.m, world),
+                       "weight_bytes_per_step": weight_bytes, "timing": "CUDA graph of one pass, replayed per step",
+                       "parallelism": f"tp{world} (rows)"},
+            "clocks": clocks.summary()}
+
+
 def run_reference(args, rank):
     """The reference's arithmetic on the host cores (see module docstring)."""
     if rank != 0:
@@ -356,10 +575,11 @@ def main():
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=2000)
     ap.add_argument("--warmup", type=int, default=16)
-    ap.add_argument("--m", type=int, default=1)
+    ap.add_argument("--rows", "--m", dest="m", type=int, default=1)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-sweep", dest="sweep", action="store_false")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--workload", choices=["gemv", "quant", "gemm", "llama"], default="gemv")
     args = ap.parse_args()
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -374,6 +594,12 @@ def main():
             print(json.dumps(line), flush=True)
         return
 
+    if args.workload in ("quant", "gemm"):
+        if rank == 0:
+            fn = run_quant_workload if args.workload == "quant" else run_gemm_workload
+            print(json.dumps(fn(args, local_rank)), flush=True)
+        return
+
     dist = None
     if world > 1:
         import datetime
@@ -384,7 +610,10 @@ def main():
                               device_id=torch.device("cuda", local_rank))
         dist = td
     try:
-        line = run_ours(args, dist, rank, world, local_rank)
+        if args.workload == "llama":
+            line = run_llama_workload(args, dist, rank, world, local_rank)
+        else:
+            line = run_ours(args, dist, rank, world, local_rank)
         if line is not None:
             print(json.dumps(line), flush=True)
     finally:

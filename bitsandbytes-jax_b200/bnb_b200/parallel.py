@@ -1,0 +1,237 @@
+"""Multi-GPU partitioning of the hot path: one process per GPU, torch.distributed.
+
+The reference runs on one device; a user of this package shards in two ways,
+neither of which exchanges data on the compute path:
+
+* **NF4 matmul by output rows.** Rank ``r`` holds rows ``[start, stop)`` of a
+  weight (N, K) -- its slice of the codes, its slice of the block scales (or of
+  the nested scale codes, with the whole second-level ``absmax2`` and the
+  shard's first global block index) -- and computes ``y[:, start:stop]`` with
+  the fused kernels. x is replicated. :func:`all_gather_rows` (NCCL all-gather,
+  or any backend torch.distributed offers) assembles the full ``y`` only when
+  the caller asks for it.
+* **Quantize / dequantize by whole blocks.** Rank ``r`` holds elements
+  ``[start, stop)`` of the flat tensor, a whole number of blocks (the partial
+  last block on the last rank), and quantizes or decodes them alone. Double
+  quantization needs the mean of all ranks' absmax: one all-reduce of a float64
+  sum and a count (:func:`global_absmax_offset`).
+
+The plans (:func:`row_partition`, :func:`block_partition`) and the collective
+steps take CPU or CUDA tensors alike; only :func:`matmul_rows`,
+:func:`quantize_shard` and :func:`dequantize_shard` launch the CUDA kernels.
+"""
+from __future__ import annotations
+
+import math
+from dataclasses import dataclass
+
+import torch
+import torch.distributed as dist
+
+from .array import _NESTED_BLOCKSIZE, QuantizedArray
+from .kernels import create_dynamic_map, quantize_blockwise, quantize_nf4
+
+__all__ = [
+    "RowShard",
+    "all_gather_flat",
+    "all_gather_rows",
+    "block_partition",
+    "dequantize_shard",
+    "global_absmax_offset",
+    "matmul_rows",
+    "matmul_sharded",
+    "quantize_shard",
+    "row_partition",
+    "shard_rows",
+]
+
+
+# ------------------------------------------------------------------ row shards
+
+def row_partition(n_rows: int, k: int, blocksize: int, world: int) -> list[tuple[int, int]]:
+    """Balanced row ranges ``[(start, stop)] * world`` of an (n_rows, k) weight
+    whose boundaries start whole blocks (``start * k % blocksize == 0``), so that
+    every shard's codes and scales are contiguous slices. Trailing ranks may be
+    empty when there are fewer row granules than ranks."""
+    if world < 1 or n_rows < 0:
+        raise ValueError(f"bad partition of {n_rows} rows over {world} ranks")
+    granule = blocksize // math.gcd(k, blocksize)  # rows per whole number of blocks
+    units = -(-n_rows // granule)
+    bounds = [min(n_rows, granule * ((units * r) // world)) for r in range(world + 1)]
+    return [(bounds[r], bounds[r + 1]) for r in range(world)]
+
+
+@dataclass
+class RowShard:
+    """Rows ``[start, stop)`` of an NF4 weight, in the form the fused kernels take.
+
+    Attributes:
+        data: packed codes of the rows, ``(stop - start) * k / 2`` bytes.
+        absmax: float32 block scales of the rows, or (double-quantized) the
+            uint8 codes of those scales.
+        nested: ``(absmax2, code2, offset, blocksize2)`` of a double-quantized
+            weight -- absmax2 whole, since it is indexed by global block -- else None.
+        block0: global index of the shard's first block (the nested scale of
+            local block ``b`` is ``absmax2[(block0 + b) // blocksize2]``).
+        start, stop: the rows. n_rows_total, k: the full weight's shape.
+    """
+
+    data: torch.Tensor
+    absmax: torch.Tensor
+    nested: tuple[torch.Tensor, torch.Tensor, torch.Tensor, int] | None
+    blocksize: int
+    block0: int
+    start: int
+    stop: int
+    n_rows_total: int
+    k: int
+
+    @property
+    def n_rows(self) -> int:
+        return self.stop - self.start
+
+    def to(self, device) -> RowShard:
+        """Copy the shard's tensors to ``device`` (each rank moves only its own rows)."""
+        nested = None
+        if self.nested is not None:
+            a2, c2, off, bs2 = self.nested
+            nested = (a2.to(device), c2.to(device), off.to(device), bs2)
+        return RowShard(self.data.to(device), self.absmax.to(device), nested, self.blocksize, self.block0,
+                        self.start, self.stop, self.n_rows_total, self.k)
+
+
+def shard_rows(w: QuantizedArray, start: int, stop: int) -> RowShard:
+    """Rows ``[start, stop)`` of a 2-D NF4 weight as views of its tensors
+    (use :func:`row_partition` for the ranges)."""
+    if w.qtype != "nf4" or w.ndim != 2:
+        raise ValueError(f"row shards are of 2-D NF4 weights, got {w.qtype} {w.shape}")
+    n, k = w.shape
+    bs = w.blocksize
+    if not 0 <= start <= stop <= n or (start * k) % bs or ((stop * k) % bs and stop != n):
+        raise ValueError(f"rows [{start}, {stop}) of a ({n}, {k}) weight do not start whole blocks of {bs}")
+    b0, b1 = start * k // bs, -(-stop * k // bs)
+    data = w.data.reshape(-1)[start * k // 2:stop * k // 2]
+    absmax = w.absmax
+    if isinstance(absmax, QuantizedArray):
+        if absmax.offset is None or absmax.code is None or isinstance(absmax.absmax, QuantizedArray):
+            raise ValueError("row shards support one level of centred 8-bit nested scales")
+        nested = (absmax.absmax.reshape(-1), absmax.code.reshape(-1), absmax.offset.reshape(()),
+                  absmax.blocksize)
+        scales = absmax.data.reshape(-1)[b0:b1]
+    else:
+        nested = None
+        scales = absmax.reshape(-1)[b0:b1]
+    return RowShard(data, scales, nested, bs, b0, start, stop, n, k)
+
+
+def matmul_rows(x: torch.Tensor, shard: RowShard, out: torch.Tensor | None = None) -> torch.Tensor:
+    """``x @ W[start:stop].T`` for an (M, K) bfloat16/float16 CUDA x: the fused
+    GEMV (M <= 20) or tcgen05 GEMM, on this rank's rows only."""
+    from .kernels.gemv import matmul_nf4
+    if x.dim() != 2 or x.shape[1] != shard.k:
+        raise ValueError(f"x {tuple(x.shape)} does not match a K={shard.k} weight")
+    if shard.n_rows == 0:  # a trailing rank with no row granule
+        return x.new_empty((x.shape[0], 0)) if out is None else out
+    return matmul_nf4(x, shard.data, shard.absmax, shard.n_rows, shard.blocksize, nested=shard.nested,
+                      absmax2_block0=shard.block0, out=out)
+
+
+def all_gather_rows(y_local: torch.Tensor, ranges: list[tuple[int, int]], group=None) -> torch.Tensor:
+    """Assemble ``y`` (M, N) from every rank's ``y[:, start:stop]``: one
+    all-gather of equal-sized, zero-padded pieces (NCCL over NVLink on GPUs),
+    then one copy into place."""
+    world = dist.get_world_size(group)
+    assert len(ranges) == world, (len(ranges), world)
+    m = y_local.shape[0]
+    width = max(b - a for a, b in ranges)
+    piece = y_local.new_zeros((m, width))
+    piece[:, :y_local.shape[1]] = y_local
+    parts = _all_gather_bytes(piece, world, group)
+    return torch.cat([p[:, :b - a] for p, (a, b) in zip(parts, ranges)], dim=1)
+
+
+def matmul_sharded(x: torch.Tensor, shard: RowShard, ranges: list[tuple[int, int]] | None = None,
+                   group=None, gather: bool = True) -> torch.Tensor:
+    """This rank's ``x @ W[start:stop].T``, all-gathered into the full (M, N)
+    product when ``gather`` (``ranges`` as from :func:`row_partition`)."""
+    y = matmul_rows(x, shard)
+    if not gather:
+        return y
+    assert ranges is not None, "gathering needs every rank's row range"
+    return all_gather_rows(y, ranges, group)
+
+
+# ---------------------------------------------------------------- block shards
+
+def block_partition(n: int, blocksize: int, world: int, align_blocks: int = 1) -> list[tuple[int, int]]:
+    """Element ranges of a flat n-element tensor, each a whole number of
+    ``blocksize * align_blocks`` elements except the last (which takes the
+    partial tail). ``align_blocks = 256`` keeps every rank's absmax a whole
+    number of nested blocks, as double quantization needs."""
+    unit = blocksize * align_blocks
+    units = -(-n // unit)
+    bounds = [min(n, unit * ((units * r) // world)) for r in range(world + 1)]
+    return [(bounds[r], bounds[r + 1]) for r in range(world)]
+
+
+def global_absmax_offset(absmax_local: torch.Tensor, group=None) -> torch.Tensor:
+    """The double-quantization offset -- mean of every rank's absmax -- from one
+    all-reduce of a float64 (sum, count) pair; a float32 scalar on
+    ``absmax_local``'s device. Without a process group: the local mean."""
+    a = absmax_local.reshape(-1)
+    acc = torch.stack([a.to(torch.float64).sum(), torch.tensor(float(a.numel()), dtype=torch.float64,
+                                                                 device=a.device)])
+    if dist.is_available() and dist.is_initialized():
+        dist.all_reduce(acc, op=dist.ReduceOp.SUM, group=group)
+    return (acc[0] / acc[1]).to(torch.float32)
+
+
+def quantize_shard(x_local: torch.Tensor, qtype: str = "nf4", blocksize: int = 64, *,
+                   code: torch.Tensor | None = None, double_quant: bool = False, group=None) -> QuantizedArray:
+    """Quantize this rank's elements ``[start, stop)`` of a flat tensor (a range
+    from :func:`block_partition`, ``align_blocks=256`` when ``double_quant``).
+    The result equals the matching slice of quantizing the whole tensor: codes
+    and absmax bitwise; with ``double_quant`` the offset is the all-reduced mean."""
+    x = x_local.reshape(-1)
+    if qtype == "nf4":
+        data, absmax = quantize_nf4(x, blocksize=blocksize)
+        code = None
+    elif qtype == "8bit":
+        code = (create_dynamic_map(device=x.device) if code is None
+                else torch.as_tensor(code, dtype=torch.float32).reshape(-1).to(x.device))
+        data, absmax = quantize_blockwise(x, code, blocksize=blocksize)
+    else:
+        raise NotImplementedError(f"quantization to {qtype!r} is not implemented")
+    if double_quant:
+        offset = global_absmax_offset(absmax, group).to(x.device)
+        code2 = create_dynamic_map(device=x.device)
+        q2, absmax2 = quantize_blockwise(absmax, code2, blocksize=_NESTED_BLOCKSIZE, offset=offset)
+        absmax = QuantizedArray(q2, absmax2, code2, offset, "8bit", _NESTED_BLOCKSIZE, tuple(absmax.shape),
+                                torch.float32)
+    return QuantizedArray(data, absmax, code, None, qtype, blocksize, (x.numel(),), x.dtype)
+
+
+def dequantize_shard(qa_local: QuantizedArray, dtype=None) -> torch.Tensor:
+    """Decode this rank's block range (no collective)."""
+    return qa_local.dequantize(dtype).reshape(-1)
+
+
+def all_gather_flat(local: torch.Tensor, ranges: list[tuple[int, int]], group=None) -> torch.Tensor:
+    """Concatenate every rank's flat piece ``[start, stop)`` into the whole tensor."""
+    world = dist.get_world_size(group)
+    assert len(ranges) == world, (len(ranges), world)
+    width = max(b - a for a, b in ranges)
+    piece = local.new_zeros(width)
+    piece[:local.numel()] = local.reshape(-1)
+    parts = _all_gather_bytes(piece, world, group)
+    return torch.cat([p[:b - a] for p, (a, b) in zip(parts, ranges)])
+
+
+def _all_gather_bytes(piece: torch.Tensor, world: int, group) -> list[torch.Tensor]:
+    """all_gather of equal-shaped pieces moved as raw bytes (bit-exact for every
+    dtype, and a type every backend carries)."""
+    piece = piece.contiguous()
+    raw = piece.view(torch.uint8)
+    parts = [torch.empty_like(raw) for _ in range(world)]
+    dist.all_gather(parts, raw, group=group)
+    return [p.view(piece.dtype) for p in parts]

@@ -1,0 +1,82 @@
+"""Row-sharded NF4 matmul and block-sharded quantize over NCCL on 2 GPUs (one
+process per GPU). Skipped on a box with fewer than two GPUs; the same logic is
+covered on CPU with gloo in test_parallel.py."""
+from __future__ import annotations
+
+import pytest
+import torch
+
+from dist_helpers import _free_port
+
+pytestmark = pytest.mark.gpu
+
+
+def _worker(rank, world, port, queue):
+    import datetime
+    import os
+    import traceback
+    try:
+        import torch.distributed as dist
+        import bnb_b200 as bnb
+        from bnb_b200.parallel import (all_gather_flat, block_partition, matmul_sharded, quantize_shard,
+                                       row_partition, shard_rows)
+        os.environ["MASTER_ADDR"] = "127.0.0.1"
+        os.environ["MASTER_PORT"] = str(port)
+        torch.cuda.set_device(rank)
+        dev = torch.device("cuda", rank)
+        dist.init_process_group("nccl", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=60),
+                                device_id=dev)
+        try:
+            g = torch.Generator(dev).manual_seed(3)  # the same weight and x on every rank
+            n, k = 1024, 2048
+            w = bnb.quantize((torch.randn(n, k, device=dev, generator=g) * 0.02).to(torch.bfloat16), "nf4", 64,
+                             double_quant=True)
+            ranges = row_partition(n, k, 64, world)
+            shard = shard_rows(w, *ranges[rank])
+            for m in (1, 7, 20, 33, 300):  # GEMV and GEMM routes
+                x = torch.randn(m, k, device=dev, generator=g).to(torch.bfloat16)
+                y = matmul_sharded(x, shard, ranges)
+                assert torch.equal(y, bnb.matmul(x, w)), m
+            # block-sharded quantize == the whole tensor's codes and absmax
+            nel = 3 * 64 * 256 + 37
+            xf = torch.randn(nel, device=dev, generator=g).to(torch.bfloat16)
+            blocks = block_partition(nel, 64, world, align_blocks=256)
+            a, b = blocks[rank]
+            qa = quantize_shard(xf[a:b], "nf4", 64, double_quant=True)
+            full = bnb.quantize(xf, "nf4", 64, double_quant=True)
+            codes = all_gather_flat(qa.data, [(s // 2, -(-e // 2)) for s, e in blocks])
+            assert torch.equal(codes, full.data)
+            assert torch.equal(qa.absmax.offset, full.absmax.offset)
+            b0 = a // 64
+            assert torch.equal(qa.absmax.data, full.absmax.data[b0:b0 + qa.absmax.data.numel()])
+            dq = all_gather_flat(qa.dequantize(torch.bfloat16).reshape(-1), blocks)
+            assert torch.equal(dq, full.dequantize(torch.bfloat16).reshape(-1))
+            torch.cuda.synchronize()
+        finally:
+            dist.destroy_process_group()
+        queue.put((rank, None))
+    except BaseException:
+        queue.put((rank, traceback.format_exc()))
+
+
+@pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device_count() < 2, reason="needs 2 GPUs")
+def test_two_gpu_row_shards_and_block_shards():
+    import multiprocessing as mp
+    ctx = mp.get_context("spawn")
+    queue = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_worker, args=(r, 2, port, queue)) for r in range(2)]
+    for p in procs:
+        p.start()
+    errs = []
+    try:
+        for _ in range(2):
+            rank, err = queue.get(timeout=240)
+            if err:
+                errs.append(f"rank {rank}:\n{err}")
+    finally:
+        for p in procs:
+            p.join(timeout=30)
+            if p.is_alive():
+                p.kill()
+    assert not errs, "\n".join(errs)
