@@ -139,7 +139,7 @@ BNBQ_API int bnbq_gemv_nf4(int dtype, const void* x, int32_t m, int32_t k,
                   int64_t absmax2_block0, void* y, int64_t ldy, void* stream);
 
 /* Same contract for any m >= 1: the GEMV for m <= BNBQ_GEMV_MAX_M, the tcgen05/TMEM
- * fused dequantize-GEMM above it (weights decoded to dtype in shared memory, i.e.
+ * fused dequantize-GEMM above it (weights decoded to dtype in tensor memory, i.e.
  * the reference fallback's precision `x @ w.dequantize(x.dtype).T`, _matmul.py:58-59,
  * accumulated in float32 in tensor memory).
  * Replaces: the router _matmul_2d (_matmul.py:46-60) for NF4 weights. */
