@@ -860,13 +860,222 @@ int launch_pairs(int m, const GemvArgs& a, cudaStream_t s) {
   return BNBQ_OK;
 }
 
+// ------------------------------------------------------------ M = 3..20
+// gemv_rows_kernel: lanes are weight rows, so x is shared by the 32 lanes of a
+// warp (shared-memory broadcasts) and the weight is decoded once for all M rows
+// of x. A CTA owns 32 rows; its 8 warps split K, each streaming its slice in
+// 32-element stages through a D-deep per-warp ring filled by cp.async (no spin
+// waits anywhere: cp.async.wait_group):
+//   * codes (16 bytes per row) and the block scale (the float32 absmax, or the
+//     4-byte word holding the nested code plus absmax2), one lane per row;
+//   * x (MT rows x 32 columns of 16-bit values) in 16-byte pieces, converted
+//     once per stage into a float32 tile the whole warp reads by broadcast.
+// Each weight pair is scaled to its exact dequantized float32 value,
+// mul.ftz(T[q], a), and accumulated with fma.rn.f32x2 into per-(x row) float2
+// partials; the 8 warps' partials are summed in a fixed order in shared
+// memory. A one-hot x therefore returns dequantize() bitwise.
+constexpr int kRowsWarps = 8;
+
+template <int MT>
+struct RowsLayout {
+  static constexpr int kDepth = MT <= 8 ? 8 : 4;             // stages in flight per warp
+  static constexpr uint32_t kCodes = kDepth * 32 * 16;       // [depth][lane] 16 B
+  static constexpr uint32_t kWords = kDepth * 32 * 4;        // [depth][lane] scale word
+  static constexpr uint32_t kA2 = kDepth * 32 * 4;           // [depth][lane] absmax2
+  static constexpr uint32_t kXRaw = kDepth * MT * 32 * 2;    // [depth][MT][32] 16-bit x
+  static constexpr uint32_t kXF = MT * 32 * 4;               // [MT][32] float32 x
+  static constexpr uint32_t kWarp = kCodes + kWords + kA2 + kXRaw + kXF;
+  static constexpr uint32_t kPartials = kRowsWarps * MT * 32 * 4;
+  static constexpr uint32_t kDynamic = kPairTableBytes + kRowsWarps * kWarp + kPartials;
+};
+
+__device__ __forceinline__ void cp_async16(uint32_t dst, const void* src) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(dst), "l"(src) : "memory");
+}
+__device__ __forceinline__ void cp_async4(uint32_t dst, const void* src) {
+  asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(dst), "l"(src) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+
+template <typename XT>
+__device__ __forceinline__ float x_to_f32(uint16_t v) {
+  if constexpr (Elem<XT>::kDtype == BNBQ_BF16) return __uint_as_float(uint32_t(v) << 16);
+  else return __half2float(__ushort_as_half(v));
+}
+
+template <typename XT, int MT, bool NESTED>
+__global__ void __launch_bounds__(kRowsWarps * 32, 1)
+gemv_rows_kernel(GemvArgs a, int m_rows, int kw) {
+  using L = RowsLayout<MT>;
+  constexpr int D = L::kDepth;
+  __shared__ float s_code2[NESTED ? 256 : 1];
+  char* const dyn = reinterpret_cast<char*>(s_pair);
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  char* const wb = dyn + kPairTableBytes + warp * L::kWarp;
+  uint4* const s_codes = reinterpret_cast<uint4*>(wb);
+  uint32_t* const s_word = reinterpret_cast<uint32_t*>(wb + L::kCodes);
+  float* const s_a2 = reinterpret_cast<float*>(wb + L::kCodes + L::kWords);
+  uint16_t* const s_xraw = reinterpret_cast<uint16_t*>(wb + L::kCodes + L::kWords + L::kA2);
+  float* const s_xf = reinterpret_cast<float*>(wb + L::kCodes + L::kWords + L::kA2 + L::kXRaw);
+  float* const s_part = reinterpret_cast<float*>(dyn + kPairTableBytes + kRowsWarps * L::kWarp);
+
+  asm volatile("griddepcontrol.launch_dependents;");
+  for (int i = tid; i < kPairTableBytes / 16; i += kRowsWarps * 32)
+    reinterpret_cast<uint4*>(s_pair)[i] = reinterpret_cast<const uint4*>(g_pair_table.v)[i];
+  if constexpr (NESTED) {
+    for (int i = tid; i < 256; i += kRowsWarps * 32) s_code2[i] = __ldg(a.code2 + i);
+  }
+
+  const int64_t row = min(int64_t(blockIdx.x) * 32 + lane, a.n_rows - 1);
+  const int k0 = warp * kw;
+  const int k1 = min(a.k, k0 + kw);
+  const int nst = k1 > k0 ? (k1 - k0) >> 5 : 0;
+  const char* const wrow = reinterpret_cast<const char*>(a.w) + row * int64_t(a.k >> 1);
+  const int64_t rowk = row * int64_t(a.k);
+  const uint16_t* const x = static_cast<const uint16_t*>(a.x);
+  const int mx = m_rows < MT ? m_rows : MT;  // x rows actually copied
+
+  auto issue_w = [&](int s) {  // weight codes and scale of stage s
+    if (s < nst) {
+      const int slot = s & (D - 1);
+      const int kk = k0 + 32 * s;
+      cp_async16(smem_u32(s_codes + slot * 32 + lane), wrow + (kk >> 1));
+      const int64_t blk = (rowk + kk) >> a.log2_bs;
+      if constexpr (NESTED) {
+        cp_async4(smem_u32(s_word + slot * 32 + lane),
+                  reinterpret_cast<const void*>(reinterpret_cast<uintptr_t>(a.absmax_q + blk) & ~uintptr_t(3)));
+        cp_async4(smem_u32(s_a2 + slot * 32 + lane), a.absmax2 + ((a.block0 + blk) >> a.log2_bs2));
+      } else {
+        cp_async4(smem_u32(s_word + slot * 32 + lane), a.absmax + blk);
+      }
+    }
+  };
+  auto issue_x = [&](int s) {  // x[m][stage s], 4 pieces of 16 bytes per x row
+    if (s < nst) {
+      const int slot = s & (D - 1);
+      const int kk = k0 + 32 * s;
+      for (int c = lane; c < 4 * mx; c += 32) {
+        const int m = c >> 2, part = c & 3;
+        cp_async16(smem_u32(s_xraw + (slot * MT + m) * 32 + part * 8), x + int64_t(m) * a.k + kk + part * 8);
+      }
+    }
+  };
+
+  // weights do not depend on the previous kernel: start them before the wait
+#pragma unroll
+  for (int s = 0; s < D - 1; ++s) issue_w(s);
+  asm volatile("griddepcontrol.wait;" ::: "memory");  // x may come from the previous kernel
+  // group g holds stage g's x and, from g = D-1 on, stage g's weights too; the
+  // prologue's weight copies ride in group 0, which completes first
+#pragma unroll
+  for (int s = 0; s < D - 1; ++s) {
+    issue_x(s);
+    cp_async_commit();
+  }
+  const float offset = NESTED ? __ldg(a.offset) : 0.0f;
+  __syncthreads();  // pair table and code2 are in place
+
+  float2 acc[MT];
+#pragma unroll
+  for (int m = 0; m < MT; ++m) acc[m] = make_float2(0.0f, 0.0f);
+  const uint32_t lane_b = uint32_t(lane) * 8u;
+
+  for (int s = 0; s < nst; ++s) {
+    issue_w(s + D - 1);
+    issue_x(s + D - 1);
+    cp_async_commit();
+    asm volatile("cp.async.wait_group %0;" ::"n"(D - 1) : "memory");  // this lane's stage-s copies
+    __syncwarp();  // ... and every lane's (x pieces were copied by other lanes)
+    const int slot = s & (D - 1);
+#pragma unroll
+    for (int m = 0; m < MT; ++m)
+      s_xf[m * 32 + lane] = m < m_rows ? x_to_f32<XT>(s_xraw[(slot * MT + m) * 32 + lane]) : 0.0f;
+    __syncwarp();
+    const uint4 cw = s_codes[slot * 32 + lane];
+    float sc;
+    if constexpr (NESTED) {
+      const int64_t blk = (rowk + k0 + 32 * s) >> a.log2_bs;
+      const uint32_t sh = 8u * uint32_t(reinterpret_cast<uintptr_t>(a.absmax_q + blk) & 3);
+      const uint32_t q = (s_word[slot * 32 + lane] >> sh) & 0xffu;
+      sc = add_rn(mul_ftz(s_code2[q], s_a2[slot * 32 + lane]), offset);
+    } else {
+      sc = __uint_as_float(s_word[slot * 32 + lane]);
+    }
+    const uint32_t words[4] = {cw.x, cw.y, cw.z, cw.w};
+#pragma unroll
+    for (int e = 0; e < 16; e += 2) {  // pairs e and e+1: elements 2e .. 2e+3
+      const float2 w0 = mul_ftz2(pair_at(words[e >> 2], lane_b, e & 3), make_float2(sc, sc));
+      const float2 w1 = mul_ftz2(pair_at(words[e >> 2], lane_b, (e & 3) + 1), make_float2(sc, sc));
+#pragma unroll
+      for (int m = 0; m < MT; ++m) {
+        const float4 x4 = *reinterpret_cast<const float4*>(s_xf + m * 32 + 2 * e);  // broadcast
+        acc[m] = __ffma2_rn(w0, make_float2(x4.x, x4.y), acc[m]);
+        acc[m] = __ffma2_rn(w1, make_float2(x4.z, x4.w), acc[m]);
+      }
+    }
+  }
+  asm volatile("cp.async.wait_all;" ::: "memory");
+
+#pragma unroll
+  for (int m = 0; m < MT; ++m) s_part[(warp * MT + m) * 32 + lane] = acc[m].x + acc[m].y;
+  __syncthreads();
+  for (int e = tid; e < MT * 32; e += kRowsWarps * 32) {
+    const int m = e >> 5, l = e & 31;
+    float v = 0.0f;
+#pragma unroll
+    for (int w = 0; w < kRowsWarps; ++w) v += s_part[(w * MT + m) * 32 + l];
+    const int64_t r = int64_t(blockIdx.x) * 32 + l;
+    if (m < m_rows && r < a.n_rows) store_y<XT>(a.y, int64_t(m) * a.ldy + r, v);
+  }
+}
+
+template <typename XT, int MT, bool NESTED>
+int launch_rows_t(int m, const GemvArgs& a, const DeviceInfo& di, cudaStream_t s) {
+  using L = RowsLayout<MT>;
+  auto kern = gemv_rows_kernel<XT, MT, NESTED>;
+  cudaFuncAttributes fa;
+  if (cudaFuncGetAttributes(&fa, kern) != cudaSuccess) return BNBQ_ERR_CUDA;
+  if (size_t(L::kDynamic) + fa.sharedSizeBytes > size_t(di.smem_optin)) return BNBQ_ERR_UNSUPPORTED;
+  if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, int(L::kDynamic)) != cudaSuccess)
+    return BNBQ_ERR_CUDA;
+  int kw = (a.k + kRowsWarps - 1) / kRowsWarps;
+  kw = (kw + 31) & ~31;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(unsigned((a.n_rows + 31) / 32));
+  cfg.blockDim = dim3(kRowsWarps * 32);
+  cfg.dynamicSmemBytes = L::kDynamic;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  if (cudaLaunchKernelEx(&cfg, kern, a, m, kw) != cudaSuccess) return BNBQ_ERR_CUDA;
+  return launch_status();
+}
+
+// M = 5..20: x rows rounded up to a multiple of 4 (the extra rows are zero).
+template <typename XT, bool NESTED>
+int launch_rows(int m, const GemvArgs& a, cudaStream_t s) {
+  DeviceInfo di;
+  if (int st = device_info(&di)) return st;
+  if (a.n_rows > (int64_t(1) << 31) - 32) return BNBQ_ERR_UNSUPPORTED;
+  if (m <= 8) return launch_rows_t<XT, 8, NESTED>(m, a, di, s);
+  if (m <= 12) return launch_rows_t<XT, 12, NESTED>(m, a, di, s);
+  if (m <= 16) return launch_rows_t<XT, 16, NESTED>(m, a, di, s);
+  return launch_rows_t<XT, 20, NESTED>(m, a, di, s);
+}
+
 template <typename XT, bool NESTED, int M = 1>
 int launch_dispatch(int m, const GemvArgs& a, cudaStream_t s) {
   if constexpr (M > BNBQ_GEMV_MAX_M) {
     return BNBQ_ERR_INVALID;
   } else {
     if (m == M) return launch_m<XT, M, NESTED>(a, s);
-    if (M == 2) return launch_pairs<XT, NESTED>(m, a, s);
+    if (M == 2) {  // M = 3, 4: two passes of the pipelined kernels; above: one pass of the rows kernel
+      const int st = m > 4 ? launch_rows<XT, NESTED>(m, a, s) : BNBQ_ERR_UNSUPPORTED;
+      return st == BNBQ_ERR_UNSUPPORTED ? launch_pairs<XT, NESTED>(m, a, s) : st;
+    }
     return launch_dispatch<XT, NESTED, M + 1>(m, a, s);
   }
 }
