@@ -284,7 +284,51 @@ __device__ __forceinline__ void center(const QuantArgs& a, int64_t e0, float (&v
   }
 }
 
-// bs <= 256: L = bs/8 lanes per block, one 256-element segment per warp step.
+// Raw 16-byte vectors of one lane's 8 elements (one for 16-bit types, two for
+// float32), loaded early and unpacked when the segment is processed, so that
+// a warp keeps several segments in flight at a modest register cost.
+template <typename InT>
+struct Raw8 {
+  static constexpr int kVec = sizeof(InT) == 4 ? 2 : 1;
+  uint4 w[kVec];
+  bool full;
+};
+
+template <typename InT>
+__device__ __forceinline__ void load_raw8(const InT* x, int64_t e0, int64_t n, Raw8<InT>& r) {
+  r.full = e0 + 8 <= n;
+  if (r.full) {
+#pragma unroll
+    for (int i = 0; i < Raw8<InT>::kVec; ++i) r.w[i] = *reinterpret_cast<const uint4*>(x + e0 + 4 * i);
+  }
+}
+
+template <typename InT>
+__device__ __forceinline__ void unpack_raw8(const InT* x, int64_t e0, int64_t n, const Raw8<InT>& r,
+                                            float (&v)[8]) {
+  if (!r.full) {  // partial segment at the end: element loads
+    load8<InT>(x, e0, n, v);
+    return;
+  }
+  if constexpr (sizeof(InT) == 4) {
+    const float4 a = *reinterpret_cast<const float4*>(&r.w[0]);
+    const float4 b = *reinterpret_cast<const float4*>(&r.w[1]);
+    v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w;
+    v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
+  } else {
+    const uint32_t ws[4] = {r.w[0].x, r.w[0].y, r.w[0].z, r.w[0].w};
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const float2 f = Elem<InT>::kDtype == BNBQ_BF16 ? unpack2_bf16(ws[j]) : unpack2_f16(ws[j]);
+      v[2 * j] = f.x;
+      v[2 * j + 1] = f.y;
+    }
+  }
+}
+
+// bs <= 256: L = bs/8 lanes per block, one 256-element segment per warp step;
+// U segments per warp are loaded before any is processed (4 for 16-bit inputs,
+// 2 for float32: 2 KB per warp in flight either way).
 template <typename InT, bool NF4, typename Choose>
 __device__ void quant_small(const QuantArgs& a, const Choose& choose) {
   const InT* x = static_cast<const InT*>(a.x);
@@ -294,29 +338,31 @@ __device__ void quant_small(const QuantArgs& a, const Choose& choose) {
   const int64_t gw = (int64_t(blockIdx.x) * kThreads + threadIdx.x) >> 5;
   const int64_t tw = (int64_t(gridDim.x) * kThreads) >> 5;
   const float off = a.offset ? __ldg(a.offset) : 0.0f;
-  constexpr int U = 2;
+  constexpr int U = sizeof(InT) == 4 ? 2 : 4;
   for (int64_t seg0 = gw; seg0 < nseg; seg0 += tw * U) {
-    float v[U][8];
+    Raw8<InT> raw[U];
 #pragma unroll
     for (int u = 0; u < U; ++u) {
       const int64_t e0 = ((seg0 + u * tw) << 8) + lane * 8;
-      load8<InT>(x, e0, a.n, v[u]);
+      load_raw8<InT>(x, e0, a.n, raw[u]);
     }
 #pragma unroll
     for (int u = 0; u < U; ++u) {
       const int64_t seg = seg0 + u * tw;
       if (seg >= nseg) break;  // warp-uniform
       const int64_t e0 = (seg << 8) + lane * 8;
-      center<InT>(a, e0, v[u], off);
+      float v[8];
+      unpack_raw8<InT>(x, e0, a.n, raw[u], v);
+      center<InT>(a, e0, v, off);
       float m = -FLT_MAX;
 #pragma unroll
-      for (int j = 0; j < 8; ++j) m = max_abs_ftz(m, v[u][j]);
+      for (int j = 0; j < 8; ++j) m = max_abs_ftz(m, v[j]);
       for (int o = L >> 1; o > 0; o >>= 1) m = max_ftz(m, __shfl_xor_sync(0xffffffffu, m, o));
       const float r = rcp_approx_ftz(m);
       const int64_t b = e0 >> a.log2_bs;
       if (b < a.nb) {
         if ((lane & (L - 1)) == 0) a.absmax[b] = m;
-        if (e0 < a.n) emit_codes<NF4>(a, e0, v[u], r, choose, lane);
+        if (e0 < a.n) emit_codes<NF4>(a, e0, v, r, choose, lane);
       }
     }
   }
