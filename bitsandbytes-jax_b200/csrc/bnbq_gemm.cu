@@ -55,19 +55,20 @@ namespace {
 constexpr int kBM = 128;                        // weight rows per CTA (MMA M)
 constexpr int kBK = 64;                         // K per stage
 constexpr int kMaxStages = 12;                  // shared-memory ring slots
-constexpr int kMaxASlots = 4;                   // tensor-memory A slots
+constexpr int kMaxASlots = 6;                   // tensor-memory A slots
 constexpr uint32_t kCodeBytes = kBM * kBK / 2;  // 4 KB of codes per stage
 constexpr uint32_t kScaleBytes = 4 * kBM * 4;   // per row, up to two blocks: scale word and absmax2
 constexpr uint32_t kAColsPerStage = kBK / 2;    // 64 16-bit values = 32 columns
 
 // Tile configuration: BN rows of x, DG decoder groups of 4 warps; the tiles up to
 // 64 wide run two CTAs per SM.
-template <int BN>
+template <int BN, bool PRECISE = false>
 struct Tile {
-  static constexpr int kDG = 2;
+  static constexpr int kDG = PRECISE ? 4 : 2;  // the precise split decodes twice as much per stage
+  static constexpr uint32_t kACols = PRECISE ? 2 * kAColsPerStage : kAColsPerStage;  // hi (+ lo) terms
   static constexpr int kWarpTma = 4 * kDG, kWarpScale = kWarpTma + 1, kWarpMma = kWarpTma + 2;
   static constexpr int kThreads = (kWarpMma + 1) * 32;
-  static constexpr bool kPair = BN <= 64;
+  static constexpr bool kPair = BN <= 64 && !PRECISE;  // the precise (GEMV) tiles run one CTA per SM
   static constexpr uint32_t kBBytes = BN * kBK * 2;
   static constexpr uint32_t kStageBytes = kBBytes + kCodeBytes + kScaleBytes;  // a multiple of 1024
 };
@@ -89,6 +90,7 @@ struct GemmArgs {
   int n_stages;
   int n_aslots;
   uint32_t tmem_cols;
+  int kb_per_split;  // K blocks per CTA of a cluster along K (gridDim.z CTAs)
 };
 
 // Shared-memory matrix descriptor (sm_100 format) of a K-major tile in the
@@ -169,6 +171,42 @@ __device__ __forceinline__ uint32_t pack2(float lo, float hi) {
   else return pack2_f16(lo, hi);
 }
 
+// Round-toward-zero pair conversion (the residual term of the precise split).
+template <typename XT>
+__device__ __forceinline__ uint32_t pack2_rz(float lo, float hi) {
+  uint32_t r;
+  if constexpr (Elem<XT>::kDtype == BNBQ_BF16) asm("cvt.rz.bf16x2.f32 %0, %1, %2;" : "=r"(r) : "f"(hi), "f"(lo));
+  else asm("cvt.rz.f16x2.f32 %0, %1, %2;" : "=r"(r) : "f"(hi), "f"(lo));
+  return r;
+}
+
+template <typename XT>
+__device__ __forceinline__ float2 unpack2x(uint32_t w) {
+  if constexpr (Elem<XT>::kDtype == BNBQ_BF16) return unpack2_bf16(w);
+  else return unpack2_f16(w);
+}
+
+__device__ __forceinline__ void cluster_sync() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+
+__device__ __forceinline__ uint32_t cluster_rank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+
+// The shared::cluster address of this CTA's shared address `addr` in CTA `rank`.
+__device__ __forceinline__ uint32_t map_to_rank(uint32_t addr, uint32_t rank) {
+  uint32_t r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(addr), "r"(rank));
+  return r;
+}
+
+__device__ __forceinline__ void st_cluster_f32(uint32_t addr, float v) {
+  asm volatile("st.shared::cluster.f32 [%0], %1;" ::"r"(addr), "f"(v) : "memory");
+}
+
 template <typename XT>
 __device__ __forceinline__ void store_out(void* y, int64_t i, float v) {
   if constexpr (Elem<XT>::kDtype == BNBQ_BF16) static_cast<__nv_bfloat16*>(y)[i] = __float2bfloat16_rn(v);
@@ -194,6 +232,34 @@ __device__ __forceinline__ void block_table(float a, uint32_t (&lo)[4], uint32_t
   }
 }
 
+// Precise split of the same 16 values w_q = mul.ftz(T[q], a): hi = dtype(w)
+// rounded to nearest (the planes lo/hi, as block_table) and the residual
+// r = dtype(w - hi) rounded toward zero (planes rlo/rhi). hi + r equals w to
+// within 2^-16 |w|, and rounding hi + r to dtype gives hi back in every case
+// (|r| < half an ulp of hi, or exactly half when w was a tie), so a one-hot
+// x still returns the decoded weights bitwise. An infinite hi gets r = 0.
+template <typename XT>
+__device__ __forceinline__ void block_table_split(float a, uint32_t (&lo)[4], uint32_t (&hi)[4], uint32_t (&rlo)[4],
+                                                  uint32_t (&rhi)[4]) {
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    float w[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) w[i] = mul_ftz(kNF4Table[4 * j + i], a);
+    const uint32_t p0 = pack2<XT>(w[0], w[1]), p1 = pack2<XT>(w[2], w[3]);
+    const float2 h0 = unpack2x<XT>(p0), h1 = unpack2x<XT>(p1);
+    const float hv[4] = {h0.x, h0.y, h1.x, h1.y};
+    float r[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) r[i] = isinf(hv[i]) ? 0.0f : sub_rn(w[i], hv[i]);
+    const uint32_t q0 = pack2_rz<XT>(r[0], r[1]), q1 = pack2_rz<XT>(r[2], r[3]);
+    lo[j] = prmt(p0, p1, 0x6420);
+    hi[j] = prmt(p0, p1, 0x7531);
+    rlo[j] = prmt(q0, q1, 0x6420);
+    rhi[j] = prmt(q0, q1, 0x7531);
+  }
+}
+
 // One 32-bit word of packed codes (byte b: value 2b in the high nibble, 2b+1 in
 // the low nibble) -> four words of two 16-bit values, value 2i in the low half
 // of word i. Per group of four codes: the low three bits of each code pick a
@@ -214,10 +280,11 @@ __device__ __forceinline__ void decode_word(uint32_t w, const uint32_t (&lo)[4],
   }
 }
 
-template <typename XT, int BN, bool NESTED>
-__global__ void __launch_bounds__(Tile<BN>::kThreads, Tile<BN>::kPair ? 2 : 1)
+template <typename XT, int BN, bool NESTED, bool PRECISE>
+__global__ void __launch_bounds__(Tile<BN, PRECISE>::kThreads, Tile<BN, PRECISE>::kPair ? 2 : 1)
 gemm_kernel(const GemmArgs a, const __grid_constant__ CUtensorMap tmap_x, const __grid_constant__ CUtensorMap tmap_w) {
-  using T = Tile<BN>;
+  using T = Tile<BN, PRECISE>;
+  constexpr uint32_t kACols = T::kACols;
   constexpr int DG = T::kDG;
   constexpr uint32_t kBBytes = T::kBBytes, kStage = T::kStageBytes;
   extern __shared__ __align__(1024) unsigned char smem_raw[];
@@ -233,7 +300,10 @@ gemm_kernel(const GemmArgs a, const __grid_constant__ CUtensorMap tmap_x, const 
   const uint32_t ring = (raw + 1023u) & ~1023u;
   unsigned char* const ring_ptr = smem_raw + (ring - raw);
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  const int kblocks = int(a.k / kBK);
+  // this CTA's K blocks: [kb_begin, kb_begin + kblocks) (the whole K unless split)
+  const int kb_begin = int(blockIdx.z) * a.kb_per_split;
+  const int kb_all = int(a.k / kBK);
+  const int kblocks = (kb_all - kb_begin) < a.kb_per_split ? (kb_all - kb_begin) : a.kb_per_split;
   const int m0 = int(blockIdx.x) * BN;
   const int64_t n0 = int64_t(blockIdx.y) * kBM;
   const uint32_t bar0 = smem_u32(s_bar);
@@ -265,7 +335,7 @@ gemm_kernel(const GemmArgs a, const __grid_constant__ CUtensorMap tmap_x, const 
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
-  const uint32_t tmem = s_tmem;  // accumulator: columns [0, BN); A slot sa: BN + 32 sa
+  const uint32_t tmem = s_tmem;  // accumulator: columns [0, BN); A slot sa: BN + kACols sa
 
   if (warp == T::kWarpTma) {
     // -------------------------------------------------------- TMA producer
@@ -280,8 +350,8 @@ gemm_kernel(const GemmArgs a, const __grid_constant__ CUtensorMap tmap_x, const 
       if (lane == 0) {
         const uint32_t slot = ring + uint32_t(st) * kStage;
         mbar_arrive_expect_tx(tma_full(st), kBBytes + kCodeBytes);
-        tma_load_2d(slot, &tmap_x, kb * kBK, m0, tma_full(st));
-        tma_load_2d(slot + kBBytes, &tmap_w, kb * (kBK / 2), int(n0), tma_full(st));
+        tma_load_2d(slot, &tmap_x, (kb_begin + kb) * kBK, m0, tma_full(st));
+        tma_load_2d(slot + kBBytes, &tmap_w, (kb_begin + kb) * (kBK / 2), int(n0), tma_full(st));
       }
       __syncwarp();
       issued = kb + 1;
@@ -310,7 +380,7 @@ gemm_kernel(const GemmArgs a, const __grid_constant__ CUtensorMap tmap_x, const 
       for (int j = 0; j < nj; ++j)
 #pragma unroll
         for (int i = 0; i < 4; ++i) {
-          const int64_t blk = (rowk[i] + int64_t(kb) * kBK + 32 * j) >> a.log2_bs;
+          const int64_t blk = (rowk[i] + int64_t(kb_begin + kb) * kBK + 32 * j) >> a.log2_bs;
           const uint32_t o = uint32_t(j * kBM + lane + 32 * i) * 4u;
           if constexpr (NESTED) {
             cp_async4(sp + o, reinterpret_cast<const void*>(reinterpret_cast<uintptr_t>(a.absmax_q + blk) &
@@ -338,10 +408,13 @@ gemm_kernel(const GemmArgs a, const __grid_constant__ CUtensorMap tmap_x, const 
       tc_fence_after();
       if (lane == 0) {
         const uint64_t db = sw128_desc(ring + uint32_t(st) * kStage);
-        const uint32_t ta = tmem + uint32_t(BN) + uint32_t(sa) * kAColsPerStage;
+        const uint32_t ta = tmem + uint32_t(BN) + uint32_t(sa) * kACols;
 #pragma unroll
-        for (int j = 0; j < kBK / 16; ++j)  // K = 16 per MMA: 8 columns of A, 32 bytes of B's rows
+        for (int j = 0; j < kBK / 16; ++j) {  // K = 16 per MMA: 8 columns of A, 32 bytes of B's rows
           mma_ts(tmem, ta + uint32_t(8 * j), db + uint64_t(2 * j), idesc, (kb | j) ? 1u : 0u);
+          if constexpr (PRECISE)  // the residual term, same B
+            mma_ts(tmem, ta + kAColsPerStage + uint32_t(8 * j), db + uint64_t(2 * j), idesc, 1u);
+        }
         mma_commit(slot_empty(st));  // ring slot st and A slot sa are free once these MMAs have read them
       }
       __syncwarp();
@@ -363,7 +436,7 @@ gemm_kernel(const GemmArgs a, const __grid_constant__ CUtensorMap tmap_x, const 
     auto scale = [&](const unsigned char* sp, int kb, int j) -> float {
       const uint32_t word = reinterpret_cast<const uint32_t*>(sp)[j * kBM + t];
       if constexpr (NESTED) {
-        const int64_t blk = (rowk + int64_t(kb) * kBK + 32 * j) >> a.log2_bs;
+        const int64_t blk = (rowk + int64_t(kb_begin + kb) * kBK + 32 * j) >> a.log2_bs;
         const uint32_t q = (word >> (8 * uint32_t(reinterpret_cast<uintptr_t>(a.absmax_q + blk) & 3))) & 0xffu;
         const float a2 = reinterpret_cast<const float*>(sp + 2 * kBM * 4)[j * kBM + t];
         return add_rn(mul_ftz(s_code2[q], a2), offset);
@@ -384,20 +457,46 @@ gemm_kernel(const GemmArgs a, const __grid_constant__ CUtensorMap tmap_x, const 
       const unsigned char* sp = slot + kBBytes + kCodeBytes;
       const uint4 c0 = *reinterpret_cast<const uint4*>(slot + kBBytes + 32 * t);
       const uint4 c1 = *reinterpret_cast<const uint4*>(slot + kBBytes + 32 * t + 16);
-      const uint32_t cols = lane_addr + uint32_t(BN) + uint32_t(sa) * kAColsPerStage;
+      const uint32_t cols = lane_addr + uint32_t(BN) + uint32_t(sa) * kACols;
       uint32_t v[16], lo[4], hi[4];
-      block_table<XT>(scale(sp, kb, 0), lo, hi);
-      decode_word(c0.x, lo, hi, v + 0);
-      decode_word(c0.y, lo, hi, v + 4);
-      decode_word(c0.z, lo, hi, v + 8);
-      decode_word(c0.w, lo, hi, v + 12);
-      tmem_st16(cols, v);
-      if (two) block_table<XT>(scale(sp, kb, 1), lo, hi);
-      decode_word(c1.x, lo, hi, v + 0);
-      decode_word(c1.y, lo, hi, v + 4);
-      decode_word(c1.z, lo, hi, v + 8);
-      decode_word(c1.w, lo, hi, v + 12);
-      tmem_st16(cols + 16, v);
+      if constexpr (PRECISE) {
+        uint32_t rlo[4], rhi[4];
+        block_table_split<XT>(scale(sp, kb, 0), lo, hi, rlo, rhi);
+        decode_word(c0.x, lo, hi, v + 0);
+        decode_word(c0.y, lo, hi, v + 4);
+        decode_word(c0.z, lo, hi, v + 8);
+        decode_word(c0.w, lo, hi, v + 12);
+        tmem_st16(cols, v);
+        decode_word(c0.x, rlo, rhi, v + 0);
+        decode_word(c0.y, rlo, rhi, v + 4);
+        decode_word(c0.z, rlo, rhi, v + 8);
+        decode_word(c0.w, rlo, rhi, v + 12);
+        tmem_st16(cols + kAColsPerStage, v);
+        if (two) block_table_split<XT>(scale(sp, kb, 1), lo, hi, rlo, rhi);
+        decode_word(c1.x, lo, hi, v + 0);
+        decode_word(c1.y, lo, hi, v + 4);
+        decode_word(c1.z, lo, hi, v + 8);
+        decode_word(c1.w, lo, hi, v + 12);
+        tmem_st16(cols + 16, v);
+        decode_word(c1.x, rlo, rhi, v + 0);
+        decode_word(c1.y, rlo, rhi, v + 4);
+        decode_word(c1.z, rlo, rhi, v + 8);
+        decode_word(c1.w, rlo, rhi, v + 12);
+        tmem_st16(cols + kAColsPerStage + 16, v);
+      } else {
+        block_table<XT>(scale(sp, kb, 0), lo, hi);
+        decode_word(c0.x, lo, hi, v + 0);
+        decode_word(c0.y, lo, hi, v + 4);
+        decode_word(c0.z, lo, hi, v + 8);
+        decode_word(c0.w, lo, hi, v + 12);
+        tmem_st16(cols, v);
+        if (two) block_table<XT>(scale(sp, kb, 1), lo, hi);
+        decode_word(c1.x, lo, hi, v + 0);
+        decode_word(c1.y, lo, hi, v + 4);
+        decode_word(c1.z, lo, hi, v + 8);
+        decode_word(c1.w, lo, hi, v + 12);
+        tmem_st16(cols + 16, v);
+      }
       asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
       tc_fence_before();
       mbar_arrive(a_full(sa));
@@ -412,21 +511,66 @@ gemm_kernel(const GemmArgs a, const __grid_constant__ CUtensorMap tmap_x, const 
 
   // -------------------------------------------------------------- epilogue
   const bool finished = mbar_wait(done, 0);  // all issued MMAs have completed
-  if (warp < 4 * DG && __all_sync(0xffffffffu, finished && !s_abort)) {
-    tc_fence_after();
-    const int g = warp >> 2, wq = warp & 3;
-    const int64_t n = n0 + wq * 32 + lane;
-    const uint32_t lane_addr = tmem + (uint32_t(wq * 32) << 16);
-    constexpr int kCols = BN / DG;  // group g stores accumulator columns [g kCols, (g + 1) kCols)
+  const int C = int(gridDim.z);             // CTAs of the cluster along K
+  const int g = warp >> 2, wq = warp & 3;
+  const int64_t n = n0 + wq * 32 + lane;
+  const uint32_t lane_addr = tmem + (uint32_t(wq * 32) << 16);
+  // group g handles accumulator columns [g kCols, (g + 1) kCols), whole 16-column loads
+  constexpr int kCols = BN / DG >= 16 ? BN / DG : 16;
+  const int col_end = (g + 1) * kCols < BN ? (g + 1) * kCols : BN;
+  if (C == 1) {
+    if (warp < 4 * DG && __all_sync(0xffffffffu, finished && !s_abort)) {
+      tc_fence_after();
 #pragma unroll 1
-    for (int col = g * kCols; col < (g + 1) * kCols && m0 + col < a.m; col += 16) {
-      uint32_t r[16];
-      tmem_ld16(lane_addr + uint32_t(col), r);
-      if (n < a.n_rows) {
+      for (int col = g * kCols; col < col_end && m0 + col < a.m; col += 16) {
+        uint32_t r[16];
+        tmem_ld16(lane_addr + uint32_t(col), r);
+        if (n < a.n_rows) {
 #pragma unroll
-        for (int j = 0; j < 16; ++j) {
-          const int mrow = m0 + col + j;
-          if (mrow < a.m) store_out<XT>(a.y, int64_t(mrow) * a.ldy + n, __uint_as_float(r[j]));
+          for (int j = 0; j < 16; ++j) {
+            const int mrow = m0 + col + j;
+            if (mrow < a.m) store_out<XT>(a.y, int64_t(mrow) * a.ldy + n, __uint_as_float(r[j]));
+          }
+        }
+      }
+    }
+  } else {
+    // K split over the cluster: ranks 1..C-1 store their partial tiles into
+    // rank 0's ring (free once every CTA's main loop is over: first cluster
+    // barrier); rank 0 adds them in rank order after the second barrier. Every
+    // thread of every CTA passes both barriers on every path.
+    const uint32_t rank = cluster_rank();
+    tc_fence_before();
+    cluster_sync();
+    if (rank > 0 && warp < 4 * DG) {
+      tc_fence_after();
+      const uint32_t dst = map_to_rank(ring, 0);
+#pragma unroll 1
+      for (int col = g * kCols; col < col_end; col += 16) {
+        uint32_t r[16];
+        tmem_ld16(lane_addr + uint32_t(col), r);
+#pragma unroll
+        for (int j = 0; j < 16; ++j)
+          st_cluster_f32(dst + 4u * uint32_t(((int(rank) - 1) * BN + col + j) * kBM + wq * 32 + lane),
+                         __uint_as_float(r[j]));
+      }
+    }
+    cluster_sync();
+    if (rank == 0 && warp < 4 * DG && __all_sync(0xffffffffu, finished && !s_abort)) {
+      tc_fence_after();
+      const float* part = reinterpret_cast<const float*>(ring_ptr);
+#pragma unroll 1
+      for (int col = g * kCols; col < col_end && m0 + col < a.m; col += 16) {
+        uint32_t r[16];
+        tmem_ld16(lane_addr + uint32_t(col), r);
+        if (n < a.n_rows) {
+#pragma unroll
+          for (int j = 0; j < 16; ++j) {
+            float v = __uint_as_float(r[j]);
+            for (int p = 1; p < C; ++p) v += part[((p - 1) * BN + col + j) * kBM + wq * 32 + lane];
+            const int mrow = m0 + col + j;
+            if (mrow < a.m) store_out<XT>(a.y, int64_t(mrow) * a.ldy + n, v);
+          }
         }
       }
     }
@@ -473,9 +617,9 @@ uint32_t pow2_at_least(uint32_t v) {
   return c;
 }
 
-template <typename XT, int BN, bool NESTED>
-int launch_t(GemmArgs a, const void* x, const uint8_t* w, const DeviceInfo& di, cudaStream_t s) {
-  using T = Tile<BN>;
+template <typename XT, int BN, bool NESTED, bool PRECISE>
+int launch_t(GemmArgs a, const void* x, const uint8_t* w, const DeviceInfo& di, cudaStream_t s, int max_split) {
+  using T = Tile<BN, PRECISE>;
   CUtensorMap map_x, map_w;
   const CUtensorMapDataType dt =
       Elem<XT>::kDtype == BNBQ_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
@@ -484,7 +628,7 @@ int launch_t(GemmArgs a, const void* x, const uint8_t* w, const DeviceInfo& di, 
       !encode_2d(&map_w, CU_TENSOR_MAP_DATA_TYPE_UINT8, w, uint64_t(a.k / 2), uint64_t(a.n_rows),
                  uint64_t(a.k / 2), kBK / 2, kBM, CU_TENSOR_MAP_SWIZZLE_NONE))
     return BNBQ_ERR_CUDA;
-  auto kern = gemm_kernel<XT, BN, NESTED>;
+  auto kern = gemm_kernel<XT, BN, NESTED, PRECISE>;
   cudaFuncAttributes fa;
   if (cudaFuncGetAttributes(&fa, kern) != cudaSuccess) return BNBQ_ERR_CUDA;
   // Paired tiles take just under half of the SM's shared memory (so that no
@@ -495,31 +639,81 @@ int launch_t(GemmArgs a, const void* x, const uint8_t* w, const DeviceInfo& di, 
   int stages = int((smem_cap - 1024) / T::kStageBytes);
   stages = stages < kMaxStages ? stages : kMaxStages;
   const uint32_t tmem_budget = T::kPair ? 256u : 512u;
-  int aslots = int((tmem_budget - uint32_t(BN)) / kAColsPerStage);
+  int aslots = int((tmem_budget - uint32_t(BN)) / T::kACols);
   aslots = aslots < kMaxASlots ? aslots : kMaxASlots;
+  aslots = aslots < stages - 1 ? aslots : stages - 1;
   if (stages <= aslots || aslots <= T::kDG) return BNBQ_ERR_UNSUPPORTED;
   a.n_stages = stages;
   a.n_aslots = aslots;
-  a.tmem_cols = pow2_at_least(uint32_t(BN) + uint32_t(aslots) * kAColsPerStage);
+  a.tmem_cols = pow2_at_least(uint32_t(BN) + uint32_t(aslots) * T::kACols);
   const size_t smem = T::kPair ? (smem_cap / 1024) * 1024 : size_t(stages) * T::kStageBytes + 1024;
   if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem)) != cudaSuccess)
     return BNBQ_ERR_CUDA;
-  const dim3 grid(unsigned((a.m + BN - 1) / BN), unsigned((a.n_rows + kBM - 1) / kBM));
-  kern<<<grid, T::kThreads, smem, s>>>(a, map_x, map_w);
+  // K split across a cluster when the tiles alone leave SMs idle: about one CTA
+  // per SM, at most 8 (portable cluster size), each with >= 2 K blocks, and
+  // the partial tiles of ranks 1.. must fit in rank 0's ring.
+  const int64_t tiles = int64_t((a.m + BN - 1) / BN) * ((a.n_rows + kBM - 1) / kBM);
+  const int kb_all = a.k / kBK;
+  int split = tiles >= di.sm_count ? 1 : int(di.sm_count / tiles);
+  split = split < max_split ? split : max_split;
+  split = split < kb_all / 2 ? split : kb_all / 2;
+  const int fit = 1 + int((size_t(stages) * T::kStageBytes) / (size_t(kBM) * BN * 4));
+  split = split < fit ? split : fit;
+  if (split < 1) split = 1;
+  a.kb_per_split = (kb_all + split - 1) / split;
+  split = (kb_all + a.kb_per_split - 1) / a.kb_per_split;  // no empty CTA
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(unsigned((a.m + BN - 1) / BN), unsigned((a.n_rows + kBM - 1) / kBM), unsigned(split));
+  cfg.blockDim = dim3(T::kThreads);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 1;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = unsigned(split);
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  if (cudaLaunchKernelEx(&cfg, kern, a, map_x, map_w) != cudaSuccess) return BNBQ_ERR_CUDA;
   return launch_status();
 }
 
 template <typename XT, bool NESTED>
 int launch_bn(const GemmArgs& a, const void* x, const uint8_t* w, const DeviceInfo& di, cudaStream_t s) {
-  if (a.m <= 32) return launch_t<XT, 32, NESTED>(a, x, w, di, s);
-  if (a.m <= 64) return launch_t<XT, 64, NESTED>(a, x, w, di, s);
-  if (a.m <= 128) return launch_t<XT, 128, NESTED>(a, x, w, di, s);
-  return launch_t<XT, 256, NESTED>(a, x, w, di, s);
+  if (a.m <= 32) return launch_t<XT, 32, NESTED, false>(a, x, w, di, s, 8);
+  if (a.m <= 64) return launch_t<XT, 64, NESTED, false>(a, x, w, di, s, 8);
+  if (a.m <= 128) return launch_t<XT, 128, NESTED, false>(a, x, w, di, s, 8);
+  return launch_t<XT, 256, NESTED, false>(a, x, w, di, s, 8);
 }
 
 }  // namespace
 
 int gemm_wait_timeouts(unsigned int* out) { return read_wait_timeouts(out); }
+
+// The GEMV's numerics on the tensor cores, for 1 <= m <= 32: every weight as
+// the exact dequantized float32 value split into hi + lo terms of x's dtype,
+// f32 accumulation, K split across a cluster to occupy the SMs. Returns
+// BNBQ_ERR_UNSUPPORTED where the tile does not apply (K % 64, sizes).
+int gemm_precise_launch(int dtype, const void* x, int32_t m, int32_t k, const uint8_t* w, int64_t n_rows,
+                        int32_t blocksize, const float* absmax, const uint8_t* absmax_q, const float* absmax2,
+                        const float* code2, const float* offset, int32_t blocksize2, int64_t absmax2_block0,
+                        void* y, int64_t ldy, cudaStream_t s) {
+  if (m < 1 || m > 32 || (k % kBK) != 0 || n_rows > (int64_t(1) << 31) - kBM || (n_rows + kBM - 1) / kBM > 65535)
+    return BNBQ_ERR_UNSUPPORTED;
+  DeviceInfo di;
+  if (int st = device_info(&di)) return st;
+  GemmArgs a{};
+  a.absmax_q = absmax_q; a.absmax = absmax; a.absmax2 = absmax2; a.code2 = code2; a.offset = offset;
+  a.y = y; a.n_rows = n_rows; a.k = k; a.ldy = ldy; a.block0 = absmax2_block0; a.m = m;
+  a.log2_bs = log2_exact(blocksize);
+  a.log2_bs2 = absmax_q ? log2_exact(blocksize2) : 0;
+  const bool nested = absmax_q != nullptr;
+  if (dtype == BNBQ_BF16)
+    return nested ? launch_t<__nv_bfloat16, 32, true, true>(a, x, w, di, s, 8)
+                  : launch_t<__nv_bfloat16, 32, false, true>(a, x, w, di, s, 8);
+  return nested ? launch_t<__half, 32, true, true>(a, x, w, di, s, 8)
+                : launch_t<__half, 32, false, true>(a, x, w, di, s, 8);
+}
 
 // Arguments are validated by the caller (gemv_validate). Shapes outside the
 // tile's reach (K not a multiple of 64, more than 2^31 - 128 weight rows or

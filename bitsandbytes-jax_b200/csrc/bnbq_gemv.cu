@@ -1084,6 +1084,11 @@ int launch_dispatch(int m, const GemvArgs& a, cudaStream_t s) {
 
 int gemv_wait_timeouts(unsigned int* out) { return read_wait_timeouts(out); }
 
+int gemm_precise_launch(int dtype, const void* x, int32_t m, int32_t k, const uint8_t* w, int64_t n_rows,
+                        int32_t blocksize, const float* absmax, const uint8_t* absmax_q, const float* absmax2,
+                        const float* code2, const float* offset, int32_t blocksize2, int64_t absmax2_block0,
+                        void* y, int64_t ldy, cudaStream_t s);
+
 // Validation shared with the GEMM path (bnbq_gemm.cu).
 int gemv_validate(int dtype, const void* x, int32_t m, int32_t k, const uint8_t* w, int64_t n_rows,
                   int32_t blocksize, const float* absmax, const uint8_t* absmax_q,
@@ -1111,6 +1116,11 @@ int gemv_launch(int dtype, const void* x, int32_t m, int32_t k, const uint8_t* w
                 int64_t absmax2_block0, void* y, int64_t ldy, cudaStream_t s) {
   DeviceInfo di;
   if (int st = device_info(&di)) return st;
+  if (m >= 5) {  // the tensor cores with the GEMV's precision (hi + lo split), where the tile applies
+    const int st = gemm_precise_launch(dtype, x, m, k, w, n_rows, blocksize, absmax, absmax_q, absmax2, code2,
+                                       offset, blocksize2, absmax2_block0, y, ldy, s);
+    if (st != BNBQ_ERR_UNSUPPORTED) return st;
+  }
   GemvArgs a{};
   a.x = x; a.w = w; a.absmax = absmax; a.absmax_q = absmax_q; a.absmax2 = absmax2;
   a.code2 = code2; a.offset = offset; a.y = y; a.n_rows = n_rows; a.ldy = ldy;
