@@ -458,7 +458,7 @@ LLAMA8B = [(4096, 4096), (1024, 4096), (1024, 4096), (4096, 4096), (14336, 4096)
 def run_llama_workload(args, dist, rank, world, local_rank):
     """Config 4: row-sharded GEMV + all-gather over a Llama-3-8B layer stack."""
     import torch
-    from bnb_b200.parallel import all_gather_rows, matmul_rows, quantize_shard, row_partition, shard_rows
+    from bnb_b200.parallel import PeerGather, all_gather_rows, matmul_rows, quantize_shard, row_partition, shard_rows
     device = torch.device("cuda", local_rank)
     torch.cuda.set_device(device)
     layers = 32
@@ -472,19 +472,26 @@ def run_llama_workload(args, dist, rank, world, local_rank):
         w_rows = (torch.randn(n, k, device=device, generator=g)[a:b] * 0.02).to(torch.bfloat16)
         qa = quantize_shard(w_rows, "nf4", BS, double_quant=True, group=None if dist is None else dist.group.WORLD)
         qa = type(qa)(qa.data, qa.absmax, qa.code, qa.offset, qa.qtype, qa.blocksize, (b - a, k), qa.dtype)
-        shards.append(shard_rows(qa, 0, b - a))
+        sh = shard_rows(qa, 0, b - a)  # local arrays (own absmax2, block0 0); global row range below
+        sh.start, sh.stop, sh.n_rows_total = a, b, n
+        shards.append(sh)
         plans.append(ranges)
         weight_bytes += n * k // 2 + n * k // BS + 4 * (n * k // BS // BS2)
         del w_rows
     torch.cuda.synchronize()
     g = torch.Generator(device).manual_seed(5)
     xs = {k: torch.randn(args.m, k, device=device, generator=g).to(torch.bfloat16) for k in (4096, 14336)}
+    peer = args.gather == "peer" and world > 1
+    pgs = {n: PeerGather(args.m, n, torch.bfloat16, device) for n in sorted({n for n, _ in LLAMA8B})} if peer else {}
 
     def step():
         for sh, ranges in zip(shards, plans):
             y = matmul_rows(xs[sh.k], sh)
             if world > 1:
-                all_gather_rows(y, ranges)
+                if peer:
+                    pgs[sh.n_rows_total].gather(y, sh.start)
+                else:
+                    all_gather_rows(y, ranges)
 
     for _ in range(max(args.warmup, 3)):
         step()
@@ -524,7 +531,8 @@ def run_llama_workload(args, dist, rank, world, local_rank):
             "value": round(weight_bytes / (per * 1e-3) / 1e9, 1), "unit": "GB/s", "n_gpus": world, "steps": steps,
             "warmup": args.warmup, "ms_per_step": round(per, 4), "higher_is_better": True, "scaling": "strong",
             "vs_baseline": None, "dtype": "bf16", "data": "synthetic (seeded torch Philox)",
-            "config": {"workload": "config 4: 32 layers x 7 NF4 matrices, M=%d, row-sharded over %d GPUs, all-gather of y" % (args.m, world),
+            "config": {"workload": "config 4: 32 layers x 7 NF4 matrices, M=%d, row-sharded over %d GPUs, all-gather of y (%s)"
+                       % (args.m, world, "NVLink peer stores" if peer else ("NCCL" if world > 1 else "none")),
                        "weight_bytes_per_step": weight_bytes, "timing": "CUDA graph of one pass, replayed per step",
                        "parallelism": f"tp{world} (rows)"},
             "clocks": clocks.summary()}
@@ -580,6 +588,7 @@ def main():
     ap.add_argument("--no-sweep", dest="sweep", action="store_false")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--workload", choices=["gemv", "quant", "gemm", "llama"], default="gemv")
+    ap.add_argument("--gather", choices=["peer", "nccl"], default="peer", help="config 4 all-gather")
     args = ap.parse_args()
 
     world = int(os.environ.get("WORLD_SIZE", "1"))

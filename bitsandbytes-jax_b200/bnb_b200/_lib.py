@@ -35,6 +35,11 @@ _SIGNATURES = {
     "bnbq_rcp_approx_ftz": "PPlP",
     "bnbq_version": "",
     "bnbq_wait_timeouts": "P",
+    "bnbq_peer_allgather_rows": "iPillllPPPiiP",
+    "bnbq_enable_peer_access": "i",
+    "bnbq_ipc_handle": "PPP",
+    "bnbq_ipc_open": "PP",
+    "bnbq_ipc_close": "P",
 }
 _KIND = {"i": C.c_int32, "l": C.c_int64, "P": C.c_void_p, "p": C.c_void_p}
 

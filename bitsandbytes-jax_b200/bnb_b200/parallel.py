@@ -32,6 +32,7 @@ from .array import _NESTED_BLOCKSIZE, QuantizedArray
 from .kernels import create_dynamic_map, quantize_blockwise, quantize_nf4
 
 __all__ = [
+    "PeerGather",
     "RowShard",
     "all_gather_flat",
     "all_gather_rows",
@@ -148,6 +149,112 @@ def all_gather_rows(y_local: torch.Tensor, ranges: list[tuple[int, int]], group=
     piece[:, :y_local.shape[1]] = y_local
     parts = _all_gather_bytes(piece, world, group)
     return torch.cat([p[:, :b - a] for p, (a, b) in zip(parts, ranges)], dim=1)
+
+
+# CUDA IPC mappings opened in this process, by (device, handle): one handle can
+# be opened only once per process, and small buffers of different owners'
+# tensors often share one allocation (and so one handle).
+_IPC_OPEN: dict[tuple[int, bytes], list[int]] = {}  # -> [base, references]
+
+
+def _ipc_open(device: torch.device, handle: bytes) -> int:
+    import ctypes as C
+    from . import _lib
+    key = (device.index, handle)
+    if key not in _IPC_OPEN:
+        base = C.c_void_p(0)
+        hb = C.create_string_buffer(handle, 64)
+        with torch.cuda.device(device):
+            _lib.call("bnbq_ipc_open", C.cast(hb, C.c_void_p), C.addressof(base))
+        _IPC_OPEN[key] = [base.value, 0]
+    _IPC_OPEN[key][1] += 1
+    return _IPC_OPEN[key][0]
+
+
+def _ipc_close(device: torch.device, handle: bytes) -> None:
+    from . import _lib
+    key = (device.index, handle)
+    entry = _IPC_OPEN[key]
+    entry[1] -= 1
+    if entry[1] == 0:
+        with torch.cuda.device(device):
+            _lib.call("bnbq_ipc_close", entry[0])
+        del _IPC_OPEN[key]
+
+
+class PeerGather:
+    """All-gather of row-sharded outputs through NVLink peer memory.
+
+    Every rank allocates a full output buffer (``max_rows`` x ``n_total``), a
+    flag array and a small state word; the buffers are shared with the other
+    ranks through CUDA IPC (torch's tensor reduction, handles exchanged with
+    ``all_gather_object``). :meth:`gather` then enqueues ONE kernel
+    (``bnbq_peer_allgather_rows``) that stores this rank's slice into every
+    rank's buffer and waits, bounded, for the peers' slices -- no NCCL call on
+    the data path. Construct it on every rank of ``group`` (a collective).
+    The returned tensor is a view of this rank's buffer: the peers overwrite it
+    during their next :meth:`gather`, so consume it on the stream before the
+    next call."""
+
+    def __init__(self, max_rows: int, n_total: int, dtype: torch.dtype, device: torch.device, group=None):
+        import ctypes as C
+        from . import _lib
+        self.world = dist.get_world_size(group)
+        self.rank = dist.get_rank(group)
+        self.n_total = n_total
+        self.max_rows = max_rows
+        self.dtype = dtype
+        self.device = torch.device(device)
+        self.y_full = torch.zeros((max_rows, n_total), dtype=dtype, device=device)
+        self.flags = torch.zeros(self.world, dtype=torch.int32, device=device)
+        self.state = torch.zeros(2, dtype=torch.int32, device=device)
+        torch.cuda.synchronize(device)
+
+        def export(t):
+            h = C.create_string_buffer(64)
+            off = C.c_int64(0)
+            with torch.cuda.device(self.device):
+                _lib.call("bnbq_ipc_handle", t.data_ptr(), C.cast(h, C.c_void_p), C.addressof(off))
+            return h.raw, off.value
+
+        mine = (export(self.y_full), export(self.flags))
+        objs: list = [None] * self.world
+        dist.all_gather_object(objs, mine, group=group)
+        self._opened: list[bytes] = []  # the peers' handles mapped here
+        y_ptrs, f_ptrs = [], []
+        for r, ((hy, oy), (hf, of)) in enumerate(objs):
+            if r == self.rank:
+                y_ptrs.append(self.y_full.data_ptr())
+                f_ptrs.append(self.flags.data_ptr())
+                continue
+            y_ptrs.append(_ipc_open(self.device, hy) + oy)
+            f_ptrs.append(_ipc_open(self.device, hf) + of)
+            self._opened += [hy, hf]
+        self.y_ptrs = torch.tensor(y_ptrs, dtype=torch.int64, device=device)
+        self.f_ptrs = torch.tensor(f_ptrs, dtype=torch.int64, device=device)
+        dist.barrier(group=group)
+
+    def close(self) -> None:
+        """Unmap the peers' buffers (every rank, after its last gather has completed)."""
+        torch.cuda.synchronize(self.device)
+        for handle in self._opened:
+            _ipc_close(self.device, handle)
+        self._opened = []
+
+    def gather(self, y_local: torch.Tensor, col0: int) -> torch.Tensor:
+        """Columns [col0, col0 + y_local.shape[1]) from this rank, the rest
+        from the peers: the full (m, n_total) output."""
+        from . import _lib
+        m, n_local = y_local.shape
+        if m > self.max_rows or y_local.dtype != self.dtype:
+            raise ValueError(f"y {tuple(y_local.shape)} {y_local.dtype} does not fit this gather "
+                             f"({self.max_rows} rows, {self.dtype})")
+        assert y_local.stride(1) == 1
+        with torch.cuda.device(y_local.device):
+            _lib.call("bnbq_peer_allgather_rows", _lib.DTYPE_CODE[y_local.dtype], y_local.data_ptr(), m, n_local,
+                      y_local.stride(0), col0, self.n_total, self.y_ptrs.data_ptr(), self.f_ptrs.data_ptr(),
+                      self.state.data_ptr(), self.world, self.rank, _lib.stream_of(y_local))
+        return self.y_full[:m]
 
 
 def matmul_sharded(x: torch.Tensor, shard: RowShard, ranges: list[tuple[int, int]] | None = None,

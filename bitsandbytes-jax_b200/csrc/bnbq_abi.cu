@@ -15,6 +15,7 @@ int gemv_launch(int dtype, const void* x, int32_t m, int32_t k, const uint8_t* w
                 int64_t absmax2_block0, void* y, int64_t ldy, cudaStream_t s);
 int gemv_wait_timeouts(unsigned int* out);
 int gemm_wait_timeouts(unsigned int* out);
+int peer_wait_timeouts(unsigned int* out);
 int gemm_launch(int dtype, const void* x, int32_t m, int32_t k, const uint8_t* w, int64_t n_rows,
                 int32_t blocksize, const float* absmax, const uint8_t* absmax_q,
                 const float* absmax2, const float* code2, const float* offset, int32_t blocksize2,
@@ -90,10 +91,26 @@ extern "C" int bnbq_wait_timeouts(unsigned int* count) {
   if (!count) return BNBQ_ERR_INVALID;
   DeviceInfo di;
   if (int st = device_info(&di)) return st;
-  unsigned int g = 0, h = 0;
-  if (gemv_wait_timeouts(&g) != 0 || gemm_wait_timeouts(&h) != 0) return BNBQ_ERR_CUDA;
-  *count = g + h;
+  unsigned int g = 0, h = 0, p = 0;
+  if (gemv_wait_timeouts(&g) != 0 || gemm_wait_timeouts(&h) != 0 || peer_wait_timeouts(&p) != 0)
+    return BNBQ_ERR_CUDA;
+  *count = g + h + p;
   return BNBQ_OK;
+}
+
+extern "C" int bnbq_enable_peer_access(int peer_device) {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return BNBQ_ERR_CUDA;
+  if (peer_device == dev) return BNBQ_OK;
+  int can = 0;
+  if (cudaDeviceCanAccessPeer(&can, dev, peer_device) != cudaSuccess) return BNBQ_ERR_CUDA;
+  if (!can) return BNBQ_ERR_UNSUPPORTED;
+  const cudaError_t e = cudaDeviceEnablePeerAccess(peer_device, 0);
+  if (e == cudaErrorPeerAccessAlreadyEnabled) {
+    cudaGetLastError();  // clear the non-sticky status
+    return BNBQ_OK;
+  }
+  return e == cudaSuccess ? BNBQ_OK : BNBQ_ERR_CUDA;
 }
 
 extern "C" const char* bnbq_error_string(int status) {

@@ -1,0 +1,173 @@
+// bnbq_peer.cu -- all-gather of row-sharded GEMV/GEMM outputs over NVLink peer
+// memory (the exchange step of the N-sharded matmul).
+//
+// Every rank computes y[:, col0 : col0 + n_local] with the fused kernels and
+// then launches bnbq_peer_allgather_rows on the same stream (programmatic
+// dependent launch: it starts while the matmul drains and waits for it with
+// griddepcontrol.wait). Its CTAs store the rank's slice into the full-y buffer
+// of EVERY rank with plain stores to peer memory (CUDA IPC mappings over
+// NVLink; no multicast, no TMA). The last CTA to finish (a local arrival
+// counter it resets) makes the stores visible system-wide and publishes the
+// rank's epoch in each peer's flag array, then waits, bounded in time, until
+// every peer has published the same epoch in this rank's flags. The epoch lives
+// in device memory (state[1]) and advances once per call, so replays of a
+// captured CUDA graph stay in step. On expiry of the wait the kernel records a
+// timeout (bnbq_wait_timeouts) and returns; the output is then incomplete.
+#include "bnbq_async.cuh"
+#include "bnbq_common.cuh"
+
+namespace bnbq {
+namespace {
+
+constexpr uint64_t kPeerWaitLimitNs = 10000000000ull;  // 10 s: a peer that is this late has failed
+
+__device__ __forceinline__ void st_release_sys(uint32_t* p, uint32_t v) {
+  asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+__device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* p) {
+  uint32_t v;
+  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+
+// y_local: m x n_local (row stride ld_local) 16-bit values; y_full[d]: rank d's
+// m x ldy buffer; flags[d]: rank d's uint32[world]; state: this rank's
+// {arrived CTAs, epoch}.
+__global__ void __launch_bounds__(256) peer_allgather_kernel(const uint16_t* y_local, int m, int64_t n_local,
+                                                             int64_t ld_local, int64_t col0, int64_t ldy,
+                                                             uint16_t* const* y_full, uint32_t* const* flags,
+                                                             uint32_t* state, int world, int rank, int vec) {
+  asm volatile("griddepcontrol.wait;" ::: "memory");  // the matmul that wrote y_local has completed
+  const uint32_t epoch = state[1] + 1u;  // read before any CTA can advance it (advanced by the last CTA only)
+  const int64_t per_row = vec ? n_local / 8 : n_local;  // 16-byte pieces or single values
+  const int64_t total = int64_t(m) * per_row;
+  for (int64_t i = int64_t(blockIdx.x) * blockDim.x + threadIdx.x; i < total; i += int64_t(gridDim.x) * blockDim.x) {
+    const int64_t r = i / per_row, c = i - r * per_row;
+    if (vec) {
+      const uint4 v = *reinterpret_cast<const uint4*>(y_local + r * ld_local + 8 * c);
+      for (int d = 0; d < world; ++d)
+        *reinterpret_cast<uint4*>(y_full[d] + r * ldy + col0 + 8 * c) = v;
+    } else {
+      const uint16_t v = y_local[r * ld_local + c];
+      for (int d = 0; d < world; ++d) y_full[d][r * ldy + col0 + c] = v;
+    }
+  }
+  __threadfence_system();  // this thread's peer stores, before the CTA reports
+  __syncthreads();
+  __shared__ int s_last;
+  if (threadIdx.x == 0) s_last = atomicAdd(&state[0], 1u) == gridDim.x - 1;
+  __syncthreads();
+  if (!s_last || threadIdx.x != 0) return;
+  // last CTA of this rank: every CTA's stores are fenced (they fenced before arriving)
+  state[0] = 0;  // no CTA of this launch touches the counter again
+  __threadfence_system();
+  for (int d = 0; d < world; ++d) st_release_sys(flags[d] + rank, epoch);
+  const uint32_t* mine = flags[rank];
+  const uint64_t t0 = global_ns();
+  for (int src = 0; src < world; ++src) {
+    while (int32_t(ld_acquire_sys(mine + src) - epoch) < 0) {
+      if (global_ns() - t0 > kPeerWaitLimitNs) {
+        atomicAdd(&g_bnbq_wait_timeouts, 1u);
+        state[1] = epoch;  // stay in step with the peers that did publish
+        return;
+      }
+      __nanosleep(256);
+    }
+  }
+  state[1] = epoch;
+}
+
+}  // namespace
+
+int peer_wait_timeouts(unsigned int* out) { return read_wait_timeouts(out); }
+
+}  // namespace bnbq
+
+using namespace bnbq;
+
+#include <cuda.h>
+#include <cudaTypedefs.h>
+
+#include <cstring>
+#include <mutex>
+
+// IPC export of the allocation that contains `ptr`: the 64-byte handle and the
+// offset of `ptr` from the allocation's base (cudaIpcGetMemHandle wants a base).
+extern "C" int bnbq_ipc_handle(const void* ptr, void* handle_out, int64_t* offset_out) {
+  if (!ptr || !handle_out || !offset_out) return BNBQ_ERR_INVALID;
+  static PFN_cuMemGetAddressRange_v3020 get_range = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* fn = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuMemGetAddressRange", &fn, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      get_range = reinterpret_cast<PFN_cuMemGetAddressRange_v3020>(fn);
+  });
+  if (!get_range) return BNBQ_ERR_CUDA;
+  CUdeviceptr base = 0;
+  size_t size = 0;
+  if (get_range(&base, &size, reinterpret_cast<CUdeviceptr>(ptr)) != CUDA_SUCCESS) return BNBQ_ERR_INVALID;
+  cudaIpcMemHandle_t h;
+  if (cudaIpcGetMemHandle(&h, reinterpret_cast<void*>(base)) != cudaSuccess) return BNBQ_ERR_CUDA;
+  std::memcpy(handle_out, &h, sizeof(h));
+  *offset_out = int64_t(reinterpret_cast<uintptr_t>(ptr) - uintptr_t(base));
+  return BNBQ_OK;
+}
+
+// Map another process's allocation into the CURRENT device's context (peer
+// access to the owner enabled as needed) and check that the mapping is device
+// memory before any kernel touches it.
+extern "C" int bnbq_ipc_open(const void* handle, void** base_out) {
+  if (!handle || !base_out) return BNBQ_ERR_INVALID;
+  cudaIpcMemHandle_t h;
+  std::memcpy(&h, handle, sizeof(h));
+  void* p = nullptr;
+  if (cudaIpcOpenMemHandle(&p, h, cudaIpcMemLazyEnablePeerAccess) != cudaSuccess) return BNBQ_ERR_CUDA;
+  cudaPointerAttributes at;
+  if (cudaPointerGetAttributes(&at, p) != cudaSuccess || at.type != cudaMemoryTypeDevice) {
+    cudaIpcCloseMemHandle(p);
+    return BNBQ_ERR_CUDA;
+  }
+  *base_out = p;
+  return BNBQ_OK;
+}
+
+extern "C" int bnbq_ipc_close(void* base) {
+  return cudaIpcCloseMemHandle(base) == cudaSuccess ? BNBQ_OK : BNBQ_ERR_CUDA;
+}
+
+extern "C" int bnbq_peer_allgather_rows(int dtype, const void* y_local, int32_t m, int64_t n_local, int64_t ld_local,
+                                        int64_t col0, int64_t ldy, void* const* y_full, uint32_t* const* flags,
+                                        uint32_t* state, int32_t world, int32_t rank, void* stream) {
+  if (dtype != BNBQ_F16 && dtype != BNBQ_BF16) return BNBQ_ERR_UNSUPPORTED;
+  if (m < 0 || n_local < 0 || world < 1 || rank < 0 || rank >= world || ld_local < n_local || col0 < 0 ||
+      ldy < col0 + n_local)
+    return BNBQ_ERR_INVALID;
+  if (!y_full || !flags || !state || (m > 0 && n_local > 0 && !y_local)) return BNBQ_ERR_INVALID;
+  if (!aligned(y_local, 2) || !aligned(state, 4) || !aligned(y_full, 8) || !aligned(flags, 8))
+    return BNBQ_ERR_MISALIGNED;
+  DeviceInfo di;
+  if (int st = device_info(&di)) return st;
+  // 16-byte pieces when every row start on both sides is 16-byte aligned (the
+  // full-y buffers themselves are 16-byte aligned allocations)
+  const int vec = (n_local % 8 == 0 && col0 % 8 == 0 && ldy % 8 == 0 && ld_local % 8 == 0 && aligned(y_local, 16)) ? 1 : 0;
+  const int64_t work = int64_t(m) * (vec ? n_local / 8 : n_local);
+  int64_t grid = (work + 255) / 256;
+  if (grid < 1) grid = 1;
+  if (grid > int64_t(di.sm_count)) grid = di.sm_count;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(unsigned(grid));
+  cfg.blockDim = dim3(256);
+  cfg.stream = static_cast<cudaStream_t>(stream);
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  if (cudaLaunchKernelEx(&cfg, peer_allgather_kernel, static_cast<const uint16_t*>(y_local), int(m), n_local,
+                         ld_local, col0, ldy, reinterpret_cast<uint16_t* const*>(y_full), flags, state, int(world),
+                         int(rank), vec) != cudaSuccess)
+    return BNBQ_ERR_CUDA;
+  return launch_status();
+}

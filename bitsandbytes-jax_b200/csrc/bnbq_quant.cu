@@ -491,18 +491,38 @@ int64_t work_warps(const QuantArgs& a) {
   return a.log2_bs <= 8 ? (a.n + 255) >> 8 : a.nb;
 }
 
-// offset[0] = mean(absmax): one CTA, double accumulation in a fixed order.
+// offset[0] = mean(absmax), float64 accumulation in a fixed order: one cluster
+// of kMeanCtas CTAs; CTA c sums the strided elements c*1024 + t (+ i*kMeanCtas*1024)
+// per thread, reduces its 1024 partials in a fixed tree, and rank 0 adds the
+// CTAs' sums in rank order (distributed shared memory, between two cluster
+// barriers that every thread passes).
+constexpr int kMeanCtas = 8;
+
 __global__ void __launch_bounds__(1024) mean_kernel(const float* a, int64_t n, float* out) {
   __shared__ double part[1024];
+  __shared__ double ctas[kMeanCtas];
+  uint32_t rank;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(rank));
   double s = 0.0;
-  for (int64_t i = threadIdx.x; i < n; i += 1024) s += double(a[i]);
+  for (int64_t i = int64_t(rank) * 1024 + threadIdx.x; i < n; i += int64_t(kMeanCtas) * 1024) s += double(a[i]);
   part[threadIdx.x] = s;
   __syncthreads();
   for (int w = 512; w > 0; w >>= 1) {
     if (threadIdx.x < w) part[threadIdx.x] += part[threadIdx.x + w];
     __syncthreads();
   }
-  if (threadIdx.x == 0) out[0] = float(part[0] / double(n));
+  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+  if (threadIdx.x == 0) {
+    uint32_t dst;
+    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(dst) : "r"(uint32_t(__cvta_generic_to_shared(&ctas[rank]))), "r"(0));
+    asm volatile("st.shared::cluster.f64 [%0], %1;" ::"r"(dst), "d"(part[0]) : "memory");
+  }
+  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+  if (rank == 0 && threadIdx.x == 0) {
+    double t = 0.0;
+    for (int c = 0; c < kMeanCtas; ++c) t += ctas[c];
+    out[0] = float(t / double(n));
+  }
 }
 
 }  // namespace
@@ -549,6 +569,17 @@ extern "C" int bnbq_absmax_mean(const float* absmax, int64_t nb, float* offset, 
   if (!aligned(absmax, 4) || !aligned(offset, 4)) return BNBQ_ERR_MISALIGNED;
   DeviceInfo di;
   if (int st = device_info(&di)) return st;
-  mean_kernel<<<1, 1024, 0, static_cast<cudaStream_t>(stream)>>>(absmax, nb, offset);
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(kMeanCtas);
+  cfg.blockDim = dim3(1024);
+  cfg.stream = static_cast<cudaStream_t>(stream);
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = kMeanCtas;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  if (cudaLaunchKernelEx(&cfg, mean_kernel, absmax, nb, offset) != cudaSuccess) return BNBQ_ERR_CUDA;
   return launch_status();
 }

@@ -151,6 +151,42 @@ BNBQ_API int bnbq_matmul_nf4(int dtype, const void* x, int32_t m, int32_t k,
 
 /* ------------------------------------------------------------ diagnostics */
 
+/* All-gather of a row-sharded matmul output over NVLink peer memory (the
+ * exchange of the N-sharded GEMV/GEMM; the reference has no counterpart -- it
+ * runs on one device -- and NCCL's all-gather is the portable alternative).
+ * y_local: this rank's m x n_local slice (row stride ld_local, dtype F16/BF16),
+ * destined for columns [col0, col0 + n_local) of every rank's full output.
+ * y_full: device array of `world` pointers, rank d's m x ldy buffer (IPC-mapped
+ * peer memory; 16-byte aligned allocations). flags: device array of `world`
+ * pointers to each rank's uint32[world] flag array (zero-initialised once).
+ * state: this rank's uint32[2] (zero-initialised once; the kernel keeps it).
+ * Enqueued on `stream` after the matmul that wrote y_local (it waits for it);
+ * on return of the kernel every rank's slice is in this rank's y_full. Every
+ * rank must make the same sequence of calls. The wait for peers is bounded
+ * (10 s); an expiry is counted by bnbq_wait_timeouts. A rank's y_full is
+ * written by its peers during their next call: consume it on the stream before
+ * calling again. */
+/* CUDA IPC of the buffers the peer all-gather writes (no counterpart in the
+ * reference). bnbq_ipc_handle exports the allocation containing `ptr`: 64
+ * bytes into handle_out and ptr's offset from the allocation base.
+ * bnbq_ipc_open maps such a handle from another process into the current
+ * device's context (peer access enabled as needed) and returns the base;
+ * bnbq_ipc_close unmaps it. */
+BNBQ_API int bnbq_ipc_handle(const void* ptr, void* handle_out, int64_t* offset_out);
+BNBQ_API int bnbq_ipc_open(const void* handle, void** base_out);
+BNBQ_API int bnbq_ipc_close(void* base);
+
+/* Let kernels on the current device access memory of `peer_device` (CUDA peer
+ * access of this process's context; needed before bnbq_peer_allgather_rows
+ * stores into IPC mappings of another device's memory). BNBQ_OK if enabled or
+ * already enabled, BNBQ_ERR_UNSUPPORTED if the devices cannot be peers. No
+ * counterpart in the reference. */
+BNBQ_API int bnbq_enable_peer_access(int peer_device);
+
+BNBQ_API int bnbq_peer_allgather_rows(int dtype, const void* y_local, int32_t m, int64_t n_local, int64_t ld_local,
+                                      int64_t col0, int64_t ldy, void* const* y_full, uint32_t* const* flags,
+                                      uint32_t* state, int32_t world, int32_t rank, void* stream);
+
 /* out[i] = rcp.approx.ftz.f32(in[i]): the hardware reciprocal the quantize kernels
  * use for 1/absmax (kernels/_ptx.py:20-22). Lets a CPU checker take the device's
  * own reciprocal instead of modelling it. */

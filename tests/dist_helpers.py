@@ -6,6 +6,7 @@ import datetime
 import multiprocessing as mp
 import os
 import socket
+import sys
 import traceback
 
 
@@ -28,7 +29,9 @@ def _entry(fn, rank, world, port, queue, args):
             dist.destroy_process_group()
         queue.put((rank, None))
     except BaseException:  # reported to the parent, which fails the test
-        queue.put((rank, traceback.format_exc()))
+        tb = traceback.format_exc()
+        print(f"rank {rank}:\n{tb}", file=sys.stderr, flush=True)  # survives a crash during teardown
+        queue.put((rank, tb))
 
 
 def run_ranks(fn, world: int, *args, timeout: float = 180.0) -> None:

@@ -18,8 +18,8 @@ def _worker(rank, world, port, queue):
     try:
         import torch.distributed as dist
         import bnb_b200 as bnb
-        from bnb_b200.parallel import (all_gather_flat, block_partition, matmul_sharded, quantize_shard,
-                                       row_partition, shard_rows)
+        from bnb_b200.parallel import (PeerGather, all_gather_flat, block_partition, matmul_rows, matmul_sharded,
+                                       quantize_shard, row_partition, shard_rows)
         os.environ["MASTER_ADDR"] = "127.0.0.1"
         os.environ["MASTER_PORT"] = str(port)
         torch.cuda.set_device(rank)
@@ -37,6 +37,29 @@ def _worker(rank, world, port, queue):
                 x = torch.randn(m, k, device=dev, generator=g).to(torch.bfloat16)
                 y = matmul_sharded(x, shard, ranges)
                 assert torch.equal(y, bnb.matmul(x, w)), m
+            # the same exchange through NVLink peer memory, eager and from a CUDA graph
+            pg = PeerGather(20, n, torch.bfloat16, dev)
+            for m in (1, 7, 20, 3):
+                x = torch.randn(m, k, device=dev, generator=g).to(torch.bfloat16)
+                y = pg.gather(matmul_rows(x, shard), ranges[rank][0]).clone()
+                assert torch.equal(y, bnb.matmul(x, w)), ("peer", m)
+            xg = torch.randn(8, k, device=dev, generator=g).to(torch.bfloat16)
+            want = bnb.matmul(xg, w)
+            out = torch.empty_like(want)
+            stream = torch.cuda.Stream(dev)
+            graph = torch.cuda.CUDAGraph()
+            with torch.cuda.stream(stream):
+                with torch.cuda.graph(graph, stream=stream):
+                    for _ in range(2):
+                        out.copy_(pg.gather(matmul_rows(xg, shard), ranges[rank][0]))
+            for _ in range(3):
+                out.zero_()
+                graph.replay()
+                torch.cuda.synchronize()
+                assert torch.equal(out, want), "graph replay"
+            del graph
+            from bnb_b200 import _lib
+            assert _lib.wait_timeouts() == 0
             # block-sharded quantize == the whole tensor's codes and absmax
             nel = 3 * 64 * 256 + 37
             xf = torch.randn(nel, device=dev, generator=g).to(torch.bfloat16)
@@ -56,7 +79,10 @@ def _worker(rank, world, port, queue):
             dist.destroy_process_group()
         queue.put((rank, None))
     except BaseException:
-        queue.put((rank, traceback.format_exc()))
+        import sys
+        tb = traceback.format_exc()
+        print(f"rank {rank}:\n{tb}", file=sys.stderr, flush=True)  # survives a crash during teardown
+        queue.put((rank, tb))
 
 
 @pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device_count() < 2, reason="needs 2 GPUs")
