@@ -18,7 +18,8 @@
 //                          the stage's barrier) of the block scales of the stage's
 //                          128 rows: float32 absmax, or the nested code word and
 //                          absmax2; the ring's depth is the prefetch distance.
-//   decoder groups         DG groups of 4 warps, group g taking stages g, g+DG, ...;
+//   decoder groups         DG groups of 4 warps (DG = 2; 4 for the precise split),
+//                          group g taking stages g, g+DG, ...;
 //                          thread t of a group owns weight row t: it decodes the
 //                          row's block scale a (nested: code2[q] * absmax2 +
 //                          offset) and builds the 16-entry table dtype(mul.ftz(T[q], a)) in
@@ -26,6 +27,13 @@
 //                          byte permutes and writes them with tcgen05.st into its
 //                          lane of an A slot in tensor memory (32 columns; a ring
 //                          of SA slots, separate from the shared-memory ring).
+//   precise split (GEMV)   the weight's exact float32 value w as hi = RN(w) plus
+//                          lo = RZ(w - hi) in x's dtype: two A terms, two MMAs per
+//                          K step into the same accumulator. Each decoder lane keeps
+//                          its block's 16 (hi | lo << 16) words in a warp-private
+//                          shared table [q][lane] (bank = lane) and decodes a value
+//                          with one load. Rounding hi + lo gives hi back in every
+//                          case, so a one-hot x returns the decoded weights bitwise.
 //   MMA warp               tensor memory allocation; one thread issues the stage's
 //                          four K=16 MMAs (A from tensor memory, x from shared
 //                          memory) and a tcgen05.commit that frees the ring slot
@@ -71,6 +79,8 @@ struct Tile {
   static constexpr bool kPair = BN <= 64 && !PRECISE;  // the precise (GEMV) tiles run one CTA per SM
   static constexpr uint32_t kBBytes = BN * kBK * 2;
   static constexpr uint32_t kStageBytes = kBBytes + kCodeBytes + kScaleBytes;  // a multiple of 1024
+  // precise decoders: a warp-private 16 x 32 table of (hi | lo << 16) words after the ring
+  static constexpr uint32_t kTableBytes = PRECISE ? 4 * kDG * 16 * 32 * 4 : 0;
 };
 
 struct GemmArgs {
@@ -229,34 +239,6 @@ __device__ __forceinline__ void block_table(float a, uint32_t (&lo)[4], uint32_t
     const uint32_t p1 = pack2<XT>(mul_ftz(kNF4Table[4 * j + 2], a), mul_ftz(kNF4Table[4 * j + 3], a));
     lo[j] = prmt(p0, p1, 0x6420);
     hi[j] = prmt(p0, p1, 0x7531);
-  }
-}
-
-// Precise split of the same 16 values w_q = mul.ftz(T[q], a): hi = dtype(w)
-// rounded to nearest (the planes lo/hi, as block_table) and the residual
-// r = dtype(w - hi) rounded toward zero (planes rlo/rhi). hi + r equals w to
-// within 2^-16 |w|, and rounding hi + r to dtype gives hi back in every case
-// (|r| < half an ulp of hi, or exactly half when w was a tie), so a one-hot
-// x still returns the decoded weights bitwise. An infinite hi gets r = 0.
-template <typename XT>
-__device__ __forceinline__ void block_table_split(float a, uint32_t (&lo)[4], uint32_t (&hi)[4], uint32_t (&rlo)[4],
-                                                  uint32_t (&rhi)[4]) {
-#pragma unroll
-  for (int j = 0; j < 4; ++j) {
-    float w[4];
-#pragma unroll
-    for (int i = 0; i < 4; ++i) w[i] = mul_ftz(kNF4Table[4 * j + i], a);
-    const uint32_t p0 = pack2<XT>(w[0], w[1]), p1 = pack2<XT>(w[2], w[3]);
-    const float2 h0 = unpack2x<XT>(p0), h1 = unpack2x<XT>(p1);
-    const float hv[4] = {h0.x, h0.y, h1.x, h1.y};
-    float r[4];
-#pragma unroll
-    for (int i = 0; i < 4; ++i) r[i] = isinf(hv[i]) ? 0.0f : sub_rn(w[i], hv[i]);
-    const uint32_t q0 = pack2_rz<XT>(r[0], r[1]), q1 = pack2_rz<XT>(r[2], r[3]);
-    lo[j] = prmt(p0, p1, 0x6420);
-    hi[j] = prmt(p0, p1, 0x7531);
-    rlo[j] = prmt(q0, q1, 0x6420);
-    rhi[j] = prmt(q0, q1, 0x7531);
   }
 }
 
@@ -460,29 +442,41 @@ gemm_kernel(const GemmArgs a, const __grid_constant__ CUtensorMap tmap_x, const 
       const uint32_t cols = lane_addr + uint32_t(BN) + uint32_t(sa) * kACols;
       uint32_t v[16], lo[4], hi[4];
       if constexpr (PRECISE) {
-        uint32_t rlo[4], rhi[4];
-        block_table_split<XT>(scale(sp, kb, 0), lo, hi, rlo, rhi);
-        decode_word(c0.x, lo, hi, v + 0);
-        decode_word(c0.y, lo, hi, v + 4);
-        decode_word(c0.z, lo, hi, v + 8);
-        decode_word(c0.w, lo, hi, v + 12);
+        // lane-private table: entry q of this lane at tab[q * 32 + lane] (bank = lane)
+        uint32_t* const tab = reinterpret_cast<uint32_t*>(ring_ptr + size_t(S) * kStage) + warp * (16 * 32);
+        auto build = [&](float a_) {
+#pragma unroll
+          for (int q = 0; q < 16; q += 2) {
+            const float w0 = mul_ftz(kNF4Table[q], a_), w1 = mul_ftz(kNF4Table[q + 1], a_);
+            const uint32_t p = pack2<XT>(w0, w1);  // hi terms, nearest
+            const float2 h = unpack2x<XT>(p);
+            const uint32_t r = pack2_rz<XT>(isinf(h.x) ? 0.0f : sub_rn(w0, h.x), isinf(h.y) ? 0.0f : sub_rn(w1, h.y));
+            tab[q * 32 + lane] = prmt(p, r, 0x5410);        // (hi, lo) of entry q
+            tab[(q + 1) * 32 + lane] = prmt(p, r, 0x7632);  // of entry q + 1
+          }
+        };
+        // 4 code words (32 values) -> 16 words of hi pairs and 16 of lo pairs
+        auto decode4 = [&](const uint32_t (&wd)[4], uint32_t (&vh)[16], uint32_t (&vl)[16]) {
+#pragma unroll
+          for (int i = 0; i < 4; ++i)
+#pragma unroll
+            for (int b = 0; b < 4; ++b) {
+              const uint32_t e0 = tab[((wd[i] >> (8 * b + 4)) & 15u) * 32 + lane];  // value 2b: high nibble
+              const uint32_t e1 = tab[((wd[i] >> (8 * b)) & 15u) * 32 + lane];
+              vh[4 * i + b] = prmt(e0, e1, 0x5410);
+              vl[4 * i + b] = prmt(e0, e1, 0x7632);
+            }
+        };
+        const uint32_t w0[4] = {c0.x, c0.y, c0.z, c0.w}, w1[4] = {c1.x, c1.y, c1.z, c1.w};
+        uint32_t vl[16];
+        build(scale(sp, kb, 0));
+        decode4(w0, v, vl);
         tmem_st16(cols, v);
-        decode_word(c0.x, rlo, rhi, v + 0);
-        decode_word(c0.y, rlo, rhi, v + 4);
-        decode_word(c0.z, rlo, rhi, v + 8);
-        decode_word(c0.w, rlo, rhi, v + 12);
-        tmem_st16(cols + kAColsPerStage, v);
-        if (two) block_table_split<XT>(scale(sp, kb, 1), lo, hi, rlo, rhi);
-        decode_word(c1.x, lo, hi, v + 0);
-        decode_word(c1.y, lo, hi, v + 4);
-        decode_word(c1.z, lo, hi, v + 8);
-        decode_word(c1.w, lo, hi, v + 12);
+        tmem_st16(cols + kAColsPerStage, vl);
+        if (two) build(scale(sp, kb, 1));
+        decode4(w1, v, vl);
         tmem_st16(cols + 16, v);
-        decode_word(c1.x, rlo, rhi, v + 0);
-        decode_word(c1.y, rlo, rhi, v + 4);
-        decode_word(c1.z, rlo, rhi, v + 8);
-        decode_word(c1.w, rlo, rhi, v + 12);
-        tmem_st16(cols + kAColsPerStage + 16, v);
+        tmem_st16(cols + kAColsPerStage + 16, vl);
       } else {
         block_table<XT>(scale(sp, kb, 0), lo, hi);
         decode_word(c0.x, lo, hi, v + 0);
@@ -636,7 +630,7 @@ int launch_t(GemmArgs a, const void* x, const uint8_t* w, const DeviceInfo& di, 
   // tensor-memory columns each.
   const size_t smem_cap = T::kPair ? size_t(di.smem_optin) / 2 - fa.sharedSizeBytes - 1024
                                    : size_t(di.smem_optin) - fa.sharedSizeBytes;
-  int stages = int((smem_cap - 1024) / T::kStageBytes);
+  int stages = int((smem_cap - 1024 - T::kTableBytes) / T::kStageBytes);
   stages = stages < kMaxStages ? stages : kMaxStages;
   const uint32_t tmem_budget = T::kPair ? 256u : 512u;
   int aslots = int((tmem_budget - uint32_t(BN)) / T::kACols);
@@ -646,7 +640,7 @@ int launch_t(GemmArgs a, const void* x, const uint8_t* w, const DeviceInfo& di, 
   a.n_stages = stages;
   a.n_aslots = aslots;
   a.tmem_cols = pow2_at_least(uint32_t(BN) + uint32_t(aslots) * T::kACols);
-  const size_t smem = T::kPair ? (smem_cap / 1024) * 1024 : size_t(stages) * T::kStageBytes + 1024;
+  const size_t smem = T::kPair ? (smem_cap / 1024) * 1024 : size_t(stages) * T::kStageBytes + T::kTableBytes + 1024;
   if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem)) != cudaSuccess)
     return BNBQ_ERR_CUDA;
   // K split across a cluster when the tiles alone leave SMs idle: about one CTA
