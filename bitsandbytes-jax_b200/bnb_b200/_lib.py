@@ -16,7 +16,7 @@ import torch
 LIB_PATH = Path(__file__).resolve().parent / "libbnbq.so"
 
 F32, F16, BF16 = 0, 1, 2
-OK, ERR_INVALID, ERR_UNSUPPORTED, ERR_MISALIGNED, ERR_CUDA, ERR_DEVICE = 0, -1, -2, -3, -4, -5
+OK, ERR_INVALID, ERR_UNSUPPORTED, ERR_MISALIGNED, ERR_CUDA, ERR_DEVICE, ERR_TOO_LARGE = 0, -1, -2, -3, -4, -5, -6
 GEMV_MAX_M = 20
 
 DTYPE_CODE = {torch.float32: F32, torch.float16: F16, torch.bfloat16: BF16}
@@ -36,6 +36,7 @@ _SIGNATURES = {
     "bnbq_version": "",
     "bnbq_wait_timeouts": "P",
     "bnbq_peer_allgather_rows": "iPillllPPPiiP",
+    "bnbq_peer_allgather_rows_noalloc": "iPillllPPiiiP",
     "bnbq_enable_peer_access": "i",
     "bnbq_ipc_handle": "PPP",
     "bnbq_ipc_open": "PP",
@@ -78,7 +79,7 @@ def check(status: int, what: str) -> None:
     if status == OK:
         return
     msg = f"{what}: {lib().bnbq_error_string(status).decode()} (status {status})"
-    if status == ERR_INVALID:
+    if status in (ERR_INVALID, ERR_TOO_LARGE):
         raise ValueError(msg)
     if status == ERR_UNSUPPORTED:
         raise NotImplementedError(msg)

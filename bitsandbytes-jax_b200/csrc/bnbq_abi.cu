@@ -121,6 +121,7 @@ extern "C" const char* bnbq_error_string(int status) {
     case BNBQ_ERR_MISALIGNED: return "misaligned pointer";
     case BNBQ_ERR_CUDA: return "CUDA error";
     case BNBQ_ERR_DEVICE: return "device is not sm_100 (B200)";
+    case BNBQ_ERR_TOO_LARGE: return "larger than the fixed scratch of a no-allocation entry point";
     default: return "unknown status";
   }
 }

@@ -171,3 +171,76 @@ extern "C" int bnbq_peer_allgather_rows(int dtype, const void* y_local, int32_t 
     return BNBQ_ERR_CUDA;
   return launch_status();
 }
+
+// ---------------------------------------------------------------------------
+// bnbq_peer_allgather_rows_noalloc: bnbq_peer_allgather_rows without the
+// caller's `state` words, for callers that may not allocate device memory.
+//
+// Who needs it: code that runs the exchange where cudaMalloc is off limits --
+// a custom-call handler inside a compiled program whose runtime owns the
+// device memory (an XLA FFI handler receives only its operand and result
+// buffers; the runtime has preallocated most of the memory, so cudaMalloc
+// there can fail, and it would synchronise the device), or a serving loop held
+// to a fixed memory plan. The state words must outlive every call (the epoch
+// advances once per call, in step with the peers) and start at zero, so such
+// a caller has nowhere to keep them. The flag arrays and full-y buffers are
+// shared with the peers and are still the caller's (created once, with the
+// group, by code that may allocate).
+//
+// Here the state lives in a fixed 256-byte array per device, held by every
+// device that loads this library until the process exits: one {arrived CTAs,
+// epoch} pair per exchange slot, kNoAllocExchanges (32) slots. A slot stands
+// for one group's sequence of exchanges; every rank of the group names the
+// same slot on every call. Slots at or beyond 32 return BNBQ_ERR_TOO_LARGE.
+namespace bnbq {
+namespace {
+
+constexpr int kNoAllocExchanges = 32;
+constexpr int kNoAllocMaxDevices = 64;
+
+// On the host this name is only a stand-in symbol, not a device address: a
+// kernel given it would fault (or reach host memory). Host code passes the
+// address that cudaGetSymbolAddress returns for the current device.
+static __device__ __align__(256) uint32_t g_allgather_state[2 * kNoAllocExchanges];
+
+std::mutex g_noalloc_mu;
+uint32_t* g_noalloc_state[kNoAllocMaxDevices] = {};  // per device, once set up
+
+// Set-up of the current device `dev`, once per process: the device address of
+// its state array, cleared. The arrival counters must be zero when a call
+// starts; after set-up the last CTA of every call puts its counter back to
+// zero. The epochs must NOT be cleared between calls: they carry the order.
+int noalloc_state(int dev, uint32_t** out) {
+  std::lock_guard<std::mutex> lock(g_noalloc_mu);
+  if (!g_noalloc_state[dev]) {
+    void* p = nullptr;
+    if (cudaGetSymbolAddress(&p, g_allgather_state) != cudaSuccess || !p) return BNBQ_ERR_CUDA;
+    if (cudaMemset(p, 0, sizeof(g_allgather_state)) != cudaSuccess) return BNBQ_ERR_CUDA;
+    g_noalloc_state[dev] = static_cast<uint32_t*>(p);
+  }
+  *out = g_noalloc_state[dev];
+  return BNBQ_OK;
+}
+
+}  // namespace
+}  // namespace bnbq
+
+// The first call on a device does the set-up (cudaGetSymbolAddress and a
+// synchronous clear); make it before any stream capture. Calls on one device
+// share the array: two calls whose kernels overlap on the GPU with the same
+// slot race on its counter and epoch.
+extern "C" int bnbq_peer_allgather_rows_noalloc(int dtype, const void* y_local, int32_t m, int64_t n_local,
+                                                int64_t ld_local, int64_t col0, int64_t ldy, void* const* y_full,
+                                                uint32_t* const* flags, int32_t exchange, int32_t world,
+                                                int32_t rank, void* stream) {
+  if (exchange < 0) return BNBQ_ERR_INVALID;
+  if (exchange >= kNoAllocExchanges) return BNBQ_ERR_TOO_LARGE;
+  if (dtype != BNBQ_F16 && dtype != BNBQ_BF16) return BNBQ_ERR_UNSUPPORTED;
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return BNBQ_ERR_CUDA;
+  if (dev >= kNoAllocMaxDevices) return BNBQ_ERR_UNSUPPORTED;
+  uint32_t* state = nullptr;
+  if (int st = noalloc_state(dev, &state)) return st;
+  return bnbq_peer_allgather_rows(dtype, y_local, m, n_local, ld_local, col0, ldy, y_full, flags,
+                                  state + 2 * exchange, world, rank, stream);
+}

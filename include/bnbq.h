@@ -47,7 +47,8 @@ enum bnbq_status {
   BNBQ_ERR_UNSUPPORTED = -2, /* dtype or shape outside what the kernel implements (NotImplementedError) */
   BNBQ_ERR_MISALIGNED = -3,  /* a pointer breaks the alignment rule above */
   BNBQ_ERR_CUDA = -4,        /* a CUDA runtime call or launch failed */
-  BNBQ_ERR_DEVICE = -5       /* the current device is not sm_100 */
+  BNBQ_ERR_DEVICE = -5,      /* the current device is not sm_100 */
+  BNBQ_ERR_TOO_LARGE = -6    /* more than a no-allocation entry point's fixed scratch holds */
 };
 
 /* Largest batch the CUDA-core GEMV handles; bnbq_matmul_nf4 uses the tcgen05
@@ -186,6 +187,26 @@ BNBQ_API int bnbq_enable_peer_access(int peer_device);
 BNBQ_API int bnbq_peer_allgather_rows(int dtype, const void* y_local, int32_t m, int64_t n_local, int64_t ld_local,
                                       int64_t col0, int64_t ldy, void* const* y_full, uint32_t* const* flags,
                                       uint32_t* state, int32_t world, int32_t rank, void* stream);
+
+/* bnbq_peer_allgather_rows for a caller that may not allocate device memory:
+ * code that runs the exchange inside a compiled program whose runtime owns
+ * the device memory (an XLA FFI handler receives only its operand and result
+ * buffers; cudaMalloc there can fail against the runtime's preallocation and
+ * would synchronise the device), or a serving loop held to a fixed memory
+ * plan. Such a caller has nowhere to keep `state`, which must outlive every
+ * call and start at zero. Here the library keeps it: a fixed 256-byte array
+ * per device (held by every device that loads the library until the process
+ * exits) with one state pair per exchange slot. Every rank of a group names
+ * the same `exchange` slot on every call; limit 32 slots (0..31), a larger
+ * slot returns BNBQ_ERR_TOO_LARGE. The other arguments and the result are
+ * bnbq_peer_allgather_rows's. The first call on a device sets the array up
+ * (its address, cleared once); make that first call before any stream
+ * capture. Calls whose kernels overlap on one device with the same slot race.
+ * No counterpart in the reference. */
+BNBQ_API int bnbq_peer_allgather_rows_noalloc(int dtype, const void* y_local, int32_t m, int64_t n_local,
+                                              int64_t ld_local, int64_t col0, int64_t ldy, void* const* y_full,
+                                              uint32_t* const* flags, int32_t exchange, int32_t world,
+                                              int32_t rank, void* stream);
 
 /* out[i] = rcp.approx.ftz.f32(in[i]): the hardware reciprocal the quantize kernels
  * use for 1/absmax (kernels/_ptx.py:20-22). Lets a CPU checker take the device's

@@ -1,0 +1,131 @@
+"""bnbq_peer_allgather_rows_noalloc: the row-shard all-gather for callers that
+may not allocate device memory (a custom-call handler inside a compiled
+program whose runtime owns the device memory, or a serving loop held to a
+fixed memory plan). It keeps the exchange's state words, which must outlive
+every call, in a fixed per-device array inside the library instead of a
+buffer the caller allocates.
+
+Checked through the C ABI against bnbq_peer_allgather_rows (the entry point
+that takes caller-allocated state) on two calls in a row: the second call
+starts from what the first left in the shared array. The copy is exact, so
+the tolerance is zero. This file is collected last on purpose."""
+from __future__ import annotations
+
+import pytest
+import torch
+
+from bnb_b200 import _lib
+from dist_helpers import _free_port
+
+pytestmark = pytest.mark.gpu
+
+
+class Exchange:
+    """The buffers a group of one rank passes to either entry point: the full-y
+    buffer, a zeroed flag array, and device arrays of their addresses. `state`
+    is used only by bnbq_peer_allgather_rows."""
+
+    def __init__(self, m, ldy, dtype, dev):
+        self.y_full = torch.full((m, ldy), 7.0, dtype=dtype, device=dev)
+        self.flags = torch.zeros(1, dtype=torch.int32, device=dev)
+        self.state = torch.zeros(2, dtype=torch.int32, device=dev)
+        self.y_ptrs = torch.tensor([self.y_full.data_ptr()], dtype=torch.int64, device=dev)
+        self.f_ptrs = torch.tensor([self.flags.data_ptr()], dtype=torch.int64, device=dev)
+
+    def args(self, y_local, col0):
+        return (_lib.DTYPE_CODE[y_local.dtype], y_local.data_ptr(), y_local.shape[0], y_local.shape[1],
+                y_local.stride(0), col0, self.y_full.stride(0), self.y_ptrs.data_ptr(), self.f_ptrs.data_ptr())
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
+@pytest.mark.parametrize("m,n_local,col0,ldy", [(1, 4096, 4096, 16384), (8, 1000, 3, 2011), (20, 14336, 0, 14336)])
+def test_noalloc_matches_existing_entry_point(cuda, m, n_local, col0, ldy, dtype):
+    """Two calls in a row on one device (world 1): bitwise the existing entry
+    point's output, and the columns outside the slice stay untouched."""
+    g = torch.Generator("cuda").manual_seed(m + n_local)
+    ref, new = Exchange(m, ldy, dtype, cuda), Exchange(m, ldy, dtype, cuda)
+    for call in range(2):
+        y_local = torch.randn(m, n_local, device=cuda, generator=g).to(dtype)
+        stream = _lib.stream_of(y_local)
+        _lib.call("bnbq_peer_allgather_rows", *ref.args(y_local, col0), ref.state.data_ptr(), 1, 0, stream)
+        _lib.call("bnbq_peer_allgather_rows_noalloc", *new.args(y_local, col0), 5, 1, 0, stream)
+        torch.cuda.synchronize()
+        assert torch.equal(new.y_full, ref.y_full), f"call {call}"
+        assert torch.equal(new.y_full[:, col0:col0 + n_local], y_local), f"call {call}"
+    assert bool((new.y_full[:, :col0] == 7.0).all()) and bool((new.y_full[:, col0 + n_local:] == 7.0).all())
+    assert _lib.wait_timeouts() == 0
+
+
+def test_noalloc_rejects_slots_beyond_its_array(cuda):
+    e = Exchange(1, 64, torch.bfloat16, cuda)
+    y = torch.zeros(1, 64, dtype=torch.bfloat16, device=cuda)
+    with pytest.raises(ValueError, match="fixed scratch"):
+        _lib.call("bnbq_peer_allgather_rows_noalloc", *e.args(y, 0), 32, 1, 0, _lib.stream_of(y))
+    with pytest.raises(ValueError):
+        _lib.call("bnbq_peer_allgather_rows_noalloc", *e.args(y, 0), -1, 1, 0, _lib.stream_of(y))
+
+
+def _worker(rank, world, port, queue):
+    import datetime
+    import os
+    import sys
+    import traceback
+    try:
+        import torch.distributed as dist
+        from bnb_b200.parallel import PeerGather
+        os.environ["MASTER_ADDR"] = "127.0.0.1"
+        os.environ["MASTER_PORT"] = str(port)
+        torch.cuda.set_device(rank)
+        dev = torch.device("cuda", rank)
+        dist.init_process_group("nccl", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=60),
+                                device_id=dev)
+        try:
+            n_local, dtype = 1536, torch.bfloat16
+            ref = PeerGather(8, world * n_local, dtype, dev)  # the existing entry point, its own state
+            new = PeerGather(8, world * n_local, dtype, dev)  # its flags and buffers, the library's state
+            g = torch.Generator(dev).manual_seed(10 + rank)
+            for call, m in enumerate((8, 3)):
+                y_local = torch.randn(m, n_local, device=dev, generator=g).to(dtype)
+                want = ref.gather(y_local, rank * n_local).clone()
+                _lib.call("bnbq_peer_allgather_rows_noalloc", _lib.DTYPE_CODE[dtype], y_local.data_ptr(), m,
+                          n_local, y_local.stride(0), rank * n_local, world * n_local, new.y_ptrs.data_ptr(),
+                          new.f_ptrs.data_ptr(), 7, world, rank, _lib.stream_of(y_local))
+                torch.cuda.synchronize()
+                assert torch.equal(new.y_full[:m], want), f"call {call}"
+            assert _lib.wait_timeouts() == 0
+            dist.barrier()
+            ref.close()
+            new.close()
+        finally:
+            dist.destroy_process_group()
+        queue.put((rank, None))
+    except BaseException:
+        tb = traceback.format_exc()
+        print(f"rank {rank}:\n{tb}", file=sys.stderr, flush=True)
+        queue.put((rank, tb))
+
+
+@pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device_count() < 2, reason="needs 2 GPUs")
+def test_noalloc_two_ranks_match_existing_entry_point():
+    """One process per GPU over CUDA IPC, as PeerGather sets it up: two
+    exchanges in a row through the library's state, bitwise the existing
+    entry point's output."""
+    import multiprocessing as mp
+    ctx = mp.get_context("spawn")
+    queue = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_worker, args=(r, 2, port, queue)) for r in range(2)]
+    for p in procs:
+        p.start()
+    errs = []
+    try:
+        for _ in range(2):
+            rank, err = queue.get(timeout=240)
+            if err:
+                errs.append(f"rank {rank}:\n{err}")
+    finally:
+        for p in procs:
+            p.join(timeout=30)
+            if p.is_alive():
+                p.kill()
+    assert not errs, "\n".join(errs)
