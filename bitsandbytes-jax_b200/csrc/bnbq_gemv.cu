@@ -99,8 +99,8 @@ __device__ __forceinline__ void load_stage(Stage<M, R, NESTED, XF>& st, const Ge
 constexpr int kPairTableBytes = 256 * 32 * 8;
 extern __shared__ float2 s_pair[];
 
-// The same table in global memory, built at compile time, so a CTA can bulk-copy
-// it into shared memory instead of storing 64 KB entry by entry.
+// The same table in global memory, built at compile time, so a CTA can copy
+// it into shared memory 16 bytes per thread at a time (the rows GEMV).
 struct PairTable {
   float2 v[256 * 32];
   constexpr PairTable() : v() {
@@ -279,6 +279,8 @@ gemv_kernel(GemvArgs a, int64_t n_groups) {
 // mbarrier. More than 100 KB per SM is in flight without using registers.
 // Consumer thread t owns chunks t, t + 32*NC, ... of every row (SLOTS of
 // them); its x never changes, so it is widened to float32 into registers once.
+// The consumers write the pair table themselves while the first stages land
+// (stores from the constant table: no 64 KB copy per CTA through L2).
 // Per stage a thread decodes its chunks through the pair table and
 // accumulates with fma.rn.f32x2. Partial sums leave each warp through a
 // transposed butterfly into shared memory; a per-stage counter tells the last
@@ -506,11 +508,9 @@ gemv_bulk_kernel(GemvArgs a, int n_groups, int n_stages, uint32_t stage_bytes, i
         mbar_init(smem_u32(bars + n_stages + st), uint32_t(ncw));  // empty
       }
       fence_mbar_init();
-      // constant tables first: pair table (4 x 16 KB) and code2
+      // code2 first (the consumers build the pair table themselves)
       const uint32_t tb = smem_u32(&s_tbl_bar);
-      mbar_arrive_expect_tx(tb, kPairTableBytes + (NESTED ? 1024u : 0u));
-      for (int off = 0; off < kPairTableBytes; off += 16384)
-        bulk_g2s(smem_u32(s_pair) + off, reinterpret_cast<const char*>(g_pair_table.v) + off, 16384, tb);
+      mbar_arrive_expect_tx(tb, NESTED ? 1024u : 0u);
       if constexpr (NESTED) bulk_g2s(smem_u32(s_code2), a.code2, 1024, tb);
     }
     __syncthreads();  // barriers ready for everyone
@@ -521,6 +521,13 @@ gemv_bulk_kernel(GemvArgs a, int n_groups, int n_stages, uint32_t stage_bytes, i
       for (int g = blockIdx.x; g < n_groups && i < kMaxGroupsPerFlush; g += gridDim.x, ++i) {
         if (s_abort) break;
         if (i >= n_stages && !mbar_wait(smem_u32(bars + n_stages + st), phase ^ 1u)) {
+          s_abort = 1;
+          break;
+        }
+        // Every CTA asks for its first two stages only and waits for the first
+        // before asking for more: the first stages of all CTAs then land ahead
+        // of the bulk of the requests, and the consumers start sooner.
+        if (i == 2 && n_stages > 2 && !mbar_wait(smem_u32(bars), 0)) {
           s_abort = 1;
           break;
         }
@@ -542,8 +549,13 @@ gemv_bulk_kernel(GemvArgs a, int n_groups, int n_stages, uint32_t stage_bytes, i
   }
 
   // ---------------------------------------------------------------- consumers
-  __syncthreads();  // barriers initialised; tables and the first stages are in flight
+  __syncthreads();  // barriers initialised; code2 and the first stages are in flight
   const uint32_t lane_b = uint32_t(lane) * 8u;
+  // The pair table, written by the consumer warps while the first stages
+  // stream in: warp w fills rows w, w + ncw, ... (row b = 32 lane copies of
+  // (T[b >> 4], T[b & 15]); b is warp-uniform, so the table reads broadcast).
+  for (int b = warp; b < 256; b += ncw) s_pair[b * 32 + lane] = make_float2(kNF4Table[b >> 4], kNF4Table[b & 15]);
+  named_bar_sync(1, ncons);
 
   // per (slot, row): the chunk's block within a group, relative to the group's
   // first block (K % bs == 0), or its global block for group g (otherwise)
@@ -558,7 +570,26 @@ gemv_bulk_kernel(GemvArgs a, int n_groups, int n_stages, uint32_t stage_bytes, i
   // not travel with the stage
   float pre0[SLOTS][R], pre1[SLOTS][R];
   int preq0[SLOTS][R], preq1[SLOTS][R];
+  // nested scales travelling with the stage: second-level scale of (slot,
+  // row) = absmax2[(block0 + (g R + r) spr + bir[slot]) >> log2_bs2], in
+  // 32-bit block numbers (the host checks that they fit)
+  int bir[SLOTS];
+#pragma unroll
+  for (int sl = 0; sl < SLOTS; ++sl) bir[sl] = cofs[sl] >> a.log2_bs;
+  const int last_row_blk = int((a.n_rows - 1) * int64_t(spr));
   auto prefetch = [&](int g, float (&p)[SLOTS][R], int (&q)[SLOTS][R]) {
+    if (NESTED && scales_in_stage) {
+      const int gb = g * (R * spr);  // the group's first block
+#pragma unroll
+      for (int sl = 0; sl < SLOTS; ++sl)
+#pragma unroll
+        for (int r = 0; r < R; ++r) {
+          q[sl][r] = 0;
+          const int rb = min(gb + r * spr, last_row_blk);  // clamped rows: results dropped
+          p[sl][r] = g < n_groups ? __ldg(a.absmax2 + ((int(a.block0) + rb + bir[sl]) >> a.log2_bs2)) : 0.0f;
+        }
+      return;
+    }
 #pragma unroll
     for (int sl = 0; sl < SLOTS; ++sl)
 #pragma unroll
@@ -746,6 +777,9 @@ int launch_bulk_t(const GemvArgs& a, const BulkPlan& p, const DeviceInfo& di, cu
     return BNBQ_ERR_CUDA;
   const int64_t n_groups = (a.n_rows + R - 1) / R;
   if (n_groups > INT32_MAX / 2) return BNBQ_ERR_UNSUPPORTED;
+  // the kernel numbers blocks in 32 bits when the scales travel with the stage
+  if (p.scales_in_stage && a.block0 + ((a.n_rows * a.k) >> a.log2_bs) + R * int64_t(a.k >> a.log2_bs) >= INT32_MAX)
+    return BNBQ_ERR_UNSUPPORTED;
   int64_t grid = n_groups < di.sm_count ? n_groups : di.sm_count;
   const int64_t min_grid = (n_groups + kMaxGroupsPerFlush - 1) / kMaxGroupsPerFlush;  // <= 32 groups per CTA
   if (grid < min_grid) grid = min_grid;
