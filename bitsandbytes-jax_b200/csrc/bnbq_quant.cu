@@ -24,15 +24,25 @@
 // kernels/quantize.py:102-125). For a strictly increasing finite codebook the
 // search equals a count of 255 strict thresholds T_j (even j: the midpoint;
 // odd j: the float just below the midpoint, or C[j] when the midpoint rounds
-// onto it). Each CTA builds, from the codebook, a monotone bucket map over the
-// float32 bits of s (sign, exponent, 4 mantissa bits; tiny and huge
-// magnitudes clamped), base[b] = #thresholds in lower buckets, and the widest
-// bucket's threshold count -> S search steps; then
-//   code = base[bucket(s)] + (binary search of S steps over T[base ...]).
-// Both tables are replicated per lane ([entry][32]) so a warp's random
-// lookups never collide in a bank. Codebooks that are not strictly increasing,
-// or whose buckets would need more than 4 steps, take the literal search.
+// onto it). Each CTA builds, from the codebook, buckets of s by sign and by
+// magnitude key |bits| >> shift (exponent and the top 23 - shift mantissa
+// bits; magnitudes below the smallest threshold's key clamped into key 0),
+// with as many mantissa bits as a 2 x 4096-entry table allows, so that no
+// bucket holds two thresholds (the dynamic map gets 7). A threshold shares
+// every bit above the low `shift` bits with the values of its bucket, so
+// "s > T" compares those low bits, in reverse for negative values. One 32-bit
+// word per bucket, E = base * 2^24 + an offset from the threshold's low bits,
+// makes the compare a carry:
+//   code = (E + low(s)) >> 24 (positive s),  (E - low(s)) >> 24 (negative s),
+// base = thresholds in lower buckets. In a symmetric codebook the middle
+// threshold is the float just below 0, whose tiny exponent would stretch the
+// table; then the threshold of smallest magnitude stays out of the table and
+// is compared directly. The per-element work (bucket, low bits, carry) is
+// integer multiply-adds on the FMA pipe, not shifts and compares on the
+// half-rate ALU pipe. Codebooks that are not strictly increasing, or whose
+// thresholds would share a bucket, take the literal search.
 #include <float.h>
+#include <limits.h>
 
 #include "bnbq_common.cuh"
 
@@ -48,21 +58,34 @@ __device__ __forceinline__ int nf4_bucket(float s) {
   return int(__float_as_uint(__fmaf_rn(fmaxf(s, -1.0f), 16.0f, 8388624.0f)) & 63u);
 }
 
-// 8-bit bucket map over float32 bits (same as the CPU oracle's or_q8_bucket).
-constexpr int kQ8MantBits = 4;
-constexpr int kQ8ExpLo = 127 - 24;
-constexpr int kQ8ExpHi = 127 + 2;
-constexpr int kQ8NMag = (kQ8ExpHi - kQ8ExpLo) << kQ8MantBits;
-constexpr int kQ8NB = 2 * kQ8NMag + 2;
-constexpr int kQ8MaxSteps = 4;
-constexpr int kQ8TLen = 255 + (1 << kQ8MaxSteps);  // +inf padded
+// 8-bit bucket table (see the header): 2 * kQ8Keys entries at most.
+constexpr int kQ8Keys = 4096;
 
-__device__ __forceinline__ int q8_bucket(float s) {
-  const uint32_t bits = __float_as_uint(fmaxf(s, -INFINITY));  // NaN -> -inf
-  int mag = int((bits & 0x7fffffffu) >> (23 - kQ8MantBits));
-  mag = min(max(mag, kQ8ExpLo << kQ8MantBits), kQ8ExpHi << kQ8MantBits) - (kQ8ExpLo << kQ8MantBits);
-  const int sgn = int(bits) >> 31;
-  return (kQ8NMag + 1) + (mag ^ sgn);
+// Per-element constants of the bucket map. The power-of-two multipliers are
+// runtime values, so the compiler keeps the multiply-adds (FMA pipe) instead
+// of turning them into shifts (ALU pipe).
+struct Q8Map {
+  int shift;         // low bits compared within a bucket
+  int kmin;          // magnitude key of bucket 0 (the clamp bucket)
+  int nkeys;         // magnitude buckets per sign
+  uint32_t m_key;    // 2^(32 - shift): umulhi(u, m_key) = u >> shift
+  uint32_t m_low;    // -2^shift: u + key * m_low = low bits
+  uint32_t m_sgnk;   // 2^(31 - shift): sign bit's share of the key
+  uint32_t m_two;    // 2: umulhi(u, 2) = sign bit
+  uint32_t m_code;   // 256: umulhi(v, 256) = v >> 24
+  int ex;            // 1: the smallest-magnitude threshold t_ex is compared directly
+  float t_ex;
+};
+
+// Table index and low bits of s (NaN as -2: code 0, below every threshold;
+// magnitudes from 2 on clamped into the top bucket, which holds no threshold).
+__device__ __forceinline__ uint32_t q8_index(const Q8Map& m, float s, uint32_t& low, uint32_t& sg) {
+  const uint32_t u = __float_as_uint(fmaxf(s, -2.0f));
+  sg = __umulhi(u, m.m_two);
+  const uint32_t kf = __umulhi(u, m.m_key);
+  low = u + kf * m.m_low;
+  const int k = max(int(kf - sg * m.m_sgnk) - m.kmin, 0);
+  return sg * uint32_t(m.nkeys) + uint32_t(min(k, m.nkeys - 1));
 }
 
 // The reference's literal search (slow path).
@@ -96,22 +119,26 @@ struct QuantArgs {
   float* absmax;
   const float* code;    // 8-bit only
   const float* offset;  // 8-bit only, nullable: x := fl32(x - offset)
+  uint32_t two;         // 2, passed at run time (see gt01)
 };
 
 // Shared memory of the 8-bit kernel.
 struct Q8Smem {
   float code[256];
-  float T[kQ8TLen];
-  int bt[kQ8TLen];
-  int maxwin;
-  int steps;  // -1: literal search
-  float T_rep[kQ8TLen * 32];
-  uint8_t base_rep[kQ8NB * 32];
+  float T[256];        // the 255 thresholds
+  int ordc[256];       // bucket ordinals (monotone in value) of the table thresholds, ascending
+  uint32_t lowc[256];  // their low bits
+  Q8Map map;
+  int kmin;
+  unsigned long long exj;  // (magnitude bits << 8) | index of the smallest-magnitude threshold
+  int mode;            // 1: bucket table, -1: literal search
+  int okflag;
+  uint32_t tab[2 * kQ8Keys];
 };
 
+// Bucket i: (its threshold or +inf, thresholds in lower buckets as int bits).
 struct NF4Smem {
-  float thr[64];
-  int base[64];
+  float2 tb[64];
 };
 
 __device__ void build_nf4_tables(NF4Smem& sm) {
@@ -129,66 +156,119 @@ __device__ void build_nf4_tables(NF4Smem& sm) {
         if (bj == i) t = tj;
       }
     }
-    sm.thr[i] = t;
-    sm.base[i] = b;
+    sm.tb[i] = make_float2(t, __int_as_float(b));
   }
 }
 
+// (x > y) as 0/1 from the sign bit of fl(y - x) (IEEE subtraction keeps the
+// sign of the exact difference; equal -> +0; a NaN x -> the positive default
+// NaN), on the FMA pipe: `two` is a runtime 2, so umulhi is not turned into a
+// shift.
+__device__ __forceinline__ uint32_t gt01(float x, float y, uint32_t two) {
+  return __umulhi(__float_as_uint(__fsub_rn(y, x)), two);
+}
+
+// Bucket ordinal of a table index (monotone in the value of s).
+__device__ __forceinline__ int q8_ord(int idx, int nkeys) { return idx >= nkeys ? nkeys - 1 - (idx - nkeys) : nkeys + idx; }
+
 __device__ void build_q8_tables(Q8Smem& sm, const float* code) {
   const int tid = threadIdx.x;
+  static_assert(kThreads >= 255, "one threshold per thread");
   for (int j = tid; j < 256; j += kThreads) sm.code[j] = __ldg(code + j);
-  if (tid == 0) sm.maxwin = 0;
+  if (tid == 0) { sm.mode = 1; sm.exj = ~0ull; }
   __syncthreads();
   bool ok = true;
   for (int j = tid; j < 256; j += kThreads) {
     const float c = sm.code[j];
     ok &= isfinite(c) && (j == 255 || c < sm.code[j + 1]);
   }
-  ok = __syncthreads_and(ok);
-  if (!ok) {
-    if (tid == 0) sm.steps = -1;
+  if (!__syncthreads_and(ok)) {
+    if (tid == 0) sm.mode = -1;
     __syncthreads();
     return;
   }
-  for (int j = tid; j < kQ8TLen; j += kThreads) {
-    float t = INFINITY;
-    if (j < 255) {
-      const float c0 = sm.code[j], c1 = sm.code[j + 1];
-      const float mid = __fmul_rn(__fadd_rn(c0, c1), 0.5f);
-      t = !(j & 1) ? mid : (mid > c0 ? __int_as_float(__float_as_int(mid) + (mid > 0.0f ? -1 : 1)) : c0);
-      // nextafter(mid, -inf): for mid == +0 step to -denorm_min
-      if ((j & 1) && mid > c0 && mid == 0.0f) t = -__int_as_float(1);
+  float t = 0.0f;  // thread j < 255: threshold j
+  if (tid < 255) {
+    const float c0 = sm.code[tid], c1 = sm.code[tid + 1];
+    const float mid = __fmul_rn(__fadd_rn(c0, c1), 0.5f);
+    t = !(tid & 1) ? mid : (mid > c0 ? __int_as_float(__float_as_int(mid) + (mid > 0.0f ? -1 : 1)) : c0);
+    // nextafter(mid, -inf): for mid == +0 step to -denorm_min
+    if ((tid & 1) && mid > c0 && mid == 0.0f) t = -__int_as_float(1);
+    sm.T[tid] = t;
+    atomicMin(&sm.exj, (static_cast<unsigned long long>(__float_as_uint(t) & 0x7fffffffu) << 8) | unsigned(tid));
+  }
+  __syncthreads();
+  const int jx = int(sm.exj & 255u);
+  const uint32_t key2 = 0x40000000u;  // |bits| of 2.0: the top (clamp) bucket starts there
+  // without, then with the smallest-magnitude threshold left out; largest mb that fits
+  for (int ex = 0; ex < 2; ++ex) {
+    for (int mb = 8; mb >= 1; --mb) {
+      const int shift = 23 - mb;
+      if (tid == 0) sm.kmin = INT_MAX;
+      __syncthreads();
+      const bool in_table = tid < 255 && !(ex && tid == jx);
+      if (in_table) atomicMin(&sm.kmin, int((__float_as_uint(t) & 0x7fffffffu) >> shift));
+      __syncthreads();
+      const int kmin = sm.kmin - 1;  // clamp bucket below every threshold
+      const int nkeys = int(key2 >> shift) - kmin + 1;
+      if (kmin < 0 || nkeys > kQ8Keys) {
+        __syncthreads();
+        continue;
+      }
+      Q8Map m;
+      m.shift = shift; m.kmin = kmin; m.nkeys = nkeys;
+      m.m_key = 1u << (32 - shift); m.m_low = 0u - (1u << shift); m.m_sgnk = 1u << (31 - shift);
+      m.m_two = 2u; m.m_code = 256u; m.ex = ex; m.t_ex = sm.T[jx];
+      // every table threshold in a bucket of its own, none in a clamp bucket
+      // (key 0 below the smallest threshold, key nkeys - 1 from |s| = 2 on)
+      const int nin = 255 - ex;  // table thresholds, in value order at i = j - (j > jx)
+      const int i = tid - (ex && tid > jx ? 1 : 0);
+      uint32_t low = 0, sg = 0;
+      const int idx = in_table ? int(q8_index(m, t, low, sg)) : 0;
+      if (tid == 0) sm.okflag = 1;
+      __syncthreads();
+      if (in_table) {
+        sm.ordc[i] = q8_ord(idx, nkeys);
+        sm.lowc[i] = low;
+        const int k = idx >= nkeys ? idx - nkeys : idx;
+        if (k == 0 || k == nkeys - 1) sm.okflag = 0;
+      }
+      __syncthreads();
+      if (in_table && i + 1 < nin && sm.ordc[i + 1] <= sm.ordc[i]) sm.okflag = 0;
+      __syncthreads();
+      if (sm.okflag) {
+        const uint32_t mask = (1u << shift) - 1u;
+        for (int b = tid; b < 2 * nkeys; b += kThreads) {
+          const int o = q8_ord(b, nkeys);
+          int lo = 0, hi = nin;  // table thresholds in lower buckets: lower_bound of o
+          while (lo < hi) {
+            const int mid = (lo + hi) >> 1;
+            if (sm.ordc[mid] < o) lo = mid + 1; else hi = mid;
+          }
+          const bool neg = b >= nkeys;
+          uint32_t lt = neg ? 0u : mask;  // no threshold: the compare never carries
+          if (lo < nin && sm.ordc[lo] == o) lt = sm.lowc[lo];
+          sm.tab[b] = uint32_t(lo) * (1u << 24) + (neg ? (1u << 24) + lt - 1u : (1u << 24) - 1u - lt);
+        }
+        if (tid == 0) sm.map = m;
+        __syncthreads();
+        return;
+      }
+      __syncthreads();
     }
-    sm.T[j] = t;
-    sm.bt[j] = j < 255 ? q8_bucket(t) : kQ8NB;
   }
-  __syncthreads();
-  for (int b = tid; b < kQ8NB; b += kThreads) {
-    int lo = 0, hi = 255;  // lower_bound of b in bt[0..255)
-    while (lo < hi) { const int mid = (lo + hi) >> 1; if (sm.bt[mid] < b) lo = mid + 1; else hi = mid; }
-    int lo2 = lo, hi2 = 255;  // upper_bound
-    while (lo2 < hi2) { const int mid = (lo2 + hi2) >> 1; if (sm.bt[mid] <= b) lo2 = mid + 1; else hi2 = mid; }
-    atomicMax(&sm.maxwin, lo2 - lo);
-    for (int l = 0; l < 32; ++l) sm.base_rep[b * 32 + l] = uint8_t(lo);
-  }
-  for (int e = tid; e < kQ8TLen * 32; e += kThreads) sm.T_rep[e] = sm.T[e >> 5];
-  __syncthreads();
-  if (tid == 0) {
-    int S = 0;
-    while ((1 << S) - 1 < sm.maxwin) ++S;
-    sm.steps = S <= kQ8MaxSteps ? S : -1;
-  }
+  if (tid == 0) sm.mode = -1;
   __syncthreads();
 }
 
-template <int S>
-__device__ __forceinline__ int code8_fast(const Q8Smem& sm, float s, int lane) {
-  int c = sm.base_rep[q8_bucket(s) * 32 + lane];
-#pragma unroll
-  for (int st = S - 1; st >= 0; --st) {
-    const float t = sm.T_rep[(c + (1 << st) - 1) * 32 + lane];
-    c += (s > t) ? (1 << st) : 0;
-  }
+// code = (E + low) >> 24 or (E - low) >> 24 (+ the directly compared threshold)
+template <bool EX>
+__device__ __forceinline__ int code8_table(const Q8Smem& sm, const Q8Map& m, float s) {
+  uint32_t low, sg;
+  const uint32_t idx = q8_index(m, s, low, sg);
+  const uint32_t e = sm.tab[idx];
+  int c = int(__umulhi(e + (1u - sg * m.m_two) * low, m.m_code));
+  if constexpr (EX) c += int(gt01(s, m.t_ex, m.m_two));
   return c;
 }
 
@@ -222,18 +302,20 @@ __device__ __forceinline__ void load8(const InT* x, int64_t e0, int64_t n, float
 
 struct NF4Choose {
   const NF4Smem* sm;
+  uint32_t two;  // 2 (runtime)
   __device__ int operator()(float s, int) const {
-    const int i = nf4_bucket(s);
-    return sm->base[i] + (s > sm->thr[i]);
+    const float2 e = sm->tb[nf4_bucket(s)];
+    return __float_as_int(e.y) + int(gt01(s, e.x, two));
   }
 };
 
-template <int S>
+template <int MODE>  // 0: table, 1: table + one direct compare, -1: literal search
 struct Q8Choose {
   const Q8Smem* sm;
-  __device__ int operator()(float s, int lane) const {
-    if constexpr (S < 0) return code8_search(sm->code, s);
-    else return code8_fast<S>(*sm, s, lane);
+  Q8Map m;
+  __device__ int operator()(float s, int) const {
+    if constexpr (MODE >= 0) return code8_table<MODE == 1>(*sm, m, s);
+    else return code8_search(sm->code, s);
   }
 };
 
@@ -249,9 +331,15 @@ __device__ __forceinline__ void emit_codes(const QuantArgs& a, int64_t e0, const
     c[j + 1] = choose(s.y, lane);
   }
   if constexpr (NF4) {
-    uint32_t w = 0;
-#pragma unroll
-    for (int j = 0; j < 4; ++j) w |= uint32_t((c[2 * j] << 4) | c[2 * j + 1]) << (8 * j);
+    // byte j = c[2j] * 16 + c[2j+1], little-endian: one multiply-add per code
+    uint32_t w = uint32_t(c[6]);
+    w = w * 16u + uint32_t(c[7]);
+    w = w * 16u + uint32_t(c[4]);
+    w = w * 16u + uint32_t(c[5]);
+    w = w * 16u + uint32_t(c[2]);
+    w = w * 16u + uint32_t(c[3]);
+    w = w * 16u + uint32_t(c[0]);
+    w = w * 16u + uint32_t(c[1]);
     if (e0 + 8 <= a.n) {
       *reinterpret_cast<uint32_t*>(a.q + (e0 >> 1)) = w;
     } else {
@@ -260,11 +348,11 @@ __device__ __forceinline__ void emit_codes(const QuantArgs& a, int64_t e0, const
         if ((e0 >> 1) + j < nq) a.q[(e0 >> 1) + j] = uint8_t(w >> (8 * j));
     }
   } else {
-    uint32_t lo = 0, hi = 0;
+    uint32_t lo = uint32_t(c[3]), hi = uint32_t(c[7]);
 #pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      lo |= uint32_t(c[j]) << (8 * j);
-      hi |= uint32_t(c[j + 4]) << (8 * j);
+    for (int j = 2; j >= 0; --j) {
+      lo = lo * 256u + uint32_t(c[j]);
+      hi = hi * 256u + uint32_t(c[j + 4]);
     }
     if (e0 + 8 <= a.n) {
       *reinterpret_cast<uint2*>(a.q + e0) = make_uint2(lo, hi);
@@ -273,6 +361,15 @@ __device__ __forceinline__ void emit_codes(const QuantArgs& a, int64_t e0, const
         if (e0 + j < a.n) a.q[e0 + j] = uint8_t((j < 4 ? lo : hi) >> (8 * (j & 3)));
     }
   }
+}
+
+// max.ftz over the warp of per-lane maxima that are >= 0 or -FLT_MAX (every
+// input NaN): such floats order like their bit patterns as signed integers,
+// so one redux replaces five shuffle-and-max steps.
+__device__ __forceinline__ float warp_max_nonneg(float m) {
+  int r;
+  asm volatile("redux.sync.max.s32 %0, %1, 0xffffffff;" : "=r"(r) : "r"(__float_as_int(m)));
+  return __int_as_float(r);
 }
 
 template <typename InT>
@@ -357,7 +454,9 @@ __device__ void quant_small(const QuantArgs& a, const Choose& choose) {
       float m = -FLT_MAX;
 #pragma unroll
       for (int j = 0; j < 8; ++j) m = max_abs_ftz(m, v[j]);
-      for (int o = L >> 1; o > 0; o >>= 1) m = max_ftz(m, __shfl_xor_sync(0xffffffffu, m, o));
+      if (L == 32) m = warp_max_nonneg(m);
+      else
+        for (int o = L >> 1; o > 0; o >>= 1) m = max_ftz(m, __shfl_xor_sync(0xffffffffu, m, o));
       const float r = rcp_approx_ftz(m);
       const int64_t b = e0 >> a.log2_bs;
       if (b < a.nb) {
@@ -403,8 +502,7 @@ __device__ void quant_large(const QuantArgs& a, const Choose& choose) {
         }
       }
     }
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) m = max_ftz(m, __shfl_xor_sync(0xffffffffu, m, o));
+    m = warp_max_nonneg(m);
     const float r = rcp_approx_ftz(m);
     if (lane == 0) a.absmax[b] = m;
     if constexpr (HOLD > 0) {
@@ -439,7 +537,7 @@ __global__ void __launch_bounds__(kThreads) quant_nf4_kernel(QuantArgs a) {
   __shared__ NF4Smem sm;
   build_nf4_tables(sm);
   __syncthreads();
-  quant_body<InT, true>(a, NF4Choose{&sm});
+  quant_body<InT, true>(a, NF4Choose{&sm, a.two});
 }
 
 template <typename InT>
@@ -447,14 +545,9 @@ __global__ void __launch_bounds__(kThreads) quant_8bit_kernel(QuantArgs a) {
   extern __shared__ __align__(16) unsigned char smem_raw[];
   Q8Smem& sm = *reinterpret_cast<Q8Smem*>(smem_raw);
   build_q8_tables(sm, a.code);
-  switch (sm.steps) {
-    case 0: quant_body<InT, false>(a, Q8Choose<0>{&sm}); break;
-    case 1: quant_body<InT, false>(a, Q8Choose<1>{&sm}); break;
-    case 2: quant_body<InT, false>(a, Q8Choose<2>{&sm}); break;
-    case 3: quant_body<InT, false>(a, Q8Choose<3>{&sm}); break;
-    case 4: quant_body<InT, false>(a, Q8Choose<4>{&sm}); break;
-    default: quant_body<InT, false>(a, Q8Choose<-1>{&sm}); break;
-  }
+  if (sm.mode > 0 && !sm.map.ex) quant_body<InT, false>(a, Q8Choose<0>{&sm, sm.map});
+  else if (sm.mode > 0) quant_body<InT, false>(a, Q8Choose<1>{&sm, sm.map});
+  else quant_body<InT, false>(a, Q8Choose<-1>{&sm, Q8Map{}});
 }
 
 template <typename Kern>
@@ -483,7 +576,7 @@ int check_quant(int dtype, const void* x, int64_t n, int32_t bs, uint8_t* q, flo
   if (a->log2_bs < 3 || a->log2_bs > 12) return BNBQ_ERR_INVALID;
   if (n > 0 && (!x || !q || !absmax)) return BNBQ_ERR_INVALID;
   if (!aligned(x, 16) || !aligned(q, 16) || !aligned(absmax, 4)) return BNBQ_ERR_MISALIGNED;
-  a->x = x; a->n = n; a->nb = (n + bs - 1) / bs; a->q = q; a->absmax = absmax;
+  a->x = x; a->n = n; a->nb = (n + bs - 1) / bs; a->q = q; a->absmax = absmax; a->two = 2u;
   return BNBQ_OK;
 }
 

@@ -424,65 +424,108 @@ int64_t or_check_nf4_buckets(int64_t stride) {
   return bad;
 }
 
-/* The 8-bit kernel's bucket of a scaled value: a monotone map of float32 bits
- * onto NB8 buckets, magnitudes below 2^-24 collapsed into one bucket per sign,
- * magnitudes at or above 2^2 (and NaN, mapped to -inf first) into the ends. */
-#define Q8_MANT_BITS 4
-#define Q8_EXP_LO (127 - 24)
-#define Q8_EXP_HI (127 + 2)
-#define Q8_NMAG ((Q8_EXP_HI - Q8_EXP_LO) << Q8_MANT_BITS)
-#define Q8_NB (2 * Q8_NMAG + 2)
+/* The 8-bit kernel's code choice (csrc/bnbq_quant.cu, build_q8_tables and
+ * code8_table), restated. Buckets by sign and magnitude key |bits| >> shift;
+ * key 0 (below the smallest table threshold) and the key of 2.0 and above are
+ * clamp buckets; NaN counts as -2. The largest mantissa-bit count mb = 23 -
+ * shift whose keys fit Q8_KEYS per sign is used, first with all 255
+ * thresholds, then with the smallest-magnitude one left out and compared
+ * directly; it applies when every table threshold has a bucket of its own
+ * that is not a clamp bucket. Entry E = base * 2^24 + (positive bucket:
+ * 2^24 - 1 - low(T); negative: 2^24 + low(T) - 1), and code = (E + low(s)) >>
+ * 24 for positive s, (E - low(s)) >> 24 for negative s. */
+#define Q8_KEYS 4096
 
-int or_q8_num_buckets(void) { return Q8_NB; }
+typedef struct {
+  int shift, kmin, nkeys, ex;
+  float t_ex;
+} q8map;
 
-int or_q8_bucket(float s) {
-  float sc = fmaxf(s, -INFINITY); /* NaN -> -inf: lowest bucket, base 0 */
-  uint32_t bits = bits_from_f32(sc);
-  int32_t mag = (int32_t)((bits & 0x7fffffffu) >> (23 - Q8_MANT_BITS));
-  mag = mag < (Q8_EXP_LO << Q8_MANT_BITS) ? (Q8_EXP_LO << Q8_MANT_BITS) : mag;
-  mag = mag > (Q8_EXP_HI << Q8_MANT_BITS) ? (Q8_EXP_HI << Q8_MANT_BITS) : mag;
-  mag -= Q8_EXP_LO << Q8_MANT_BITS;          /* 0 .. Q8_NMAG */
-  int32_t sgn = (int32_t)bits >> 31;         /* 0 or -1 */
-  return (Q8_NMAG + 1) + (mag ^ sgn);        /* negative: NMAG - mag, positive: NMAG + 1 + mag */
+static uint32_t q8_fine_index(const q8map* m, float s, uint32_t* low, uint32_t* sg) {
+  uint32_t u = bits_from_f32(fmaxf(s, -2.0f)); /* NaN -> -2 */
+  *sg = u >> 31;
+  *low = u & ((1u << m->shift) - 1u);
+  int32_t k = (int32_t)((u & 0x7fffffffu) >> m->shift) - m->kmin;
+  k = k < 0 ? 0 : (k > m->nkeys - 1 ? m->nkeys - 1 : k);
+  return *sg * (uint32_t)m->nkeys + (uint32_t)k;
 }
 
-/* Restates the device build (base = #thresholds in lower buckets; window =
- * thresholds sharing the bucket) and returns the number of search steps S. */
-int or_q8_bucket_tables(const float* T, int32_t* base) {
-  int maxwin = 0;
-  for (int b = 0; b < Q8_NB; ++b) {
-    int lo = 0, win = 0;
-    for (int j = 0; j < 255; ++j) {
-      int bt = or_q8_bucket(T[j]);
-      lo += (bt < b);
-      win += (bt == b);
+static int q8_ord(int idx, int nkeys) { return idx >= nkeys ? nkeys - 1 - (idx - nkeys) : nkeys + idx; }
+
+/* Builds the table from the 255 thresholds; returns mb, or -1 when the
+ * formulation does not apply (the kernel then runs the literal search). */
+int or_q8_fine_tables(const float* T, int32_t* map_out, uint32_t* tab, float* t_ex) {
+  int jx = 0;
+  for (int j = 1; j < 255; ++j)
+    if ((bits_from_f32(T[j]) & 0x7fffffffu) < (bits_from_f32(T[jx]) & 0x7fffffffu)) jx = j;
+  for (int ex = 0; ex < 2; ++ex) {
+    for (int mb = 8; mb >= 1; --mb) {
+      int shift = 23 - mb, kmin = 0x7fffffff;
+      for (int j = 0; j < 255; ++j) {
+        if (ex && j == jx) continue;
+        int k = (int)((bits_from_f32(T[j]) & 0x7fffffffu) >> shift);
+        kmin = k < kmin ? k : kmin;
+      }
+      kmin -= 1;
+      int nkeys = (int)(0x40000000u >> shift) - kmin + 1;
+      if (kmin < 0 || nkeys > Q8_KEYS) continue;
+      q8map m = {shift, kmin, nkeys, ex, T[jx]};
+      int ordc[255];
+      uint32_t lowc[255];
+      int nin = 0, ok = 1;
+      for (int j = 0; j < 255 && ok; ++j) {
+        if (ex && j == jx) continue;
+        uint32_t low, sg;
+        int idx = (int)q8_fine_index(&m, T[j], &low, &sg);
+        int k = idx >= nkeys ? idx - nkeys : idx;
+        if (k == 0 || k == nkeys - 1) ok = 0;
+        ordc[nin] = q8_ord(idx, nkeys);
+        lowc[nin] = low;
+        if (nin > 0 && ordc[nin] <= ordc[nin - 1]) ok = 0;
+        ++nin;
+      }
+      if (!ok) continue;
+      uint32_t mask = (1u << shift) - 1u;
+      for (int b = 0; b < 2 * nkeys; ++b) {
+        int o = q8_ord(b, nkeys), lo = 0;
+        while (lo < nin && ordc[lo] < o) ++lo;
+        int neg = b >= nkeys;
+        uint32_t lt = neg ? 0u : mask;
+        if (lo < nin && ordc[lo] == o) lt = lowc[lo];
+        tab[b] = (uint32_t)lo * (1u << 24) + (neg ? (1u << 24) + lt - 1u : (1u << 24) - 1u - lt);
+      }
+      map_out[0] = shift;
+      map_out[1] = kmin;
+      map_out[2] = nkeys;
+      map_out[3] = ex;
+      *t_ex = T[jx];
+      return mb;
     }
-    base[b] = lo;
-    if (win > maxwin) maxwin = win;
   }
-  int S = 0;
-  while ((1 << S) - 1 < maxwin) ++S;
-  return S;
+  return -1;
 }
 
-uint8_t or_code_8bit_buckets(const float* T, const int32_t* base, int S, float s) {
-  int c = base[or_q8_bucket(s)];
-  for (int st = S - 1; st >= 0; --st) {
-    int idx = c + (1 << st) - 1;
-    float t = idx < 255 ? T[idx] : INFINITY;
-    if (s > t) c += 1 << st;
-  }
+static uint8_t q8_fine_code(const q8map* m, const uint32_t* tab, float s) {
+  uint32_t low, sg;
+  uint32_t e = tab[q8_fine_index(m, s, &low, &sg)];
+  uint32_t c = (sg ? e - low : e + low) >> 24;
+  if (m->ex && s > m->t_ex) c += 1;
   return (uint8_t)c;
 }
 
 /* Walks float32 values in [-1.01, 1.01] at the given bit stride (plus NaN and
- * infinities) comparing the bucket formulation with the literal search. */
-int64_t or_check_q8_buckets(const float* C, int64_t stride, int* steps_out) {
+ * infinities) comparing the table formulation with the literal search.
+ * Returns the mismatches (-1: the formulation does not apply), mb in *mb_out. */
+int64_t or_check_q8_buckets(const float* C, int64_t stride, int* mb_out) {
   float T[255];
-  int32_t base[Q8_NB];
+  int32_t mp[4];
+  static uint32_t tab[2 * Q8_KEYS];
   if (!or_q8_thresholds(C, T)) return -1;
-  int S = or_q8_bucket_tables(T, base);
-  if (steps_out) *steps_out = S;
+  float t_ex;
+  int mb = or_q8_fine_tables(T, mp, tab, &t_ex);
+  if (mb_out) *mb_out = mb;
+  if (mb < 0) return -1;
+  q8map m = {mp[0], mp[1], mp[2], mp[3], t_ex};
   const uint32_t hi_pos = bits_from_f32(1.01f);
   int64_t bad = 0;
   if (stride < 1) stride = 1;
@@ -490,11 +533,21 @@ int64_t or_check_q8_buckets(const float* C, int64_t stride, int* steps_out) {
   for (int64_t u = 0; u <= (int64_t)hi_pos; u += stride) {
     for (int sgn = 0; sgn < 2; ++sgn) {
       float s = f32_from_bits((uint32_t)u | (sgn ? 0x80000000u : 0u));
-      bad += (or_code_8bit_buckets(T, base, S, s) != or_code_8bit(C, s));
+      bad += (q8_fine_code(&m, tab, s) != or_code_8bit(C, s));
     }
   }
-  const float sp[4] = {NAN, -NAN, INFINITY, -INFINITY};
-  for (int k = 0; k < 4; ++k) bad += (or_code_8bit_buckets(T, base, S, sp[k]) != or_code_8bit(C, sp[k]));
+  /* every threshold and its neighbours within 3 ulp, both directions */
+  for (int j = 0; j < 255; ++j) {
+    float up = T[j], dn = T[j];
+    for (int k = 0; k < 4; ++k) {
+      bad += (q8_fine_code(&m, tab, up) != or_code_8bit(C, up));
+      bad += (q8_fine_code(&m, tab, dn) != or_code_8bit(C, dn));
+      up = nextafterf(up, INFINITY);
+      dn = nextafterf(dn, -INFINITY);
+    }
+  }
+  const float sp[6] = {NAN, -NAN, INFINITY, -INFINITY, 0.0f, -0.0f};
+  for (int k = 0; k < 6; ++k) bad += (q8_fine_code(&m, tab, sp[k]) != or_code_8bit(C, sp[k]));
   return bad;
 }
 

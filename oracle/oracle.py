@@ -59,8 +59,7 @@ def _declare(L: C.CDLL) -> None:
         "or_gemv_f64": ([i32, p, i32, i32, p, i64, i32, p, p, p], None),
         "or_gemv_ref": ([i32, p, i32, i32, p, i64, i32, p, p], None),
         "or_nf4_bucket_tables": ([p, p], i32), "or_check_nf4_buckets": ([i64], i64),
-        "or_q8_num_buckets": ([], i32), "or_q8_bucket": ([f32], i32),
-        "or_q8_bucket_tables": ([p, p], i32), "or_check_q8_buckets": ([p, i64, p], i64),
+        "or_q8_fine_tables": ([p, p, p, p], i32), "or_check_q8_buckets": ([p, i64, p], i64),
         "or_codes_nf4": ([p, i64, p], None), "or_codes_8bit": ([p, p, i64, p], None),
         "or_codes_8bit_count": ([p, p, i64, p], None), "or_mul_ftz": ([p, p, i64, p], None),
     }
@@ -247,10 +246,13 @@ def nf4_bucket_tables():
 
 
 def check_q8_buckets(code, stride: int = 1):
+    """(mismatches, mb) of the 8-bit kernel's bucket-table code choice against
+    the literal search; mismatches -1 when the table formulation does not
+    apply to this codebook (the kernel then runs the literal search)."""
     code = _c(code, np.float32)
-    steps = C.c_int(0)
-    bad = lib().or_check_q8_buckets(_p(code), stride, C.byref(steps))
-    return int(bad), int(steps.value)
+    mb = C.c_int(0)
+    bad = lib().or_check_q8_buckets(_p(code), stride, C.byref(mb))
+    return int(bad), int(mb.value)
 
 
 # ----------------------------------------------------- create_dynamic_map

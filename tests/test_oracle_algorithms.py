@@ -32,19 +32,53 @@ def _random_codebooks(n, seed):
     return books
 
 
-def test_q8_bucket_search_dynamic_map():
-    """Bucketed threshold search == the reference's binary search, dynamic map,
-    every 3rd float32 bit pattern in [-1.01, 1.01]; 2 search steps suffice."""
-    bad, steps = O.check_q8_buckets(O.create_dynamic_map(), stride=3)
+def test_q8_bucket_table_dynamic_map():
+    """The 8-bit kernel's one-lookup code choice (a threshold per bucket of
+    sign, exponent and mb mantissa bits; code = (E +- low bits) >> 24) == the
+    reference's binary search, dynamic map, every 3rd float32 bit pattern in
+    [-1.01, 1.01], every threshold +-3 ulp, NaN, infinities, zeros."""
+    bad, mb = O.check_q8_buckets(O.create_dynamic_map(), stride=3)
     assert bad == 0
-    assert steps <= 2
+    assert mb == 7
+
+
+def _common_codebooks():
+    """Codebooks of the bitsandbytes family besides the signed dynamic map:
+    the unsigned dynamic map, a linear map and a normal-quantile map."""
+    from statistics import NormalDist
+    lin = np.linspace(-1.0, 1.0, 256).astype(np.float32)
+    nd = NormalDist()
+    q = np.array([nd.inv_cdf((i + 0.5) / 256) for i in range(256)])
+    quant = (q / np.abs(q).max()).astype(np.float32)
+    return {"dynamic_unsigned": O.create_dynamic_map(False).astype(np.float32), "linear": lin, "quantile": quant}
+
+
+@pytest.mark.parametrize("name", ["dynamic_unsigned", "linear", "quantile"])
+def test_q8_bucket_table_common_codebooks(name):
+    code = _common_codebooks()[name]
+    bad, mb = O.check_q8_buckets(code, stride=97)
+    assert bad == 0 and mb >= 5, (bad, mb)
 
 
 @pytest.mark.parametrize("seed", [1, 2])
-def test_q8_bucket_search_random_codebooks(seed):
+def test_q8_bucket_table_random_codebooks(seed):
+    """Uniformly random codebooks: exact where the table applies; where two
+    thresholds are closer than the finest bucket it is declined (the kernel
+    then runs the literal search, checked on the GPU)."""
     for code in _random_codebooks(2, seed):
-        bad, steps = O.check_q8_buckets(code, stride=97)
-        assert bad == 0, steps
+        bad, mb = O.check_q8_buckets(code, stride=97)
+        assert bad == 0 or (bad == -1 and mb == -1), (bad, mb)
+
+
+def test_q8_bucket_table_declines_crowded_codebooks():
+    """Thresholds closer than the finest bucket (here: codes 1 ulp apart) ->
+    the table formulation is refused; the kernel runs the literal search."""
+    code = O.create_dynamic_map().astype(np.float32).copy()
+    code[200] = np.nextafter(code[201], np.float32(-np.inf))
+    code[199] = np.nextafter(code[200], np.float32(-np.inf))
+    assert np.all(np.diff(code) > 0)
+    bad, mb = O.check_q8_buckets(code, stride=1 << 20)
+    assert bad == -1 and mb == -1
 
 
 def test_q8_thresholds_reject_unsorted():
