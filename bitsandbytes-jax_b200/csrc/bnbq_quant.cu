@@ -524,30 +524,32 @@ __device__ void quant_large(const QuantArgs& a, const Choose& choose) {
   }
 }
 
-template <typename InT, bool NF4, typename Choose>
+// Blocks of up to 256 elements and larger blocks are separate kernels (LARGE),
+// so that each gets its own register allocation and occupancy.
+template <typename InT, bool NF4, bool LARGE, typename Choose>
 __device__ __forceinline__ void quant_body(const QuantArgs& a, const Choose& choose) {
-  if (a.log2_bs <= 8) quant_small<InT, NF4>(a, choose);
+  if constexpr (!LARGE) quant_small<InT, NF4>(a, choose);
   else if (a.log2_bs == 9) quant_large<InT, NF4, 2>(a, choose);
   else if (a.log2_bs == 10) quant_large<InT, NF4, 4>(a, choose);
   else quant_large<InT, NF4, 0>(a, choose);
 }
 
-template <typename InT>
+template <typename InT, bool LARGE>
 __global__ void __launch_bounds__(kThreads) quant_nf4_kernel(QuantArgs a) {
   __shared__ NF4Smem sm;
   build_nf4_tables(sm);
   __syncthreads();
-  quant_body<InT, true>(a, NF4Choose{&sm, a.two});
+  quant_body<InT, true, LARGE>(a, NF4Choose{&sm, a.two});
 }
 
-template <typename InT>
+template <typename InT, bool LARGE>
 __global__ void __launch_bounds__(kThreads) quant_8bit_kernel(QuantArgs a) {
   extern __shared__ __align__(16) unsigned char smem_raw[];
   Q8Smem& sm = *reinterpret_cast<Q8Smem*>(smem_raw);
   build_q8_tables(sm, a.code);
-  if (sm.mode > 0 && !sm.map.ex) quant_body<InT, false>(a, Q8Choose<0>{&sm, sm.map});
-  else if (sm.mode > 0) quant_body<InT, false>(a, Q8Choose<1>{&sm, sm.map});
-  else quant_body<InT, false>(a, Q8Choose<-1>{&sm, Q8Map{}});
+  if (sm.mode > 0 && !sm.map.ex) quant_body<InT, false, LARGE>(a, Q8Choose<0>{&sm, sm.map});
+  else if (sm.mode > 0) quant_body<InT, false, LARGE>(a, Q8Choose<1>{&sm, sm.map});
+  else quant_body<InT, false, LARGE>(a, Q8Choose<-1>{&sm, Q8Map{}});
 }
 
 template <typename Kern>
@@ -631,9 +633,15 @@ extern "C" int bnbq_quantize_nf4(int dtype, const void* x, int64_t n, int32_t bl
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   const int64_t ww = work_warps(a);
   switch (dtype) {
-    case BNBQ_F32: return launch_grid(quant_nf4_kernel<float>, 0, ww, a, s);
-    case BNBQ_F16: return launch_grid(quant_nf4_kernel<__half>, 0, ww, a, s);
-    default: return launch_grid(quant_nf4_kernel<__nv_bfloat16>, 0, ww, a, s);
+    case BNBQ_F32:
+      return a.log2_bs > 8 ? launch_grid(quant_nf4_kernel<float, true>, 0, ww, a, s)
+                           : launch_grid(quant_nf4_kernel<float, false>, 0, ww, a, s);
+    case BNBQ_F16:
+      return a.log2_bs > 8 ? launch_grid(quant_nf4_kernel<__half, true>, 0, ww, a, s)
+                           : launch_grid(quant_nf4_kernel<__half, false>, 0, ww, a, s);
+    default:
+      return a.log2_bs > 8 ? launch_grid(quant_nf4_kernel<__nv_bfloat16, true>, 0, ww, a, s)
+                           : launch_grid(quant_nf4_kernel<__nv_bfloat16, false>, 0, ww, a, s);
   }
 }
 
@@ -651,9 +659,15 @@ extern "C" int bnbq_quantize_blockwise(int dtype, const void* x, int64_t n, int3
   const int64_t ww = work_warps(a);
   const size_t smem = sizeof(Q8Smem);
   switch (dtype) {
-    case BNBQ_F32: return launch_grid(quant_8bit_kernel<float>, smem, ww, a, s);
-    case BNBQ_F16: return launch_grid(quant_8bit_kernel<__half>, smem, ww, a, s);
-    default: return launch_grid(quant_8bit_kernel<__nv_bfloat16>, smem, ww, a, s);
+    case BNBQ_F32:
+      return a.log2_bs > 8 ? launch_grid(quant_8bit_kernel<float, true>, smem, ww, a, s)
+                           : launch_grid(quant_8bit_kernel<float, false>, smem, ww, a, s);
+    case BNBQ_F16:
+      return a.log2_bs > 8 ? launch_grid(quant_8bit_kernel<__half, true>, smem, ww, a, s)
+                           : launch_grid(quant_8bit_kernel<__half, false>, smem, ww, a, s);
+    default:
+      return a.log2_bs > 8 ? launch_grid(quant_8bit_kernel<__nv_bfloat16, true>, smem, ww, a, s)
+                           : launch_grid(quant_8bit_kernel<__nv_bfloat16, false>, smem, ww, a, s);
   }
 }
 
