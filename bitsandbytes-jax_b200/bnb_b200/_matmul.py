@@ -32,7 +32,11 @@ def matmul(x: torch.Tensor, w: QuantizedArray) -> torch.Tensor:
     n, k = w.shape
     if x.shape[-1] != k:
         raise ValueError(f"contraction mismatch: x {tuple(x.shape)} @ w.T {w.shape[::-1]}")
-    out = _Matmul2d.apply(x.reshape(-1, k), w)
+    xm = x.reshape(-1, k)
+    if torch.is_grad_enabled() and xm.requires_grad:
+        out = _Matmul2d.apply(xm, w)
+    else:  # no gradient wanted: skip the autograd node (host time per call)
+        out = _forward(xm, w)
     return out.reshape(*x.shape[:-1], n)
 
 

@@ -26,6 +26,14 @@ def _rows_per_warp(m: int) -> int:
     return 2 if m <= 2 else 4
 
 
+def _f32_on(t, device) -> torch.Tensor:
+    """``t`` as a float32 tensor on ``device``; no conversion call when it
+    already is one (the common case: the arrays of a QuantizedArray)."""
+    if isinstance(t, torch.Tensor) and t.dtype == torch.float32 and t.device == device:
+        return t
+    return torch.as_tensor(t, dtype=torch.float32).to(device)
+
+
 def _prepare(x, data, absmax, n_rows, blocksize, nested, what):
     if x.dim() != 2:
         raise ValueError(f"x must be 2-D (M, K), got shape {tuple(x.shape)}")
@@ -50,9 +58,9 @@ def _prepare(x, data, absmax, n_rows, blocksize, nested, what):
         assert absmax.dtype == torch.uint8, absmax.dtype
         _log2_blocksize(blocksize2)
         aq = _lib.aligned(absmax.reshape(-1))
-        a2 = _lib.aligned(absmax2.reshape(-1).to(torch.float32), 4)
-        c2 = _lib.aligned(torch.as_tensor(code2, dtype=torch.float32).reshape(-1).to(x.device), 4)
-        off = _lib.aligned(torch.as_tensor(offset, dtype=torch.float32).reshape(1).to(x.device), 4)
+        a2 = _lib.aligned(_f32_on(absmax2, x.device).reshape(-1), 4)
+        c2 = _lib.aligned(_f32_on(code2, x.device).reshape(-1), 4)
+        off = _lib.aligned(_f32_on(offset, x.device).reshape(1), 4)
         extra = (None, aq, a2, c2, off, blocksize2)
     return xs, w, extra
 
@@ -64,10 +72,14 @@ def _run(entry, x, data, absmax, n_rows, blocksize, nested, absmax2_block0, out)
         out = torch.empty((m, n_rows), dtype=x.dtype, device=x.device)
     ldy = out.stride(0)
     assert out.dtype == x.dtype and out.stride(1) == 1 and out.shape == (m, n_rows)
-    with torch.cuda.device(x.device):
-        _lib.call(entry, _lib.DTYPE_CODE[x.dtype], xs.data_ptr(), m, k, w.data_ptr(), n_rows,
-                  blocksize, _lib.ptr(a), _lib.ptr(aq), _lib.ptr(a2), _lib.ptr(c2), _lib.ptr(off),
-                  bs2, absmax2_block0, out.data_ptr(), ldy, _lib.stream_of(xs))
+    args = (entry, _lib.DTYPE_CODE[x.dtype], xs.data_ptr(), m, k, w.data_ptr(), n_rows, blocksize, _lib.ptr(a),
+            _lib.ptr(aq), _lib.ptr(a2), _lib.ptr(c2), _lib.ptr(off), bs2, absmax2_block0, out.data_ptr(), ldy,
+            _lib.stream_of(xs))
+    if x.device.index == torch.cuda.current_device():
+        _lib.call(*args)
+    else:
+        with torch.cuda.device(x.device):
+            _lib.call(*args)
     return out
 
 
