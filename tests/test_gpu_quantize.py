@@ -71,8 +71,9 @@ def test_quantize_blockwise(cuda, dtype, bs):
 
 
 def test_quantize_blockwise_user_codebooks(cuda):
-    """A strictly increasing user codebook (fast path with more search
-    steps) and an unsorted one (the literal search path)."""
+    """A strictly increasing random codebook (thresholds too close for the
+    bucket table: the literal search), an unsorted one and one with a
+    repeated value (both the literal search)."""
     rng = np.random.default_rng(9)
     sorted_code = np.sort(rng.uniform(-1, 1, 256).astype(np.float32))
     sorted_code = np.sort(np.sign(sorted_code) * np.abs(sorted_code) ** 3).astype(np.float32)
@@ -83,6 +84,42 @@ def test_quantize_blockwise_user_codebooks(cuda):
     for code in (sorted_code, unsorted, dup):
         check_8bit(randn(3 * 256 + 5, seed=4), O.F32, 256, code)
         check_8bit(host_input(randn(1 << 14, seed=5), O.BF16), O.BF16, 64, code)
+
+
+def _common_codebooks():
+    from statistics import NormalDist
+    nd = NormalDist()
+    q = np.array([nd.inv_cdf((i + 0.5) / 256) for i in range(256)])
+    return {"dynamic_unsigned": O.create_dynamic_map(False).astype(np.float32),
+            "linear": np.linspace(-1.0, 1.0, 256).astype(np.float32),
+            "quantile": (q / np.abs(q).max()).astype(np.float32)}
+
+
+def _blocks_of(vals, bs):
+    """vals in blocks of bs - 1 with a 1.0 closing each block (absmax 1)."""
+    x = np.zeros(-(-len(vals) // (bs - 1)) * bs, np.float32)
+    for i, start in enumerate(range(0, len(vals), bs - 1)):
+        chunk = vals[start:start + bs - 1]
+        x[i * bs:i * bs + len(chunk)] = chunk
+        x[(i + 1) * bs - 1] = 1.0
+    return x
+
+
+@pytest.mark.parametrize("name", ["dynamic_unsigned", "linear", "quantile"])
+def test_quantize_blockwise_common_codebooks(cuda, name):
+    """Codebooks of the bitsandbytes family besides the signed dynamic map:
+    the bucket table, and for the symmetric ones (middle threshold just below
+    0) the table plus one direct compare. Every code, every midpoint and one
+    ulp either side, zeros and the smallest denormals, and random values."""
+    code = _common_codebooks()[name]
+    mid = ((code[1:] + code[:-1]) * np.float32(0.5)).astype(np.float32)
+    tiny = np.array([0.0, -0.0, 1e-45, -1e-45, 1.2e-38, -1.2e-38], np.float32)
+    vals = np.concatenate([code, mid, np.nextafter(mid, np.float32(np.inf)),
+                           np.nextafter(mid, np.float32(-np.inf)), tiny])
+    check_8bit(_blocks_of(vals, 256), O.F32, 256, code)
+    for dtype in (O.F16, O.BF16):
+        check_8bit(host_input(mixed_outliers(3 * 4096 + 7, seed=77), dtype), dtype, 4096, code)
+        check_8bit(host_input(mixed_outliers(1 << 16, seed=78), dtype), dtype, 256, code)
 
 
 def test_quantize_nf4_thresholds(cuda):
