@@ -475,9 +475,12 @@ constexpr int kMaxRows = 4;
 constexpr int kMaxStages = 8;
 constexpr int kMaxGroupsPerFlush = 32;  // partial sums held in shared memory between flushes
 
-template <typename XT, int M, int R, bool NESTED, int SLOTS>
+// SIS: the block scales travel with the stage (a compile-time choice, so that
+// the other layout's registers and code drop out).
+template <typename XT, int M, int R, bool NESTED, int SLOTS, bool SIS>
 __global__ void __launch_bounds__(kMaxWarps * 32, 1)
-gemv_bulk_kernel(GemvArgs a, int n_groups, int n_stages, uint32_t stage_bytes, int scales_in_stage) {
+gemv_bulk_kernel(GemvArgs a, int n_groups, int n_stages, uint32_t stage_bytes) {
+  constexpr bool scales_in_stage = SIS;
   __shared__ __align__(16) float s_code2[256];
   __shared__ float s_part[kMaxGroupsPerFlush][kMaxWarps - 1][M * R];
   __shared__ __align__(8) uint64_t s_tbl_bar;
@@ -608,13 +611,11 @@ gemv_bulk_kernel(GemvArgs a, int n_groups, int n_stages, uint32_t stage_bytes, i
       }
   };
   prefetch(blockIdx.x, pre0, preq0);
-  prefetch(blockIdx.x + gridDim.x, pre1, preq1);
   // within-group scale index of (slot, row) when scales travel with the stage
-  int sidx[SLOTS][R];
+  // (row r's index = sidx0 + r * spr, K % bs == 0 there)
+  int sidx0[SLOTS];
 #pragma unroll
-  for (int sl = 0; sl < SLOTS; ++sl)
-#pragma unroll
-    for (int r = 0; r < R; ++r) sidx[sl][r] = (r * a.k + cofs[sl]) >> a.log2_bs;
+  for (int sl = 0; sl < SLOTS; ++sl) sidx0[sl] = cofs[sl] >> a.log2_bs;
 
   asm volatile("griddepcontrol.wait;" ::: "memory");  // x may come from the previous kernel
   const XT* x = static_cast<const XT*>(a.x);
@@ -650,29 +651,20 @@ gemv_bulk_kernel(GemvArgs a, int n_groups, int n_stages, uint32_t stage_bytes, i
     if (!ok) { s_abort = 1; break; }
     const char* stage = stages + size_t(st) * stage_bytes;
 
-    float scale[SLOTS][R];
-#pragma unroll
-    for (int sl = 0; sl < SLOTS; ++sl)
-#pragma unroll
-      for (int r = 0; r < R; ++r) {
-        float s_;
-        if (scales_in_stage) {
-          if constexpr (NESTED) {
-            const int q2 = reinterpret_cast<const uint8_t*>(stage + codes_bytes)[sidx[sl][r]];
-            s_ = add_rn(mul_ftz(s_code2[q2], pre0[sl][r]), offset);
-          } else {
-            s_ = reinterpret_cast<const float*>(stage + codes_bytes)[sidx[sl][r]];
-          }
+    // a row's block scale, decoded where it is used (fewer live registers)
+    auto scale_of = [&](int sl, int r) -> float {
+      if (scales_in_stage) {
+        const int si = sidx0[sl] + r * spr;
+        if constexpr (NESTED) {
+          const int q2 = reinterpret_cast<const uint8_t*>(stage + codes_bytes)[si];
+          return add_rn(mul_ftz(s_code2[q2], pre0[sl][r]), offset);
         } else {
-          s_ = NESTED ? add_rn(mul_ftz(s_code2[preq0[sl][r]], pre0[sl][r]), offset) : pre0[sl][r];
+          return reinterpret_cast<const float*>(stage + codes_bytes)[si];
         }
-        scale[sl][r] = s_;
+      } else {
+        return NESTED ? add_rn(mul_ftz(s_code2[preq0[sl][r]], pre0[sl][r]), offset) : pre0[sl][r];
       }
-#pragma unroll
-    for (int sl = 0; sl < SLOTS; ++sl)
-#pragma unroll
-      for (int r = 0; r < R; ++r) { pre0[sl][r] = pre1[sl][r]; preq0[sl][r] = preq1[sl][r]; }
-    prefetch(g + 2 * int(gridDim.x), pre1, preq1);
+    };
 
     float acc[M * R];
 #pragma unroll
@@ -685,24 +677,33 @@ gemv_bulk_kernel(GemvArgs a, int n_groups, int n_stages, uint32_t stage_bytes, i
         for (int r = 0; r < R; ++r) {
           const uint4 cw = *reinterpret_cast<const uint4*>(stage + r * row_bytes + c * 16);
           const uint32_t words[4] = {cw.x, cw.y, cw.z, cw.w};
-          float2 wv[16];  // all 16 lookups first, then 4 independent fma chains
+          float2 t[M][4];
 #pragma unroll
-          for (int wi = 0; wi < 4; ++wi)
+          for (int m = 0; m < M; ++m)
 #pragma unroll
-            for (int j = 0; j < 4; ++j) wv[4 * wi + j] = pair_at(words[wi], lane_b, j);
+            for (int q = 0; q < 4; ++q) t[m][q] = make_float2(0.0f, 0.0f);
+#pragma unroll
+          for (int h = 0; h < 2; ++h) {  // 8 lookups, then their 4 fma chains per row of x
+            float2 wv[8];
+#pragma unroll
+            for (int wi = 0; wi < 2; ++wi)
+#pragma unroll
+              for (int j = 0; j < 4; ++j) wv[4 * wi + j] = pair_at(words[2 * h + wi], lane_b, j);
+#pragma unroll
+            for (int m = 0; m < M; ++m)
+#pragma unroll
+              for (int e = 0; e < 8; ++e) t[m][e & 3] = __ffma2_rn(wv[e], xr[sl][m][8 * h + e], t[m][e & 3]);
+          }
 #pragma unroll
           for (int m = 0; m < M; ++m) {
-            float2 t[4];
-#pragma unroll
-            for (int q = 0; q < 4; ++q) t[q] = make_float2(0.0f, 0.0f);
-#pragma unroll
-            for (int e = 0; e < 16; ++e) t[e & 3] = __ffma2_rn(wv[e], xr[sl][m][e], t[e & 3]);
-            const float2 u = __fadd2_rn(__fadd2_rn(t[0], t[1]), __fadd2_rn(t[2], t[3]));
-            acc[m * R + r] = __fmaf_rn(scale[sl][r], u.x + u.y, acc[m * R + r]);
+            if (false) {}
+            const float2 u = __fadd2_rn(__fadd2_rn(t[m][0], t[m][1]), __fadd2_rn(t[m][2], t[m][3]));
+            acc[m * R + r] = __fmaf_rn(scale_of(sl, r), u.x + u.y, acc[m * R + r]);
           }
         }
       }
     }
+    prefetch(g + int(gridDim.x), pre0, preq0);  // one group ahead
     __syncwarp();
     if (lane == 0) mbar_arrive(smem_u32(bars + n_stages + st));  // stage consumed
     if (++st == n_stages) { st = 0; phase ^= 1u; }
@@ -765,7 +766,8 @@ bool plan_bulk(int m, int k, int log2_bs, bool nested, int smem_optin, BulkPlan*
 
 template <typename XT, int M, int R, bool NESTED, int SLOTS>
 int launch_bulk_t(const GemvArgs& a, const BulkPlan& p, const DeviceInfo& di, cudaStream_t s) {
-  auto kern = gemv_bulk_kernel<XT, M, R, NESTED, SLOTS>;
+  auto kern = p.scales_in_stage ? gemv_bulk_kernel<XT, M, R, NESTED, SLOTS, true>
+                                : gemv_bulk_kernel<XT, M, R, NESTED, SLOTS, false>;
   cudaFuncAttributes fa;
   if (cudaFuncGetAttributes(&fa, kern) != cudaSuccess) return BNBQ_ERR_CUDA;
   const size_t room = size_t(di.smem_optin) - size_t(kPairTableBytes) - fa.sharedSizeBytes - 1024;
@@ -793,7 +795,7 @@ int launch_bulk_t(const GemvArgs& a, const BulkPlan& p, const DeviceInfo& di, cu
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  if (cudaLaunchKernelEx(&cfg, kern, a, int(n_groups), stages, p.stage_bytes, p.scales_in_stage) != cudaSuccess)
+  if (cudaLaunchKernelEx(&cfg, kern, a, int(n_groups), stages, p.stage_bytes) != cudaSuccess)
     return BNBQ_ERR_CUDA;
   return launch_status();
 }
