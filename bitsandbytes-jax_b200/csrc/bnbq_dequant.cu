@@ -10,7 +10,8 @@
 // 16-bit type, 4 of float32); each thread of a persistent grid (a whole number
 // of CTAs per SM) streams vectors with stride gridDim*blockDim, so every warp
 // store is one fully coalesced 512-byte run and every code load a coalesced
-// 64..256-byte run. Four vectors per thread per iteration keep loads in flight.
+// 64..256-byte run. Several vectors per thread per iteration keep loads in
+// flight (unroll_for).
 // bs >= 8 guarantees a vector never straddles two blocks.
 // The NF4 table lives in shared memory (16 floats, conflict-free). The 8-bit
 // codebook is replicated once per lane (256 x 32 floats): a lane reads its own
@@ -23,7 +24,12 @@ namespace bnbq {
 namespace {
 
 constexpr int kThreads = 256;
-constexpr int kUnroll = 4;
+// Output vectors per thread per iteration (their code loads are issued
+// together): measured on config 3, 8 for 8-bit codes to 16-bit outputs and 2
+// for float32 outputs (whose 16-byte vector holds only 4 elements) keep HBM
+// busiest; NF4 (half the code bytes per vector) keeps 4.
+template <typename OutT, bool NF4>
+constexpr int unroll_for() { return NF4 ? 4 : (sizeof(OutT) == 4 ? 2 : 8); }
 
 template <typename OutT>
 struct Vec;  // 16 bytes of output
@@ -95,6 +101,7 @@ __global__ void __launch_bounds__(kThreads)
 dequant_kernel(DequantArgs a) {
   constexpr int EPV = Vec<OutT>::kEPV;
   constexpr int CB = NF4 ? EPV / 2 : EPV;  // code bytes per vector
+  constexpr int kUnroll = unroll_for<OutT, NF4>();
   extern __shared__ float smem[];
   float* s_table = smem;
   float* s_code2 = smem + Smem<NF4, NESTED>::kTable;
@@ -202,6 +209,7 @@ int launch_t(const DequantArgs& a, cudaStream_t s) {
     return BNBQ_ERR_CUDA;
   if (per_sm < 1) per_sm = 1;
   const int64_t nvec = a.n / EPV;
+  constexpr int kUnroll = unroll_for<OutT, NF4>();
   const int64_t want = (nvec + int64_t(kThreads) * kUnroll - 1) / (int64_t(kThreads) * kUnroll);
   int64_t grid = int64_t(di.sm_count) * per_sm;
   if (want < grid) grid = want > 0 ? want : 1;
