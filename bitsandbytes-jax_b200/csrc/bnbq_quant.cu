@@ -305,7 +305,7 @@ struct NF4Choose {
   uint32_t two;  // 2 (runtime)
   __device__ int operator()(float s, int) const {
     const float2 e = sm->tb[nf4_bucket(s)];
-    return __float_as_int(e.y) + int(gt01(s, e.x, two));
+    return __float_as_int(e.y) + (s > e.x ? 1 : 0);  // a plain compare measured faster here than gt01
   }
 };
 
