@@ -16,9 +16,27 @@ graph that holds the K timed calls. `e2e` is the same metric through the
 public API (bnb_b200.matmul) with x copied from pinned host memory and y read
 back every step. `m_sweep` repeats the device timing at M = 2..20.
 
-Multi-GPU (torchrun, one process per GPU): every rank runs the same workload
-on its own weights (independent objects, no collective; weak scaling); the
-timed region is bracketed by barriers and the max over ranks is reported.
+Multi-GPU (torchrun, one process per GPU): the north star's split. The
+weight is partitioned by output rows (row_partition, whole nested blocks per
+rank); a step is every rank's fused GEMV on its rows followed by the NVLink
+all-gather of y (PeerGather: one kernel, peer stores, bounded handshakes), so
+every rank holds the full (M, 4096) product when the step ends -- strong
+scaling of one call. Each rank rotates 8 x N copies of its shard (242 MB per
+rank whatever N is, more than L2). Before timing, every rank checks the
+gathered y bitwise against the one-GPU product of the whole weight. The timed
+region is bracketed by barriers and the max over ranks is reported.
+
+Timing: after the barrier and a synchronize, a ~50 us spin kernel is queued
+ahead of the start event so that the graph launch is already queued when the
+clock starts (NVBench's blocking-kernel method); the K timed calls are one
+graph replay.
+
+Extra keys of the default line (N=1): `config1` (NF4 quantize and dequantize
+of a 4096x4096 bf16 tensor), `config3` (8-bit blockwise of 2^28+37 elements,
+f32/f16/bf16, blocksizes 256 and 4096), `config5` (the fused GEMM on the
+Llama-3-70B MLP shapes at M=2048 beside dequantize+matmul) and, at every N,
+`config4` (one pass over a Llama-3-8B decode stack with every GEMV
+row-sharded and its y all-gathered).
 
 `--workload quant` and `--workload gemm` (not read by the driver) measure the
 other configurations the same way: config 1 (NF4 quantize + dequantize round
@@ -147,48 +165,62 @@ class ClockSampler:
 
 # ------------------------------------------------------------------ ours
 
-def make_weights(torch, bnb, device, seed: int):
-    ws = []
-    for i in range(ROTATE):
-        g = torch.Generator(device).manual_seed(seed * 100 + i)
-        w = (torch.randn(N_ROWS, K_COLS, device=device, generator=g) * 0.02).to(torch.bfloat16)
-        ws.append(bnb.quantize(w, "nf4", BS, double_quant=True))
+def spin_ahead(torch, stream, us: float = 50.0) -> None:
+    """Queue a ~`us` spin kernel on `stream`, so the work enqueued right after
+    it is already queued when the GPU reaches the next event (untimed)."""
+    with torch.cuda.stream(stream):
+        torch.cuda._sleep(int(us * 1e-6 * 1.965e9))
+
+
+class Shard:
+    """One rotation copy as the timed call takes it: the rank's rows of the
+    weight (the whole weight on one GPU)."""
+
+    def __init__(self, rs, full=None):
+        self.rs = rs        # bnb_b200.parallel.RowShard
+        self.full = full    # the whole QuantizedArray (kept for copy 0 only)
+
+
+def make_shards(torch, bnb, device, copies: int, rank: int, world: int):
+    """`copies` independent weights (the same on every rank), each cut to this
+    rank's rows; the full weight of copy 0 is kept for the bitwise check."""
+    from bnb_b200.parallel import row_partition, shard_rows
+    ranges = row_partition(N_ROWS, K_COLS, BS * BS2, world)
+    a, b = ranges[rank]
+    shards = []
+    for i in range(copies):
+        g = torch.Generator(device).manual_seed(100 + i)
+        w = bnb.quantize((torch.randn(N_ROWS, K_COLS, device=device, generator=g) * 0.02).to(torch.bfloat16),
+                         "nf4", BS, double_quant=True)
+        rs = shard_rows(w, a, b)
+        if world > 1:  # own copies of the rank's slices; the full weight is dropped
+            rs.data, rs.absmax = rs.data.clone(), rs.absmax.clone()
+        shards.append(Shard(rs, w if (i == 0 or world == 1) else None))
         del w
     torch.cuda.synchronize()
-    return ws
+    return shards, ranges
 
 
-def gemv_args(w):
-    a = w.absmax
-    return w.data, a.data, (a.absmax, a.code, a.offset, a.blocksize)
-
-
-def time_device(torch, gemv_nf4, ws, x, steps: int, warmup: int, dist=None):
-    """Device time of `steps` GEMV calls replayed from one CUDA graph."""
-    m = x.shape[0]
-    ys = [torch.empty(m, N_ROWS, dtype=torch.bfloat16, device=x.device) for _ in range(ROTATE)]
-    args = [gemv_args(w) for w in ws]
-
-    def call(i):
-        d, aq, nested = args[i % ROTATE]
-        gemv_nf4(x, d, aq, N_ROWS, BS, nested=nested, out=ys[i % ROTATE])
-
+def time_device(torch, step, steps: int, warmup: int, device, dist=None):
+    """Device time (ms) of `steps` calls step(i) replayed from one CUDA graph."""
     for i in range(max(warmup, 3)):  # eager warm-up (also primes per-device setup)
-        call(i)
+        step(i)
     torch.cuda.synchronize()
-    stream = torch.cuda.Stream(device=x.device)
+    stream = torch.cuda.Stream(device=device)
     graph = torch.cuda.CUDAGraph()
     with torch.cuda.stream(stream):
         with torch.cuda.graph(graph, stream=stream):
             for i in range(steps):
-                call(i)
-    for _ in range(max(warmup // max(steps, 1), 1) + 2):  # graph warm-up replays
-        graph.replay()
+                step(i)
+    for _ in range(2):  # graph warm-up replays
+        with torch.cuda.stream(stream):
+            graph.replay()
     torch.cuda.synchronize()
     if dist is not None:
         dist.barrier()
     torch.cuda.synchronize()
     start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    spin_ahead(torch, stream)
     start.record(stream)
     with torch.cuda.stream(stream):
         graph.replay()
@@ -198,31 +230,65 @@ def time_device(torch, gemv_nf4, ws, x, steps: int, warmup: int, dist=None):
         dist.barrier()
     ms = start.elapsed_time(end)
     del graph
-    return ms, ys[0]
+    return ms
 
 
-def time_e2e(torch, bnb, ws, m: int, steps: int, warmup: int):
-    """The public API with host buffers: pinned x -> device, matmul, y -> host."""
-    dev = ws[0].data.device
+def make_step(torch, shards, x, ranges, rank, world, pg):
+    """One call: the fused GEMV on this rank's rows (+ the all-gather of y)."""
+    from bnb_b200.kernels import gemv_nf4
+    from bnb_b200.parallel import matmul_rows
+    m = x.shape[0]
+    copies = len(shards)
+    if world == 1:
+        ys = [torch.empty(m, N_ROWS, dtype=torch.bfloat16, device=x.device) for _ in range(copies)]
+        args = []
+        for sh in shards:
+            a = sh.full.absmax
+            args.append((sh.full.data, a.data, (a.absmax, a.code, a.offset, a.blocksize)))
+
+        def step(i):
+            d, aq, nested = args[i % copies]
+            gemv_nf4(x, d, aq, N_ROWS, BS, nested=nested, out=ys[i % copies])
+            return ys[i % copies]
+        return step
+    col0 = ranges[rank][0]
+    n_local = ranges[rank][1] - col0
+    ys = [torch.empty(m, n_local, dtype=torch.bfloat16, device=x.device) for _ in range(2)]
+
+    def step(i):
+        y = matmul_rows(x, shards[i % copies].rs, out=ys[i % 2])
+        return pg.gather(y, col0)
+    return step
+
+
+def time_e2e(torch, step_fn, device, m: int, steps: int, warmup: int, dist=None):
+    """The public API with host buffers: pinned x -> device, the call, y -> host."""
     g = torch.Generator().manual_seed(7)
     xh = torch.randn(m, K_COLS, generator=g).to(torch.bfloat16).pin_memory()
     yh = torch.empty(m, N_ROWS, dtype=torch.bfloat16).pin_memory()
+    xd = torch.empty(m, K_COLS, dtype=torch.bfloat16, device=device)
 
-    def step(i):
-        xd = xh.to(dev, non_blocking=True)
-        y = bnb.matmul(xd, ws[i % ROTATE])
+    def one(i):
+        xd.copy_(xh, non_blocking=True)
+        y = step_fn(xd, i)
         yh.copy_(y, non_blocking=True)
 
     for i in range(max(warmup, 3)):
-        step(i)
+        one(i)
     torch.cuda.synchronize()
+    if dist is not None:
+        dist.barrier()
     start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     start.record()
     for i in range(steps):
-        step(i)
+        one(i)
     end.record()
     torch.cuda.synchronize()
     ms = start.elapsed_time(end)
+    if dist is not None:
+        t = torch.tensor([ms], device=device, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
     return ms, m * K_COLS * 2, m * N_ROWS * 2
 
 
@@ -231,6 +297,7 @@ def cpu_baseline_gemv(seconds: float = 12.0):
     numerics), M=1 on the full 4096x14336 weight, OpenMP on every host core."""
     import numpy as np
     from oracle import oracle as O
+    O.set_threads(os.cpu_count() or 1)
     rng = np.random.default_rng(0)
     w = (rng.standard_normal(N_ROWS * K_COLS) * 0.02).astype(np.float32)
     q, am = O.quantize_nf4(w, O.F32, BS)
@@ -254,41 +321,85 @@ def cpu_baseline_gemv(seconds: float = 12.0):
             "sample": f"{calls} full M=1 GEMV calls (4096x14336, double-quantized) in {el:.1f} s"}
 
 
+def bench_config(m: int, world: int) -> dict:
+    """The `config` object both arms print (identical keys and values)."""
+    return {"workload": WORKLOAD, "m": m, "n": N_ROWS, "k": K_COLS, "blocksize": BS,
+            "blocksize2": BS2, "weight_bytes": W_BYTES, "algorithmic_bytes_per_call": algo_bytes(m),
+            "l2": "rotated weight copies: 242 MB per GPU (8 x N shards of 30.3/N MB), more than the 126 MB L2",
+            "timing": "CUDA graph of the K calls, queued behind a spin kernel",
+            "parallelism": f"tp{world} (rows) + NVLink all-gather of y" if world > 1 else "1 GPU"}
+
+
 def run_ours(args, dist, rank, world, local_rank):
     import torch
     import bnb_b200 as bnb
-    from bnb_b200.kernels import gemv_nf4
+    from bnb_b200.parallel import PeerGather
 
     device = torch.device("cuda", local_rank)
     torch.cuda.set_device(device)
-    ws = make_weights(torch, bnb, device, seed=rank + 1)
+    copies = ROTATE * world
+    shards, ranges = make_shards(torch, bnb, device, copies, rank, world)
     g = torch.Generator(device).manual_seed(1234)
     x = torch.randn(args.m, K_COLS, device=device, generator=g).to(torch.bfloat16)
+    pg = PeerGather(GEMV_MAX_ROWS, N_ROWS, torch.bfloat16, device) if world > 1 else None
+    step = make_step(torch, shards, x, ranges, rank, world, pg)
+
+    # every rank: the gathered (or single-GPU) y of copy 0 equals the one-GPU product bitwise
+    want = bnb.matmul(x, shards[0].full)
+    ok = torch.equal(step(0), want)
+    torch.cuda.synchronize()
+    if dist is not None:
+        flag = torch.tensor([0 if ok else 1], device=device, dtype=torch.int32)
+        dist.all_reduce(flag, op=dist.ReduceOp.MAX)
+        ok = int(flag.item()) == 0
+    if not ok:
+        raise RuntimeError("the gathered product differs from the one-GPU product")
+    del want
 
     with ClockSampler(local_rank) as clocks:
-        ms, _ = time_device(torch, gemv_nf4, ws, x, args.steps, args.warmup, dist)
+        ms = time_device(torch, step, args.steps, args.warmup, device, dist)
     ms_t = torch.tensor([ms], device=device, dtype=torch.float64)
     if dist is not None:
         dist.all_reduce(ms_t, op=dist.ReduceOp.MAX)
     ms_max = float(ms_t.item())
 
     sweep = {}
-    for m in ([2, 4, 8, 16, 20] if args.sweep else []):
+    for m in ([2, 4, 8, 16, 20] if (args.sweep and world == 1) else []):
         xm = torch.randn(m, K_COLS, device=device, generator=g).to(torch.bfloat16)
-        t, _ = time_device(torch, gemv_nf4, ws, xm, max(args.steps // 4, 64), args.warmup)
-        per = t / max(args.steps // 4, 64)
+        sm = make_step(torch, shards, xm, ranges, rank, world, pg)
+        k = max(args.steps // 4, 64)
+        per = time_device(torch, sm, k, args.warmup, device) / k
         sweep[f"m{m}"] = {"us": round(per * 1e3, 3), "gbs": round(algo_bytes(m) / (per * 1e-3) / 1e9, 1)}
 
-    e2e_ms, h2d, d2h = time_e2e(torch, bnb, ws, args.m, min(args.steps, 500), args.warmup)
     e2e_steps = min(args.steps, 500)
+    if world == 1:
+        def e2e_call(xd, i):
+            return bnb.matmul(xd, shards[i % copies].full)
+    else:
+        from bnb_b200.parallel import matmul_rows
+        n_local = ranges[rank][1] - ranges[rank][0]
+
+        def e2e_call(xd, i):
+            return pg.gather(matmul_rows(xd, shards[i % copies].rs), ranges[rank][0])
+    e2e_ms, h2d, d2h = time_e2e(torch, e2e_call, device, args.m, e2e_steps, args.warmup, dist)
+
+    extras = {}
+    if not args.no_extras:
+        extras["config4"] = llama_pass(args, dist, rank, world, local_rank)
+        if world == 1:
+            extras["config1"], extras["config3"] = quant_cases(torch, device, args.warmup)
+            extras["config5"] = gemm_cases(torch, bnb, device)
+    if pg is not None:
+        torch.cuda.synchronize()
+        dist.barrier()
+        pg.close()
 
     if rank != 0:
         return None
     per_call_ms = ms_max / args.steps
-    value = algo_bytes(args.m) * args.steps * world / (ms_max * 1e-3) / 1e9
+    value = algo_bytes(args.m) * args.steps / (ms_max * 1e-3) / 1e9
     peak, peak_kind = measured_peaks()
     achieved = algo_bytes(args.m) / (per_call_ms * 1e-3) / 1e9
-    traffic = profiled_traffic(args.m)
     line = {
         "metric": METRIC,
         "value": round(value, 2),
@@ -299,27 +410,42 @@ def run_ours(args, dist, rank, world, local_rank):
         "ms_per_step": round(per_call_ms, 6),
         "us_per_call": round(per_call_ms * 1e3, 3),
         "higher_is_better": True,
-        "scaling": "weak",
+        "scaling": "strong" if world > 1 else "weak",
         "vs_baseline": None,
         "dtype": "bf16",
         "data": "synthetic (seeded torch Philox: W ~ N(0, 0.02^2), x ~ N(0, 1))",
-        "config": {"workload": WORKLOAD, "m": args.m, "n": N_ROWS, "k": K_COLS, "blocksize": BS,
-                   "blocksize2": BS2, "weight_bytes": W_BYTES, "algorithmic_bytes_per_call": algo_bytes(args.m),
-                   "l2": "8 rotated weight copies, 242 MB > 126 MB L2", "timing": "CUDA graph of the K calls",
-                   "parallelism": f"replicas x{world}" if world > 1 else "1 GPU"},
-        "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
-                     "frac": round(achieved / peak, 4), "peak_source": peak_kind,
-                     "traffic": traffic, "kernel": "gemv_bulk_kernel"},
+        "config": bench_config(args.m, world),
+        "verified": "gathered y == one-GPU product, bitwise, every rank" if world > 1 else "y == bnb.matmul(x, w)",
+        "roofline": roofline_entry(args.m, per_call_ms, peak, peak_kind, world),
         "e2e": {"value": round(algo_bytes(args.m) * e2e_steps / (e2e_ms * 1e-3) / 1e9, 2), "unit": "GB/s",
                 "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
                 "us_per_step": round(e2e_ms / e2e_steps * 1e3, 3)},
-        "gpu_launches": args.steps,
+        "gpu_launches": args.steps * (2 if world > 1 else 1),
         "clocks": clocks.summary(),
-        "m_sweep": sweep,
     }
+    if sweep:
+        line["m_sweep"] = sweep
+    line.update(extras)
     if world == 1 and not args.no_cpu_baseline:
         line["cpu_baseline"] = cpu_baseline_gemv()
     return line
+
+
+GEMV_MAX_ROWS = 20
+
+
+def roofline_entry(m, per_call_ms, peak, peak_kind, world):
+    """The dominant kernel: the GEMV (the whole call at N=1)."""
+    achieved = algo_bytes(m) / (per_call_ms * 1e-3) / 1e9
+    entry = {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
+             "frac": round(achieved / peak, 4), "peak_source": peak_kind,
+             "traffic": profiled_traffic(m), "kernel": GEMV_KERNEL}
+    if world > 1:
+        entry["note"] = "whole-call rate (GEMV on 1/N of the rows + all-gather) against one GPU's peak"
+    return entry
+
+
+GEMV_KERNEL = "gemv_bulk_kernel"
 
 
 def time_graph(torch, call, steps: int, warmup: int, device):
@@ -346,121 +472,134 @@ def time_graph(torch, call, steps: int, warmup: int, device):
     return ms
 
 
-def run_quant_workload(args, local_rank):
-    """Configs 1 and 3: blockwise quantize / dequantize bandwidth."""
-    import torch
+def quant_cases(torch, device, warmup: int, steps: int = 8):
+    """Configs 1 and 3: blockwise quantize / dequantize bandwidth (device time
+    per call, CUDA graph of `steps` calls); returns (config1, config3) dicts."""
     from bnb_b200.kernels import (create_dynamic_map, dequantize_blockwise, dequantize_nf4,
                                   quantize_blockwise, quantize_nf4)
+    peak, _ = measured_peaks()
+    # config 1: 4096 x 4096 bf16, NF4 bs 64, 8 rotated copies (256 MiB)
+    n1 = 4096 * 4096
+    g = torch.Generator(device).manual_seed(0)
+    xs = [(torch.randn(n1, device=device, generator=g) * 0.02).to(torch.bfloat16) for _ in range(8)]
+    qs = [quantize_nf4(x, 64) for x in xs]
+    b1 = n1 * 2 + n1 // 2 + 4 * (n1 // 64)
+    s1 = max(steps, 16)
+    tq = time_graph(torch, lambda i: quantize_nf4(xs[i % 8], 64), s1, warmup, device) / s1
+    td = time_graph(torch, lambda i: dequantize_nf4(qs[i % 8][0], qs[i % 8][1], 64, torch.bfloat16),
+                    s1, warmup, device) / s1
+    c1 = {"workload": "NF4 bs64 of one 4096x4096 bf16 tensor (8 rotated copies)", "bytes_per_call": b1,
+          "quantize_us": round(tq * 1e3, 2), "quantize_gbs": round(b1 / (tq * 1e-3) / 1e9, 1),
+          "quantize_frac": round(b1 / (tq * 1e-3) / 1e9 / peak, 3),
+          "dequantize_us": round(td * 1e3, 2), "dequantize_gbs": round(b1 / (td * 1e-3) / 1e9, 1),
+          "dequantize_frac": round(b1 / (td * 1e-3) / 1e9 / peak, 3)}
+    del xs, qs
+    # config 3: 2^28 + 37 elements, 90% N(0,1) + 10% Laplace(0,8), 8-bit dynamic map
+    n3 = (1 << 28) + 37
+    code = create_dynamic_map().to(device)
+    base = torch.randn(n3, device=device, generator=g)
+    mask = torch.rand(n3, device=device, generator=g) < 0.1
+    u = torch.rand(n3, device=device, generator=g) - 0.5  # Laplace(0, 8) by inverse CDF
+    lap = -8.0 * torch.sign(u) * torch.log1p(-2.0 * u.abs())
+    del u
+    base = torch.where(mask, lap, base)
+    del mask, lap
+    c3 = {"workload": "8-bit dynamic map, 2^28+37 elements, 90% N(0,1) + 10% Laplace(0,8)"}
+    for dt, name in [(torch.float32, "f32"), (torch.float16, "f16"), (torch.bfloat16, "bf16")]:
+        x = base.to(dt)
+        for bs in (256, 4096):
+            q, a = quantize_blockwise(x, code, bs)
+            b3 = n3 * x.element_size() + n3 + 4 * (-(-n3 // bs))
+            s3 = 3
+            tq = time_graph(torch, lambda i: quantize_blockwise(x, code, bs), s3, 1, device) / s3
+            td = time_graph(torch, lambda i: dequantize_blockwise(q, a, code, bs, dt), s3, 1, device) / s3
+            c3[f"{name}_bs{bs}"] = {
+                "bytes_per_call": b3,
+                "quantize_us": round(tq * 1e3, 1), "quantize_gbs": round(b3 / (tq * 1e-3) / 1e9, 1),
+                "quantize_frac": round(b3 / (tq * 1e-3) / 1e9 / peak, 3),
+                "dequantize_us": round(td * 1e3, 1), "dequantize_gbs": round(b3 / (td * 1e-3) / 1e9, 1),
+                "dequantize_frac": round(b3 / (td * 1e-3) / 1e9 / peak, 3)}
+            del q, a
+        del x
+    del base
+    torch.cuda.synchronize()
+    torch.cuda.empty_cache()
+    return c1, c3
+
+
+def run_quant_workload(args, local_rank):
+    import torch
     device = torch.device("cuda", local_rank)
     torch.cuda.set_device(device)
-    peak, peak_kind = measured_peaks()
-    steps = max(args.steps // 100, 8)
-    out = {}
     with ClockSampler(local_rank) as clocks:
-        # config 1: 4096 x 4096 bf16, NF4 bs 64, 8 rotated copies (256 MiB)
-        n1 = 4096 * 4096
-        g = torch.Generator(device).manual_seed(0)
-        xs = [(torch.randn(n1, device=device, generator=g) * 0.02).to(torch.bfloat16) for _ in range(8)]
-        qs = [quantize_nf4(x, 64) for x in xs]
-        b1 = n1 * 2 + n1 // 2 + 4 * (n1 // 64)
-        tq = time_graph(torch, lambda i: quantize_nf4(xs[i % 8], 64), steps, args.warmup, device) / steps
-        td = time_graph(torch, lambda i: dequantize_nf4(qs[i % 8][0], qs[i % 8][1], 64, torch.bfloat16),
-                        steps, args.warmup, device) / steps
-        out["config1_nf4_bf16_bs64"] = {
-            "quantize_us": round(tq * 1e3, 2), "quantize_gbs": round(b1 / (tq * 1e-3) / 1e9, 1),
-            "dequantize_us": round(td * 1e3, 2), "dequantize_gbs": round(b1 / (td * 1e-3) / 1e9, 1),
-            "bytes_per_call": b1}
-        del xs, qs
-        # config 3: 2^28 + 37 elements, 90% N(0,1) + 10% Laplace(0,8), 8-bit dynamic map
-        n3 = (1 << 28) + 37
-        code = create_dynamic_map().to(device)
-        base = torch.randn(n3, device=device, generator=g)
-        mask = torch.rand(n3, device=device, generator=g) < 0.1
-        u = torch.rand(n3, device=device, generator=g) - 0.5  # Laplace(0, 8) by inverse CDF
-        lap = -8.0 * torch.sign(u) * torch.log1p(-2.0 * u.abs())
-        del u
-        base = torch.where(mask, lap, base)
-        del mask, lap
-        for dt, name in [(torch.float32, "f32"), (torch.float16, "f16"), (torch.bfloat16, "bf16")]:
-            x = base.to(dt)
-            for bs in (256, 4096):
-                q, a = quantize_blockwise(x, code, bs)
-                b3 = n3 * x.element_size() + n3 + 4 * (-(-n3 // bs))
-                s3 = max(steps // 4, 3)
-                tq = time_graph(torch, lambda i: quantize_blockwise(x, code, bs), s3, 1, device) / s3
-                td = time_graph(torch, lambda i: dequantize_blockwise(q, a, code, bs, dt), s3, 1, device) / s3
-                out[f"config3_8bit_{name}_bs{bs}"] = {
-                    "quantize_us": round(tq * 1e3, 1), "quantize_gbs": round(b3 / (tq * 1e-3) / 1e9, 1),
-                    "dequantize_us": round(td * 1e3, 1), "dequantize_gbs": round(b3 / (td * 1e-3) / 1e9, 1),
-                    "bytes_per_call": b3}
-                del q, a
-            del x
-    c1 = out["config1_nf4_bf16_bs64"]
+        c1, c3 = quant_cases(torch, device, args.warmup, max(args.steps // 100, 8))
     rt_us = c1["quantize_us"] + c1["dequantize_us"]
     value = 2 * c1["bytes_per_call"] / (rt_us * 1e-6) / 1e9
-    return {
-        "metric": "blockwise quantize/dequantize effective HBM GB/s (configs 1 and 3)",
-        "value": round(value, 1), "unit": "GB/s", "n_gpus": 1, "steps": steps, "warmup": args.warmup,
-        "ms_per_step": round(rt_us * 1e-3, 5), "higher_is_better": True, "scaling": "weak",
-        "vs_baseline": None, "dtype": "bf16/f16/f32", "data": "synthetic (seeded torch Philox)",
-        "config": {"workload": "config 1 NF4 round trip (value) + config 3 8-bit blockwise (details)",
-                   "l2": "config 1: 8 rotated 32 MiB inputs; config 3: inputs of 0.5-1 GB"},
-        "roofline": {"bound": "hbm", "peak": peak, "unit": "GB/s", "peak_source": peak_kind,
-                     "frac_by_case": {k: {"quantize": round(v["quantize_gbs"] / peak, 3),
-                                          "dequantize": round(v["dequantize_gbs"] / peak, 3)}
-                                      for k, v in out.items()}},
-        "cases": out, "clocks": clocks.summary(),
-    }
+    return {"metric": "blockwise quantize/dequantize effective HBM GB/s (configs 1 and 3)",
+            "value": round(value, 1), "unit": "GB/s", "n_gpus": 1, "higher_is_better": True,
+            "dtype": "bf16/f16/f32", "data": "synthetic (seeded torch Philox)",
+            "config": {"workload": "config 1 NF4 round trip (value) + config 3 8-bit blockwise (details)"},
+            "config1": c1, "config3": c3, "clocks": clocks.summary()}
 
 
-def run_gemm_workload(args, local_rank):
-    """Config 5: fused NF4 dequantize-GEMM on the Llama-3-70B MLP shapes."""
-    import torch
-    import bnb_b200 as bnb
+def gemm_cases(torch, bnb, device, ms=(64, 512, 2048)):
+    """Config 5: the fused NF4 dequantize-GEMM on the Llama-3-70B MLP shapes,
+    beside the reference's fallback (dequantize + matmul)."""
     from bnb_b200.kernels.gemv import matmul_nf4
-    device = torch.device("cuda", local_rank)
-    torch.cuda.set_device(device)
     out = {}
     peak_tf = 1669.8
     p = ROOT / "MEASURED_PEAKS.json"
     if p.exists():
         peak_tf = float(json.loads(p.read_text()).get("bf16_tflops", peak_tf))
+    for (n, k) in [(28672, 8192), (8192, 28672)]:
+        g = torch.Generator(device).manual_seed(n)
+        w = bnb.quantize((torch.randn(n, k, device=device, generator=g) * 0.015).to(torch.bfloat16),
+                         "nf4", 64, double_quant=True)
+        a = w.absmax
+        nested = (a.absmax, a.code, a.offset, a.blocksize)
+        for m in ms:
+            x = torch.randn(m, k, device=device, generator=g).to(torch.bfloat16)
+            s5 = 5 if m == 2048 else 10
+            tf = time_graph(torch, lambda i: matmul_nf4(x, w.data, a.data, n, 64, nested=nested),
+                            s5, 2, device) / s5
+            tr = time_graph(torch, lambda i: x @ w.dequantize(torch.bfloat16).T, s5, 2, device) / s5
+            fl = 2.0 * m * n * k
+            out[f"{n}x{k}_m{m}"] = {"fused_us": round(tf * 1e3, 1),
+                                    "fused_tflops": round(fl / (tf * 1e-3) / 1e12, 1),
+                                    "dequant_matmul_us": round(tr * 1e3, 1),
+                                    "speedup_vs_dequant_matmul": round(tr / tf, 2),
+                                    "frac_of_bf16_peak": round(fl / (tf * 1e-3) / 1e12 / peak_tf, 3)}
+        del w, a
+    torch.cuda.synchronize()
+    torch.cuda.empty_cache()
+    out["peak_tflops"] = peak_tf
+    return out
+
+
+def run_gemm_workload(args, local_rank):
+    import torch
+    import bnb_b200 as bnb
+    device = torch.device("cuda", local_rank)
+    torch.cuda.set_device(device)
     with ClockSampler(local_rank) as clocks:
-        for (n, k) in [(28672, 8192), (8192, 28672)]:
-            g = torch.Generator(device).manual_seed(n)
-            w = bnb.quantize((torch.randn(n, k, device=device, generator=g) * 0.015).to(torch.bfloat16),
-                             "nf4", 64, double_quant=True)
-            a = w.absmax
-            nested = (a.absmax, a.code, a.offset, a.blocksize)
-            for m in (64, 512, 2048):
-                x = torch.randn(m, k, device=device, generator=g).to(torch.bfloat16)
-                s5 = 5 if m == 2048 else 10
-                tf = time_graph(torch, lambda i: matmul_nf4(x, w.data, a.data, n, 64, nested=nested),
-                                s5, 2, device) / s5
-                tr = time_graph(torch, lambda i: x @ w.dequantize(torch.bfloat16).T, s5, 2, device) / s5
-                fl = 2.0 * m * n * k
-                out[f"{n}x{k}_m{m}"] = {"fused_us": round(tf * 1e3, 1), "fused_tflops": round(fl / (tf * 1e-3) / 1e12, 1),
-                                        "dequant_matmul_us": round(tr * 1e3, 1),
-                                        "speedup_vs_dequant_matmul": round(tr / tf, 2),
-                                        "frac_of_bf16_peak": round(fl / (tf * 1e-3) / 1e12 / peak_tf, 3)}
-            del w, a
+        out = gemm_cases(torch, bnb, device)
     return {"metric": "fused NF4 dequantize-GEMM TFLOP/s (config 5)", "value": out["28672x8192_m2048"]["fused_tflops"],
             "unit": "TFLOP/s", "n_gpus": 1, "higher_is_better": True, "dtype": "bf16",
             "data": "synthetic (seeded torch Philox)",
             "config": {"workload": "config 5: Llama-3-70B MLP gate/up 28672x8192 and down 8192x28672, NF4 bs64 nested"},
-            "roofline": {"bound": "tensor", "peak": peak_tf, "unit": "TFLOP/s"},
-            "cases": out, "clocks": clocks.summary()}
+            "config5": out, "clocks": clocks.summary()}
 
 
 LLAMA8B = [(4096, 4096), (1024, 4096), (1024, 4096), (4096, 4096), (14336, 4096), (14336, 4096), (4096, 14336)]
 
 
-def run_llama_workload(args, dist, rank, world, local_rank):
-    """Config 4: row-sharded GEMV + all-gather over a Llama-3-8B layer stack."""
+def llama_pass(args, dist, rank, world, local_rank, m: int = 1, gather: str = "peer"):
+    """Config 4: device time of one pass over a Llama-3-8B decode stack (32
+    layers x 7 NF4 matrices), every GEMV row-sharded over the ranks and its y
+    all-gathered. Max over ranks; every rank returns the same dict."""
     import torch
     from bnb_b200.parallel import PeerGather, all_gather_rows, matmul_rows, quantize_shard, row_partition, shard_rows
     device = torch.device("cuda", local_rank)
-    torch.cuda.set_device(device)
     layers = 32
     shards, plans = [], []
     weight_bytes = 0
@@ -480,9 +619,9 @@ def run_llama_workload(args, dist, rank, world, local_rank):
         del w_rows
     torch.cuda.synchronize()
     g = torch.Generator(device).manual_seed(5)
-    xs = {k: torch.randn(args.m, k, device=device, generator=g).to(torch.bfloat16) for k in (4096, 14336)}
-    peer = args.gather == "peer" and world > 1
-    pgs = {n: PeerGather(args.m, n, torch.bfloat16, device) for n in sorted({n for n, _ in LLAMA8B})} if peer else {}
+    xs = {k: torch.randn(m, k, device=device, generator=g).to(torch.bfloat16) for k in (4096, 14336)}
+    peer = gather == "peer" and world > 1
+    pgs = {n: PeerGather(m, n, torch.bfloat16, device) for n in sorted({n for n, _ in LLAMA8B})} if peer else {}
 
     def step():
         for sh, ranges in zip(shards, plans):
@@ -493,7 +632,7 @@ def run_llama_workload(args, dist, rank, world, local_rank):
                 else:
                     all_gather_rows(y, ranges)
 
-    for _ in range(max(args.warmup, 3)):
+    for _ in range(3):
         step()
     torch.cuda.synchronize()
     stream = torch.cuda.Stream(device=device)
@@ -501,49 +640,64 @@ def run_llama_workload(args, dist, rank, world, local_rank):
     with torch.cuda.stream(stream):
         with torch.cuda.graph(graph, stream=stream):
             step()
-    graph.replay()
+    with torch.cuda.stream(stream):
+        graph.replay()
     torch.cuda.synchronize()
-    steps = max(args.steps // 200, 5)
-    with ClockSampler(local_rank) as clocks:
-        if dist is not None:
-            dist.barrier()
-        torch.cuda.synchronize()
-        start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        start.record(stream)
-        with torch.cuda.stream(stream):
-            for _ in range(steps):
-                graph.replay()
-        end.record(stream)
-        torch.cuda.synchronize()
-        if dist is not None:
-            dist.barrier()
+    steps = 5
+    if dist is not None:
+        dist.barrier()
+    torch.cuda.synchronize()
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    spin_ahead(torch, stream)
+    start.record(stream)
+    with torch.cuda.stream(stream):
+        for _ in range(steps):
+            graph.replay()
+    end.record(stream)
+    torch.cuda.synchronize()
+    if dist is not None:
+        dist.barrier()
     ms = start.elapsed_time(end)
     del graph
     torch.cuda.synchronize()
     ms_t = torch.tensor([ms], device=device, dtype=torch.float64)
     if dist is not None:
         dist.all_reduce(ms_t, op=dist.ReduceOp.MAX)
-    ms = float(ms_t.item())
+    for pg in pgs.values():
+        pg.close()
+    if dist is not None:
+        dist.barrier()
+    per = float(ms_t.item()) / steps
+    del shards, xs
+    torch.cuda.empty_cache()
+    return {"workload": "Llama-3-8B decode stack, 32 layers x 7 NF4 matrices (bs64 nested), M=%d" % m,
+            "ms_per_pass": round(per, 4), "weight_gbs": round(weight_bytes / (per * 1e-3) / 1e9, 1),
+            "weight_bytes_per_pass": weight_bytes, "n_gpus": world,
+            "exchange": "NVLink peer stores" if peer else ("NCCL" if world > 1 else "none"),
+            "parallelism": f"tp{world} (rows), y all-gathered after every GEMV" if world > 1 else "1 GPU"}
+
+
+def run_llama_workload(args, dist, rank, world, local_rank):
+    import torch
+    torch.cuda.set_device(local_rank)
+    with ClockSampler(local_rank) as clocks:
+        c4 = llama_pass(args, dist, rank, world, local_rank, args.m, args.gather)
     if rank != 0:
         return None
-    per = ms / steps
     return {"metric": "Llama-3-8B NF4 decode stack: effective weight GB/s, every GEMV row-sharded + all-gathered (config 4)",
-            "value": round(weight_bytes / (per * 1e-3) / 1e9, 1), "unit": "GB/s", "n_gpus": world, "steps": steps,
-            "warmup": args.warmup, "ms_per_step": round(per, 4), "higher_is_better": True, "scaling": "strong",
-            "vs_baseline": None, "dtype": "bf16", "data": "synthetic (seeded torch Philox)",
-            "config": {"workload": "config 4: 32 layers x 7 NF4 matrices, M=%d, row-sharded over %d GPUs, all-gather of y (%s)"
-                       % (args.m, world, "NVLink peer stores" if peer else ("NCCL" if world > 1 else "none")),
-                       "weight_bytes_per_step": weight_bytes, "timing": "CUDA graph of one pass, replayed per step",
-                       "parallelism": f"tp{world} (rows)"},
-            "clocks": clocks.summary()}
+            "value": c4["weight_gbs"], "unit": "GB/s", "n_gpus": world, "ms_per_step": c4["ms_per_pass"],
+            "higher_is_better": True, "scaling": "strong", "dtype": "bf16", "data": "synthetic (seeded torch Philox)",
+            "config": c4, "clocks": clocks.summary()}
 
 
 def run_reference(args, rank):
-    """The reference's arithmetic on the host cores (see module docstring)."""
+    """The reference's arithmetic on the host cores (see module docstring), on
+    every core of the host (torchrun's OMP_NUM_THREADS=1 is overridden)."""
     if rank != 0:
         return None
     import numpy as np
     from oracle import oracle as O
+    O.set_threads(os.cpu_count() or 1)
     rng = np.random.default_rng(0)
     w = (rng.standard_normal(N_ROWS * K_COLS) * 0.02).astype(np.float32)
     q, am = O.quantize_nf4(w, O.F32, BS)
@@ -564,16 +718,17 @@ def run_reference(args, rank):
         step()
     el = time.perf_counter() - t0
     value = algo_bytes(args.m) * args.steps / el / 1e9
+    world = int(os.environ.get("WORLD_SIZE", "1"))
     return {
         "impl": "reference",
-        "metric": METRIC, "value": round(value, 3), "unit": "GB/s", "n_gpus": 1,
+        "metric": METRIC, "value": round(value, 3), "unit": "GB/s", "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(el / args.steps * 1e3, 4),
-        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
-        "data": "synthetic (numpy default_rng(0): W ~ N(0, 0.02^2), x ~ N(0, 1))",
-        "config": {"workload": WORKLOAD, "m": args.m, "n": N_ROWS, "k": K_COLS, "blocksize": BS,
-                   "blocksize2": BS2, "algorithmic_bytes_per_call": algo_bytes(args.m)},
+        "higher_is_better": True, "scaling": "strong" if world > 1 else "weak", "vs_baseline": None, "dtype": "bf16",
+        "data": "synthetic (numpy default_rng(0): W ~ N(0, 0.02^2), x ~ N(0, 1), the GPU arm's distributions)",
+        "config": bench_config(args.m, world),
         "cpu_baseline": {"value": round(value, 3), "unit": "GB/s", "cores": cores, "kind": "port",
-                         "sample": f"{args.steps} full GEMV calls at M={args.m} on the host"},
+                         "sample": f"{args.steps} full GEMV calls at M={args.m} on the host "
+                                   f"(numpy default_rng(0) data of the same distributions)"},
         "e2e": {"value": round(value, 3), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
 
@@ -587,6 +742,7 @@ def main():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-sweep", dest="sweep", action="store_false")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-extras", action="store_true", help="skip the config 1/3/4/5 keys")
     ap.add_argument("--workload", choices=["gemv", "quant", "gemm", "llama"], default="gemv")
     ap.add_argument("--gather", choices=["peer", "nccl"], default="peer", help="config 4 all-gather")
     args = ap.parse_args()

@@ -37,12 +37,15 @@ _SIGNATURES = {
     "bnbq_wait_timeouts": "P",
     "bnbq_peer_allgather_rows": "iPillllPPPiiP",
     "bnbq_peer_allgather_rows_noalloc": "iPillllPPiiiP",
+    "bnbq_peer_allgather_noalloc_setup": "",
+    "bnbq_peer_allgather_noalloc_reset": "iP",
+    "bnbq_set_wait_limit_ns": "u",
     "bnbq_enable_peer_access": "i",
     "bnbq_ipc_handle": "PPP",
     "bnbq_ipc_open": "PP",
     "bnbq_ipc_close": "P",
 }
-_KIND = {"i": C.c_int32, "l": C.c_int64, "P": C.c_void_p, "p": C.c_void_p}
+_KIND = {"i": C.c_int32, "l": C.c_int64, "u": C.c_uint64, "P": C.c_void_p, "p": C.c_void_p}
 
 _lock = threading.Lock()
 _lib: C.CDLL | None = None
@@ -123,6 +126,12 @@ def wait_timeouts() -> int:
     n = C.c_uint32(0)
     check(lib().bnbq_wait_timeouts(C.byref(n)), "bnbq_wait_timeouts")
     return int(n.value)
+
+
+def set_wait_limit_ns(ns: int) -> None:
+    """Time limit of the current device's bounded device-side waits (a test
+    hook: shorten it to make a wait expire on purpose); 0 restores the defaults."""
+    check(lib().bnbq_set_wait_limit_ns(int(ns)), "bnbq_set_wait_limit_ns")
 
 
 def call(name: str, *args) -> None:

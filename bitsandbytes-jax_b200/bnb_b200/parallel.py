@@ -192,9 +192,10 @@ class PeerGather:
     (``bnbq_peer_allgather_rows``) that stores this rank's slice into every
     rank's buffer and waits, bounded, for the peers' slices -- no NCCL call on
     the data path. Construct it on every rank of ``group`` (a collective).
-    The returned tensor is a view of this rank's buffer: the peers overwrite it
-    during their next :meth:`gather`, so consume it on the stream before the
-    next call."""
+    The returned tensor is a view of this rank's buffer. It stays valid until
+    this rank's next :meth:`gather` runs on the stream: a peer stores into it
+    only after this rank's next gather kernel has started, so work enqueued
+    in between may read it."""
 
     def __init__(self, max_rows: int, n_total: int, dtype: torch.dtype, device: torch.device, group=None):
         import ctypes as C
@@ -206,7 +207,7 @@ class PeerGather:
         self.dtype = dtype
         self.device = torch.device(device)
         self.y_full = torch.zeros((max_rows, n_total), dtype=dtype, device=device)
-        self.flags = torch.zeros(self.world, dtype=torch.int32, device=device)
+        self.flags = torch.zeros(2 * self.world, dtype=torch.int32, device=device)  # done | ready epochs
         self.state = torch.zeros(2, dtype=torch.int32, device=device)
         torch.cuda.synchronize(device)
 

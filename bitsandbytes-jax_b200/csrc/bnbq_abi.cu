@@ -16,6 +16,9 @@ int gemv_launch(int dtype, const void* x, int32_t m, int32_t k, const uint8_t* w
 int gemv_wait_timeouts(unsigned int* out);
 int gemm_wait_timeouts(unsigned int* out);
 int peer_wait_timeouts(unsigned int* out);
+int gemv_set_wait_limit(uint64_t ns);
+int gemm_set_wait_limit(uint64_t ns);
+int peer_set_wait_limit(uint64_t ns);
 int gemm_launch(int dtype, const void* x, int32_t m, int32_t k, const uint8_t* w, int64_t n_rows,
                 int32_t blocksize, const float* absmax, const uint8_t* absmax_q,
                 const float* absmax2, const float* code2, const float* offset, int32_t blocksize2,
@@ -111,6 +114,14 @@ extern "C" int bnbq_enable_peer_access(int peer_device) {
     return BNBQ_OK;
   }
   return e == cudaSuccess ? BNBQ_OK : BNBQ_ERR_CUDA;
+}
+
+extern "C" int bnbq_set_wait_limit_ns(uint64_t ns) {
+  DeviceInfo di;
+  if (int st = device_info(&di)) return st;
+  if (gemv_set_wait_limit(ns) != 0 || gemm_set_wait_limit(ns) != 0 || peer_set_wait_limit(ns) != 0)
+    return BNBQ_ERR_CUDA;
+  return BNBQ_OK;
 }
 
 extern "C" const char* bnbq_error_string(int status) {

@@ -20,8 +20,22 @@ static inline int read_wait_timeouts(unsigned int* out) {
   return cudaMemcpyFromSymbol(out, g_bnbq_wait_timeouts, sizeof(unsigned int)) == cudaSuccess ? 0 : -1;
 }
 
-// A wait gives up after this long (the kernels that wait run for microseconds).
-constexpr uint64_t kWaitLimitNs = 1000000000ull;  // 1 s
+// A wait gives up after this long (the kernels that wait run for microseconds;
+// a translation unit whose waits are on other GPUs defines a longer default
+// before including this header).
+#ifndef BNBQ_WAIT_LIMIT_DEFAULT_NS
+#define BNBQ_WAIT_LIMIT_DEFAULT_NS 1000000000ull  // 1 s
+#endif
+constexpr uint64_t kWaitLimitNs = BNBQ_WAIT_LIMIT_DEFAULT_NS;
+
+// The limit the kernels of this translation unit read (per device). Tests
+// shorten it to make a wait expire on purpose; 0 restores the default.
+static __device__ uint64_t g_bnbq_wait_limit_ns = kWaitLimitNs;
+
+static inline int write_wait_limit(uint64_t ns) {
+  const uint64_t v = ns ? ns : kWaitLimitNs;
+  return cudaMemcpyToSymbol(g_bnbq_wait_limit_ns, &v, sizeof(v)) == cudaSuccess ? 0 : -1;
+}
 
 __device__ __forceinline__ uint64_t global_ns() {
   uint64_t t;
@@ -69,9 +83,10 @@ __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
 __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity) {
   if (mbar_try_wait(bar, parity)) return true;
   const uint64_t t0 = global_ns();
+  const uint64_t limit = g_bnbq_wait_limit_ns;
   while (true) {
     if (mbar_try_wait(bar, parity)) return true;
-    if (global_ns() - t0 > kWaitLimitNs) break;
+    if (global_ns() - t0 > limit) break;
   }
   atomicAdd(&g_bnbq_wait_timeouts, 1u);
   return false;

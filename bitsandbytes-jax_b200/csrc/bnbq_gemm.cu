@@ -683,6 +683,7 @@ int launch_bn(const GemmArgs& a, const void* x, const uint8_t* w, const DeviceIn
 }  // namespace
 
 int gemm_wait_timeouts(unsigned int* out) { return read_wait_timeouts(out); }
+int gemm_set_wait_limit(uint64_t ns) { return write_wait_limit(ns); }
 
 // The GEMV's numerics on the tensor cores, for 1 <= m <= 32: every weight as
 // the exact dequantized float32 value split into hi + lo terms of x's dtype,

@@ -1119,6 +1119,7 @@ int launch_dispatch(int m, const GemvArgs& a, cudaStream_t s) {
 }  // namespace
 
 int gemv_wait_timeouts(unsigned int* out) { return read_wait_timeouts(out); }
+int gemv_set_wait_limit(uint64_t ns) { return write_wait_limit(ns); }
 
 int gemm_precise_launch(int dtype, const void* x, int32_t m, int32_t k, const uint8_t* w, int64_t n_rows,
                         int32_t blocksize, const float* absmax, const uint8_t* absmax_q, const float* absmax2,

@@ -159,14 +159,16 @@ BNBQ_API int bnbq_matmul_nf4(int dtype, const void* x, int32_t m, int32_t k,
  * destined for columns [col0, col0 + n_local) of every rank's full output.
  * y_full: device array of `world` pointers, rank d's m x ldy buffer (IPC-mapped
  * peer memory; 16-byte aligned allocations). flags: device array of `world`
- * pointers to each rank's uint32[world] flag array (zero-initialised once).
+ * pointers to each rank's uint32[2 * world] flag array (zero-initialised once).
  * state: this rank's uint32[2] (zero-initialised once; the kernel keeps it).
- * Enqueued on `stream` after the matmul that wrote y_local (it waits for it);
- * on return of the kernel every rank's slice is in this rank's y_full. Every
- * rank must make the same sequence of calls. The wait for peers is bounded
- * (10 s); an expiry is counted by bnbq_wait_timeouts. A rank's y_full is
- * written by its peers during their next call: consume it on the stream before
- * calling again. */
+ * 1 <= world <= 32. Enqueued on `stream` after the matmul that wrote y_local
+ * (it waits for it); on return of the kernel every rank's slice is in this
+ * rank's y_full. Every rank must make the same sequence of calls. A rank's
+ * y_full stays unchanged until its next call on `stream` starts: no peer
+ * stores into it before this rank's kernel of that next call has begun
+ * (a "ready" handshake), so anything enqueued in between may read it. The
+ * waits for peers are bounded (10 s by default); an expiry is counted by
+ * bnbq_wait_timeouts and leaves the output incomplete. */
 /* CUDA IPC of the buffers the peer all-gather writes (no counterpart in the
  * reference). bnbq_ipc_handle exports the allocation containing `ptr`: 64
  * bytes into handle_out and ptr's offset from the allocation base.
@@ -198,15 +200,28 @@ BNBQ_API int bnbq_peer_allgather_rows(int dtype, const void* y_local, int32_t m,
  * per device (held by every device that loads the library until the process
  * exits) with one state pair per exchange slot. Every rank of a group names
  * the same `exchange` slot on every call; limit 32 slots (0..31), a larger
- * slot returns BNBQ_ERR_TOO_LARGE. The other arguments and the result are
- * bnbq_peer_allgather_rows's. The first call on a device sets the array up
- * (its address, cleared once); make that first call before any stream
- * capture. Calls whose kernels overlap on one device with the same slot race.
- * No counterpart in the reference. */
+ * slot returns BNBQ_ERR_TOO_LARGE. A slot belongs to one group and one set of
+ * zeroed flag arrays: before another group (or new flag arrays) uses it,
+ * every rank calls bnbq_peer_allgather_noalloc_reset. The other arguments and
+ * the result are bnbq_peer_allgather_rows's. The first call on a device looks
+ * up the array's device address (bnbq_peer_allgather_noalloc_setup does only
+ * that: make it before capturing exchanges into a graph). The address is
+ * cached per device for the life of the process, so it does not survive a
+ * cudaDeviceReset. Calls whose kernels overlap on one device with the same
+ * slot race. No counterpart in the reference. */
 BNBQ_API int bnbq_peer_allgather_rows_noalloc(int dtype, const void* y_local, int32_t m, int64_t n_local,
                                               int64_t ld_local, int64_t col0, int64_t ldy, void* const* y_full,
                                               uint32_t* const* flags, int32_t exchange, int32_t world,
                                               int32_t rank, void* stream);
+
+/* The no-allocation exchange's set-up for the current device (the device
+ * address of the library's state array), with no exchange; BNBQ_OK when done.
+ * No counterpart in the reference. */
+BNBQ_API int bnbq_peer_allgather_noalloc_setup(void);
+
+/* Zero slot `exchange` of the current device's no-allocation state, enqueued
+ * on `stream`. No counterpart in the reference. */
+BNBQ_API int bnbq_peer_allgather_noalloc_reset(int32_t exchange, void* stream);
 
 /* out[i] = rcp.approx.ftz.f32(in[i]): the hardware reciprocal the quantize kernels
  * use for 1/absmax (kernels/_ptx.py:20-22). Lets a CPU checker take the device's
@@ -218,6 +233,14 @@ BNBQ_API int bnbq_rcp_approx_ftz(const float* in, float* out, int64_t n, void* s
  * each wait gives up after a fixed spin count instead of hanging, and the
  * kernel then stops early). 0 in normal operation. Synchronous. */
 BNBQ_API int bnbq_wait_timeouts(unsigned int* count);
+
+/* Test hook: the time limit of every bounded device-side wait on the current
+ * device (the pipelined kernels' waits on their own copies, 1 s by default;
+ * the peer all-gather's waits for other ranks, 10 s by default), in
+ * nanoseconds; 0 restores the defaults. A test shortens it to make a wait run
+ * out on purpose and checks that the kernel returns and counts the expiry.
+ * Synchronous. No counterpart in the reference. */
+BNBQ_API int bnbq_set_wait_limit_ns(uint64_t ns);
 
 /* Human-readable name of a status code (static storage). */
 BNBQ_API const char* bnbq_error_string(int status);

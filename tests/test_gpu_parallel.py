@@ -58,6 +58,20 @@ def _worker(rank, world, port, queue):
                 torch.cuda.synchronize()
                 assert torch.equal(out, want), "graph replay"
             del graph
+            # back-to-back gathers with different inputs on one PeerGather, each
+            # result read by a consumer kernel enqueued before the next gather;
+            # rank 1 delays its consumers so rank 0 runs ahead into the next call
+            # (whose stores must wait for rank 1's next gather to start)
+            xs = [torch.randn(4, k, device=dev, generator=g).to(torch.bfloat16) for _ in range(6)]
+            consumed = []
+            for xi in xs:
+                y = pg.gather(matmul_rows(xi, shard), ranges[rank][0])
+                if rank == 1:
+                    torch.cuda._sleep(2_000_000)
+                consumed.append(y.float() * 1.0)
+            torch.cuda.synchronize()
+            for i, (xi, got) in enumerate(zip(xs, consumed)):
+                assert torch.equal(got, bnb.matmul(xi, w).float()), ("back-to-back", i)
             from bnb_b200 import _lib
             assert _lib.wait_timeouts() == 0
             # block-sharded quantize == the whole tensor's codes and absmax

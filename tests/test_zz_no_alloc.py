@@ -27,7 +27,7 @@ class Exchange:
 
     def __init__(self, m, ldy, dtype, dev):
         self.y_full = torch.full((m, ldy), 7.0, dtype=dtype, device=dev)
-        self.flags = torch.zeros(1, dtype=torch.int32, device=dev)
+        self.flags = torch.zeros(2, dtype=torch.int32, device=dev)  # done | ready epochs of a group of one
         self.state = torch.zeros(2, dtype=torch.int32, device=dev)
         self.y_ptrs = torch.tensor([self.y_full.data_ptr()], dtype=torch.int64, device=dev)
         self.f_ptrs = torch.tensor([self.flags.data_ptr()], dtype=torch.int64, device=dev)
@@ -53,6 +53,31 @@ def test_noalloc_matches_existing_entry_point(cuda, m, n_local, col0, ldy, dtype
         assert torch.equal(new.y_full, ref.y_full), f"call {call}"
         assert torch.equal(new.y_full[:, col0:col0 + n_local], y_local), f"call {call}"
     assert bool((new.y_full[:, :col0] == 7.0).all()) and bool((new.y_full[:, col0 + n_local:] == 7.0).all())
+    assert _lib.wait_timeouts() == 0
+
+
+def test_noalloc_setup_and_slot_reset(cuda):
+    """The set-up call alone succeeds; a reset slot starts its epochs from
+    zero again, so a group with new zeroed flags can take it over. With a
+    group of one the epoch is visible in the caller's flags (done and ready
+    entries hold the call's epoch)."""
+    _lib.call("bnbq_peer_allgather_noalloc_setup")
+    y = torch.randn(2, 64, device=cuda).to(torch.bfloat16)
+    stream = _lib.stream_of(y)
+    _lib.call("bnbq_peer_allgather_noalloc_reset", 11, stream)
+    first = Exchange(2, 64, torch.bfloat16, cuda)
+    for _ in range(3):
+        _lib.call("bnbq_peer_allgather_rows_noalloc", *first.args(y, 0), 11, 1, 0, stream)
+    torch.cuda.synchronize()
+    assert first.flags.tolist() == [3, 3]
+    second = Exchange(2, 64, torch.bfloat16, cuda)  # new flags: the slot must start over
+    _lib.call("bnbq_peer_allgather_noalloc_reset", 11, stream)
+    _lib.call("bnbq_peer_allgather_rows_noalloc", *second.args(y, 0), 11, 1, 0, stream)
+    torch.cuda.synchronize()
+    assert second.flags.tolist() == [1, 1]
+    assert torch.equal(second.y_full, y)
+    with pytest.raises(ValueError, match="fixed scratch"):
+        _lib.call("bnbq_peer_allgather_noalloc_reset", 32, stream)
     assert _lib.wait_timeouts() == 0
 
 
@@ -92,10 +117,24 @@ def _worker(rank, world, port, queue):
                           new.f_ptrs.data_ptr(), 7, world, rank, _lib.stream_of(y_local))
                 torch.cuda.synchronize()
                 assert torch.equal(new.y_full[:m], want), f"call {call}"
+            # a second group (new zeroed flags) takes the slot over after a reset
+            other = PeerGather(8, world * n_local, dtype, dev)
+            _lib.call("bnbq_peer_allgather_noalloc_reset", 7, _lib.stream_of(other.y_full))
+            torch.cuda.synchronize()
+            dist.barrier()
+            for call in range(2):
+                y_local = torch.randn(4, n_local, device=dev, generator=g).to(dtype)
+                want = ref.gather(y_local, rank * n_local).clone()
+                _lib.call("bnbq_peer_allgather_rows_noalloc", _lib.DTYPE_CODE[dtype], y_local.data_ptr(), 4,
+                          n_local, y_local.stride(0), rank * n_local, world * n_local, other.y_ptrs.data_ptr(),
+                          other.f_ptrs.data_ptr(), 7, world, rank, _lib.stream_of(y_local))
+                torch.cuda.synchronize()
+                assert torch.equal(other.y_full[:4], want), f"second group, call {call}"
             assert _lib.wait_timeouts() == 0
             dist.barrier()
             ref.close()
             new.close()
+            other.close()
         finally:
             dist.destroy_process_group()
         queue.put((rank, None))
