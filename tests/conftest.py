@@ -37,3 +37,14 @@ def cuda():
     if (major, minor) != (10, 0):
         pytest.skip(f"needs sm_100 (B200), found sm_{major}{minor}")
     return torch.device("cuda:0")
+
+
+@pytest.fixture(scope="module")
+def timeouts_at_start(cuda):
+    """The device's count of expired bounded waits when the module starts
+    (the count is process-wide; a test that makes waits expire on purpose
+    raises it for every later module)."""
+    import torch
+    from bnb_b200 import _lib
+    torch.cuda.synchronize()
+    return _lib.wait_timeouts()

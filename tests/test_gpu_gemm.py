@@ -15,7 +15,7 @@ import torch
 import bnb_b200
 from bnb_b200.kernels.gemv import GEMV_MAX_M, matmul_nf4
 
-pytestmark = pytest.mark.gpu
+pytestmark = [pytest.mark.gpu, pytest.mark.usefixtures("timeouts_at_start")]
 
 # |y - y64| <= REL[dtype] * |y64| + ACC * (|x| @ |w|): one rounding of the output
 # plus float32 accumulation over K terms.
@@ -175,8 +175,8 @@ def test_gemm_grad_matches_fallback(cuda):
     assert torch.equal(g, x.grad)
 
 
-def test_gemm_no_wait_timeouts(cuda):
+def test_gemm_no_wait_timeouts(cuda, timeouts_at_start):
     """The GEMM's bounded waits never expired during these tests."""
     from bnb_b200 import _lib
     torch.cuda.synchronize()
-    assert _lib.wait_timeouts() == 0
+    assert _lib.wait_timeouts() == timeouts_at_start

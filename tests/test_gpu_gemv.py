@@ -14,7 +14,7 @@ from bnb_b200.kernels.gemv import GEMV_MAX_M
 from helpers import GEMV_ATOL, GEMV_RTOL, TORCH_DTYPES, bits, to_host
 from oracle import oracle as O
 
-pytestmark = pytest.mark.gpu
+pytestmark = [pytest.mark.gpu, pytest.mark.usefixtures("timeouts_at_start")]
 
 
 def weight(n, k, blocksize=64, double_quant=True, qtype="nf4", seed=0):
@@ -190,8 +190,8 @@ def test_gemv_writes_into_wider_output(cuda):
     assert torch.all(big[:, :256] == 7.0) and torch.all(big[:, 512:] == 7.0)
 
 
-def test_no_wait_timeouts(cuda):
+def test_no_wait_timeouts(cuda, timeouts_at_start):
     """The pipelined kernels' bounded waits never expired during these tests."""
     from bnb_b200 import _lib
     torch.cuda.synchronize()
-    assert _lib.wait_timeouts() == 0
+    assert _lib.wait_timeouts() == timeouts_at_start

@@ -17,7 +17,7 @@ import torch
 from bnb_b200 import _lib
 from dist_helpers import _free_port
 
-pytestmark = pytest.mark.gpu
+pytestmark = [pytest.mark.gpu, pytest.mark.usefixtures("timeouts_at_start")]
 
 
 class Exchange:
@@ -39,7 +39,7 @@ class Exchange:
 
 @pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
 @pytest.mark.parametrize("m,n_local,col0,ldy", [(1, 4096, 4096, 16384), (8, 1000, 3, 2011), (20, 14336, 0, 14336)])
-def test_noalloc_matches_existing_entry_point(cuda, m, n_local, col0, ldy, dtype):
+def test_noalloc_matches_existing_entry_point(cuda, m, n_local, col0, ldy, dtype, timeouts_at_start):
     """Two calls in a row on one device (world 1): bitwise the existing entry
     point's output, and the columns outside the slice stay untouched."""
     g = torch.Generator("cuda").manual_seed(m + n_local)
@@ -53,10 +53,10 @@ def test_noalloc_matches_existing_entry_point(cuda, m, n_local, col0, ldy, dtype
         assert torch.equal(new.y_full, ref.y_full), f"call {call}"
         assert torch.equal(new.y_full[:, col0:col0 + n_local], y_local), f"call {call}"
     assert bool((new.y_full[:, :col0] == 7.0).all()) and bool((new.y_full[:, col0 + n_local:] == 7.0).all())
-    assert _lib.wait_timeouts() == 0
+    assert _lib.wait_timeouts() == timeouts_at_start
 
 
-def test_noalloc_setup_and_slot_reset(cuda):
+def test_noalloc_setup_and_slot_reset(cuda, timeouts_at_start):
     """The set-up call alone succeeds; a reset slot starts its epochs from
     zero again, so a group with new zeroed flags can take it over. With a
     group of one the epoch is visible in the caller's flags (done and ready
@@ -78,7 +78,7 @@ def test_noalloc_setup_and_slot_reset(cuda):
     assert torch.equal(second.y_full, y)
     with pytest.raises(ValueError, match="fixed scratch"):
         _lib.call("bnbq_peer_allgather_noalloc_reset", 32, stream)
-    assert _lib.wait_timeouts() == 0
+    assert _lib.wait_timeouts() == timeouts_at_start
 
 
 def test_noalloc_rejects_slots_beyond_its_array(cuda):
