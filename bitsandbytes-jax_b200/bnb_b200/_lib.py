@@ -32,6 +32,9 @@ _SIGNATURES = {
     "bnbq_dequantize_blockwise_nested": "iPPPPPPliiPP",
     "bnbq_gemv_nf4": "iPiiPliPPPPPilPlP",
     "bnbq_matmul_nf4": "iPiiPliPPPPPilPlP",
+    "bnbq_gemv_nf4_ws": "iPiiPliPPPPPilPlPlP",
+    "bnbq_matmul_nf4_ws": "iPiiPliPPPPPilPlPlP",
+    "bnbq_gemv_workspace_bytes": "iilP",
     "bnbq_rcp_approx_ftz": "PPlP",
     "bnbq_version": "",
     "bnbq_wait_timeouts": "P",
@@ -132,6 +135,29 @@ def set_wait_limit_ns(ns: int) -> None:
     """Time limit of the current device's bounded device-side waits (a test
     hook: shorten it to make a wait expire on purpose); 0 restores the defaults."""
     check(lib().bnbq_set_wait_limit_ns(int(ns)), "bnbq_set_wait_limit_ns")
+
+
+_WORKSPACES: dict[tuple[int, int], torch.Tensor] = {}
+
+
+def workspace(device: torch.device, stream: int, nbytes: int) -> torch.Tensor:
+    """A zero-filled device buffer of at least `nbytes` for the kernels that
+    split K across SMs, one per (device, stream): calls on one stream are
+    ordered, and each call leaves the buffer zero-filled again. Allocated on
+    first use (inside a CUDA graph capture the zero-fill becomes part of the
+    graph) and kept for the life of the process."""
+    key = (device.index, stream)
+    ws = _WORKSPACES.get(key)
+    if ws is None or ws.numel() < nbytes:
+        ws = torch.zeros(max(nbytes, 1 << 20), dtype=torch.uint8, device=device)
+        _WORKSPACES[key] = ws
+    return ws
+
+
+def gemv_workspace_bytes(m: int, k: int, n_rows: int) -> int:
+    n = C.c_int64(0)
+    check(lib().bnbq_gemv_workspace_bytes(m, k, n_rows, C.byref(n)), "bnbq_gemv_workspace_bytes")
+    return int(n.value)
 
 
 def call(name: str, *args) -> None:

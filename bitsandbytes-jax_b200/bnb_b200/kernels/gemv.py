@@ -72,9 +72,12 @@ def _run(entry, x, data, absmax, n_rows, blocksize, nested, absmax2_block0, out)
         out = torch.empty((m, n_rows), dtype=x.dtype, device=x.device)
     ldy = out.stride(0)
     assert out.dtype == x.dtype and out.stride(1) == 1 and out.shape == (m, n_rows)
-    args = (entry, _lib.DTYPE_CODE[x.dtype], xs.data_ptr(), m, k, w.data_ptr(), n_rows, blocksize, _lib.ptr(a),
-            _lib.ptr(aq), _lib.ptr(a2), _lib.ptr(c2), _lib.ptr(off), bs2, absmax2_block0, out.data_ptr(), ldy,
-            _lib.stream_of(xs))
+    stream = _lib.stream_of(xs)
+    wsb = _lib.gemv_workspace_bytes(m, k, n_rows) if m <= GEMV_MAX_M else 0
+    ws = _lib.workspace(x.device, stream, wsb) if wsb else None
+    args = (entry + "_ws", _lib.DTYPE_CODE[x.dtype], xs.data_ptr(), m, k, w.data_ptr(), n_rows, blocksize,
+            _lib.ptr(a), _lib.ptr(aq), _lib.ptr(a2), _lib.ptr(c2), _lib.ptr(off), bs2, absmax2_block0,
+            out.data_ptr(), ldy, _lib.ptr(ws), 0 if ws is None else ws.numel(), stream)
     if x.device.index == torch.cuda.current_device():
         _lib.call(*args)
     else:

@@ -78,6 +78,24 @@ extern "C" int bnbq_matmul_nf4(int dtype, const void* x, int32_t m, int32_t k, c
                      offset, blocksize2, absmax2_block0, y, ldy, s);
 }
 
+extern "C" int bnbq_gemv_nf4_ws(int dtype, const void* x, int32_t m, int32_t k, const uint8_t* w,
+                                int64_t n_rows, int32_t blocksize, const float* absmax,
+                                const uint8_t* absmax_q, const float* absmax2, const float* code2,
+                                const float* offset, int32_t blocksize2, int64_t absmax2_block0,
+                                void* y, int64_t ldy, void* workspace, int64_t workspace_bytes, void* stream);
+
+extern "C" int bnbq_matmul_nf4_ws(int dtype, const void* x, int32_t m, int32_t k, const uint8_t* w,
+                                  int64_t n_rows, int32_t blocksize, const float* absmax,
+                                  const uint8_t* absmax_q, const float* absmax2, const float* code2,
+                                  const float* offset, int32_t blocksize2, int64_t absmax2_block0,
+                                  void* y, int64_t ldy, void* workspace, int64_t workspace_bytes, void* stream) {
+  if (m >= 1 && m <= BNBQ_GEMV_MAX_M)
+    return bnbq_gemv_nf4_ws(dtype, x, m, k, w, n_rows, blocksize, absmax, absmax_q, absmax2, code2, offset,
+                            blocksize2, absmax2_block0, y, ldy, workspace, workspace_bytes, stream);
+  return bnbq_matmul_nf4(dtype, x, m, k, w, n_rows, blocksize, absmax, absmax_q, absmax2, code2, offset,
+                         blocksize2, absmax2_block0, y, ldy, stream);
+}
+
 extern "C" int bnbq_rcp_approx_ftz(const float* in, float* out, int64_t n, void* stream) {
   if (n < 0 || (n > 0 && (!in || !out))) return BNBQ_ERR_INVALID;
   if (!aligned(in, 4) || !aligned(out, 4)) return BNBQ_ERR_MISALIGNED;

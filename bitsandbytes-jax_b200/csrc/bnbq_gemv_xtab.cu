@@ -1,0 +1,606 @@
+// bnbq_gemv_xtab.cu -- fused NF4 GEMV for one or two rows of x (the decode
+// batch sizes), with x held in a shared-memory table of pair sums.
+//
+// y[m, r] = sum_k x[m, k] * W[r, k] for an NF4 weight W (n_rows x K), never
+// decoded to memory.
+//
+// Decode. K is cut into groups of GK elements (GK = 256 for one row of x, 128
+// for two). For the group a CTA works on, a 128 KB table in shared memory holds
+// for every element pair j of the group and every code byte b (high nibble =
+// the even element, as the codes are packed) the float32 partial sum
+//     P[j][b][m] = fma(T[b & 15], x[m][2j + 1], T[b >> 4] * x[m][2j]).
+// One code byte -- two weights -- then costs one table load and one add; the
+// weight itself is never formed. A warp takes 32 weight rows of a group (lane
+// l = row l). At each step lane l reads one 32-bit code word w_l of its row and
+// the four table entries of that word's pairs. The lanes walk the words of
+// their rows diagonally (w_l differs between lanes at every step), and entry
+// (j, b) lives in the bank of j's word: the 32 lanes' table loads always hit
+// 32 distinct banks, whatever the code bytes are.
+//   one row of x:  entry (j, b) at byte ((j & 3) << 15) | (b << 7) | ((j >> 2) << 2)
+//   two rows of x: entry (j, b) (a float2) at ((j & 3) << 15) | (b << 7) | ((j >> 2) << 3)
+// (for two rows the halves of a warp are served separately by the 64-bit
+// loads, and the lanes of a half walk distinct words).
+//
+// Scales. The words of a block are summed first; each block's scale a -- the
+// float32 absmax, or, double-quantized, fl32(mul.ftz(code2[q2], absmax2[..]) +
+// offset) exactly as QuantizedArray.dequantize forms it (array.py:95-108) -- is
+// applied once per block and lane: acc = fma.rn.ftz(a, block sum, acc). With a
+// one-hot x every table value but one is +0 or -0 and the remaining one is
+// T[q] itself, so the result is mul.ftz(T[q], a) rounded once to x's dtype: the
+// dequantized weight, bitwise (as kernels/gemv.py:97-123 gives it).
+//
+// Work. A unit is (group, 32-row block); the units, in group-major order, are
+// split evenly over one CTA per SM, so a CTA's units span one group or two (the
+// table is rebuilt between them, all consumer warps at a barrier). A producer
+// warp streams each unit's 32 x GK/2 code bytes with one TMA load into a ring
+// of shared-memory stages (mbarrier full/empty pairs); the consumer warps take
+// the units round-robin, each lane fetching its row's scale words one unit
+// ahead. Every unit's 32 (x M) float32 results go to the caller's workspace;
+// the last unit of a row block to arrive (one counter per row block) adds that
+// block's partials in a fixed order, rounds once to x's dtype and writes y, and
+// puts the counter back to zero. Results are therefore deterministic.
+//
+// Every mbarrier wait is bounded in time; on an expiry the CTA stops working,
+// still waits (bounded) for every copy it issued, counts the expiry
+// (bnbq_wait_timeouts) and leaves y and the row-block counters it touched
+// unfinished: the caller then clears the workspace before reusing it.
+//
+// Programmatic dependent launch: the producer starts streaming codes before
+// the previous kernel on the stream has finished (the weight is an input that
+// kernel does not write); x, the workspace and y are touched only after
+// griddepcontrol.wait.
+#include <cuda.h>
+#include <cudaTypedefs.h>
+
+#include <atomic>
+#include <mutex>
+
+#include "bnbq_async.cuh"
+#include "bnbq_common.cuh"
+
+namespace bnbq {
+namespace {
+
+constexpr uint32_t kTabBytes = 131072;  // the pair table, for either row count
+constexpr int kRows = 32;               // weight rows per unit (one per lane)
+constexpr int kMaxStages = 40;
+constexpr int kMaxConsumers = 16;       // consumer warps per CTA
+constexpr int kMaxDevices = 64;
+
+template <int M>
+struct Cfg {
+  static constexpr int kGroupK = M == 1 ? 256 : 128;          // elements of K per table
+  static constexpr int kWords = kGroupK / 8;                   // 32-bit code words per row and group
+  static constexpr uint32_t kStageBytes = kRows * kWords * 4;  // 4 KB / 2 KB of codes per unit
+};
+
+struct XtabArgs {
+  const void* x;
+  const float* absmax;      // plain scales (absmax_q == nullptr)
+  const uint8_t* absmax_q;  // double-quantized scales
+  const float* absmax2;
+  const float* code2;
+  const float* offset;
+  void* y;
+  uint32_t* counters;  // [row_blocks], zero between calls
+  float* partial;      // [row_blocks][groups][M][32]
+  int64_t n_rows, ldy, block0, units;
+  int k, log2_bs, log2_bs2, groups, row_blocks, n_stages;
+};
+
+__device__ __forceinline__ uint32_t lds_u32(uint32_t a) {
+  uint32_t v;
+  asm volatile("ld.shared.u32 %0, [%1];" : "=r"(v) : "r"(a));
+  return v;
+}
+__device__ __forceinline__ float lds_f32(uint32_t a) {
+  float v;
+  asm volatile("ld.shared.f32 %0, [%1];" : "=f"(v) : "r"(a));
+  return v;
+}
+__device__ __forceinline__ float2 lds_f32x2(uint32_t a) {
+  float2 v;
+  asm volatile("ld.shared.v2.f32 {%0, %1}, [%2];" : "=f"(v.x), "=f"(v.y) : "r"(a));
+  return v;
+}
+__device__ __forceinline__ void sts_f32(uint32_t a, float v) {
+  asm volatile("st.shared.f32 [%0], %1;" ::"r"(a), "f"(v) : "memory");
+}
+__device__ __forceinline__ void sts_f32x2(uint32_t a, float v0, float v1) {
+  asm volatile("st.shared.v2.f32 [%0], {%1, %2};" ::"r"(a), "f"(v0), "f"(v1) : "memory");
+}
+__device__ __forceinline__ float fma_ftz(float a, float b, float c) {
+  float r;
+  asm("fma.rn.ftz.f32 %0, %1, %2, %3;" : "=f"(r) : "f"(a), "f"(b), "f"(c));
+  return r;
+}
+__device__ __forceinline__ float4 ldcg4(const float* p) {
+  float4 v;
+  asm volatile("ld.global.cg.v4.f32 {%0, %1, %2, %3}, [%4];" : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w) : "l"(p));
+  return v;
+}
+
+__device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap* map, int x, int y, uint32_t bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::"r"(
+          dst),
+      "l"(map), "r"(x), "r"(y), "r"(bar)
+      : "memory");
+}
+
+template <typename XT>
+__device__ __forceinline__ float2 x_pair(const XT* x, int64_t i) {  // elements i, i + 1 (i even)
+  const uint32_t w = *reinterpret_cast<const uint32_t*>(x + i);
+  if constexpr (Elem<XT>::kDtype == BNBQ_BF16) return unpack2_bf16(w);
+  else return unpack2_f16(w);
+}
+
+template <typename XT>
+__device__ __forceinline__ void store_y(void* y, int64_t i, float v) {
+  if constexpr (Elem<XT>::kDtype == BNBQ_BF16) static_cast<__nv_bfloat16*>(y)[i] = __float2bfloat16_rn(v);
+  else static_cast<__half*>(y)[i] = __float2half_rn(v);
+}
+
+// The pair table of group g, written by the consumer warps (cw of ncw).
+// Thread (lane) owns the pairs j with j >> 2 == jq; the iterations (pair j & 3,
+// high nibble) are spread over the warps (and, for two rows, the half-warps).
+template <typename XT, int M>
+__device__ __forceinline__ void build_table(uint32_t tab, const XtabArgs& a, int g, int cw, int ncw, int lane) {
+  constexpr int GK = Cfg<M>::kGroupK;
+  const XT* x = static_cast<const XT*>(a.x);
+  const int jq = M == 1 ? lane : (lane & 15);
+  const int slot = M == 1 ? cw : 2 * cw + (lane >> 4);
+  const int nslots = M == 1 ? ncw : 2 * ncw;
+  for (int it = slot; it < 64; it += nslots) {
+    const int jl = it >> 4, hi = it & 15;
+    const int j = 4 * jq + jl;
+    const int64_t e = int64_t(g) * GK + 2 * j;
+    float u[M], x1[M];
+#pragma unroll
+    for (int m = 0; m < M; ++m) {
+      const float2 xp = x_pair<XT>(x + int64_t(m) * a.k, e);
+      u[m] = __fmul_rn(kNF4Table[hi], xp.x);
+      x1[m] = xp.y;
+    }
+    const uint32_t base = tab + (uint32_t(jl) << 15) + (uint32_t(hi * 16) << 7) + uint32_t(jq) * (4 * M);
+#pragma unroll
+    for (int lo = 0; lo < 16; ++lo) {
+      const float t = kNF4Table[lo];
+      if constexpr (M == 1) sts_f32(base + (lo << 7), __fmaf_rn(t, x1[0], u[0]));
+      else sts_f32x2(base + (lo << 7), __fmaf_rn(t, x1[0], u[0]), __fmaf_rn(t, x1[1], u[1]));
+    }
+  }
+}
+
+// The scale words of one unit for this lane's row: the NB double-quantized
+// codes (one aligned load) and the one or two absmax2 values they use, or NB
+// plain float32 scales.
+template <int NB, bool NESTED>
+struct ScaleWords {
+  uint32_t q[NESTED ? (NB + 3) / 4 : 1];
+  float v[NESTED ? 2 : NB];
+  int64_t gb0;
+  bool valid;
+};
+
+template <int M, int NB, bool NESTED>
+__device__ __forceinline__ void fetch_scales(ScaleWords<NB, NESTED>& s, const XtabArgs& a, int64_t unit, int lane) {
+  const int g = int(unit / a.row_blocks);
+  const int64_t row = (unit - int64_t(g) * a.row_blocks) * kRows + lane;
+  s.valid = row < a.n_rows;
+  if (!s.valid) return;
+  const int64_t bpr = int64_t(a.k) >> a.log2_bs;  // blocks per row
+  s.gb0 = row * bpr + ((int64_t(g) * Cfg<M>::kGroupK) >> a.log2_bs);
+  if constexpr (NESTED) {
+    if constexpr (NB == 8) {
+      const uint2 w = __ldg(reinterpret_cast<const uint2*>(a.absmax_q + s.gb0));
+      s.q[0] = w.x;
+      s.q[1] = w.y;
+    } else if constexpr (NB == 4) {
+      s.q[0] = __ldg(reinterpret_cast<const uint32_t*>(a.absmax_q + s.gb0));
+    } else if constexpr (NB == 2) {
+      s.q[0] = __ldg(reinterpret_cast<const uint16_t*>(a.absmax_q + s.gb0));
+    } else {
+      s.q[0] = __ldg(a.absmax_q + s.gb0);
+    }
+    const int64_t i0 = (a.block0 + s.gb0) >> a.log2_bs2;
+    const int64_t i1 = (a.block0 + s.gb0 + NB - 1) >> a.log2_bs2;
+    s.v[0] = __ldg(a.absmax2 + i0);
+    s.v[1] = i1 != i0 ? __ldg(a.absmax2 + i1) : s.v[0];
+  } else {
+#pragma unroll
+    for (int b = 0; b < NB; ++b) s.v[b] = __ldg(a.absmax + s.gb0 + b);
+  }
+}
+
+// a_rot[p] = the scale of the block this lane visits in phase p, block (p + al) mod NB.
+template <int NB, bool NESTED>
+__device__ __forceinline__ void decode_scales(float (&a_rot)[NB], const ScaleWords<NB, NESTED>& s, const XtabArgs& a,
+                                              const float* s_code2, float offset, int al) {
+#pragma unroll
+  for (int p = 0; p < NB; ++p) {
+    const int blk = (p + al) & (NB - 1);
+    if (!s.valid) {
+      a_rot[p] = 0.0f;
+      continue;
+    }
+    if constexpr (NESTED) {
+      const uint32_t word = NB == 8 ? (blk < 4 ? s.q[0] : s.q[NB == 8 ? 1 : 0]) : s.q[0];
+      const uint32_t q2 = (word >> (8 * (blk & 3))) & 0xffu;
+      const int64_t i0 = (a.block0 + s.gb0) >> a.log2_bs2;
+      const float a2 = ((a.block0 + s.gb0 + blk) >> a.log2_bs2) != i0 ? s.v[1] : s.v[0];
+      a_rot[p] = add_rn(mul_ftz(s_code2[q2], a2), offset);
+    } else {
+      float v = s.v[0];
+#pragma unroll
+      for (int b = 1; b < NB; ++b)
+        if (blk == b) v = s.v[b];
+      a_rot[p] = v;
+    }
+  }
+}
+
+// The unit's dot products for this lane's row: phases over the NB blocks of
+// the group, in a lane-dependent order (block (p + al) mod NB), words of a
+// block along the lane's diagonal.
+template <int M, int NB>
+__device__ __forceinline__ void unit_dot(uint32_t row_codes, uint32_t tab, int lane, const float (&a_rot)[NB],
+                                         float (&acc)[M]) {
+  constexpr int GW = Cfg<M>::kWords;
+  constexpr int WB = GW / NB;
+  const int li = M == 1 ? lane : (lane & 15);
+  const int al = li / WB;
+  const int orot = M == 1 ? lane : li + (lane >> 4);
+#pragma unroll
+  for (int p = 0; p < NB; ++p) {
+    const int wb = ((p + al) & (NB - 1)) * WB;
+    float ps[M];
+#pragma unroll
+    for (int m = 0; m < M; ++m) ps[m] = 0.0f;
+#pragma unroll
+    for (int s = 0; s < WB; ++s) {
+      const int w = wb + ((s + orot) & (WB - 1));
+      const uint32_t cw = lds_u32(row_codes + 4 * w);
+      const uint32_t tw = tab + uint32_t(w) * (4 * M);
+      if constexpr (M == 1) {
+        const float v0 = lds_f32(__byte_perm(cw, 0, 0x4440) * 128u + tw);
+        const float v1 = lds_f32(__byte_perm(cw, 0, 0x4441) * 128u + tw + (1u << 15));
+        const float v2 = lds_f32(__byte_perm(cw, 0, 0x4442) * 128u + tw + (2u << 15));
+        const float v3 = lds_f32(__byte_perm(cw, 0, 0x4443) * 128u + tw + (3u << 15));
+        ps[0] += (v0 + v1) + (v2 + v3);
+      } else {
+        const float2 v0 = lds_f32x2(__byte_perm(cw, 0, 0x4440) * 128u + tw);
+        const float2 v1 = lds_f32x2(__byte_perm(cw, 0, 0x4441) * 128u + tw + (1u << 15));
+        const float2 v2 = lds_f32x2(__byte_perm(cw, 0, 0x4442) * 128u + tw + (2u << 15));
+        const float2 v3 = lds_f32x2(__byte_perm(cw, 0, 0x4443) * 128u + tw + (3u << 15));
+        ps[0] += (v0.x + v1.x) + (v2.x + v3.x);
+        ps[1] += (v0.y + v1.y) + (v2.y + v3.y);
+      }
+    }
+#pragma unroll
+    for (int m = 0; m < M; ++m) acc[m] = fma_ftz(a_rot[p], ps[m], acc[m]);
+  }
+}
+
+// The last unit of row block rb: sum its partials (fixed order), round, store.
+template <typename XT, int M>
+__device__ __forceinline__ void finish_row_block(const XtabArgs& a, int64_t rb, int lane) {
+  const float* part = a.partial + rb * int64_t(a.groups) * M * kRows;
+  const int nf4 = a.groups * M * 8;  // float4 pieces of the row block
+  float4 s = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+  constexpr int kBatch = 16;
+  for (int t0 = lane; t0 < nf4; t0 += 32 * kBatch) {
+    float4 v[kBatch];
+#pragma unroll
+    for (int b = 0; b < kBatch; ++b) {
+      const int f = t0 + 32 * b;
+      v[b] = f < nf4 ? ldcg4(part + 4 * f) : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+    }
+#pragma unroll
+    for (int b = 0; b < kBatch; ++b) {
+      s.x += v[b].x;
+      s.y += v[b].y;
+      s.z += v[b].z;
+      s.w += v[b].w;
+    }
+  }
+  // lanes with the same (x row, 4 weight rows) hold partial sums of different groups
+#pragma unroll
+  for (int d = 8 * M; d < 32; d <<= 1) {
+    s.x += __shfl_xor_sync(0xffffffffu, s.x, d);
+    s.y += __shfl_xor_sync(0xffffffffu, s.y, d);
+    s.z += __shfl_xor_sync(0xffffffffu, s.z, d);
+    s.w += __shfl_xor_sync(0xffffffffu, s.w, d);
+  }
+  if (lane < 8 * M) {
+    const int m = (lane >> 3) % M;
+    const int64_t r0 = rb * kRows + 4 * (lane & 7);
+    const float vals[4] = {s.x, s.y, s.z, s.w};
+#pragma unroll
+    for (int e = 0; e < 4; ++e)
+      if (r0 + e < a.n_rows) store_y<XT>(a.y, int64_t(m) * a.ldy + r0 + e, vals[e]);
+  }
+}
+
+template <typename XT, int M, int NB, bool NESTED>
+__global__ void __launch_bounds__((kMaxConsumers + 1) * 32, 1)
+    gemv_xtab_kernel(const __grid_constant__ CUtensorMap tmap, const XtabArgs a) {
+  constexpr uint32_t kStage = Cfg<M>::kStageBytes;
+  constexpr int GW = Cfg<M>::kWords;
+  extern __shared__ __align__(1024) uint8_t smem[];
+  __shared__ float s_code2[256];
+  __shared__ __align__(8) uint64_t s_bar[2 * kMaxStages];
+  __shared__ volatile int s_abort;
+  __shared__ volatile int s_issued;
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int ncw = int(blockDim.x >> 5) - 1;  // consumer warps; the last warp produces
+  const int S = a.n_stages;
+  const int64_t u0 = int64_t(blockIdx.x) * a.units / gridDim.x;
+  const int64_t u1 = int64_t(blockIdx.x + 1) * a.units / gridDim.x;
+  const int n_units = int(u1 - u0);
+  const uint32_t tab = smem_u32(smem);
+  const uint32_t stages = tab + kTabBytes;
+  const uint32_t full0 = smem_u32(s_bar), empty0 = full0 + 8u * kMaxStages;
+
+  if (threadIdx.x == 0) {
+    s_abort = 0;
+    s_issued = 0;
+    for (int s = 0; s < S; ++s) {
+      mbar_init(full0 + 8u * s, 1);   // the producer's arrival (plus the copy's bytes)
+      mbar_init(empty0 + 8u * s, 1);  // the one consumer warp that took the unit
+    }
+    fence_mbar_init();
+  }
+  __syncthreads();
+  asm volatile("griddepcontrol.launch_dependents;");
+
+  if (warp == ncw) {  // ------------------------------------------------ producer
+    if (lane == 0) {
+      asm volatile("prefetch.tensormap [%0];" ::"l"(&tmap) : "memory");
+      int i = 0;
+      for (; i < n_units; ++i) {
+        const int slot = i % S;
+        if (i >= S && !mbar_wait(empty0 + 8u * slot, uint32_t((i / S - 1) & 1))) break;
+        const int64_t u = u0 + i;
+        const int g = int(u / a.row_blocks);
+        const int rb = int(u - int64_t(g) * a.row_blocks);
+        const uint32_t full = full0 + 8u * slot;
+        mbar_arrive_expect_tx(full, kStage);
+        tma_load_2d(stages + uint32_t(slot) * kStage, &tmap, g * (GW * 4), rb * kRows, full);
+      }
+      s_issued = i;
+      if (i < n_units) {
+        __threadfence_block();
+        s_abort = 1;
+      }
+    }
+    return;
+  }
+
+  // ---------------------------------------------------------------- consumers
+  asm volatile("griddepcontrol.wait;" ::: "memory");  // x, workspace and y: after the previous kernel
+  const int ncons = ncw * 32;
+  float offset = 0.0f;
+  if constexpr (NESTED) {
+    for (int i = threadIdx.x; i < 256; i += ncons) s_code2[i] = a.code2[i];
+    offset = *a.offset;
+  }
+  constexpr int WB = GW / NB;
+  const int al = (M == 1 ? lane : (lane & 15)) / WB;
+
+  ScaleWords<NB, NESTED> sw;
+  int i = warp;
+  if (i < n_units) fetch_scales<M, NB, NESTED>(sw, a, u0 + i, lane);
+  int seg = 0;
+  while (seg < n_units) {
+    const int g = int((u0 + seg) / a.row_blocks);
+    const int seg_end = int(min(int64_t(n_units), int64_t(g + 1) * a.row_blocks - u0));
+    named_bar_sync(1, ncons);  // the previous group's table is no longer read
+    build_table<XT, M>(tab, a, g, warp, ncw, lane);
+    named_bar_sync(1, ncons);  // the table (and code2) are complete
+    for (; i < seg_end; i += ncw) {
+      const int slot = i % S;
+      const uint32_t parity = uint32_t((i / S) & 1);
+      bool ok;
+      if (s_abort) {  // drain: wait (bounded) only for copies that were issued
+        ok = false;
+        if (i < s_issued) mbar_wait(full0 + 8u * slot, parity);
+      } else {
+        ok = mbar_wait(full0 + 8u * slot, parity);
+        if (!ok) s_abort = 1;
+      }
+      float a_rot[NB];
+      decode_scales<NB, NESTED>(a_rot, sw, a, s_code2, offset, al);
+      const int64_t u = u0 + i;
+      if (i + ncw < n_units) fetch_scales<M, NB, NESTED>(sw, a, u0 + i + ncw, lane);
+      float acc[M];
+#pragma unroll
+      for (int m = 0; m < M; ++m) acc[m] = 0.0f;
+      if (ok) unit_dot<M, NB>(stages + uint32_t(slot) * kStage + uint32_t(lane) * (GW * 4), tab, lane, a_rot, acc);
+      __syncwarp();
+      if (lane == 0) mbar_arrive(empty0 + 8u * slot);
+      if (!ok) continue;
+      const int64_t rb = u - int64_t(g) * a.row_blocks;
+      float* part = a.partial + ((rb * a.groups + g) * M) * kRows;
+#pragma unroll
+      for (int m = 0; m < M; ++m) __stcg(part + m * kRows + lane, acc[m]);
+      __threadfence();
+      __syncwarp();
+      uint32_t old = 0;
+      if (lane == 0) old = atomicAdd(a.counters + rb, 1u);
+      old = __shfl_sync(0xffffffffu, old, 0);
+      if (old == uint32_t(a.groups - 1)) {  // every group of this row block is in
+        __threadfence();
+        finish_row_block<XT, M>(a, rb, lane);
+        if (lane == 0) a.counters[rb] = 0u;
+      }
+    }
+    seg = seg_end;
+  }
+}
+
+// --------------------------------------------------------------- host side
+
+PFN_cuTensorMapEncodeTiled_v12000 encoder() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+  });
+  return fn;
+}
+
+constexpr int64_t kCounterBytes(int64_t row_blocks) { return (row_blocks * 4 + 255) / 256 * 256; }
+
+int64_t workspace_bytes_for(int m, int k, int64_t n_rows) {
+  const int gk = m == 1 ? Cfg<1>::kGroupK : Cfg<2>::kGroupK;
+  const int mm = m == 1 ? 1 : 2;
+  const int64_t rbs = (n_rows + kRows - 1) / kRows;
+  const int64_t groups = k / gk;
+  return kCounterBytes(rbs) + rbs * groups * mm * kRows * 4;
+}
+
+template <typename XT, int M, int NB, bool NESTED>
+int launch_t(const CUtensorMap& map, const XtabArgs& a0, const DeviceInfo& di, cudaStream_t s) {
+  constexpr uint32_t kStage = Cfg<M>::kStageBytes;
+  auto kern = gemv_xtab_kernel<XT, M, NB, NESTED>;
+  XtabArgs a = a0;
+  const int ncw = 12;
+  const int max_dyn = di.smem_optin - 4096;  // leave the static arrays their room
+  int stages = int((int64_t(max_dyn) - kTabBytes) / kStage);
+  if (stages > kMaxStages) stages = kMaxStages;
+  if (stages < ncw + 2) return BNBQ_ERR_UNSUPPORTED;
+  a.n_stages = stages;
+  const int dyn = int(kTabBytes + uint32_t(stages) * kStage);
+  static std::atomic<int> attr_set[kMaxDevices];  // per device: the attribute is set once
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return BNBQ_ERR_CUDA;
+  if (attr_set[dev].load(std::memory_order_acquire) != dyn) {
+    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, dyn) != cudaSuccess)
+      return BNBQ_ERR_CUDA;
+    attr_set[dev].store(dyn, std::memory_order_release);
+  }
+  int64_t grid = di.sm_count;
+  if (grid > a.units) grid = a.units;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(unsigned(grid));
+  cfg.blockDim = dim3(unsigned((ncw + 1) * 32));
+  cfg.dynamicSmemBytes = size_t(dyn);
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  if (cudaLaunchKernelEx(&cfg, kern, map, a) != cudaSuccess) return BNBQ_ERR_CUDA;
+  return launch_status();
+}
+
+template <typename XT, int M, bool NESTED>
+int launch_nb(int nb, const CUtensorMap& map, const XtabArgs& a, const DeviceInfo& di, cudaStream_t s) {
+  switch (nb) {
+    case 1: return launch_t<XT, M, 1, NESTED>(map, a, di, s);
+    case 2: return launch_t<XT, M, 2, NESTED>(map, a, di, s);
+    case 4: return launch_t<XT, M, 4, NESTED>(map, a, di, s);
+    case 8:
+      if constexpr (M == 1) return launch_t<XT, M, 8, NESTED>(map, a, di, s);
+      else return BNBQ_ERR_UNSUPPORTED;
+    default: return BNBQ_ERR_UNSUPPORTED;
+  }
+}
+
+// One pass over rows [m0, m0 + mm) of x (mm = 1 or 2).
+template <typename XT>
+int launch_rows(int mm, const XtabArgs& base, const uint8_t* w, bool nested, const DeviceInfo& di,
+                cudaStream_t s) {
+  const int gk = mm == 1 ? Cfg<1>::kGroupK : Cfg<2>::kGroupK;
+  const int bs = 1 << base.log2_bs;
+  const int nb = bs >= gk ? 1 : gk / bs;
+  XtabArgs a = base;
+  a.groups = base.k / gk;
+  a.row_blocks = int((base.n_rows + kRows - 1) / kRows);
+  a.units = int64_t(a.groups) * a.row_blocks;
+  a.partial = reinterpret_cast<float*>(reinterpret_cast<char*>(a.counters) + kCounterBytes(a.row_blocks));
+  auto encode = encoder();
+  if (!encode) return BNBQ_ERR_CUDA;
+  CUtensorMap map;
+  const cuuint64_t dims[2] = {cuuint64_t(base.k / 2), cuuint64_t(base.n_rows)};
+  const cuuint64_t strides[1] = {cuuint64_t(base.k / 2)};
+  const cuuint32_t box[2] = {cuuint32_t(gk / 2), cuuint32_t(kRows)};
+  const cuuint32_t estr[2] = {1, 1};
+  if (encode(&map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<uint8_t*>(w), dims, strides, box, estr,
+             CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+    return BNBQ_ERR_UNSUPPORTED;
+  if (mm == 1)
+    return nested ? launch_nb<XT, 1, true>(nb, map, a, di, s) : launch_nb<XT, 1, false>(nb, map, a, di, s);
+  return nested ? launch_nb<XT, 2, true>(nb, map, a, di, s) : launch_nb<XT, 2, false>(nb, map, a, di, s);
+}
+
+}  // namespace
+
+// Bytes of workspace the table GEMV needs for m rows of x (0 when it does not
+// apply to m).
+int64_t gemv_xtab_workspace_bytes(int m, int k, int64_t n_rows) {
+  if (m < 1 || m > 4 || n_rows < 1 || k < 1) return 0;
+  return workspace_bytes_for(m, k, n_rows);
+}
+
+// BNBQ_ERR_UNSUPPORTED when the table GEMV does not take this call (the caller
+// then uses the other GEMV kernels).
+int gemv_xtab_launch(int dtype, const void* x, int m, int k, const uint8_t* w, int64_t n_rows, int blocksize,
+                     const float* absmax, const uint8_t* absmax_q, const float* absmax2, const float* code2,
+                     const float* offset, int blocksize2, int64_t absmax2_block0, void* y, int64_t ldy,
+                     void* workspace, int64_t workspace_bytes, cudaStream_t s) {
+  if (m < 1 || m > 4 || !workspace) return BNBQ_ERR_UNSUPPORTED;
+  const int gk = m == 1 ? Cfg<1>::kGroupK : Cfg<2>::kGroupK;
+  if (k % Cfg<1>::kGroupK != 0 && (m == 1 || k % gk != 0)) return BNBQ_ERR_UNSUPPORTED;
+  if (m >= 3 && k % Cfg<1>::kGroupK != 0) return BNBQ_ERR_UNSUPPORTED;  // the one-row pass of m = 3
+  if (k % gk != 0) return BNBQ_ERR_UNSUPPORTED;
+  const int l2 = log2_exact(blocksize);
+  if (l2 < 5) return BNBQ_ERR_UNSUPPORTED;
+  const int nb_max = blocksize >= 256 ? 1 : 256 / blocksize;
+  if (absmax_q) {
+    if (log2_exact(blocksize2) < 0 || blocksize2 < nb_max) return BNBQ_ERR_UNSUPPORTED;
+    if (!aligned(absmax_q, uint64_t(nb_max))) return BNBQ_ERR_UNSUPPORTED;
+  }
+  if (workspace_bytes < workspace_bytes_for(m, k, n_rows) || !aligned(workspace, 256)) return BNBQ_ERR_UNSUPPORTED;
+  if (uint64_t(k / 2) % 16 != 0) return BNBQ_ERR_UNSUPPORTED;  // the tensor map's row pitch
+  DeviceInfo di;
+  if (int st = device_info(&di)) return st;
+  XtabArgs a{};
+  a.absmax = absmax;
+  a.absmax_q = absmax_q;
+  a.absmax2 = absmax2;
+  a.code2 = code2;
+  a.offset = offset;
+  a.counters = static_cast<uint32_t*>(workspace);
+  a.n_rows = n_rows;
+  a.ldy = ldy;
+  a.block0 = absmax2_block0;
+  a.k = k;
+  a.log2_bs = l2;
+  a.log2_bs2 = absmax_q ? log2_exact(blocksize2) : 0;
+  const size_t es = dtype == BNBQ_F32 ? 4 : 2;
+  const bool nested = absmax_q != nullptr;
+  // passes of two rows, then one of one row (m = 1, 3)
+  for (int m0 = 0; m0 < m;) {
+    const int mm = (m - m0 >= 2) ? 2 : 1;
+    a.x = static_cast<const char*>(x) + size_t(m0) * size_t(k) * es;
+    a.y = static_cast<char*>(y) + size_t(m0) * size_t(ldy) * es;
+    int st;
+    if (dtype == BNBQ_BF16) st = launch_rows<__nv_bfloat16>(mm, a, w, nested, di, s);
+    else if (dtype == BNBQ_F16) st = launch_rows<__half>(mm, a, w, nested, di, s);
+    else return BNBQ_ERR_UNSUPPORTED;
+    if (st != BNBQ_OK) return st;
+    m0 += mm;
+  }
+  return BNBQ_OK;
+}
+
+}  // namespace bnbq

@@ -150,6 +150,36 @@ BNBQ_API int bnbq_matmul_nf4(int dtype, const void* x, int32_t m, int32_t k,
                     const float* code2, const float* offset, int32_t blocksize2,
                     int64_t absmax2_block0, void* y, int64_t ldy, void* stream);
 
+/* bnbq_gemv_nf4 / bnbq_matmul_nf4 with a workspace: device memory the caller
+ * allocates once (bnbq_gemv_workspace_bytes gives its size for a shape),
+ * zero-filled before its first use, and passes to every call; each call that
+ * completes leaves it zero-filled again. With it, 1 <= m <= 4 runs the
+ * shared-memory pair-table GEMV, whose split of K across SMs adds its
+ * partial sums there (a fixed order: the results are deterministic); other
+ * shapes, or a workspace that is NULL or too small, run the kernels of
+ * bnbq_gemv_nf4. Calls that share a workspace must be ordered on one stream.
+ * After a bounded device wait has expired (bnbq_wait_timeouts), clear the
+ * workspace before its next use. Same numerics contract and one-hot exactness
+ * as bnbq_gemv_nf4. The weight codes and scales are read before the kernel
+ * waits for the preceding kernel on the stream (programmatic dependent
+ * launch); x is read and y written after it. */
+BNBQ_API int bnbq_gemv_nf4_ws(int dtype, const void* x, int32_t m, int32_t k,
+                     const uint8_t* w, int64_t n_rows, int32_t blocksize,
+                     const float* absmax, const uint8_t* absmax_q, const float* absmax2,
+                     const float* code2, const float* offset, int32_t blocksize2,
+                     int64_t absmax2_block0, void* y, int64_t ldy,
+                     void* workspace, int64_t workspace_bytes, void* stream);
+BNBQ_API int bnbq_matmul_nf4_ws(int dtype, const void* x, int32_t m, int32_t k,
+                       const uint8_t* w, int64_t n_rows, int32_t blocksize,
+                       const float* absmax, const uint8_t* absmax_q, const float* absmax2,
+                       const float* code2, const float* offset, int32_t blocksize2,
+                       int64_t absmax2_block0, void* y, int64_t ldy,
+                       void* workspace, int64_t workspace_bytes, void* stream);
+
+/* Workspace bytes bnbq_gemv_nf4_ws / bnbq_matmul_nf4_ws use for an (m x k) x
+ * and an n_rows x k weight (0: that shape needs none). */
+BNBQ_API int bnbq_gemv_workspace_bytes(int32_t m, int32_t k, int64_t n_rows, int64_t* bytes);
+
 /* ------------------------------------------------------------ diagnostics */
 
 /* All-gather of a row-sharded matmul output over NVLink peer memory (the
