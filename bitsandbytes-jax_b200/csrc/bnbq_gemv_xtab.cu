@@ -88,27 +88,6 @@ struct XtabArgs {
   int k, log2_bs, log2_bs2, groups, row_blocks, n_stages;
 };
 
-__device__ __forceinline__ uint32_t lds_u32(uint32_t a) {
-  uint32_t v;
-  asm volatile("ld.shared.u32 %0, [%1];" : "=r"(v) : "r"(a));
-  return v;
-}
-__device__ __forceinline__ float lds_f32(uint32_t a) {
-  float v;
-  asm volatile("ld.shared.f32 %0, [%1];" : "=f"(v) : "r"(a));
-  return v;
-}
-__device__ __forceinline__ float2 lds_f32x2(uint32_t a) {
-  float2 v;
-  asm volatile("ld.shared.v2.f32 {%0, %1}, [%2];" : "=f"(v.x), "=f"(v.y) : "r"(a));
-  return v;
-}
-__device__ __forceinline__ void sts_f32(uint32_t a, float v) {
-  asm volatile("st.shared.f32 [%0], %1;" ::"r"(a), "f"(v) : "memory");
-}
-__device__ __forceinline__ void sts_f32x2(uint32_t a, float v0, float v1) {
-  asm volatile("st.shared.v2.f32 [%0], {%1, %2};" ::"r"(a), "f"(v0), "f"(v1) : "memory");
-}
 __device__ __forceinline__ float fma_ftz(float a, float b, float c) {
   float r;
   asm("fma.rn.ftz.f32 %0, %1, %2, %3;" : "=f"(r) : "f"(a), "f"(b), "f"(c));
@@ -129,45 +108,62 @@ __device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap* map
 }
 
 template <typename XT>
-__device__ __forceinline__ float2 x_pair(const XT* x, int64_t i) {  // elements i, i + 1 (i even)
-  const uint32_t w = *reinterpret_cast<const uint32_t*>(x + i);
-  if constexpr (Elem<XT>::kDtype == BNBQ_BF16) return unpack2_bf16(w);
-  else return unpack2_f16(w);
-}
-
-template <typename XT>
 __device__ __forceinline__ void store_y(void* y, int64_t i, float v) {
   if constexpr (Elem<XT>::kDtype == BNBQ_BF16) static_cast<__nv_bfloat16*>(y)[i] = __float2bfloat16_rn(v);
   else static_cast<__half*>(y)[i] = __float2half_rn(v);
 }
 
-// The pair table of group g, written by the consumer warps (cw of ncw).
-// Thread (lane) owns the pairs j with j >> 2 == jq; the iterations (pair j & 3,
-// high nibble) are spread over the warps (and, for two rows, the half-warps).
+// 8 consecutive elements of x as float32 (one 16-byte load).
+template <typename XT>
+__device__ __forceinline__ void load_x8(float (&v)[8], const XT* p) {
+  const uint4 w = __ldg(reinterpret_cast<const uint4*>(p));
+  const uint32_t u[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    float2 f;
+    if constexpr (Elem<XT>::kDtype == BNBQ_BF16) f = unpack2_bf16(u[i]);
+    else f = unpack2_f16(u[i]);
+    v[2 * i] = f.x;
+    v[2 * i + 1] = f.y;
+  }
+}
+
+// x's elements of group g that this thread's table entries need: pairs
+// 4 jq .. 4 jq + 3, for every row of x.
 template <typename XT, int M>
-__device__ __forceinline__ void build_table(uint32_t tab, const XtabArgs& a, int g, int cw, int ncw, int lane) {
-  constexpr int GK = Cfg<M>::kGroupK;
+__device__ __forceinline__ void load_group_x(float (&xs)[M][8], const XtabArgs& a, int g, int lane) {
+  const int jq = M == 1 ? lane : (lane & 15);
   const XT* x = static_cast<const XT*>(a.x);
+#pragma unroll
+  for (int m = 0; m < M; ++m) load_x8<XT>(xs[m], x + int64_t(m) * a.k + int64_t(g) * Cfg<M>::kGroupK + 8 * jq);
+}
+
+// The pair table from this thread's x values, written by the consumer warps
+// (warp cw of ncw). A thread owns the pairs j with j >> 2 == jq; the (j & 3,
+// high nibble) combinations are spread over the warps (and, for two rows, the
+// half-warps); each writes the 16 entries of its low nibbles.
+template <int M>
+__device__ __forceinline__ void build_table(uint8_t* tab, const float (&xs)[M][8], int cw, int ncw, int lane) {
   const int jq = M == 1 ? lane : (lane & 15);
   const int slot = M == 1 ? cw : 2 * cw + (lane >> 4);
   const int nslots = M == 1 ? ncw : 2 * ncw;
-  for (int it = slot; it < 64; it += nslots) {
-    const int jl = it >> 4, hi = it & 15;
-    const int j = 4 * jq + jl;
-    const int64_t e = int64_t(g) * GK + 2 * j;
-    float u[M], x1[M];
 #pragma unroll
-    for (int m = 0; m < M; ++m) {
-      const float2 xp = x_pair<XT>(x + int64_t(m) * a.k, e);
-      u[m] = __fmul_rn(kNF4Table[hi], xp.x);
-      x1[m] = xp.y;
-    }
-    const uint32_t base = tab + (uint32_t(jl) << 15) + (uint32_t(hi * 16) << 7) + uint32_t(jq) * (4 * M);
+  for (int jl = 0; jl < 4; ++jl) {
+    for (int hi = ((slot - 16 * jl) % nslots + nslots) % nslots; hi < 16; hi += nslots) {
+      float u[M];
 #pragma unroll
-    for (int lo = 0; lo < 16; ++lo) {
-      const float t = kNF4Table[lo];
-      if constexpr (M == 1) sts_f32(base + (lo << 7), __fmaf_rn(t, x1[0], u[0]));
-      else sts_f32x2(base + (lo << 7), __fmaf_rn(t, x1[0], u[0]), __fmaf_rn(t, x1[1], u[1]));
+      for (int m = 0; m < M; ++m) u[m] = __fmul_rn(kNF4Table[hi], xs[m][2 * jl]);
+      uint8_t* base = tab + (jl << 15) + ((hi * 16) << 7) + jq * (4 * M);
+#pragma unroll
+      for (int lo = 0; lo < 16; ++lo) {
+        const float t = kNF4Table[lo];
+        if constexpr (M == 1) {
+          *reinterpret_cast<float*>(base + (lo << 7)) = __fmaf_rn(t, xs[0][2 * jl + 1], u[0]);
+        } else {
+          *reinterpret_cast<float2*>(base + (lo << 7)) =
+              make_float2(__fmaf_rn(t, xs[0][2 * jl + 1], u[0]), __fmaf_rn(t, xs[1][2 * jl + 1], u[1]));
+        }
+      }
     }
   }
 }
@@ -184,9 +180,8 @@ struct ScaleWords {
 };
 
 template <int M, int NB, bool NESTED>
-__device__ __forceinline__ void fetch_scales(ScaleWords<NB, NESTED>& s, const XtabArgs& a, int64_t unit, int lane) {
-  const int g = int(unit / a.row_blocks);
-  const int64_t row = (unit - int64_t(g) * a.row_blocks) * kRows + lane;
+__device__ __forceinline__ void fetch_scales(ScaleWords<NB, NESTED>& s, const XtabArgs& a, int g, int rb, int lane) {
+  const int64_t row = int64_t(rb) * kRows + lane;
   s.valid = row < a.n_rows;
   if (!s.valid) return;
   const int64_t bpr = int64_t(a.k) >> a.log2_bs;  // blocks per row
@@ -225,7 +220,8 @@ __device__ __forceinline__ void decode_scales(float (&a_rot)[NB], const ScaleWor
       continue;
     }
     if constexpr (NESTED) {
-      const uint32_t word = NB == 8 ? (blk < 4 ? s.q[0] : s.q[NB == 8 ? 1 : 0]) : s.q[0];
+      uint32_t word = s.q[0];
+      if constexpr (NB == 8) word = blk < 4 ? s.q[0] : s.q[(NB + 3) / 4 - 1];
       const uint32_t q2 = (word >> (8 * (blk & 3))) & 0xffu;
       const int64_t i0 = (a.block0 + s.gb0) >> a.log2_bs2;
       const float a2 = ((a.block0 + s.gb0 + blk) >> a.log2_bs2) != i0 ? s.v[1] : s.v[0];
@@ -244,8 +240,8 @@ __device__ __forceinline__ void decode_scales(float (&a_rot)[NB], const ScaleWor
 // the group, in a lane-dependent order (block (p + al) mod NB), words of a
 // block along the lane's diagonal.
 template <int M, int NB>
-__device__ __forceinline__ void unit_dot(uint32_t row_codes, uint32_t tab, int lane, const float (&a_rot)[NB],
-                                         float (&acc)[M]) {
+__device__ __forceinline__ void unit_dot(const uint32_t* row_codes, const uint8_t* tab, int lane,
+                                         const float (&a_rot)[NB], float (&acc)[M]) {
   constexpr int GW = Cfg<M>::kWords;
   constexpr int WB = GW / NB;
   const int li = M == 1 ? lane : (lane & 15);
@@ -260,19 +256,19 @@ __device__ __forceinline__ void unit_dot(uint32_t row_codes, uint32_t tab, int l
 #pragma unroll
     for (int s = 0; s < WB; ++s) {
       const int w = wb + ((s + orot) & (WB - 1));
-      const uint32_t cw = lds_u32(row_codes + 4 * w);
-      const uint32_t tw = tab + uint32_t(w) * (4 * M);
+      const uint32_t cw = row_codes[w];
+      const uint8_t* tw = tab + w * (4 * M);
       if constexpr (M == 1) {
-        const float v0 = lds_f32(__byte_perm(cw, 0, 0x4440) * 128u + tw);
-        const float v1 = lds_f32(__byte_perm(cw, 0, 0x4441) * 128u + tw + (1u << 15));
-        const float v2 = lds_f32(__byte_perm(cw, 0, 0x4442) * 128u + tw + (2u << 15));
-        const float v3 = lds_f32(__byte_perm(cw, 0, 0x4443) * 128u + tw + (3u << 15));
+        const float v0 = *reinterpret_cast<const float*>(tw + __byte_perm(cw, 0, 0x4440) * 128u);
+        const float v1 = *reinterpret_cast<const float*>(tw + __byte_perm(cw, 0, 0x4441) * 128u + (1u << 15));
+        const float v2 = *reinterpret_cast<const float*>(tw + __byte_perm(cw, 0, 0x4442) * 128u + (2u << 15));
+        const float v3 = *reinterpret_cast<const float*>(tw + __byte_perm(cw, 0, 0x4443) * 128u + (3u << 15));
         ps[0] += (v0 + v1) + (v2 + v3);
       } else {
-        const float2 v0 = lds_f32x2(__byte_perm(cw, 0, 0x4440) * 128u + tw);
-        const float2 v1 = lds_f32x2(__byte_perm(cw, 0, 0x4441) * 128u + tw + (1u << 15));
-        const float2 v2 = lds_f32x2(__byte_perm(cw, 0, 0x4442) * 128u + tw + (2u << 15));
-        const float2 v3 = lds_f32x2(__byte_perm(cw, 0, 0x4443) * 128u + tw + (3u << 15));
+        const float2 v0 = *reinterpret_cast<const float2*>(tw + __byte_perm(cw, 0, 0x4440) * 128u);
+        const float2 v1 = *reinterpret_cast<const float2*>(tw + __byte_perm(cw, 0, 0x4441) * 128u + (1u << 15));
+        const float2 v2 = *reinterpret_cast<const float2*>(tw + __byte_perm(cw, 0, 0x4442) * 128u + (2u << 15));
+        const float2 v3 = *reinterpret_cast<const float2*>(tw + __byte_perm(cw, 0, 0x4443) * 128u + (3u << 15));
         ps[0] += (v0.x + v1.x) + (v2.x + v3.x);
         ps[1] += (v0.y + v1.y) + (v2.y + v3.y);
       }
@@ -322,6 +318,32 @@ __device__ __forceinline__ void finish_row_block(const XtabArgs& a, int64_t rb, 
   }
 }
 
+// This warp's unit of row block rb has stored its partials: count it in (a
+// release that also covers the other lanes' stores, through the warp
+// barrier) and, if it is the row block's last, finish the row block.
+template <typename XT, int M>
+__device__ __forceinline__ void arrive_row_block(const XtabArgs& a, int rb, int lane) {
+  __syncwarp();
+  uint32_t old = 0;
+  if (lane == 0)
+    asm volatile("atom.acq_rel.gpu.global.add.u32 %0, [%1], 1;" : "=r"(old) : "l"(a.counters + rb) : "memory");
+  old = __shfl_sync(0xffffffffu, old, 0);
+  if (old == uint32_t(a.groups - 1)) {  // every group of this row block is in
+    finish_row_block<XT, M>(a, rb, lane);
+    __syncwarp();
+    if (lane == 0) a.counters[rb] = 0u;
+  }
+}
+
+// (g, rb) of the unit `step` units after (g, rb), in group-major order.
+__device__ __forceinline__ void advance_unit(int& g, int& rb, int step, int row_blocks) {
+  rb += step;
+  while (rb >= row_blocks) {
+    rb -= row_blocks;
+    ++g;
+  }
+}
+
 template <typename XT, int M, int NB, bool NESTED>
 __global__ void __launch_bounds__((kMaxConsumers + 1) * 32, 1)
     gemv_xtab_kernel(const __grid_constant__ CUtensorMap tmap, const XtabArgs a) {
@@ -339,8 +361,9 @@ __global__ void __launch_bounds__((kMaxConsumers + 1) * 32, 1)
   const int64_t u0 = int64_t(blockIdx.x) * a.units / gridDim.x;
   const int64_t u1 = int64_t(blockIdx.x + 1) * a.units / gridDim.x;
   const int n_units = int(u1 - u0);
-  const uint32_t tab = smem_u32(smem);
-  const uint32_t stages = tab + kTabBytes;
+  const int g_first = int(u0 / a.row_blocks), rb_first = int(u0 - int64_t(g_first) * a.row_blocks);
+  uint8_t* tab = smem;
+  uint8_t* stages = smem + kTabBytes;
   const uint32_t full0 = smem_u32(s_bar), empty0 = full0 + 8u * kMaxStages;
 
   if (threadIdx.x == 0) {
@@ -358,16 +381,15 @@ __global__ void __launch_bounds__((kMaxConsumers + 1) * 32, 1)
   if (warp == ncw) {  // ------------------------------------------------ producer
     if (lane == 0) {
       asm volatile("prefetch.tensormap [%0];" ::"l"(&tmap) : "memory");
+      int g = g_first, rb = rb_first;
       int i = 0;
       for (; i < n_units; ++i) {
         const int slot = i % S;
         if (i >= S && !mbar_wait(empty0 + 8u * slot, uint32_t((i / S - 1) & 1))) break;
-        const int64_t u = u0 + i;
-        const int g = int(u / a.row_blocks);
-        const int rb = int(u - int64_t(g) * a.row_blocks);
         const uint32_t full = full0 + 8u * slot;
         mbar_arrive_expect_tx(full, kStage);
-        tma_load_2d(stages + uint32_t(slot) * kStage, &tmap, g * (GW * 4), rb * kRows, full);
+        tma_load_2d(smem_u32(stages) + uint32_t(slot) * kStage, &tmap, g * (GW * 4), rb * kRows, full);
+        advance_unit(g, rb, 1, a.row_blocks);
       }
       s_issued = i;
       if (i < n_units) {
@@ -389,15 +411,23 @@ __global__ void __launch_bounds__((kMaxConsumers + 1) * 32, 1)
   constexpr int WB = GW / NB;
   const int al = (M == 1 ? lane : (lane & 15)) / WB;
 
+  // this warp's units: i = warp, warp + ncw, ...; (g, rb) of unit i and of the next one
+  int g = g_first, rb = rb_first;
+  advance_unit(g, rb, warp, a.row_blocks);
+  int gn = g, rbn = rb;
+  advance_unit(gn, rbn, ncw, a.row_blocks);
   ScaleWords<NB, NESTED> sw;
+  if (warp < n_units) fetch_scales<M, NB, NESTED>(sw, a, g, rb, lane);
+  float xs[M][8];
+  load_group_x<XT, M>(xs, a, g_first, lane);
+  int pend_rb = -1;  // row block whose partials were stored but not yet counted
   int i = warp;
-  if (i < n_units) fetch_scales<M, NB, NESTED>(sw, a, u0 + i, lane);
-  int seg = 0;
+  int seg = 0, seg_g = g_first;
   while (seg < n_units) {
-    const int g = int((u0 + seg) / a.row_blocks);
-    const int seg_end = int(min(int64_t(n_units), int64_t(g + 1) * a.row_blocks - u0));
+    const int seg_end = int(min(int64_t(n_units), int64_t(seg_g + 1) * a.row_blocks - u0));
     named_bar_sync(1, ncons);  // the previous group's table is no longer read
-    build_table<XT, M>(tab, a, g, warp, ncw, lane);
+    build_table<M>(tab, xs, warp, ncw, lane);
+    if (seg_end < n_units) load_group_x<XT, M>(xs, a, seg_g + 1, lane);  // in flight during the segment
     named_bar_sync(1, ncons);  // the table (and code2) are complete
     for (; i < seg_end; i += ncw) {
       const int slot = i % S;
@@ -412,32 +442,31 @@ __global__ void __launch_bounds__((kMaxConsumers + 1) * 32, 1)
       }
       float a_rot[NB];
       decode_scales<NB, NESTED>(a_rot, sw, a, s_code2, offset, al);
-      const int64_t u = u0 + i;
-      if (i + ncw < n_units) fetch_scales<M, NB, NESTED>(sw, a, u0 + i + ncw, lane);
+      if (i + ncw < n_units) fetch_scales<M, NB, NESTED>(sw, a, gn, rbn, lane);
       float acc[M];
 #pragma unroll
       for (int m = 0; m < M; ++m) acc[m] = 0.0f;
-      if (ok) unit_dot<M, NB>(stages + uint32_t(slot) * kStage + uint32_t(lane) * (GW * 4), tab, lane, a_rot, acc);
+      if (ok)
+        unit_dot<M, NB>(reinterpret_cast<const uint32_t*>(stages + size_t(slot) * kStage) + lane * GW, tab, lane,
+                        a_rot, acc);
       __syncwarp();
       if (lane == 0) mbar_arrive(empty0 + 8u * slot);
-      if (!ok) continue;
-      const int64_t rb = u - int64_t(g) * a.row_blocks;
-      float* part = a.partial + ((rb * a.groups + g) * M) * kRows;
+      if (ok) {
+        // count the previous unit in now (its stores have drained meanwhile), store this one's
+        if (pend_rb >= 0) arrive_row_block<XT, M>(a, pend_rb, lane);
+        float* part = a.partial + ((int64_t(rb) * a.groups + g) * M) * kRows;
 #pragma unroll
-      for (int m = 0; m < M; ++m) __stcg(part + m * kRows + lane, acc[m]);
-      __threadfence();
-      __syncwarp();
-      uint32_t old = 0;
-      if (lane == 0) old = atomicAdd(a.counters + rb, 1u);
-      old = __shfl_sync(0xffffffffu, old, 0);
-      if (old == uint32_t(a.groups - 1)) {  // every group of this row block is in
-        __threadfence();
-        finish_row_block<XT, M>(a, rb, lane);
-        if (lane == 0) a.counters[rb] = 0u;
+        for (int m = 0; m < M; ++m) __stcg(part + m * kRows + lane, acc[m]);
+        pend_rb = rb;
       }
+      g = gn;
+      rb = rbn;
+      advance_unit(gn, rbn, ncw, a.row_blocks);
     }
     seg = seg_end;
+    ++seg_g;
   }
+  if (pend_rb >= 0 && !s_abort) arrive_row_block<XT, M>(a, pend_rb, lane);
 }
 
 // --------------------------------------------------------------- host side
@@ -455,14 +484,17 @@ PFN_cuTensorMapEncodeTiled_v12000 encoder() {
   return fn;
 }
 
-constexpr int64_t kCounterBytes(int64_t row_blocks) { return (row_blocks * 4 + 255) / 256 * 256; }
+// Workspace: a fixed region of row-block counters (which must stay zero
+// between calls, whatever shapes share the workspace), then the partials.
+constexpr int64_t kMaxRowBlocks = 16384;  // n_rows <= 524288
+constexpr int64_t kCounterBytes = kMaxRowBlocks * 4;
 
 int64_t workspace_bytes_for(int m, int k, int64_t n_rows) {
   const int gk = m == 1 ? Cfg<1>::kGroupK : Cfg<2>::kGroupK;
   const int mm = m == 1 ? 1 : 2;
   const int64_t rbs = (n_rows + kRows - 1) / kRows;
   const int64_t groups = k / gk;
-  return kCounterBytes(rbs) + rbs * groups * mm * kRows * 4;
+  return kCounterBytes + rbs * groups * mm * kRows * 4;
 }
 
 template <typename XT, int M, int NB, bool NESTED>
@@ -470,7 +502,7 @@ int launch_t(const CUtensorMap& map, const XtabArgs& a0, const DeviceInfo& di, c
   constexpr uint32_t kStage = Cfg<M>::kStageBytes;
   auto kern = gemv_xtab_kernel<XT, M, NB, NESTED>;
   XtabArgs a = a0;
-  const int ncw = 12;
+  const int ncw = kMaxConsumers;
   const int max_dyn = di.smem_optin - 4096;  // leave the static arrays their room
   int stages = int((int64_t(max_dyn) - kTabBytes) / kStage);
   if (stages > kMaxStages) stages = kMaxStages;
@@ -525,7 +557,7 @@ int launch_rows(int mm, const XtabArgs& base, const uint8_t* w, bool nested, con
   a.groups = base.k / gk;
   a.row_blocks = int((base.n_rows + kRows - 1) / kRows);
   a.units = int64_t(a.groups) * a.row_blocks;
-  a.partial = reinterpret_cast<float*>(reinterpret_cast<char*>(a.counters) + kCounterBytes(a.row_blocks));
+  a.partial = reinterpret_cast<float*>(reinterpret_cast<char*>(a.counters) + kCounterBytes);
   auto encode = encoder();
   if (!encode) return BNBQ_ERR_CUDA;
   CUtensorMap map;
@@ -547,7 +579,7 @@ int launch_rows(int mm, const XtabArgs& base, const uint8_t* w, bool nested, con
 // Bytes of workspace the table GEMV needs for m rows of x (0 when it does not
 // apply to m).
 int64_t gemv_xtab_workspace_bytes(int m, int k, int64_t n_rows) {
-  if (m < 1 || m > 4 || n_rows < 1 || k < 1) return 0;
+  if (m < 1 || m > 4 || n_rows < 1 || n_rows > kMaxRowBlocks * kRows || k < 1) return 0;
   return workspace_bytes_for(m, k, n_rows);
 }
 
@@ -557,7 +589,7 @@ int gemv_xtab_launch(int dtype, const void* x, int m, int k, const uint8_t* w, i
                      const float* absmax, const uint8_t* absmax_q, const float* absmax2, const float* code2,
                      const float* offset, int blocksize2, int64_t absmax2_block0, void* y, int64_t ldy,
                      void* workspace, int64_t workspace_bytes, cudaStream_t s) {
-  if (m < 1 || m > 4 || !workspace) return BNBQ_ERR_UNSUPPORTED;
+  if (m < 1 || m > 4 || !workspace || n_rows > kMaxRowBlocks * kRows) return BNBQ_ERR_UNSUPPORTED;
   const int gk = m == 1 ? Cfg<1>::kGroupK : Cfg<2>::kGroupK;
   if (k % Cfg<1>::kGroupK != 0 && (m == 1 || k % gk != 0)) return BNBQ_ERR_UNSUPPORTED;
   if (m >= 3 && k % Cfg<1>::kGroupK != 0) return BNBQ_ERR_UNSUPPORTED;  // the one-row pass of m = 3

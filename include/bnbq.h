@@ -151,9 +151,11 @@ BNBQ_API int bnbq_matmul_nf4(int dtype, const void* x, int32_t m, int32_t k,
                     int64_t absmax2_block0, void* y, int64_t ldy, void* stream);
 
 /* bnbq_gemv_nf4 / bnbq_matmul_nf4 with a workspace: device memory the caller
- * allocates once (bnbq_gemv_workspace_bytes gives its size for a shape),
- * zero-filled before its first use, and passes to every call; each call that
- * completes leaves it zero-filled again. With it, 1 <= m <= 4 runs the
+ * allocates once (bnbq_gemv_workspace_bytes gives its size for a shape; one
+ * buffer as large as the largest serves every shape), zero-filled before its
+ * first use, and passes to every call; each call that completes leaves the
+ * part that must start at zero (its first 64 KB) zero again. With it,
+ * 1 <= m <= 4 (and n_rows <= 524288) runs the
  * shared-memory pair-table GEMV, whose split of K across SMs adds its
  * partial sums there (a fixed order: the results are deterministic); other
  * shapes, or a workspace that is NULL or too small, run the kernels of

@@ -162,6 +162,23 @@ def test_table_gemv_row_shard_and_wide_output(cuda):
     assert bool((big[:, :100] == 7.0).all()) and bool((big[:, 100 + (r1 - r0):] == 7.0).all())
 
 
+def test_table_gemv_one_workspace_many_shapes(cuda):
+    """One workspace shared by calls of different shapes (the partial sums of
+    one shape land where another shape's row-block counts are not)."""
+    shapes = [(160, 512), (4096, 14336), (1000, 4096), (14336, 4096), (33, 256)]
+    nbytes = max(_lib.gemv_workspace_bytes(m, k, n) for n, k in shapes for m in (1, 2, 4))
+    ws = torch.zeros(nbytes, dtype=torch.uint8, device="cuda")
+    for rep in range(2):
+        for i, (n, k) in enumerate(shapes):
+            w = weight(n, k, seed=30 + i)
+            for m in (1, 2, 4):
+                x = torch.randn(m, k, device="cuda").to(torch.bfloat16)
+                got = call("bnbq_gemv_nf4_ws", x, w, n, ws)
+                fresh = call("bnbq_gemv_nf4_ws", x, w, n, new_ws(m, k, n))
+                torch.cuda.synchronize()
+                assert torch.equal(got, fresh), (rep, n, k, m)
+
+
 def test_table_gemv_workspace_size_and_fallback(cuda):
     """The size query; a too-small workspace or K not a multiple of 256 runs
     the other kernels, with the same result."""
