@@ -64,7 +64,7 @@ namespace {
 constexpr uint32_t kTabBytes = 131072;  // the pair table, for either row count
 constexpr int kRows = 32;               // weight rows per unit (one per lane)
 constexpr int kMaxStages = 40;
-constexpr int kMaxConsumers = 16;       // consumer warps per CTA
+constexpr int kMaxConsumers = 15;       // consumer warps per CTA (16 warps: 128 registers each)
 constexpr int kMaxDevices = 64;
 
 template <int M>
@@ -87,6 +87,24 @@ struct XtabArgs {
   int64_t n_rows, ldy, block0, units;
   int k, log2_bs, log2_bs2, groups, row_blocks, n_stages;
 };
+
+// Shared-memory loads by 32-bit shared-window address. The code-word load
+// carries a memory clobber so that it stays after the wait for its stage.
+__device__ __forceinline__ uint32_t lds_code(uint32_t a) {
+  uint32_t v;
+  asm volatile("ld.shared.u32 %0, [%1];" : "=r"(v) : "r"(a) : "memory");
+  return v;
+}
+__device__ __forceinline__ float lds_f32(uint32_t a) {
+  float v;
+  asm volatile("ld.shared.f32 %0, [%1];" : "=f"(v) : "r"(a));
+  return v;
+}
+__device__ __forceinline__ float2 lds_f32x2(uint32_t a) {
+  float2 v;
+  asm volatile("ld.shared.v2.f32 {%0, %1}, [%2];" : "=f"(v.x), "=f"(v.y) : "r"(a));
+  return v;
+}
 
 __device__ __forceinline__ float fma_ftz(float a, float b, float c) {
   float r;
@@ -236,39 +254,59 @@ __device__ __forceinline__ void decode_scales(float (&a_rot)[NB], const ScaleWor
   }
 }
 
-// The unit's dot products for this lane's row: phases over the NB blocks of
-// the group, in a lane-dependent order (block (p + al) mod NB), words of a
-// block along the lane's diagonal.
+// Walk order of a lane's code words within a unit: phase p covers block
+// (p + al) mod NB, and within it the lane starts at word (orot mod WB).
 template <int M, int NB>
-__device__ __forceinline__ void unit_dot(const uint32_t* row_codes, const uint8_t* tab, int lane,
-                                         const float (&a_rot)[NB], float (&acc)[M]) {
-  constexpr int GW = Cfg<M>::kWords;
-  constexpr int WB = GW / NB;
-  const int li = M == 1 ? lane : (lane & 15);
-  const int al = li / WB;
-  const int orot = M == 1 ? lane : li + (lane >> 4);
+struct Walk {
+  static constexpr int GW = Cfg<M>::kWords;
+  static constexpr int WB = GW / NB;
+  int al, orot;
+  __device__ __forceinline__ explicit Walk(int lane) {
+    const int li = M == 1 ? lane : (lane & 15);
+    al = li / WB;
+    orot = M == 1 ? lane : li + (lane >> 4);
+  }
+  __device__ __forceinline__ int word(int p, int s) const {
+    return ((p + al) & (NB - 1)) * WB + ((s + orot) & (WB - 1));
+  }
+};
+
+// The unit's code words of this lane's row, from its stage into registers in
+// walk order (conflict-free: the lanes' words differ at every step).
+template <int M, int NB>
+__device__ __forceinline__ void load_codes(uint32_t (&cw)[NB][Walk<M, NB>::WB], uint32_t row_codes,
+                                           const Walk<M, NB>& wk) {
+#pragma unroll
+  for (int p = 0; p < NB; ++p)
+#pragma unroll
+    for (int s = 0; s < Walk<M, NB>::WB; ++s) cw[p][s] = lds_code(row_codes + 4u * uint32_t(wk.word(p, s)));
+}
+
+// The unit's dot products for this lane's row, from its code words: per
+// block, the table values of its words summed, then scaled once.
+template <int M, int NB>
+__device__ __forceinline__ void unit_dot(const uint32_t (&cw)[NB][Walk<M, NB>::WB], uint32_t tab,
+                                         const Walk<M, NB>& wk, const float (&a_rot)[NB], float (&acc)[M]) {
 #pragma unroll
   for (int p = 0; p < NB; ++p) {
-    const int wb = ((p + al) & (NB - 1)) * WB;
     float ps[M];
 #pragma unroll
     for (int m = 0; m < M; ++m) ps[m] = 0.0f;
 #pragma unroll
-    for (int s = 0; s < WB; ++s) {
-      const int w = wb + ((s + orot) & (WB - 1));
-      const uint32_t cw = row_codes[w];
-      const uint8_t* tw = tab + w * (4 * M);
+    for (int s = 0; s < Walk<M, NB>::WB; ++s) {
+      const uint32_t c = cw[p][s];
+      const uint32_t tw = tab + uint32_t(wk.word(p, s)) * (4 * M);
       if constexpr (M == 1) {
-        const float v0 = *reinterpret_cast<const float*>(tw + __byte_perm(cw, 0, 0x4440) * 128u);
-        const float v1 = *reinterpret_cast<const float*>(tw + __byte_perm(cw, 0, 0x4441) * 128u + (1u << 15));
-        const float v2 = *reinterpret_cast<const float*>(tw + __byte_perm(cw, 0, 0x4442) * 128u + (2u << 15));
-        const float v3 = *reinterpret_cast<const float*>(tw + __byte_perm(cw, 0, 0x4443) * 128u + (3u << 15));
+        const float v0 = lds_f32(__byte_perm(c, 0, 0x4440) * 128u + tw);
+        const float v1 = lds_f32(__byte_perm(c, 0, 0x4441) * 128u + tw + (1u << 15));
+        const float v2 = lds_f32(__byte_perm(c, 0, 0x4442) * 128u + tw + (2u << 15));
+        const float v3 = lds_f32(__byte_perm(c, 0, 0x4443) * 128u + tw + (3u << 15));
         ps[0] += (v0 + v1) + (v2 + v3);
       } else {
-        const float2 v0 = *reinterpret_cast<const float2*>(tw + __byte_perm(cw, 0, 0x4440) * 128u);
-        const float2 v1 = *reinterpret_cast<const float2*>(tw + __byte_perm(cw, 0, 0x4441) * 128u + (1u << 15));
-        const float2 v2 = *reinterpret_cast<const float2*>(tw + __byte_perm(cw, 0, 0x4442) * 128u + (2u << 15));
-        const float2 v3 = *reinterpret_cast<const float2*>(tw + __byte_perm(cw, 0, 0x4443) * 128u + (3u << 15));
+        const float2 v0 = lds_f32x2(__byte_perm(c, 0, 0x4440) * 128u + tw);
+        const float2 v1 = lds_f32x2(__byte_perm(c, 0, 0x4441) * 128u + tw + (1u << 15));
+        const float2 v2 = lds_f32x2(__byte_perm(c, 0, 0x4442) * 128u + tw + (2u << 15));
+        const float2 v3 = lds_f32x2(__byte_perm(c, 0, 0x4443) * 128u + tw + (3u << 15));
         ps[0] += (v0.x + v1.x) + (v2.x + v3.x);
         ps[1] += (v0.y + v1.y) + (v2.y + v3.y);
       }
@@ -326,9 +364,10 @@ __device__ __forceinline__ void arrive_row_block(const XtabArgs& a, int rb, int 
   __syncwarp();
   uint32_t old = 0;
   if (lane == 0)
-    asm volatile("atom.acq_rel.gpu.global.add.u32 %0, [%1], 1;" : "=r"(old) : "l"(a.counters + rb) : "memory");
+    asm volatile("atom.release.gpu.global.add.u32 %0, [%1], 1;" : "=r"(old) : "l"(a.counters + rb) : "memory");
   old = __shfl_sync(0xffffffffu, old, 0);
   if (old == uint32_t(a.groups - 1)) {  // every group of this row block is in
+    asm volatile("fence.acq_rel.gpu;" ::: "memory");
     finish_row_block<XT, M>(a, rb, lane);
     __syncwarp();
     if (lane == 0) a.counters[rb] = 0u;
@@ -408,8 +447,9 @@ __global__ void __launch_bounds__((kMaxConsumers + 1) * 32, 1)
     for (int i = threadIdx.x; i < 256; i += ncons) s_code2[i] = a.code2[i];
     offset = *a.offset;
   }
-  constexpr int WB = GW / NB;
-  const int al = (M == 1 ? lane : (lane & 15)) / WB;
+  const Walk<M, NB> wk(lane);
+  const uint32_t tab_a = smem_u32(tab);
+  const uint32_t lane_codes = smem_u32(stages) + uint32_t(lane) * (GW * 4);
 
   // this warp's units: i = warp, warp + ncw, ...; (g, rb) of unit i and of the next one
   int g = g_first, rb = rb_first;
@@ -422,6 +462,8 @@ __global__ void __launch_bounds__((kMaxConsumers + 1) * 32, 1)
   load_group_x<XT, M>(xs, a, g_first, lane);
   int pend_rb = -1;  // row block whose partials were stored but not yet counted
   int i = warp;
+  int slot = warp % S;
+  uint32_t parity = uint32_t((warp / S) & 1);
   int seg = 0, seg_g = g_first;
   while (seg < n_units) {
     const int seg_end = int(min(int64_t(n_units), int64_t(seg_g + 1) * a.row_blocks - u0));
@@ -430,8 +472,6 @@ __global__ void __launch_bounds__((kMaxConsumers + 1) * 32, 1)
     if (seg_end < n_units) load_group_x<XT, M>(xs, a, seg_g + 1, lane);  // in flight during the segment
     named_bar_sync(1, ncons);  // the table (and code2) are complete
     for (; i < seg_end; i += ncw) {
-      const int slot = i % S;
-      const uint32_t parity = uint32_t((i / S) & 1);
       bool ok;
       if (s_abort) {  // drain: wait (bounded) only for copies that were issued
         ok = false;
@@ -440,18 +480,23 @@ __global__ void __launch_bounds__((kMaxConsumers + 1) * 32, 1)
         ok = mbar_wait(full0 + 8u * slot, parity);
         if (!ok) s_abort = 1;
       }
-      float a_rot[NB];
-      decode_scales<NB, NESTED>(a_rot, sw, a, s_code2, offset, al);
-      if (i + ncw < n_units) fetch_scales<M, NB, NESTED>(sw, a, gn, rbn, lane);
-      float acc[M];
-#pragma unroll
-      for (int m = 0; m < M; ++m) acc[m] = 0.0f;
-      if (ok)
-        unit_dot<M, NB>(reinterpret_cast<const uint32_t*>(stages + size_t(slot) * kStage) + lane * GW, tab, lane,
-                        a_rot, acc);
+      uint32_t cw[NB][Walk<M, NB>::WB];
+      if (ok) load_codes<M, NB>(cw, lane_codes + uint32_t(slot) * kStage, wk);
       __syncwarp();
-      if (lane == 0) mbar_arrive(empty0 + 8u * slot);
+      if (lane == 0) mbar_arrive(empty0 + 8u * slot);  // the stage is free again
+      slot += ncw;  // this warp's next unit (ncw < S: at most one wrap)
+      if (slot >= S) {
+        slot -= S;
+        parity ^= 1u;
+      }
+      float a_rot[NB];
+      decode_scales<NB, NESTED>(a_rot, sw, a, s_code2, offset, wk.al);
+      if (i + ncw < n_units) fetch_scales<M, NB, NESTED>(sw, a, gn, rbn, lane);
       if (ok) {
+        float acc[M];
+#pragma unroll
+        for (int m = 0; m < M; ++m) acc[m] = 0.0f;
+        unit_dot<M, NB>(cw, tab_a, wk, a_rot, acc);
         // count the previous unit in now (its stores have drained meanwhile), store this one's
         if (pend_rb >= 0) arrive_row_block<XT, M>(a, pend_rb, lane);
         float* part = a.partial + ((int64_t(rb) * a.groups + g) * M) * kRows;
