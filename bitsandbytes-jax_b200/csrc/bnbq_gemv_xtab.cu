@@ -66,6 +66,7 @@ constexpr int kRows = 32;               // weight rows per unit (one per lane)
 constexpr int kMaxStages = 40;
 constexpr int kMaxConsumers = 15;       // consumer warps per CTA (16 warps: 128 registers each)
 constexpr int kMaxDevices = 64;
+constexpr int kMaxFinish = 256;  // row blocks one CTA can complete (>= its units)
 
 template <int M>
 struct Cfg {
@@ -282,33 +283,62 @@ __device__ __forceinline__ void load_codes(uint32_t (&cw)[NB][Walk<M, NB>::WB], 
     for (int s = 0; s < Walk<M, NB>::WB; ++s) cw[p][s] = lds_code(row_codes + 4u * uint32_t(wk.word(p, s)));
 }
 
+__device__ __forceinline__ float2 add2(float2 a, float2 b) {  // two add.rn.f32 in one instruction
+  float2 r;
+  asm("{\n\t.reg .b64 pa, pb, pr;\n\tmov.b64 pa, {%2, %3};\n\tmov.b64 pb, {%4, %5};\n\t"
+      "add.rn.f32x2 pr, pa, pb;\n\tmov.b64 {%0, %1}, pr;\n\t}"
+      : "=f"(r.x), "=f"(r.y)
+      : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y));
+  return r;
+}
+
 // The unit's dot products for this lane's row, from its code words: per
-// block, the table values of its words summed, then scaled once.
+// block, the table values of its words summed, then scaled once. All table
+// loads of a block are issued before its adds. The sum of a word is
+// (v0 + v1) + (v2 + v3) and the words are added in walk order.
 template <int M, int NB>
-__device__ __forceinline__ void unit_dot(const uint32_t (&cw)[NB][Walk<M, NB>::WB], uint32_t tab,
-                                         const Walk<M, NB>& wk, const float (&a_rot)[NB], float (&acc)[M]) {
+__device__ __forceinline__ void unit_dot(const uint32_t (&cw)[NB][Walk<M, NB>::WB], const uint32_t (&tp)[NB],
+                                         const uint32_t (&off)[Walk<M, NB>::WB], const float (&a_rot)[NB],
+                                         float (&acc)[M]) {
+  constexpr int WB = Walk<M, NB>::WB;
+  constexpr int kBatch = WB < 8 ? WB : 8;
 #pragma unroll
   for (int p = 0; p < NB; ++p) {
     float ps[M];
 #pragma unroll
     for (int m = 0; m < M; ++m) ps[m] = 0.0f;
 #pragma unroll
-    for (int s = 0; s < Walk<M, NB>::WB; ++s) {
-      const uint32_t c = cw[p][s];
-      const uint32_t tw = tab + uint32_t(wk.word(p, s)) * (4 * M);
+    for (int s0 = 0; s0 < WB; s0 += kBatch) {
       if constexpr (M == 1) {
-        const float v0 = lds_f32(__byte_perm(c, 0, 0x4440) * 128u + tw);
-        const float v1 = lds_f32(__byte_perm(c, 0, 0x4441) * 128u + tw + (1u << 15));
-        const float v2 = lds_f32(__byte_perm(c, 0, 0x4442) * 128u + tw + (2u << 15));
-        const float v3 = lds_f32(__byte_perm(c, 0, 0x4443) * 128u + tw + (3u << 15));
-        ps[0] += (v0 + v1) + (v2 + v3);
+        float v[kBatch][4];
+#pragma unroll
+        for (int j = 0; j < kBatch; ++j) {
+          const uint32_t c = cw[p][s0 + j];
+          const uint32_t tw = tp[p] + off[s0 + j];
+#pragma unroll
+          for (int i = 0; i < 4; ++i) v[j][i] = lds_f32(__byte_perm(c, 0, 0x4440 + i) * 128u + tw + (uint32_t(i) << 15));
+        }
+#pragma unroll
+        for (int j = 0; j < kBatch; ++j) {
+          const float2 h = add2(make_float2(v[j][0], v[j][2]), make_float2(v[j][1], v[j][3]));
+          ps[0] += h.x + h.y;
+        }
       } else {
-        const float2 v0 = lds_f32x2(__byte_perm(c, 0, 0x4440) * 128u + tw);
-        const float2 v1 = lds_f32x2(__byte_perm(c, 0, 0x4441) * 128u + tw + (1u << 15));
-        const float2 v2 = lds_f32x2(__byte_perm(c, 0, 0x4442) * 128u + tw + (2u << 15));
-        const float2 v3 = lds_f32x2(__byte_perm(c, 0, 0x4443) * 128u + tw + (3u << 15));
-        ps[0] += (v0.x + v1.x) + (v2.x + v3.x);
-        ps[1] += (v0.y + v1.y) + (v2.y + v3.y);
+        float2 v[kBatch][4];
+#pragma unroll
+        for (int j = 0; j < kBatch; ++j) {
+          const uint32_t c = cw[p][s0 + j];
+          const uint32_t tw = tp[p] + off[s0 + j];
+#pragma unroll
+          for (int i = 0; i < 4; ++i)
+            v[j][i] = lds_f32x2(__byte_perm(c, 0, 0x4440 + i) * 128u + tw + (uint32_t(i) << 15));
+        }
+#pragma unroll
+        for (int j = 0; j < kBatch; ++j) {
+          const float2 h = add2(add2(v[j][0], v[j][1]), add2(v[j][2], v[j][3]));
+          ps[0] += h.x;
+          ps[1] += h.y;
+        }
       }
     }
 #pragma unroll
@@ -353,24 +383,6 @@ __device__ __forceinline__ void finish_row_block(const XtabArgs& a, int64_t rb, 
 #pragma unroll
     for (int e = 0; e < 4; ++e)
       if (r0 + e < a.n_rows) store_y<XT>(a.y, int64_t(m) * a.ldy + r0 + e, vals[e]);
-  }
-}
-
-// This warp's unit of row block rb has stored its partials: count it in (a
-// release that also covers the other lanes' stores, through the warp
-// barrier) and, if it is the row block's last, finish the row block.
-template <typename XT, int M>
-__device__ __forceinline__ void arrive_row_block(const XtabArgs& a, int rb, int lane) {
-  __syncwarp();
-  uint32_t old = 0;
-  if (lane == 0)
-    asm volatile("atom.release.gpu.global.add.u32 %0, [%1], 1;" : "=r"(old) : "l"(a.counters + rb) : "memory");
-  old = __shfl_sync(0xffffffffu, old, 0);
-  if (old == uint32_t(a.groups - 1)) {  // every group of this row block is in
-    asm volatile("fence.acq_rel.gpu;" ::: "memory");
-    finish_row_block<XT, M>(a, rb, lane);
-    __syncwarp();
-    if (lane == 0) a.counters[rb] = 0u;
   }
 }
 
@@ -448,7 +460,11 @@ __global__ void __launch_bounds__((kMaxConsumers + 1) * 32, 1)
     offset = *a.offset;
   }
   const Walk<M, NB> wk(lane);
-  const uint32_t tab_a = smem_u32(tab);
+  uint32_t tp[NB], off[Walk<M, NB>::WB];  // table address of a word = tp[phase] + off[step]
+#pragma unroll
+  for (int p = 0; p < NB; ++p) tp[p] = smem_u32(tab) + uint32_t(wk.word(p, 0) - (wk.orot & (Walk<M, NB>::WB - 1))) * (4 * M);
+#pragma unroll
+  for (int st = 0; st < Walk<M, NB>::WB; ++st) off[st] = uint32_t((st + wk.orot) & (Walk<M, NB>::WB - 1)) * (4 * M);
   const uint32_t lane_codes = smem_u32(stages) + uint32_t(lane) * (GW * 4);
 
   // this warp's units: i = warp, warp + ncw, ...; (g, rb) of unit i and of the next one
@@ -460,7 +476,6 @@ __global__ void __launch_bounds__((kMaxConsumers + 1) * 32, 1)
   if (warp < n_units) fetch_scales<M, NB, NESTED>(sw, a, g, rb, lane);
   float xs[M][8];
   load_group_x<XT, M>(xs, a, g_first, lane);
-  int pend_rb = -1;  // row block whose partials were stored but not yet counted
   int i = warp;
   int slot = warp % S;
   uint32_t parity = uint32_t((warp / S) & 1);
@@ -496,13 +511,10 @@ __global__ void __launch_bounds__((kMaxConsumers + 1) * 32, 1)
         float acc[M];
 #pragma unroll
         for (int m = 0; m < M; ++m) acc[m] = 0.0f;
-        unit_dot<M, NB>(cw, tab_a, wk, a_rot, acc);
-        // count the previous unit in now (its stores have drained meanwhile), store this one's
-        if (pend_rb >= 0) arrive_row_block<XT, M>(a, pend_rb, lane);
+        unit_dot<M, NB>(cw, tp, off, a_rot, acc);
         float* part = a.partial + ((int64_t(rb) * a.groups + g) * M) * kRows;
 #pragma unroll
         for (int m = 0; m < M; ++m) __stcg(part + m * kRows + lane, acc[m]);
-        pend_rb = rb;
       }
       g = gn;
       rb = rbn;
@@ -511,7 +523,30 @@ __global__ void __launch_bounds__((kMaxConsumers + 1) * 32, 1)
     seg = seg_end;
     ++seg_g;
   }
-  if (pend_rb >= 0 && !s_abort) arrive_row_block<XT, M>(a, pend_rb, lane);
+  // Count this CTA's units in: one release atomic per unit, by as many threads
+  // in parallel (the barrier orders every consumer's partial stores before
+  // them); the units that complete a row block are finished here.
+  named_bar_sync(1, ncons);
+  if (s_abort) return;
+  __shared__ int s_fin[kMaxFinish];
+  __shared__ int s_nfin;
+  if (threadIdx.x == 0) s_nfin = 0;
+  named_bar_sync(1, ncons);
+  for (int t = threadIdx.x; t < n_units; t += ncons) {
+    int ug = g_first, urb = rb_first;
+    advance_unit(ug, urb, t, a.row_blocks);
+    uint32_t old;
+    asm volatile("atom.release.gpu.global.add.u32 %0, [%1], 1;" : "=r"(old) : "l"(a.counters + urb) : "memory");
+    if (old == uint32_t(a.groups - 1)) s_fin[atomicAdd(&s_nfin, 1)] = urb;
+  }
+  named_bar_sync(1, ncons);
+  const int nfin = s_nfin;
+  if (nfin) asm volatile("fence.acq_rel.gpu;" ::: "memory");
+  for (int f = warp; f < nfin; f += ncw) {
+    finish_row_block<XT, M>(a, s_fin[f], lane);
+    __syncwarp();
+    if (lane == 0) a.counters[s_fin[f]] = 0u;
+  }
 }
 
 // --------------------------------------------------------------- host side
@@ -564,6 +599,7 @@ int launch_t(const CUtensorMap& map, const XtabArgs& a0, const DeviceInfo& di, c
   }
   int64_t grid = di.sm_count;
   if (grid > a.units) grid = a.units;
+  if ((a.units + grid - 1) / grid > kMaxFinish) return BNBQ_ERR_UNSUPPORTED;  // a CTA's completions are listed
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(unsigned(grid));
   cfg.blockDim = dim3(unsigned((ncw + 1) * 32));
