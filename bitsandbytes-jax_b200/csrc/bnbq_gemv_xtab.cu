@@ -66,7 +66,6 @@ constexpr int kRows = 32;               // weight rows per unit (one per lane)
 constexpr int kMaxStages = 40;
 constexpr int kMaxConsumers = 15;       // consumer warps per CTA (16 warps: 128 registers each)
 constexpr int kMaxDevices = 64;
-constexpr int kMaxFinish = 256;  // row blocks one CTA can complete (>= its units)
 
 template <int M>
 struct Cfg {
@@ -386,14 +385,35 @@ __device__ __forceinline__ void finish_row_block(const XtabArgs& a, int64_t rb, 
   }
 }
 
-// (g, rb) of the unit `step` units after (g, rb), in group-major order.
-__device__ __forceinline__ void advance_unit(int& g, int& rb, int step, int row_blocks) {
-  rb += step;
-  while (rb >= row_blocks) {
-    rb -= row_blocks;
-    ++g;
+// A CTA's units [u0, u1) (group-major numbering) in processing order: from
+// the first unit that starts a group (row block 0), to the end, then the
+// units before it. Every CTA then walks the row blocks in about the same
+// order at the same time, so the code slabs that all CTAs read at a given
+// moment are the same whole rows of W: contiguous memory, not 128-byte
+// pieces strided by a row.
+struct Order {
+  uint32_t u0, u1, us, n1, rbs;
+  __device__ __forceinline__ Order(int64_t a, int64_t b, int row_blocks) {
+    u0 = uint32_t(a);
+    u1 = uint32_t(b);
+    rbs = uint32_t(row_blocks);
+    const uint32_t up = (u0 + rbs - 1) / rbs * rbs;  // first group start at or after u0
+    us = up < u1 ? up : u0;
+    n1 = u1 - us;
   }
-}
+  __device__ __forceinline__ uint32_t unit(uint32_t p) const { return p < n1 ? us + p : u0 + (p - n1); }
+  __device__ __forceinline__ void at(uint32_t p, int& g, int& rb) const {
+    const uint32_t u = unit(p);
+    g = int(u / rbs);
+    rb = int(u - uint32_t(g) * rbs);
+  }
+  // end (exclusive) of the run of positions from p that share p's group
+  __device__ __forceinline__ uint32_t seg_end(uint32_t p) const {
+    const uint32_t u = unit(p);
+    const uint32_t gend = (u / rbs + 1) * rbs;
+    return p < n1 ? min(u1, gend) - us : n1 + (min(us, gend) - u0);
+  }
+};
 
 template <typename XT, int M, int NB, bool NESTED>
 __global__ void __launch_bounds__((kMaxConsumers + 1) * 32, 1)
@@ -412,7 +432,7 @@ __global__ void __launch_bounds__((kMaxConsumers + 1) * 32, 1)
   const int64_t u0 = int64_t(blockIdx.x) * a.units / gridDim.x;
   const int64_t u1 = int64_t(blockIdx.x + 1) * a.units / gridDim.x;
   const int n_units = int(u1 - u0);
-  const int g_first = int(u0 / a.row_blocks), rb_first = int(u0 - int64_t(g_first) * a.row_blocks);
+  const Order ord(u0, u1, a.row_blocks);
   uint8_t* tab = smem;
   uint8_t* stages = smem + kTabBytes;
   const uint32_t full0 = smem_u32(s_bar), empty0 = full0 + 8u * kMaxStages;
@@ -432,15 +452,19 @@ __global__ void __launch_bounds__((kMaxConsumers + 1) * 32, 1)
   if (warp == ncw) {  // ------------------------------------------------ producer
     if (lane == 0) {
       asm volatile("prefetch.tensormap [%0];" ::"l"(&tmap) : "memory");
-      int g = g_first, rb = rb_first;
-      int i = 0;
+      int i = 0, slot = 0;
+      uint32_t parity = 0;
       for (; i < n_units; ++i) {
-        const int slot = i % S;
-        if (i >= S && !mbar_wait(empty0 + 8u * slot, uint32_t((i / S - 1) & 1))) break;
+        if (i >= S && !mbar_wait(empty0 + 8u * slot, parity ^ 1u)) break;
+        int g, rb;
+        ord.at(uint32_t(i), g, rb);
         const uint32_t full = full0 + 8u * slot;
         mbar_arrive_expect_tx(full, kStage);
         tma_load_2d(smem_u32(stages) + uint32_t(slot) * kStage, &tmap, g * (GW * 4), rb * kRows, full);
-        advance_unit(g, rb, 1, a.row_blocks);
+        if (++slot == S) {
+          slot = 0;
+          parity ^= 1u;
+        }
       }
       s_issued = i;
       if (i < n_units) {
@@ -467,26 +491,34 @@ __global__ void __launch_bounds__((kMaxConsumers + 1) * 32, 1)
   for (int st = 0; st < Walk<M, NB>::WB; ++st) off[st] = uint32_t((st + wk.orot) & (Walk<M, NB>::WB - 1)) * (4 * M);
   const uint32_t lane_codes = smem_u32(stages) + uint32_t(lane) * (GW * 4);
 
-  // this warp's units: i = warp, warp + ncw, ...; (g, rb) of unit i and of the next one
-  int g = g_first, rb = rb_first;
-  advance_unit(g, rb, warp, a.row_blocks);
-  int gn = g, rbn = rb;
-  advance_unit(gn, rbn, ncw, a.row_blocks);
+  // this warp's positions: i = warp, warp + ncw, ...
+  int g = 0, rb = 0;
   ScaleWords<NB, NESTED> sw;
-  if (warp < n_units) fetch_scales<M, NB, NESTED>(sw, a, g, rb, lane);
+  if (warp < n_units) {
+    ord.at(uint32_t(warp), g, rb);
+    fetch_scales<M, NB, NESTED>(sw, a, g, rb, lane);
+  }
   float xs[M][8];
-  load_group_x<XT, M>(xs, a, g_first, lane);
+  {
+    int g0, rb0;
+    ord.at(0u, g0, rb0);
+    load_group_x<XT, M>(xs, a, g0, lane);
+  }
   int i = warp;
   int slot = warp % S;
   uint32_t parity = uint32_t((warp / S) & 1);
-  int seg = 0, seg_g = g_first;
-  while (seg < n_units) {
-    const int seg_end = int(min(int64_t(n_units), int64_t(seg_g + 1) * a.row_blocks - u0));
+  uint32_t seg = 0;
+  while (seg < uint32_t(n_units)) {
+    const uint32_t seg_end = ord.seg_end(seg);
     named_bar_sync(1, ncons);  // the previous group's table is no longer read
     build_table<M>(tab, xs, warp, ncw, lane);
-    if (seg_end < n_units) load_group_x<XT, M>(xs, a, seg_g + 1, lane);  // in flight during the segment
+    if (seg_end < uint32_t(n_units)) {  // the next group's x, in flight during this segment
+      int gx, rbx;
+      ord.at(seg_end, gx, rbx);
+      load_group_x<XT, M>(xs, a, gx, lane);
+    }
     named_bar_sync(1, ncons);  // the table (and code2) are complete
-    for (; i < seg_end; i += ncw) {
+    for (; i < int(seg_end); i += ncw) {
       bool ok;
       if (s_abort) {  // drain: wait (bounded) only for copies that were issued
         ok = false;
@@ -499,53 +531,56 @@ __global__ void __launch_bounds__((kMaxConsumers + 1) * 32, 1)
       if (ok) load_codes<M, NB>(cw, lane_codes + uint32_t(slot) * kStage, wk);
       __syncwarp();
       if (lane == 0) mbar_arrive(empty0 + 8u * slot);  // the stage is free again
-      slot += ncw;  // this warp's next unit (ncw < S: at most one wrap)
+      slot += ncw;  // this warp's next position (ncw < S: at most one wrap)
       if (slot >= S) {
         slot -= S;
         parity ^= 1u;
       }
       float a_rot[NB];
       decode_scales<NB, NESTED>(a_rot, sw, a, s_code2, offset, wk.al);
-      if (i + ncw < n_units) fetch_scales<M, NB, NESTED>(sw, a, gn, rbn, lane);
+      const int gc = g, rbc = rb;
+      if (i + ncw < n_units) {
+        ord.at(uint32_t(i + ncw), g, rb);
+        fetch_scales<M, NB, NESTED>(sw, a, g, rb, lane);
+      }
       if (ok) {
         float acc[M];
 #pragma unroll
         for (int m = 0; m < M; ++m) acc[m] = 0.0f;
         unit_dot<M, NB>(cw, tp, off, a_rot, acc);
-        float* part = a.partial + ((int64_t(rb) * a.groups + g) * M) * kRows;
+        float* part = a.partial + ((int64_t(rbc) * a.groups + gc) * M) * kRows;
 #pragma unroll
         for (int m = 0; m < M; ++m) __stcg(part + m * kRows + lane, acc[m]);
       }
-      g = gn;
-      rb = rbn;
-      advance_unit(gn, rbn, ncw, a.row_blocks);
     }
     seg = seg_end;
-    ++seg_g;
   }
-  // Count this CTA's units in: one release atomic per unit, by as many threads
-  // in parallel (the barrier orders every consumer's partial stores before
-  // them); the units that complete a row block are finished here.
-  named_bar_sync(1, ncons);
+  // Count this warp's units in, lane t taking its t-th unit: a release atomic
+  // per unit (the warp barrier orders every lane's partial stores before it).
+  // A unit that completes its row block has the warp finish that row block.
   if (s_abort) return;
-  __shared__ int s_fin[kMaxFinish];
-  __shared__ int s_nfin;
-  if (threadIdx.x == 0) s_nfin = 0;
-  named_bar_sync(1, ncons);
-  for (int t = threadIdx.x; t < n_units; t += ncons) {
-    int ug = g_first, urb = rb_first;
-    advance_unit(ug, urb, t, a.row_blocks);
-    uint32_t old;
-    asm volatile("atom.release.gpu.global.add.u32 %0, [%1], 1;" : "=r"(old) : "l"(a.counters + urb) : "memory");
-    if (old == uint32_t(a.groups - 1)) s_fin[atomicAdd(&s_nfin, 1)] = urb;
-  }
-  named_bar_sync(1, ncons);
-  const int nfin = s_nfin;
-  if (nfin) asm volatile("fence.acq_rel.gpu;" ::: "memory");
-  for (int f = warp; f < nfin; f += ncw) {
-    finish_row_block<XT, M>(a, s_fin[f], lane);
-    __syncwarp();
-    if (lane == 0) a.counters[s_fin[f]] = 0u;
+  __syncwarp();
+  for (int t0 = 0; warp + t0 * ncw < n_units; t0 += 32) {
+    const int t = t0 + lane;
+    const int pos = warp + t * ncw;
+    int urb = -1;
+    if (pos < n_units) {
+      int ug;
+      ord.at(uint32_t(pos), ug, urb);
+      uint32_t old;
+      asm volatile("atom.release.gpu.global.add.u32 %0, [%1], 1;" : "=r"(old) : "l"(a.counters + urb) : "memory");
+      if (old != uint32_t(a.groups - 1)) urb = -1;
+    }
+    uint32_t last = __ballot_sync(0xffffffffu, urb >= 0);
+    if (last) asm volatile("fence.acq_rel.gpu;" ::: "memory");
+    while (last) {
+      const int src = __ffs(last) - 1;
+      last &= last - 1;
+      const int frb = __shfl_sync(0xffffffffu, urb, src);
+      finish_row_block<XT, M>(a, frb, lane);
+      __syncwarp();
+      if (lane == 0) a.counters[frb] = 0u;
+    }
   }
 }
 
@@ -599,7 +634,6 @@ int launch_t(const CUtensorMap& map, const XtabArgs& a0, const DeviceInfo& di, c
   }
   int64_t grid = di.sm_count;
   if (grid > a.units) grid = a.units;
-  if ((a.units + grid - 1) / grid > kMaxFinish) return BNBQ_ERR_UNSUPPORTED;  // a CTA's completions are listed
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(unsigned(grid));
   cfg.blockDim = dim3(unsigned((ncw + 1) * 32));
