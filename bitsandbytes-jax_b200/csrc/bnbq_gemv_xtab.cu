@@ -11,15 +11,18 @@
 //     P[j][b][m] = fma(T[b & 15], x[m][2j + 1], T[b >> 4] * x[m][2j]).
 // One code byte -- two weights -- then costs one table load and one add; the
 // weight itself is never formed. A warp takes 32 weight rows of a group (lane
-// l = row l). At each step lane l reads one 32-bit code word w_l of its row and
-// the four table entries of that word's pairs. The lanes walk the words of
-// their rows diagonally (w_l differs between lanes at every step), and entry
-// (j, b) lives in the bank of j's word: the 32 lanes' table loads always hit
-// 32 distinct banks, whatever the code bytes are.
-//   one row of x:  entry (j, b) at byte ((j & 3) << 15) | (b << 7) | ((j >> 2) << 2)
-//   two rows of x: entry (j, b) (a float2) at ((j & 3) << 15) | (b << 7) | ((j >> 2) << 3)
-// (for two rows the halves of a warp are served separately by the 64-bit
-// loads, and the lanes of a half walk distinct words).
+// l = row l). Lane l reads the code words w of its row in a lane-dependent
+// order (a different word for every lane at every step), and entry (j, b)
+// lives in the bank of j's word w = j >> 2: the 32 lanes' table loads always
+// hit 32 distinct banks, whatever the code bytes are. The table is placed at a
+// 64 KB-aligned shared address and entry (j, b) sits at byte offset
+//     ((j >> 1) & 1) << 16 | b << 8 | (j & 1) << 7 | w << 2   (one row of x)
+//     ((j >> 1) & 1) << 16 | b << 8 | (j & 1) << 7 | w << 3   (two rows: float2)
+// so one byte permute -- the code byte dropped into bits 8-15 of the word's
+// base address -- forms the address of a table load, whose constant part
+// ((j & 3) of the pair) is the load's immediate offset. The two halves of a
+// warp are served separately by 64-bit loads, and for two rows of x the lanes
+// of each half read distinct words.
 //
 // Scales. The words of a block are summed first; each block's scale a -- the
 // float32 absmax, or, double-quantized, fl32(mul.ftz(code2[q2], absmax2[..]) +
@@ -31,14 +34,19 @@
 //
 // Work. A unit is (group, 32-row block); the units, in group-major order, are
 // split evenly over one CTA per SM, so a CTA's units span one group or two (the
-// table is rebuilt between them, all consumer warps at a barrier). A producer
+// table is rebuilt between them, all consumer warps at a barrier). Each CTA
+// processes its units starting from its first row block 0, so that all CTAs
+// walk the row blocks together and read whole rows of W at a time. A producer
 // warp streams each unit's 32 x GK/2 code bytes with one TMA load into a ring
-// of shared-memory stages (mbarrier full/empty pairs); the consumer warps take
-// the units round-robin, each lane fetching its row's scale words one unit
-// ahead. Every unit's 32 (x M) float32 results go to the caller's workspace;
-// the last unit of a row block to arrive (one counter per row block) adds that
-// block's partials in a fixed order, rounds once to x's dtype and writes y, and
-// puts the counter back to zero. Results are therefore deterministic.
+// of shared-memory stages placed around the table (mbarrier full/empty
+// pairs); the consumer warps take the units round-robin, copy a unit's codes
+// into registers (releasing the stage at once) and fetch their row's scale
+// words one unit ahead. Every unit's 32 (x M) float32 results go to the
+// caller's workspace; when a warp has finished its units it counts each in
+// (one release atomic per unit and row block) and the unit that completes a
+// row block has its warp add the row block's partials in a fixed order, round
+// once to x's dtype, write y and put the counter back to zero. Results are
+// therefore deterministic.
 //
 // Every mbarrier wait is bounded in time; on an expiry the CTA stops working,
 // still waits (bounded) for every copy it issued, counts the expiry
@@ -62,9 +70,10 @@ namespace bnbq {
 namespace {
 
 constexpr uint32_t kTabBytes = 131072;  // the pair table, for either row count
+constexpr uint32_t kTabAlign = 65536;   // its shared address has zero bits 8-15
 constexpr int kRows = 32;               // weight rows per unit (one per lane)
-constexpr int kMaxStages = 40;
-constexpr int kMaxConsumers = 15;       // consumer warps per CTA (16 warps: 128 registers each)
+constexpr int kMaxStages = 56;
+constexpr int kConsumers = 15;          // consumer warps per CTA (16 warps: 128 registers each)
 constexpr int kMaxDevices = 64;
 
 template <int M>
@@ -85,7 +94,8 @@ struct XtabArgs {
   uint32_t* counters;  // [row_blocks], zero between calls
   float* partial;      // [row_blocks][groups][M][32]
   int64_t n_rows, ldy, block0, units;
-  int k, log2_bs, log2_bs2, groups, row_blocks, n_stages;
+  int k, log2_bs, log2_bs2, groups, row_blocks;
+  uint32_t dyn_bytes;  // dynamic shared memory of the launch
 };
 
 // Shared-memory loads by 32-bit shared-window address. The code-word load
@@ -95,20 +105,36 @@ __device__ __forceinline__ uint32_t lds_code(uint32_t a) {
   asm volatile("ld.shared.u32 %0, [%1];" : "=r"(v) : "r"(a) : "memory");
   return v;
 }
+template <int OFF>
 __device__ __forceinline__ float lds_f32(uint32_t a) {
   float v;
-  asm volatile("ld.shared.f32 %0, [%1];" : "=f"(v) : "r"(a));
+  asm volatile("ld.shared.f32 %0, [%1+%2];" : "=f"(v) : "r"(a), "n"(OFF));
   return v;
 }
+template <int OFF>
 __device__ __forceinline__ float2 lds_f32x2(uint32_t a) {
   float2 v;
-  asm volatile("ld.shared.v2.f32 {%0, %1}, [%2];" : "=f"(v.x), "=f"(v.y) : "r"(a));
+  asm volatile("ld.shared.v2.f32 {%0, %1}, [%2+%3];" : "=f"(v.x), "=f"(v.y) : "r"(a), "n"(OFF));
   return v;
+}
+__device__ __forceinline__ void sts_f32(uint32_t a, float v) {
+  asm volatile("st.shared.f32 [%0], %1;" ::"r"(a), "f"(v) : "memory");
+}
+__device__ __forceinline__ void sts_f32x2(uint32_t a, float v0, float v1) {
+  asm volatile("st.shared.v2.f32 [%0], {%1, %2};" ::"r"(a), "f"(v0), "f"(v1) : "memory");
 }
 
 __device__ __forceinline__ float fma_ftz(float a, float b, float c) {
   float r;
   asm("fma.rn.ftz.f32 %0, %1, %2, %3;" : "=f"(r) : "f"(a), "f"(b), "f"(c));
+  return r;
+}
+__device__ __forceinline__ float2 add2(float2 a, float2 b) {  // two add.rn.f32 in one instruction
+  float2 r;
+  asm("{\n\t.reg .b64 pa, pb, pr;\n\tmov.b64 pa, {%2, %3};\n\tmov.b64 pb, {%4, %5};\n\t"
+      "add.rn.f32x2 pr, pa, pb;\n\tmov.b64 {%0, %1}, pr;\n\t}"
+      : "=f"(r.x), "=f"(r.y)
+      : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y));
   return r;
 }
 __device__ __forceinline__ float4 ldcg4(const float* p) {
@@ -156,12 +182,18 @@ __device__ __forceinline__ void load_group_x(float (&xs)[M][8], const XtabArgs& 
   for (int m = 0; m < M; ++m) load_x8<XT>(xs[m], x + int64_t(m) * a.k + int64_t(g) * Cfg<M>::kGroupK + 8 * jq);
 }
 
-// The pair table from this thread's x values, written by the consumer warps
-// (warp cw of ncw). A thread owns the pairs j with j >> 2 == jq; the (j & 3,
-// high nibble) combinations are spread over the warps (and, for two rows, the
-// half-warps); each writes the 16 entries of its low nibbles.
+// Byte offset of entry (pair j, code byte b) in the table.
 template <int M>
-__device__ __forceinline__ void build_table(uint8_t* tab, const float (&xs)[M][8], int cw, int ncw, int lane) {
+__device__ __forceinline__ uint32_t entry_offset(int j, int b) {
+  return (uint32_t((j >> 1) & 1) << 16) | (uint32_t(b) << 8) | (uint32_t(j & 1) << 7) | (uint32_t(j >> 2) << (M == 1 ? 2 : 3));
+}
+
+// The pair table from this thread's x values, written by the consumer warps
+// (warp cw of ncw). A thread owns the pairs j with j >> 2 == jq (its bank);
+// the (j & 3, high nibble) combinations are spread over the warps (and, for
+// two rows, the half-warps); each writes the 16 entries of its low nibbles.
+template <int M>
+__device__ __forceinline__ void build_table(uint32_t tab, const float (&xs)[M][8], int cw, int ncw, int lane) {
   const int jq = M == 1 ? lane : (lane & 15);
   const int slot = M == 1 ? cw : 2 * cw + (lane >> 4);
   const int nslots = M == 1 ? ncw : 2 * ncw;
@@ -171,16 +203,12 @@ __device__ __forceinline__ void build_table(uint8_t* tab, const float (&xs)[M][8
       float u[M];
 #pragma unroll
       for (int m = 0; m < M; ++m) u[m] = __fmul_rn(kNF4Table[hi], xs[m][2 * jl]);
-      uint8_t* base = tab + (jl << 15) + ((hi * 16) << 7) + jq * (4 * M);
+      const uint32_t base = tab + entry_offset<M>(4 * jq + jl, hi * 16);
 #pragma unroll
       for (int lo = 0; lo < 16; ++lo) {
         const float t = kNF4Table[lo];
-        if constexpr (M == 1) {
-          *reinterpret_cast<float*>(base + (lo << 7)) = __fmaf_rn(t, xs[0][2 * jl + 1], u[0]);
-        } else {
-          *reinterpret_cast<float2*>(base + (lo << 7)) =
-              make_float2(__fmaf_rn(t, xs[0][2 * jl + 1], u[0]), __fmaf_rn(t, xs[1][2 * jl + 1], u[1]));
-        }
+        if constexpr (M == 1) sts_f32(base + (lo << 8), __fmaf_rn(t, xs[0][2 * jl + 1], u[0]));
+        else sts_f32x2(base + (lo << 8), __fmaf_rn(t, xs[0][2 * jl + 1], u[0]), __fmaf_rn(t, xs[1][2 * jl + 1], u[1]));
       }
     }
   }
@@ -255,7 +283,9 @@ __device__ __forceinline__ void decode_scales(float (&a_rot)[NB], const ScaleWor
 }
 
 // Walk order of a lane's code words within a unit: phase p covers block
-// (p + al) mod NB, and within it the lane starts at word (orot mod WB).
+// (p + al) mod NB, and within it the lane starts at word (orot mod WB). Word
+// (p, s) is wbase(p) + o(s) with wbase(p) = ((p + al) mod NB) * WB and
+// o(s) = (s + orot) mod WB.
 template <int M, int NB>
 struct Walk {
   static constexpr int GW = Cfg<M>::kWords;
@@ -266,46 +296,39 @@ struct Walk {
     al = li / WB;
     orot = M == 1 ? lane : li + (lane >> 4);
   }
-  __device__ __forceinline__ int word(int p, int s) const {
-    return ((p + al) & (NB - 1)) * WB + ((s + orot) & (WB - 1));
-  }
+  __device__ __forceinline__ int wbase(int p) const { return ((p + al) & (NB - 1)) * WB; }
+  __device__ __forceinline__ int o(int s) const { return (s + orot) & (WB - 1); }
 };
 
 // The unit's code words of this lane's row, from its stage into registers in
 // walk order (conflict-free: the lanes' words differ at every step).
 template <int M, int NB>
 __device__ __forceinline__ void load_codes(uint32_t (&cw)[NB][Walk<M, NB>::WB], uint32_t row_codes,
-                                           const Walk<M, NB>& wk) {
+                                           const uint32_t (&cb)[NB], const uint32_t (&co)[Walk<M, NB>::WB]) {
 #pragma unroll
   for (int p = 0; p < NB; ++p)
 #pragma unroll
-    for (int s = 0; s < Walk<M, NB>::WB; ++s) cw[p][s] = lds_code(row_codes + 4u * uint32_t(wk.word(p, s)));
+    for (int s = 0; s < Walk<M, NB>::WB; ++s) cw[p][s] = lds_code(row_codes + cb[p] + co[s]);
 }
 
-__device__ __forceinline__ float2 add2(float2 a, float2 b) {  // two add.rn.f32 in one instruction
-  float2 r;
-  asm("{\n\t.reg .b64 pa, pb, pr;\n\tmov.b64 pa, {%2, %3};\n\tmov.b64 pb, {%4, %5};\n\t"
-      "add.rn.f32x2 pr, pa, pb;\n\tmov.b64 {%0, %1}, pr;\n\t}"
-      : "=f"(r.x), "=f"(r.y)
-      : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y));
-  return r;
-}
-
-// The unit's dot products for this lane's row, from its code words: per
-// block, the table values of its words summed, then scaled once. All table
-// loads of a block are issued before its adds. The sum of a word is
-// (v0 + v1) + (v2 + v3) and the words are added in walk order.
+// The unit's dot products for this lane's row, from its code words. Word
+// (p, s)'s table entries are at prmt(code byte i into bits 8-15 of
+// tp[p] + to[s]) + the pair's constant offset. Per block, the words' values
+// are summed pairwise into a two-lane accumulator in walk order, then scaled
+// once: acc = fma.ftz(a, sum, acc). All table loads of a batch of words are
+// issued before their adds.
 template <int M, int NB>
 __device__ __forceinline__ void unit_dot(const uint32_t (&cw)[NB][Walk<M, NB>::WB], const uint32_t (&tp)[NB],
-                                         const uint32_t (&off)[Walk<M, NB>::WB], const float (&a_rot)[NB],
+                                         const uint32_t (&to)[Walk<M, NB>::WB], const float (&a_rot)[NB],
                                          float (&acc)[M]) {
   constexpr int WB = Walk<M, NB>::WB;
   constexpr int kBatch = WB < 8 ? WB : 8;
+  constexpr int kOff1 = 1 << 7, kOff2 = 1 << 16, kOff3 = (1 << 16) | (1 << 7);  // pairs j & 3 = 1, 2, 3
 #pragma unroll
   for (int p = 0; p < NB; ++p) {
-    float ps[M];
+    float2 ps[M];
 #pragma unroll
-    for (int m = 0; m < M; ++m) ps[m] = 0.0f;
+    for (int m = 0; m < M; ++m) ps[m] = make_float2(0.0f, 0.0f);
 #pragma unroll
     for (int s0 = 0; s0 < WB; s0 += kBatch) {
       if constexpr (M == 1) {
@@ -313,35 +336,36 @@ __device__ __forceinline__ void unit_dot(const uint32_t (&cw)[NB][Walk<M, NB>::W
 #pragma unroll
         for (int j = 0; j < kBatch; ++j) {
           const uint32_t c = cw[p][s0 + j];
-          const uint32_t tw = tp[p] + off[s0 + j];
-#pragma unroll
-          for (int i = 0; i < 4; ++i) v[j][i] = lds_f32(__byte_perm(c, 0, 0x4440 + i) * 128u + tw + (uint32_t(i) << 15));
+          const uint32_t tw = tp[p] + to[s0 + j];
+          v[j][0] = lds_f32<0>(__byte_perm(c, tw, 0x7604));
+          v[j][1] = lds_f32<kOff1>(__byte_perm(c, tw, 0x7614));
+          v[j][2] = lds_f32<kOff2>(__byte_perm(c, tw, 0x7624));
+          v[j][3] = lds_f32<kOff3>(__byte_perm(c, tw, 0x7634));
         }
 #pragma unroll
-        for (int j = 0; j < kBatch; ++j) {
-          const float2 h = add2(make_float2(v[j][0], v[j][2]), make_float2(v[j][1], v[j][3]));
-          ps[0] += h.x + h.y;
-        }
+        for (int j = 0; j < kBatch; ++j)
+          ps[0] = add2(ps[0], add2(make_float2(v[j][0], v[j][2]), make_float2(v[j][1], v[j][3])));
       } else {
         float2 v[kBatch][4];
 #pragma unroll
         for (int j = 0; j < kBatch; ++j) {
           const uint32_t c = cw[p][s0 + j];
-          const uint32_t tw = tp[p] + off[s0 + j];
-#pragma unroll
-          for (int i = 0; i < 4; ++i)
-            v[j][i] = lds_f32x2(__byte_perm(c, 0, 0x4440 + i) * 128u + tw + (uint32_t(i) << 15));
+          const uint32_t tw = tp[p] + to[s0 + j];
+          v[j][0] = lds_f32x2<0>(__byte_perm(c, tw, 0x7604));
+          v[j][1] = lds_f32x2<kOff1>(__byte_perm(c, tw, 0x7614));
+          v[j][2] = lds_f32x2<kOff2>(__byte_perm(c, tw, 0x7624));
+          v[j][3] = lds_f32x2<kOff3>(__byte_perm(c, tw, 0x7634));
         }
 #pragma unroll
         for (int j = 0; j < kBatch; ++j) {
-          const float2 h = add2(add2(v[j][0], v[j][1]), add2(v[j][2], v[j][3]));
-          ps[0] += h.x;
-          ps[1] += h.y;
+          const float2 h01 = add2(v[j][0], v[j][1]), h23 = add2(v[j][2], v[j][3]);
+          ps[0] = add2(ps[0], make_float2(h01.x, h23.x));
+          ps[1] = add2(ps[1], make_float2(h01.y, h23.y));
         }
       }
     }
 #pragma unroll
-    for (int m = 0; m < M; ++m) acc[m] = fma_ftz(a_rot[p], ps[m], acc[m]);
+    for (int m = 0; m < M; ++m) acc[m] = fma_ftz(a_rot[p], ps[m].x + ps[m].y, acc[m]);
   }
 }
 
@@ -416,10 +440,11 @@ struct Order {
 };
 
 template <typename XT, int M, int NB, bool NESTED>
-__global__ void __launch_bounds__((kMaxConsumers + 1) * 32, 1)
+__global__ void __launch_bounds__((kConsumers + 1) * 32, 1)
     gemv_xtab_kernel(const __grid_constant__ CUtensorMap tmap, const XtabArgs a) {
   constexpr uint32_t kStage = Cfg<M>::kStageBytes;
   constexpr int GW = Cfg<M>::kWords;
+  constexpr int WB = Walk<M, NB>::WB;
   extern __shared__ __align__(1024) uint8_t smem[];
   __shared__ float s_code2[256];
   __shared__ __align__(8) uint64_t s_bar[2 * kMaxStages];
@@ -428,17 +453,22 @@ __global__ void __launch_bounds__((kMaxConsumers + 1) * 32, 1)
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int ncw = int(blockDim.x >> 5) - 1;  // consumer warps; the last warp produces
-  const int S = a.n_stages;
   const int64_t u0 = int64_t(blockIdx.x) * a.units / gridDim.x;
   const int64_t u1 = int64_t(blockIdx.x + 1) * a.units / gridDim.x;
   const int n_units = int(u1 - u0);
   const Order ord(u0, u1, a.row_blocks);
-  uint8_t* tab = smem;
-  uint8_t* stages = smem + kTabBytes;
+  // Shared layout: stages below the table (from the dynamic base up to the
+  // 64 KB-aligned table), the table, stages above it.
+  const uint32_t dyn0 = smem_u32(smem);
+  const uint32_t tab = (dyn0 + kTabAlign - 1) & ~(kTabAlign - 1);
+  const int s_lo = int((tab - dyn0) / kStage);
+  int S = s_lo + int((dyn0 + a.dyn_bytes - (tab + kTabBytes)) / kStage);
+  if (S > kMaxStages) S = kMaxStages;
+  const uint32_t stage_hi = tab + kTabBytes;
   const uint32_t full0 = smem_u32(s_bar), empty0 = full0 + 8u * kMaxStages;
 
   if (threadIdx.x == 0) {
-    s_abort = 0;
+    s_abort = S < ncw + 2 || dyn0 + a.dyn_bytes < tab + kTabBytes;  // (the host sizes the launch for this)
     s_issued = 0;
     for (int s = 0; s < S; ++s) {
       mbar_init(full0 + 8u * s, 1);   // the producer's arrival (plus the copy's bytes)
@@ -448,6 +478,13 @@ __global__ void __launch_bounds__((kMaxConsumers + 1) * 32, 1)
   }
   __syncthreads();
   asm volatile("griddepcontrol.launch_dependents;");
+  if (s_abort) {  // a layout this kernel cannot use: count it like an expired wait, write nothing
+    if (threadIdx.x == 0) atomicAdd(&g_bnbq_wait_timeouts, 1u);
+    return;
+  }
+  auto stage_addr = [&](int slot) -> uint32_t {
+    return slot < s_lo ? dyn0 + uint32_t(slot) * kStage : stage_hi + uint32_t(slot - s_lo) * kStage;
+  };
 
   if (warp == ncw) {  // ------------------------------------------------ producer
     if (lane == 0) {
@@ -460,7 +497,7 @@ __global__ void __launch_bounds__((kMaxConsumers + 1) * 32, 1)
         ord.at(uint32_t(i), g, rb);
         const uint32_t full = full0 + 8u * slot;
         mbar_arrive_expect_tx(full, kStage);
-        tma_load_2d(smem_u32(stages) + uint32_t(slot) * kStage, &tmap, g * (GW * 4), rb * kRows, full);
+        tma_load_2d(stage_addr(slot), &tmap, g * (GW * 4), rb * kRows, full);
         if (++slot == S) {
           slot = 0;
           parity ^= 1u;
@@ -484,12 +521,19 @@ __global__ void __launch_bounds__((kMaxConsumers + 1) * 32, 1)
     offset = *a.offset;
   }
   const Walk<M, NB> wk(lane);
-  uint32_t tp[NB], off[Walk<M, NB>::WB];  // table address of a word = tp[phase] + off[step]
+  // word (p, s): code at row_codes + cb[p] + co[s]; table base tp[p] + to[s]
+  uint32_t cb[NB], co[WB], tp[NB], to[WB];
 #pragma unroll
-  for (int p = 0; p < NB; ++p) tp[p] = smem_u32(tab) + uint32_t(wk.word(p, 0) - (wk.orot & (Walk<M, NB>::WB - 1))) * (4 * M);
+  for (int p = 0; p < NB; ++p) {
+    cb[p] = uint32_t(wk.wbase(p)) * 4u;
+    tp[p] = tab + uint32_t(wk.wbase(p)) * (4u * M);
+  }
 #pragma unroll
-  for (int st = 0; st < Walk<M, NB>::WB; ++st) off[st] = uint32_t((st + wk.orot) & (Walk<M, NB>::WB - 1)) * (4 * M);
-  const uint32_t lane_codes = smem_u32(stages) + uint32_t(lane) * (GW * 4);
+  for (int s = 0; s < WB; ++s) {
+    co[s] = uint32_t(wk.o(s)) * 4u;
+    to[s] = uint32_t(wk.o(s)) * (4u * M);
+  }
+  const uint32_t lane_row = uint32_t(lane) * (GW * 4);
 
   // this warp's positions: i = warp, warp + ncw, ...
   int g = 0, rb = 0;
@@ -527,8 +571,8 @@ __global__ void __launch_bounds__((kMaxConsumers + 1) * 32, 1)
         ok = mbar_wait(full0 + 8u * slot, parity);
         if (!ok) s_abort = 1;
       }
-      uint32_t cw[NB][Walk<M, NB>::WB];
-      if (ok) load_codes<M, NB>(cw, lane_codes + uint32_t(slot) * kStage, wk);
+      uint32_t cw[NB][WB];
+      if (ok) load_codes<M, NB>(cw, stage_addr(slot) + lane_row, cb, co);
       __syncwarp();
       if (lane == 0) mbar_arrive(empty0 + 8u * slot);  // the stage is free again
       slot += ncw;  // this warp's next position (ncw < S: at most one wrap)
@@ -547,7 +591,7 @@ __global__ void __launch_bounds__((kMaxConsumers + 1) * 32, 1)
         float acc[M];
 #pragma unroll
         for (int m = 0; m < M; ++m) acc[m] = 0.0f;
-        unit_dot<M, NB>(cw, tp, off, a_rot, acc);
+        unit_dot<M, NB>(cw, tp, to, a_rot, acc);
         float* part = a.partial + ((int64_t(rbc) * a.groups + gc) * M) * kRows;
 #pragma unroll
         for (int m = 0; m < M; ++m) __stcg(part + m * kRows + lane, acc[m]);
@@ -555,6 +599,7 @@ __global__ void __launch_bounds__((kMaxConsumers + 1) * 32, 1)
     }
     seg = seg_end;
   }
+
   // Count this warp's units in, lane t taking its t-th unit: a release atomic
   // per unit (the warp barrier orders every lane's partial stores before it).
   // A unit that completes its row block has the warp finish that row block.
@@ -617,13 +662,13 @@ int launch_t(const CUtensorMap& map, const XtabArgs& a0, const DeviceInfo& di, c
   constexpr uint32_t kStage = Cfg<M>::kStageBytes;
   auto kern = gemv_xtab_kernel<XT, M, NB, NESTED>;
   XtabArgs a = a0;
-  const int ncw = kMaxConsumers;
-  const int max_dyn = di.smem_optin - 4096;  // leave the static arrays their room
-  int stages = int((int64_t(max_dyn) - kTabBytes) / kStage);
-  if (stages > kMaxStages) stages = kMaxStages;
-  if (stages < ncw + 2) return BNBQ_ERR_UNSUPPORTED;
-  a.n_stages = stages;
-  const int dyn = int(kTabBytes + uint32_t(stages) * kStage);
+  const int ncw = kConsumers;
+  // All the shared memory the block may have, less its static arrays; the
+  // kernel places the table at a 64 KB-aligned address inside it and the
+  // stages around it (at least ncw + 2 of them).
+  const int dyn = (di.smem_optin - 4096) / 1024 * 1024;
+  if (dyn < int(kTabBytes + kTabAlign) + (ncw + 2) * int(kStage)) return BNBQ_ERR_UNSUPPORTED;
+  a.dyn_bytes = uint32_t(dyn);
   static std::atomic<int> attr_set[kMaxDevices];  // per device: the attribute is set once
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return BNBQ_ERR_CUDA;
