@@ -445,7 +445,7 @@ def roofline_entry(m, per_call_ms, peak, peak_kind, world):
     return entry
 
 
-GEMV_KERNEL = "gemv_bulk_kernel"
+GEMV_KERNEL = "gemv_xtab_kernel"
 
 
 def time_graph(torch, call, steps: int, warmup: int, device):

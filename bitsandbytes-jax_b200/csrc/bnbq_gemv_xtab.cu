@@ -666,8 +666,10 @@ int launch_t(const CUtensorMap& map, const XtabArgs& a0, const DeviceInfo& di, c
   // All the shared memory the block may have, less its static arrays; the
   // kernel places the table at a 64 KB-aligned address inside it and the
   // stages around it (at least ncw + 2 of them).
+  // The table then fits whatever the dynamic base address below 64 KB is, and
+  // what it leaves below and above the table holds the stages.
   const int dyn = (di.smem_optin - 4096) / 1024 * 1024;
-  if (dyn < int(kTabBytes + kTabAlign) + (ncw + 2) * int(kStage)) return BNBQ_ERR_UNSUPPORTED;
+  if (dyn < int(kTabBytes + kTabAlign) || (dyn - int(kTabBytes)) / int(kStage) < ncw + 4) return BNBQ_ERR_UNSUPPORTED;
   a.dyn_bytes = uint32_t(dyn);
   static std::atomic<int> attr_set[kMaxDevices];  // per device: the attribute is set once
   int dev = 0;
