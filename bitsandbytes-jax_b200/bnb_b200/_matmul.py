@@ -17,7 +17,7 @@ from __future__ import annotations
 import torch
 
 from .array import QuantizedArray
-from .kernels.gemv import _CHUNK, GEMV_MAX_M, gemv_nf4, matmul_nf4
+from .kernels.gemv import _CHUNK, plan_for
 
 __all__ = ["matmul"]
 
@@ -50,13 +50,12 @@ def _fused_args(w: QuantizedArray):
 
 
 def _forward(xm: torch.Tensor, w: QuantizedArray) -> torch.Tensor:
-    n = w.shape[0]
-    m = xm.shape[0]
     if _fused_applies(xm, w):
-        absmax, nested = _fused_args(w)
-        if m <= GEMV_MAX_M:
-            return gemv_nf4(xm, w.data, absmax, n, w.blocksize, nested=nested)
-        return matmul_nf4(xm, w.data, absmax, n, w.blocksize, nested=nested)
+        plan = w.__dict__.get("_bnbq_plan")
+        if plan is None or plan.data is not w.data or plan.absmax is not w.absmax or plan.device != xm.device:
+            scales, nested = _fused_args(w)
+            plan = plan_for(w, scales, nested, xm.device)
+        return plan.run(xm)
     return xm @ w.dequantize(xm.dtype).T
 
 

@@ -139,3 +139,78 @@ def matmul_nf4(
     if x.shape[0] < 1:
         raise ValueError("matmul_nf4 needs at least one row of x")
     return _run("bnbq_matmul_nf4", x, data, absmax, n_rows, blocksize, nested, absmax2_block0, out)
+
+
+class FusedPlan:
+    """The C-ABI arguments of one NF4 weight, prepared once: its codes and
+    (nested) scales as aligned float32/uint8 device tensors and their
+    addresses. :meth:`run` is then one ctypes call per matmul, with checks on
+    x only (dtype, device, contiguity, alignment). Built by :func:`plan_for`
+    and cached on the weight object."""
+
+    __slots__ = ("data", "absmax", "n", "k", "bs", "ptrs", "bs2", "keep", "device", "_ws_bytes")
+
+    def __init__(self, data, absmax, scales, n_rows, k, blocksize, nested, device):
+        self.data, self.absmax = data, absmax  # the weight's own fields (identity checked on reuse)
+        self.n, self.k, self.bs = n_rows, k, blocksize
+        self.device = device
+        w = _lib.aligned(data.reshape(-1))
+        if nested is None:
+            a = _lib.aligned(scales.reshape(-1), 4)
+            self.keep = (w, a)
+            self.ptrs = (w.data_ptr(), a.data_ptr(), None, None, None, None)
+            self.bs2 = 0
+        else:
+            absmax2, code2, offset, blocksize2 = nested
+            _log2_blocksize(blocksize2)
+            aq = _lib.aligned(scales.reshape(-1))
+            a2 = _lib.aligned(_f32_on(absmax2, device).reshape(-1), 4)
+            c2 = _lib.aligned(_f32_on(code2, device).reshape(-1), 4)
+            off = _lib.aligned(_f32_on(offset, device).reshape(1), 4)
+            self.keep = (w, aq, a2, c2, off)
+            self.ptrs = (w.data_ptr(), None, aq.data_ptr(), a2.data_ptr(), c2.data_ptr(), off.data_ptr())
+            self.bs2 = blocksize2
+        self._ws_bytes: dict[int, int] = {}
+
+    def run(self, x: torch.Tensor) -> torch.Tensor:
+        m = x.shape[0]
+        dev = x.device
+        if not x.is_contiguous() or x.data_ptr() % 16:
+            x = _lib.aligned(x)
+        out = torch.empty((m, self.n), dtype=x.dtype, device=dev)
+        stream = torch._C._cuda_getCurrentRawStream(dev.index)
+        ws_ptr, ws_n = None, 0
+        if m <= GEMV_MAX_M:
+            nb = self._ws_bytes.get(m)
+            if nb is None:
+                nb = self._ws_bytes[m] = _lib.gemv_workspace_bytes(m, self.k, self.n)
+            if nb:
+                ws = _lib.workspace(dev, stream, nb)
+                ws_ptr, ws_n = ws.data_ptr(), ws.numel()
+        wp, ap, aqp, a2p, c2p, offp = self.ptrs
+        args = (_lib.DTYPE_CODE[x.dtype], x.data_ptr(), m, self.k, wp, self.n, self.bs, ap, aqp, a2p, c2p, offp,
+                self.bs2, 0, out.data_ptr(), self.n, ws_ptr, ws_n, stream)
+        if torch._C._cuda_getDevice() == dev.index:
+            st = _lib.lib().bnbq_matmul_nf4_ws(*args)
+        else:
+            with torch.cuda.device(dev):
+                st = _lib.lib().bnbq_matmul_nf4_ws(*args)
+        if st:
+            _lib.check(st, "bnbq_matmul_nf4_ws")
+        return out
+
+
+def plan_for(w, scales, nested, device) -> FusedPlan:
+    """The FusedPlan of the 2-D NF4 QuantizedArray `w` (`scales`: its float32
+    absmax, or the codes of its nested absmax; `nested`: the rest of the
+    nested absmax or None), cached on `w` and re-made when `w`'s data or
+    absmax object is no longer the one it was made from."""
+    plan = w.__dict__.get("_bnbq_plan")
+    if plan is None or plan.data is not w.data or plan.absmax is not w.absmax or plan.device != device:
+        n, k = w.shape
+        if k % _CHUNK:
+            raise ValueError(f"K must be a multiple of {_CHUNK}, got {k}")
+        _log2_blocksize(w.blocksize)
+        plan = FusedPlan(w.data, w.absmax, scales, n, k, w.blocksize, nested, device)
+        w.__dict__["_bnbq_plan"] = plan
+    return plan

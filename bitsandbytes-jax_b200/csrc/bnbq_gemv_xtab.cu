@@ -73,7 +73,8 @@ constexpr uint32_t kTabBytes = 131072;  // the pair table, for either row count
 constexpr uint32_t kTabAlign = 65536;   // its shared address has zero bits 8-15
 constexpr int kRows = 32;               // weight rows per unit (one per lane)
 constexpr int kMaxStages = 56;
-constexpr int kConsumers = 15;          // consumer warps per CTA (16 warps: 128 registers each)
+constexpr int kProducers = 2;           // producer warps per CTA (TMA issue is per-thread latency-bound)
+constexpr int kConsumers = 14;          // consumer warps per CTA (16 warps in all: 128 registers each)
 constexpr int kMaxDevices = 64;
 
 template <int M>
@@ -369,6 +370,21 @@ __device__ __forceinline__ void unit_dot(const uint32_t (&cw)[NB][Walk<M, NB>::W
   }
 }
 
+// Wait (bounded, one lane's view is the warp's) until `uses` uses of a ring
+// slot have been taken; false on expiry (counted).
+__device__ __forceinline__ bool wait_taken(volatile uint32_t* taken, uint32_t uses) {
+  if (*taken >= uses) return true;
+  const uint64_t t0 = global_ns();
+  const uint64_t limit = g_bnbq_wait_limit_ns;
+  while (*taken < uses) {
+    if (global_ns() - t0 > limit) {
+      atomicAdd(&g_bnbq_wait_timeouts, 1u);
+      return false;
+    }
+  }
+  return true;
+}
+
 // The last unit of row block rb: sum its partials (fixed order), round, store.
 template <typename XT, int M>
 __device__ __forceinline__ void finish_row_block(const XtabArgs& a, int64_t rb, int lane) {
@@ -431,6 +447,18 @@ struct Order {
     g = int(u / rbs);
     rb = int(u - uint32_t(g) * rbs);
   }
+  // (g, rb) of position p + step from (g, rb) of position p (p + step < n)
+  __device__ __forceinline__ void advance(uint32_t p, uint32_t step, int& g, int& rb) const {
+    if (p < n1 && p + step >= n1) {  // wraps to the units before us
+      at(p + step, g, rb);
+      return;
+    }
+    rb += int(step);
+    while (rb >= int(rbs)) {
+      rb -= int(rbs);
+      ++g;
+    }
+  }
   // end (exclusive) of the run of positions from p that share p's group
   __device__ __forceinline__ uint32_t seg_end(uint32_t p) const {
     const uint32_t u = unit(p);
@@ -440,7 +468,7 @@ struct Order {
 };
 
 template <typename XT, int M, int NB, bool NESTED>
-__global__ void __launch_bounds__((kConsumers + 1) * 32, 1)
+__global__ void __launch_bounds__((kConsumers + kProducers) * 32, 1)
     gemv_xtab_kernel(const __grid_constant__ CUtensorMap tmap, const XtabArgs a) {
   constexpr uint32_t kStage = Cfg<M>::kStageBytes;
   constexpr int GW = Cfg<M>::kWords;
@@ -449,10 +477,11 @@ __global__ void __launch_bounds__((kConsumers + 1) * 32, 1)
   __shared__ float s_code2[256];
   __shared__ __align__(8) uint64_t s_bar[2 * kMaxStages];
   __shared__ volatile int s_abort;
-  __shared__ volatile int s_issued;
+  __shared__ volatile int s_next[kProducers];
+  __shared__ volatile uint32_t s_taken[kMaxStages];
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int ncw = int(blockDim.x >> 5) - 1;  // consumer warps; the last warp produces
+  const int ncw = int(blockDim.x >> 5) - kProducers;  // consumer warps; the last kProducers warps produce
   const int64_t u0 = int64_t(blockIdx.x) * a.units / gridDim.x;
   const int64_t u1 = int64_t(blockIdx.x + 1) * a.units / gridDim.x;
   const int n_units = int(u1 - u0);
@@ -469,8 +498,9 @@ __global__ void __launch_bounds__((kConsumers + 1) * 32, 1)
 
   if (threadIdx.x == 0) {
     s_abort = S < ncw + 2 || dyn0 + a.dyn_bytes < tab + kTabBytes;  // (the host sizes the launch for this)
-    s_issued = 0;
+    for (int q = 0; q < kProducers; ++q) s_next[q] = -1;  // set by producer q when it stops
     for (int s = 0; s < S; ++s) {
+      s_taken[s] = 0u;
       mbar_init(full0 + 8u * s, 1);   // the producer's arrival (plus the copy's bytes)
       mbar_init(empty0 + 8u * s, 1);  // the one consumer warp that took the unit
     }
@@ -486,28 +516,42 @@ __global__ void __launch_bounds__((kConsumers + 1) * 32, 1)
     return slot < s_lo ? dyn0 + uint32_t(slot) * kStage : stage_hi + uint32_t(slot - s_lo) * kStage;
   };
 
-  if (warp == ncw) {  // ------------------------------------------------ producer
-    if (lane == 0) {
-      asm volatile("prefetch.tensormap [%0];" ::"l"(&tmap) : "memory");
-      int i = 0, slot = 0;
-      uint32_t parity = 0;
-      for (; i < n_units; ++i) {
-        if (i >= S && !mbar_wait(empty0 + 8u * slot, parity ^ 1u)) break;
-        int g, rb;
-        ord.at(uint32_t(i), g, rb);
+  if (warp >= ncw) {  // ----------------------------------------------- producers
+    // producer q issues positions q, q + P, ...; a slot's next use waits until
+    // every earlier use has been taken (counts, then the empty barrier)
+    const int q = warp - ncw;
+    if (lane == 0 && q < n_units) {
+      if (q == 0) asm volatile("prefetch.tensormap [%0];" ::"l"(&tmap) : "memory");
+      int i = q, slot = q % S, g, rb;
+      uint32_t use = uint32_t(q / S);
+      ord.at(uint32_t(q), g, rb);
+      bool ok = true;
+      int unissued = 0x7fffffff;  // first position of this producer not issued
+      while (true) {
+        if (use > 0) ok = wait_taken(&s_taken[slot], use) && mbar_wait(empty0 + 8u * slot, (use - 1u) & 1u);
+        if (!ok || s_abort) {
+          unissued = i;
+          break;
+        }
         const uint32_t full = full0 + 8u * slot;
         mbar_arrive_expect_tx(full, kStage);
         tma_load_2d(stage_addr(slot), &tmap, g * (GW * 4), rb * kRows, full);
-        if (++slot == S) {
-          slot = 0;
-          parity ^= 1u;
+        if (i + kProducers >= n_units) break;
+        ord.advance(uint32_t(i), kProducers, g, rb);
+        i += kProducers;
+        slot += kProducers;
+        if (slot >= S) {
+          slot -= S;
+          ++use;
         }
       }
-      s_issued = i;
-      if (i < n_units) {
+      if (!ok) {
         __threadfence_block();
         s_abort = 1;
       }
+      s_next[q] = unissued;
+    } else if (lane == 0) {
+      s_next[q] = 0x7fffffff;
     }
     return;
   }
@@ -550,7 +594,8 @@ __global__ void __launch_bounds__((kConsumers + 1) * 32, 1)
   }
   int i = warp;
   int slot = warp % S;
-  uint32_t parity = uint32_t((warp / S) & 1);
+  uint32_t use = uint32_t(warp / S);  // which use of its slot position i is
+  uint32_t parity = use & 1u;
   uint32_t seg = 0;
   while (seg < uint32_t(n_units)) {
     const uint32_t seg_end = ord.seg_end(seg);
@@ -566,19 +611,32 @@ __global__ void __launch_bounds__((kConsumers + 1) * 32, 1)
       bool ok;
       if (s_abort) {  // drain: wait (bounded) only for copies that were issued
         ok = false;
-        if (i < s_issued) mbar_wait(full0 + 8u * slot, parity);
+        const int q = i % kProducers;
+        const uint64_t t0 = global_ns();
+        while (s_next[q] < 0 && global_ns() - t0 < g_bnbq_wait_limit_ns) {
+        }
+        if (i < s_next[q]) mbar_wait(full0 + 8u * slot, parity);
       } else {
-        ok = mbar_wait(full0 + 8u * slot, parity);
+        // A parity wait cannot tell this use of the slot from an earlier one:
+        // first make sure every earlier use has been taken (a warp running a
+        // whole ring ahead of another must not take the other's unit).
+        ok = use == 0 || wait_taken(&s_taken[slot], use);
+        ok = ok && mbar_wait(full0 + 8u * slot, parity);
+        ok = __shfl_sync(0xffffffffu, ok, 0);  // one decision for the warp
         if (!ok) s_abort = 1;
       }
       uint32_t cw[NB][WB];
       if (ok) load_codes<M, NB>(cw, stage_addr(slot) + lane_row, cb, co);
       __syncwarp();
-      if (lane == 0) mbar_arrive(empty0 + 8u * slot);  // the stage is free again
+      if (lane == 0) {
+        mbar_arrive(empty0 + 8u * slot);  // the stage is free again
+        s_taken[slot] = use + 1u;         // uses of this slot taken so far
+      }
       slot += ncw;  // this warp's next position (ncw < S: at most one wrap)
       if (slot >= S) {
         slot -= S;
         parity ^= 1u;
+        ++use;
       }
       float a_rot[NB];
       decode_scales<NB, NESTED>(a_rot, sw, a, s_code2, offset, wk.al);
@@ -663,6 +721,7 @@ int launch_t(const CUtensorMap& map, const XtabArgs& a0, const DeviceInfo& di, c
   auto kern = gemv_xtab_kernel<XT, M, NB, NESTED>;
   XtabArgs a = a0;
   const int ncw = kConsumers;
+  const int nwarps = kConsumers + kProducers;
   // All the shared memory the block may have, less its static arrays; the
   // kernel places the table at a 64 KB-aligned address inside it and the
   // stages around it (at least ncw + 2 of them).
@@ -683,7 +742,7 @@ int launch_t(const CUtensorMap& map, const XtabArgs& a0, const DeviceInfo& di, c
   if (grid > a.units) grid = a.units;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(unsigned(grid));
-  cfg.blockDim = dim3(unsigned((ncw + 1) * 32));
+  cfg.blockDim = dim3(unsigned(nwarps * 32));
   cfg.dynamicSmemBytes = size_t(dyn);
   cfg.stream = s;
   cudaLaunchAttribute attr[1];
