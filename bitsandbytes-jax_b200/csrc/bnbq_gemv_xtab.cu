@@ -73,12 +73,15 @@ constexpr uint32_t kTabBytes = 131072;  // the pair table, for either row count
 constexpr uint32_t kTabAlign = 65536;   // its shared address has zero bits 8-15
 constexpr int kRows = 32;               // weight rows per unit (one per lane)
 constexpr int kMaxStages = 56;
-constexpr int kProducers = 2;           // producer warps per CTA (TMA issue is per-thread latency-bound)
-constexpr int kConsumers = 14;          // consumer warps per CTA (16 warps in all: 128 registers each)
+constexpr int kProducers = 2;  // producer warps per CTA (TMA issue is per-thread latency-bound)
 constexpr int kMaxDevices = 64;
 
 template <int M>
 struct Cfg {
+  // consumer warps; the ring is a whole number of rounds of them, so a slot is
+  // always taken by the same consumer warp and filled by the same producer
+  static constexpr int kConsumers = M == 1 ? 11 : 14;
+  static constexpr int kRound = kConsumers * kProducers / (kConsumers % kProducers == 0 ? kProducers : 1);
   static constexpr int kGroupK = M == 1 ? 256 : 128;          // elements of K per table
   static constexpr int kWords = kGroupK / 8;                   // 32-bit code words per row and group
   static constexpr uint32_t kStageBytes = kRows * kWords * 4;  // 4 KB / 2 KB of codes per unit
@@ -370,21 +373,6 @@ __device__ __forceinline__ void unit_dot(const uint32_t (&cw)[NB][Walk<M, NB>::W
   }
 }
 
-// Wait (bounded, one lane's view is the warp's) until `uses` uses of a ring
-// slot have been taken; false on expiry (counted).
-__device__ __forceinline__ bool wait_taken(volatile uint32_t* taken, uint32_t uses) {
-  if (*taken >= uses) return true;
-  const uint64_t t0 = global_ns();
-  const uint64_t limit = g_bnbq_wait_limit_ns;
-  while (*taken < uses) {
-    if (global_ns() - t0 > limit) {
-      atomicAdd(&g_bnbq_wait_timeouts, 1u);
-      return false;
-    }
-  }
-  return true;
-}
-
 // The last unit of row block rb: sum its partials (fixed order), round, store.
 template <typename XT, int M>
 __device__ __forceinline__ void finish_row_block(const XtabArgs& a, int64_t rb, int lane) {
@@ -468,7 +456,7 @@ struct Order {
 };
 
 template <typename XT, int M, int NB, bool NESTED>
-__global__ void __launch_bounds__((kConsumers + kProducers) * 32, 1)
+__global__ void __launch_bounds__((Cfg<M>::kConsumers + kProducers) * 32, 1)
     gemv_xtab_kernel(const __grid_constant__ CUtensorMap tmap, const XtabArgs a) {
   constexpr uint32_t kStage = Cfg<M>::kStageBytes;
   constexpr int GW = Cfg<M>::kWords;
@@ -478,7 +466,6 @@ __global__ void __launch_bounds__((kConsumers + kProducers) * 32, 1)
   __shared__ __align__(8) uint64_t s_bar[2 * kMaxStages];
   __shared__ volatile int s_abort;
   __shared__ volatile int s_next[kProducers];
-  __shared__ volatile uint32_t s_taken[kMaxStages];
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int ncw = int(blockDim.x >> 5) - kProducers;  // consumer warps; the last kProducers warps produce
@@ -493,14 +480,14 @@ __global__ void __launch_bounds__((kConsumers + kProducers) * 32, 1)
   const int s_lo = int((tab - dyn0) / kStage);
   int S = s_lo + int((dyn0 + a.dyn_bytes - (tab + kTabBytes)) / kStage);
   if (S > kMaxStages) S = kMaxStages;
+  S -= S % Cfg<M>::kRound;
   const uint32_t stage_hi = tab + kTabBytes;
   const uint32_t full0 = smem_u32(s_bar), empty0 = full0 + 8u * kMaxStages;
 
   if (threadIdx.x == 0) {
-    s_abort = S < ncw + 2 || dyn0 + a.dyn_bytes < tab + kTabBytes;  // (the host sizes the launch for this)
+    s_abort = S < Cfg<M>::kRound || dyn0 + a.dyn_bytes < tab + kTabBytes;  // (the host sizes the launch for this)
     for (int q = 0; q < kProducers; ++q) s_next[q] = -1;  // set by producer q when it stops
     for (int s = 0; s < S; ++s) {
-      s_taken[s] = 0u;
       mbar_init(full0 + 8u * s, 1);   // the producer's arrival (plus the copy's bytes)
       mbar_init(empty0 + 8u * s, 1);  // the one consumer warp that took the unit
     }
@@ -517,8 +504,9 @@ __global__ void __launch_bounds__((kConsumers + kProducers) * 32, 1)
   };
 
   if (warp >= ncw) {  // ----------------------------------------------- producers
-    // producer q issues positions q, q + P, ...; a slot's next use waits until
-    // every earlier use has been taken (counts, then the empty barrier)
+    // producer q issues positions q, q + P, ...: the slots q, q + P, ... and
+    // every use of them (S is a multiple of P), in order, each after the
+    // slot's previous use has been taken (its empty barrier)
     const int q = warp - ncw;
     if (lane == 0 && q < n_units) {
       if (q == 0) asm volatile("prefetch.tensormap [%0];" ::"l"(&tmap) : "memory");
@@ -528,7 +516,7 @@ __global__ void __launch_bounds__((kConsumers + kProducers) * 32, 1)
       bool ok = true;
       int unissued = 0x7fffffff;  // first position of this producer not issued
       while (true) {
-        if (use > 0) ok = wait_taken(&s_taken[slot], use) && mbar_wait(empty0 + 8u * slot, (use - 1u) & 1u);
+        if (use > 0) ok = mbar_wait(empty0 + 8u * slot, (use - 1u) & 1u);
         if (!ok || s_abort) {
           unissued = i;
           break;
@@ -594,8 +582,7 @@ __global__ void __launch_bounds__((kConsumers + kProducers) * 32, 1)
   }
   int i = warp;
   int slot = warp % S;
-  uint32_t use = uint32_t(warp / S);  // which use of its slot position i is
-  uint32_t parity = use & 1u;
+  uint32_t parity = uint32_t((warp / S) & 1);
   uint32_t seg = 0;
   while (seg < uint32_t(n_units)) {
     const uint32_t seg_end = ord.seg_end(seg);
@@ -617,26 +604,20 @@ __global__ void __launch_bounds__((kConsumers + kProducers) * 32, 1)
         }
         if (i < s_next[q]) mbar_wait(full0 + 8u * slot, parity);
       } else {
-        // A parity wait cannot tell this use of the slot from an earlier one:
-        // first make sure every earlier use has been taken (a warp running a
-        // whole ring ahead of another must not take the other's unit).
-        ok = use == 0 || wait_taken(&s_taken[slot], use);
-        ok = ok && mbar_wait(full0 + 8u * slot, parity);
+        // this warp took the slot's previous use itself (S is a multiple of
+        // ncw), so the parity wait can only see this use's data
+        ok = mbar_wait(full0 + 8u * slot, parity);
         ok = __shfl_sync(0xffffffffu, ok, 0);  // one decision for the warp
         if (!ok) s_abort = 1;
       }
       uint32_t cw[NB][WB];
       if (ok) load_codes<M, NB>(cw, stage_addr(slot) + lane_row, cb, co);
       __syncwarp();
-      if (lane == 0) {
-        mbar_arrive(empty0 + 8u * slot);  // the stage is free again
-        s_taken[slot] = use + 1u;         // uses of this slot taken so far
-      }
+      if (lane == 0) mbar_arrive(empty0 + 8u * slot);  // the stage is free again
       slot += ncw;  // this warp's next position (ncw < S: at most one wrap)
       if (slot >= S) {
         slot -= S;
         parity ^= 1u;
-        ++use;
       }
       float a_rot[NB];
       decode_scales<NB, NESTED>(a_rot, sw, a, s_code2, offset, wk.al);
@@ -720,15 +701,16 @@ int launch_t(const CUtensorMap& map, const XtabArgs& a0, const DeviceInfo& di, c
   constexpr uint32_t kStage = Cfg<M>::kStageBytes;
   auto kern = gemv_xtab_kernel<XT, M, NB, NESTED>;
   XtabArgs a = a0;
-  const int ncw = kConsumers;
-  const int nwarps = kConsumers + kProducers;
+  const int ncw = Cfg<M>::kConsumers;
+  const int nwarps = ncw + kProducers;
   // All the shared memory the block may have, less its static arrays; the
   // kernel places the table at a 64 KB-aligned address inside it and the
   // stages around it (at least ncw + 2 of them).
   // The table then fits whatever the dynamic base address below 64 KB is, and
   // what it leaves below and above the table holds the stages.
   const int dyn = (di.smem_optin - 4096) / 1024 * 1024;
-  if (dyn < int(kTabBytes + kTabAlign) || (dyn - int(kTabBytes)) / int(kStage) < ncw + 4) return BNBQ_ERR_UNSUPPORTED;
+  if (dyn < int(kTabBytes + kTabAlign) || (dyn - int(kTabBytes)) / int(kStage) < Cfg<M>::kRound + 2)
+    return BNBQ_ERR_UNSUPPORTED;
   a.dyn_bytes = uint32_t(dyn);
   static std::atomic<int> attr_set[kMaxDevices];  // per device: the attribute is set once
   int dev = 0;
