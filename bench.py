@@ -394,6 +394,14 @@ def run_ours(args, dist, rank, world, local_rank):
         dist.barrier()
         pg.close()
 
+    # which kernels the timed call ran (the table GEMV unless it does not apply)
+    from bnb_b200 import _lib
+    nb = _lib.gemv_workspace_bytes(args.m, K_COLS, ranges[rank][1] - ranges[rank][0])
+    wsp = _lib.workspace(device, torch._C._cuda_getCurrentRawStream(device.index), nb) if nb else None
+    route = _lib.gemv_route(args.m, K_COLS, ranges[rank][1] - ranges[rank][0], BS,
+                            shards[0].rs.absmax.data_ptr(), BS2, _lib.ptr(wsp), 0 if wsp is None else wsp.numel())
+    kernel = {_lib.ROUTE_TABLE_GEMV: "gemv_xtab_kernel", _lib.ROUTE_GEMV: "gemv_bulk_kernel / gemm_kernel (precise)",
+              _lib.ROUTE_GEMM: "gemm_kernel"}[route]
     if rank != 0:
         return None
     per_call_ms = ms_max / args.steps
@@ -416,7 +424,7 @@ def run_ours(args, dist, rank, world, local_rank):
         "data": "synthetic (seeded torch Philox: W ~ N(0, 0.02^2), x ~ N(0, 1))",
         "config": bench_config(args.m, world),
         "verified": "gathered y == one-GPU product, bitwise, every rank" if world > 1 else "y == bnb.matmul(x, w)",
-        "roofline": roofline_entry(args.m, per_call_ms, peak, peak_kind, world),
+        "roofline": roofline_entry(args.m, per_call_ms, peak, peak_kind, world, kernel),
         "e2e": {"value": round(algo_bytes(args.m) * e2e_steps / (e2e_ms * 1e-3) / 1e9, 2), "unit": "GB/s",
                 "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
                 "us_per_step": round(e2e_ms / e2e_steps * 1e3, 3)},
@@ -434,18 +442,15 @@ def run_ours(args, dist, rank, world, local_rank):
 GEMV_MAX_ROWS = 20
 
 
-def roofline_entry(m, per_call_ms, peak, peak_kind, world):
+def roofline_entry(m, per_call_ms, peak, peak_kind, world, kernel):
     """The dominant kernel: the GEMV (the whole call at N=1)."""
     achieved = algo_bytes(m) / (per_call_ms * 1e-3) / 1e9
     entry = {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
              "frac": round(achieved / peak, 4), "peak_source": peak_kind,
-             "traffic": profiled_traffic(m), "kernel": GEMV_KERNEL}
+             "traffic": profiled_traffic(m), "kernel": kernel}
     if world > 1:
         entry["note"] = "whole-call rate (GEMV on 1/N of the rows + all-gather) against one GPU's peak"
     return entry
-
-
-GEMV_KERNEL = "gemv_xtab_kernel"
 
 
 def time_graph(torch, call, steps: int, warmup: int, device):

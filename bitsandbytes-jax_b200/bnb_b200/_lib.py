@@ -35,6 +35,7 @@ _SIGNATURES = {
     "bnbq_gemv_nf4_ws": "iPiiPliPPPPPilPlPlP",
     "bnbq_matmul_nf4_ws": "iPiiPliPPPPPilPlPlP",
     "bnbq_gemv_workspace_bytes": "iilP",
+    "bnbq_gemv_route": "iiliPiPlP",
     "bnbq_rcp_approx_ftz": "PPlP",
     "bnbq_version": "",
     "bnbq_wait_timeouts": "P",
@@ -158,6 +159,17 @@ def gemv_workspace_bytes(m: int, k: int, n_rows: int) -> int:
     n = C.c_int64(0)
     check(lib().bnbq_gemv_workspace_bytes(m, k, n_rows, C.byref(n)), "bnbq_gemv_workspace_bytes")
     return int(n.value)
+
+
+ROUTE_TABLE_GEMV, ROUTE_GEMV, ROUTE_GEMM = 1, 2, 3
+
+
+def gemv_route(m: int, k: int, n_rows: int, blocksize: int, absmax_q_ptr, blocksize2: int, ws_ptr, ws_bytes: int) -> int:
+    """Which kernels bnbq_matmul_nf4_ws runs for such a call (ROUTE_*)."""
+    r = C.c_int32(0)
+    check(lib().bnbq_gemv_route(m, k, n_rows, blocksize, absmax_q_ptr, blocksize2, ws_ptr, ws_bytes, C.byref(r)),
+          "bnbq_gemv_route")
+    return int(r.value)
 
 
 def call(name: str, *args) -> None:

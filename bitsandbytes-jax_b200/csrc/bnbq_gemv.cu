@@ -1181,6 +1181,24 @@ int gemv_xtab_launch(int dtype, const void* x, int m, int k, const uint8_t* w, i
                      void* workspace, int64_t workspace_bytes, cudaStream_t s);
 }  // namespace bnbq
 
+namespace bnbq {
+int gemv_xtab_applies(int m, int k, int64_t n_rows, int blocksize, const uint8_t* absmax_q, int blocksize2,
+                      const void* workspace, int64_t workspace_bytes);
+}  // namespace bnbq
+
+extern "C" int bnbq_gemv_route(int32_t m, int32_t k, int64_t n_rows, int32_t blocksize, const uint8_t* absmax_q,
+                               int32_t blocksize2, const void* workspace, int64_t workspace_bytes, int32_t* route) {
+  if (!route || m < 1 || k < 1 || n_rows < 1) return BNBQ_ERR_INVALID;
+  if (m > BNBQ_GEMV_MAX_M) {
+    *route = BNBQ_ROUTE_GEMM;
+    return BNBQ_OK;
+  }
+  const int st = gemv_xtab_applies(m, k, n_rows, blocksize, absmax_q, blocksize2, workspace, workspace_bytes);
+  if (st != BNBQ_OK && st != BNBQ_ERR_UNSUPPORTED) return st;
+  *route = st == BNBQ_OK ? BNBQ_ROUTE_TABLE_GEMV : BNBQ_ROUTE_GEMV;
+  return BNBQ_OK;
+}
+
 extern "C" int bnbq_gemv_workspace_bytes(int32_t m, int32_t k, int64_t n_rows, int64_t* bytes) {
   if (!bytes || m < 1 || k < 1 || n_rows < 1) return BNBQ_ERR_INVALID;
   *bytes = m <= BNBQ_GEMV_MAX_M ? gemv_xtab_workspace_bytes(m, k, n_rows) : 0;

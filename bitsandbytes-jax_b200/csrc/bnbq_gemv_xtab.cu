@@ -696,6 +696,16 @@ int64_t workspace_bytes_for(int m, int k, int64_t n_rows) {
   return kCounterBytes + rbs * groups * mm * kRows * 4;
 }
 
+// Dynamic shared memory of a launch: all the block may have, less its static
+// arrays. The kernel places the table at a 64 KB-aligned address inside it and
+// the stages below and above it; the alignment can cost up to one stage.
+int dyn_bytes(const DeviceInfo& di) { return (di.smem_optin - 4096) / 1024 * 1024; }
+
+template <int M>
+bool fits(int dyn) {
+  return dyn >= int(kTabBytes + kTabAlign) && (dyn - int(kTabBytes)) / int(Cfg<M>::kStageBytes) - 1 >= Cfg<M>::kRound;
+}
+
 template <typename XT, int M, int NB, bool NESTED>
 int launch_t(const CUtensorMap& map, const XtabArgs& a0, const DeviceInfo& di, cudaStream_t s) {
   constexpr uint32_t kStage = Cfg<M>::kStageBytes;
@@ -708,9 +718,8 @@ int launch_t(const CUtensorMap& map, const XtabArgs& a0, const DeviceInfo& di, c
   // stages around it (at least ncw + 2 of them).
   // The table then fits whatever the dynamic base address below 64 KB is, and
   // what it leaves below and above the table holds the stages.
-  const int dyn = (di.smem_optin - 4096) / 1024 * 1024;
-  if (dyn < int(kTabBytes + kTabAlign) || (dyn - int(kTabBytes)) / int(kStage) < Cfg<M>::kRound + 2)
-    return BNBQ_ERR_UNSUPPORTED;
+  const int dyn = dyn_bytes(di);
+  if (!fits<M>(dyn)) return BNBQ_ERR_UNSUPPORTED;
   a.dyn_bytes = uint32_t(dyn);
   static std::atomic<int> attr_set[kMaxDevices];  // per device: the attribute is set once
   int dev = 0;
@@ -788,15 +797,12 @@ int64_t gemv_xtab_workspace_bytes(int m, int k, int64_t n_rows) {
 
 // BNBQ_ERR_UNSUPPORTED when the table GEMV does not take this call (the caller
 // then uses the other GEMV kernels).
-int gemv_xtab_launch(int dtype, const void* x, int m, int k, const uint8_t* w, int64_t n_rows, int blocksize,
-                     const float* absmax, const uint8_t* absmax_q, const float* absmax2, const float* code2,
-                     const float* offset, int blocksize2, int64_t absmax2_block0, void* y, int64_t ldy,
-                     void* workspace, int64_t workspace_bytes, cudaStream_t s) {
-  if (m < 1 || m > 4 || !workspace || n_rows > kMaxRowBlocks * kRows) return BNBQ_ERR_UNSUPPORTED;
-  const int gk = m == 1 ? Cfg<1>::kGroupK : Cfg<2>::kGroupK;
-  if (k % Cfg<1>::kGroupK != 0 && (m == 1 || k % gk != 0)) return BNBQ_ERR_UNSUPPORTED;
-  if (m >= 3 && k % Cfg<1>::kGroupK != 0) return BNBQ_ERR_UNSUPPORTED;  // the one-row pass of m = 3
-  if (k % gk != 0) return BNBQ_ERR_UNSUPPORTED;
+// BNBQ_OK when the table GEMV takes a call of this shape (with a workspace of
+// workspace_bytes at `workspace`), else BNBQ_ERR_UNSUPPORTED (or a device error).
+int gemv_xtab_applies(int m, int k, int64_t n_rows, int blocksize, const uint8_t* absmax_q, int blocksize2,
+                      const void* workspace, int64_t workspace_bytes) {
+  if (m < 1 || m > 4 || !workspace || n_rows < 1 || n_rows > kMaxRowBlocks * kRows) return BNBQ_ERR_UNSUPPORTED;
+  if (k % Cfg<1>::kGroupK != 0) return BNBQ_ERR_UNSUPPORTED;  // (covers the two-row group too)
   const int l2 = log2_exact(blocksize);
   if (l2 < 5) return BNBQ_ERR_UNSUPPORTED;
   const int nb_max = blocksize >= 256 ? 1 : 256 / blocksize;
@@ -805,7 +811,19 @@ int gemv_xtab_launch(int dtype, const void* x, int m, int k, const uint8_t* w, i
     if (!aligned(absmax_q, uint64_t(nb_max))) return BNBQ_ERR_UNSUPPORTED;
   }
   if (workspace_bytes < workspace_bytes_for(m, k, n_rows) || !aligned(workspace, 256)) return BNBQ_ERR_UNSUPPORTED;
-  if (uint64_t(k / 2) % 16 != 0) return BNBQ_ERR_UNSUPPORTED;  // the tensor map's row pitch
+  DeviceInfo di;
+  if (int st = device_info(&di)) return st;
+  if (!fits<1>(dyn_bytes(di)) || (m >= 2 && !fits<2>(dyn_bytes(di)))) return BNBQ_ERR_UNSUPPORTED;
+  return BNBQ_OK;
+}
+
+int gemv_xtab_launch(int dtype, const void* x, int m, int k, const uint8_t* w, int64_t n_rows, int blocksize,
+                     const float* absmax, const uint8_t* absmax_q, const float* absmax2, const float* code2,
+                     const float* offset, int blocksize2, int64_t absmax2_block0, void* y, int64_t ldy,
+                     void* workspace, int64_t workspace_bytes, cudaStream_t s) {
+  if (int st = gemv_xtab_applies(m, k, n_rows, blocksize, absmax_q, blocksize2, workspace, workspace_bytes))
+    return st;
+  const int l2 = log2_exact(blocksize);
   DeviceInfo di;
   if (int st = device_info(&di)) return st;
   XtabArgs a{};

@@ -178,6 +178,15 @@ BNBQ_API int bnbq_matmul_nf4_ws(int dtype, const void* x, int32_t m, int32_t k,
                        int64_t absmax2_block0, void* y, int64_t ldy,
                        void* workspace, int64_t workspace_bytes, void* stream);
 
+/* Which kernels bnbq_matmul_nf4_ws runs for a call of this shape with this
+ * workspace (the scales' pointer matters only through its alignment):
+ * BNBQ_ROUTE_TABLE_GEMV (the pair-table GEMV, 1 <= m <= 4), BNBQ_ROUTE_GEMV
+ * (the other GEMV kernels, m <= BNBQ_GEMV_MAX_M) or BNBQ_ROUTE_GEMM (the
+ * tcgen05 GEMM). Host-only. No counterpart in the reference. */
+enum bnbq_route { BNBQ_ROUTE_TABLE_GEMV = 1, BNBQ_ROUTE_GEMV = 2, BNBQ_ROUTE_GEMM = 3 };
+BNBQ_API int bnbq_gemv_route(int32_t m, int32_t k, int64_t n_rows, int32_t blocksize, const uint8_t* absmax_q,
+                             int32_t blocksize2, const void* workspace, int64_t workspace_bytes, int32_t* route);
+
 /* Workspace bytes bnbq_gemv_nf4_ws / bnbq_matmul_nf4_ws use for an (m x k) x
  * and an n_rows x k weight (0: that shape needs none). */
 BNBQ_API int bnbq_gemv_workspace_bytes(int32_t m, int32_t k, int64_t n_rows, int64_t* bytes);

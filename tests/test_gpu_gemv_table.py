@@ -103,6 +103,20 @@ def test_table_gemv_tolerance_against_oracle(cuda, shape, m):
     assert counters_zero(ws, n)
 
 
+def test_table_gemv_takes_the_benchmark_shapes(cuda):
+    """The table GEMV (not a fallback) runs for the benchmark's shapes, plain and
+    double-quantized, M = 1..4."""
+    for n, k in [(4096, 14336), (1024, 4096), (14336, 4096), (28672, 8192), (8192, 28672)]:
+        for m in (1, 2, 3, 4):
+            ws = new_ws(m, k, n)
+            for dq in (True, False):
+                aq = ws if dq else None  # only the pointer's alignment matters here
+                route = _lib.gemv_route(m, k, n, 64, _lib.ptr(aq), 256, ws.data_ptr(), ws.numel())
+                assert route == _lib.ROUTE_TABLE_GEMV, (n, k, m, dq, route)
+    assert _lib.gemv_route(5, 14336, 4096, 64, None, 0, None, 0) == _lib.ROUTE_GEMV
+    assert _lib.gemv_route(21, 14336, 4096, 64, None, 0, None, 0) == _lib.ROUTE_GEMM
+
+
 def test_table_gemv_deterministic_and_reusable(cuda):
     """Bitwise equal results over repeated calls on one workspace (the fixed
     summation order), and every call leaves the counters at zero."""
