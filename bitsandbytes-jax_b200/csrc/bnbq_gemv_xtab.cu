@@ -75,6 +75,7 @@ constexpr int kRows = 32;               // weight rows per unit (one per lane)
 constexpr int kMaxStages = 56;
 constexpr int kProducers = 2;  // producer warps per CTA (TMA issue is per-thread latency-bound)
 constexpr int kMaxDevices = 64;
+constexpr int kMaxFinish = 512;  // row blocks one CTA can complete (at most its units)
 
 template <int M>
 struct Cfg {
@@ -140,6 +141,30 @@ __device__ __forceinline__ float2 add2(float2 a, float2 b) {  // two add.rn.f32 
       : "=f"(r.x), "=f"(r.y)
       : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y));
   return r;
+}
+// Read-only global loads kept where they are written (issued a unit ahead of use).
+__device__ __forceinline__ uint32_t ldg_u32(const void* p) {
+  uint32_t v;
+  asm volatile("ld.global.nc.u32 %0, [%1];" : "=r"(v) : "l"(p));
+  return v;
+}
+__device__ __forceinline__ void ldg_u32x2(const void* p, uint32_t& a, uint32_t& b) {
+  asm volatile("ld.global.nc.v2.u32 {%0, %1}, [%2];" : "=r"(a), "=r"(b) : "l"(p));
+}
+__device__ __forceinline__ uint32_t ldg_u16(const void* p) {
+  uint16_t v;
+  asm volatile("ld.global.nc.u16 %0, [%1];" : "=h"(v) : "l"(p));
+  return v;
+}
+__device__ __forceinline__ uint32_t ldg_u8(const void* p) {
+  uint16_t v;
+  asm volatile("ld.global.nc.u8 %0, [%1];" : "=h"(v) : "l"(p));
+  return v & 0xffu;
+}
+__device__ __forceinline__ float ldg_f32(const float* p) {
+  float v;
+  asm volatile("ld.global.nc.f32 %0, [%1];" : "=f"(v) : "l"(p));
+  return v;
 }
 __device__ __forceinline__ float4 ldcg4(const float* p) {
   float4 v;
@@ -238,23 +263,21 @@ __device__ __forceinline__ void fetch_scales(ScaleWords<NB, NESTED>& s, const Xt
   s.gb0 = row * bpr + ((int64_t(g) * Cfg<M>::kGroupK) >> a.log2_bs);
   if constexpr (NESTED) {
     if constexpr (NB == 8) {
-      const uint2 w = __ldg(reinterpret_cast<const uint2*>(a.absmax_q + s.gb0));
-      s.q[0] = w.x;
-      s.q[1] = w.y;
+      ldg_u32x2(a.absmax_q + s.gb0, s.q[0], s.q[1]);
     } else if constexpr (NB == 4) {
-      s.q[0] = __ldg(reinterpret_cast<const uint32_t*>(a.absmax_q + s.gb0));
+      s.q[0] = ldg_u32(a.absmax_q + s.gb0);
     } else if constexpr (NB == 2) {
-      s.q[0] = __ldg(reinterpret_cast<const uint16_t*>(a.absmax_q + s.gb0));
+      s.q[0] = ldg_u16(a.absmax_q + s.gb0);
     } else {
-      s.q[0] = __ldg(a.absmax_q + s.gb0);
+      s.q[0] = ldg_u8(a.absmax_q + s.gb0);
     }
     const int64_t i0 = (a.block0 + s.gb0) >> a.log2_bs2;
     const int64_t i1 = (a.block0 + s.gb0 + NB - 1) >> a.log2_bs2;
-    s.v[0] = __ldg(a.absmax2 + i0);
-    s.v[1] = i1 != i0 ? __ldg(a.absmax2 + i1) : s.v[0];
+    s.v[0] = ldg_f32(a.absmax2 + i0);
+    s.v[1] = ldg_f32(a.absmax2 + i1);
   } else {
 #pragma unroll
-    for (int b = 0; b < NB; ++b) s.v[b] = __ldg(a.absmax + s.gb0 + b);
+    for (int b = 0; b < NB; ++b) s.v[b] = ldg_f32(a.absmax + s.gb0 + b);
   }
 }
 
@@ -373,7 +396,8 @@ __device__ __forceinline__ void unit_dot(const uint32_t (&cw)[NB][Walk<M, NB>::W
   }
 }
 
-// The last unit of row block rb: sum its partials (fixed order), round, store.
+// Row block rb, once all its groups are in: sum its partials (fixed order),
+// round, store.
 template <typename XT, int M>
 __device__ __forceinline__ void finish_row_block(const XtabArgs& a, int64_t rb, int lane) {
   const float* part = a.partial + rb * int64_t(a.groups) * M * kRows;
@@ -466,6 +490,8 @@ __global__ void __launch_bounds__((Cfg<M>::kConsumers + kProducers) * 32, 1)
   __shared__ __align__(8) uint64_t s_bar[2 * kMaxStages];
   __shared__ volatile int s_abort;
   __shared__ volatile int s_next[kProducers];
+  __shared__ int s_fin[kMaxFinish];  // row blocks this CTA completed
+  __shared__ int s_nfin;
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int ncw = int(blockDim.x >> 5) - kProducers;  // consumer warps; the last kProducers warps produce
@@ -487,6 +513,7 @@ __global__ void __launch_bounds__((Cfg<M>::kConsumers + kProducers) * 32, 1)
   if (threadIdx.x == 0) {
     s_abort = S < Cfg<M>::kRound || dyn0 + a.dyn_bytes < tab + kTabBytes;  // (the host sizes the launch for this)
     for (int q = 0; q < kProducers; ++q) s_next[q] = -1;  // set by producer q when it stops
+    s_nfin = 0;
     for (int s = 0; s < S; ++s) {
       mbar_init(full0 + 8u * s, 1);   // the producer's arrival (plus the copy's bytes)
       mbar_init(empty0 + 8u * s, 1);  // the one consumer warp that took the unit
@@ -641,30 +668,27 @@ __global__ void __launch_bounds__((Cfg<M>::kConsumers + kProducers) * 32, 1)
 
   // Count this warp's units in, lane t taking its t-th unit: a release atomic
   // per unit (the warp barrier orders every lane's partial stores before it).
-  // A unit that completes its row block has the warp finish that row block.
-  if (s_abort) return;
+  // The units that complete a row block put it on the CTA's list; after a
+  // barrier, the CTA's consumer warps finish the listed row blocks in parallel.
+  // Every consumer warp reaches the barrier below, aborted or not.
   __syncwarp();
-  for (int t0 = 0; warp + t0 * ncw < n_units; t0 += 32) {
-    const int t = t0 + lane;
-    const int pos = warp + t * ncw;
-    int urb = -1;
-    if (pos < n_units) {
-      int ug;
-      ord.at(uint32_t(pos), ug, urb);
+  if (!s_abort) {
+    for (int t = lane; warp + t * ncw < n_units; t += 32) {
+      int ug, urb;
+      ord.at(uint32_t(warp + t * ncw), ug, urb);
       uint32_t old;
       asm volatile("atom.release.gpu.global.add.u32 %0, [%1], 1;" : "=r"(old) : "l"(a.counters + urb) : "memory");
-      if (old != uint32_t(a.groups - 1)) urb = -1;
+      if (old == uint32_t(a.groups - 1)) s_fin[atomicAdd(&s_nfin, 1)] = urb;
     }
-    uint32_t last = __ballot_sync(0xffffffffu, urb >= 0);
-    if (last) asm volatile("fence.acq_rel.gpu;" ::: "memory");
-    while (last) {
-      const int src = __ffs(last) - 1;
-      last &= last - 1;
-      const int frb = __shfl_sync(0xffffffffu, urb, src);
-      finish_row_block<XT, M>(a, frb, lane);
-      __syncwarp();
-      if (lane == 0) a.counters[frb] = 0u;
-    }
+  }
+  named_bar_sync(1, ncons);
+  if (s_abort) return;  // final by now: the producers have stopped
+  const int nfin = s_nfin;
+  if (warp < nfin) asm volatile("fence.acq_rel.gpu;" ::: "memory");
+  for (int f = warp; f < nfin; f += ncw) {
+    finish_row_block<XT, M>(a, s_fin[f], lane);
+    __syncwarp();
+    if (lane == 0) a.counters[s_fin[f]] = 0u;
   }
 }
 
@@ -731,6 +755,7 @@ int launch_t(const CUtensorMap& map, const XtabArgs& a0, const DeviceInfo& di, c
   }
   int64_t grid = di.sm_count;
   if (grid > a.units) grid = a.units;
+  if ((a.units + grid - 1) / grid > kMaxFinish) return BNBQ_ERR_UNSUPPORTED;  // a CTA lists its completions
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(unsigned(grid));
   cfg.blockDim = dim3(unsigned(nwarps * 32));
