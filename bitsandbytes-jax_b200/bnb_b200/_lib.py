@@ -142,15 +142,14 @@ _WORKSPACES: dict[tuple[int, int], torch.Tensor] = {}
 
 
 def workspace(device: torch.device, stream: int, nbytes: int) -> torch.Tensor:
-    """A zero-filled device buffer of at least `nbytes` for the kernels that
-    split K across SMs, one per (device, stream): calls on one stream are
-    ordered, and each call leaves the buffer zero-filled again. Allocated on
-    first use (inside a CUDA graph capture the zero-fill becomes part of the
-    graph) and kept for the life of the process."""
+    """A device buffer of at least `nbytes` for the kernels that split K
+    across SMs (their partial sums; no initial contents needed), one per
+    (device, stream) so that the calls sharing one are ordered. Allocated on
+    first use and kept for the life of the process."""
     key = (device.index, stream)
     ws = _WORKSPACES.get(key)
     if ws is None or ws.numel() < nbytes:
-        ws = torch.zeros(max(nbytes, 1 << 20), dtype=torch.uint8, device=device)
+        ws = torch.empty(max(nbytes, 1 << 20), dtype=torch.uint8, device=device)
         _WORKSPACES[key] = ws
     return ws
 

@@ -42,20 +42,20 @@
 // pairs); the consumer warps take the units round-robin, copy a unit's codes
 // into registers (releasing the stage at once) and fetch their row's scale
 // words one unit ahead. Every unit's 32 (x M) float32 results go to the
-// caller's workspace; when a warp has finished its units it counts each in
-// (one release atomic per unit and row block) and the unit that completes a
-// row block has its warp add the row block's partials in a fixed order, round
-// once to x's dtype, write y and put the counter back to zero. Results are
-// therefore deterministic.
+// caller's workspace. A second, small kernel (launched right behind, waiting
+// for this one with griddepcontrol.wait, so that all partials are visible
+// without fences or counters) adds each row's partials in a fixed order,
+// rounds once to x's dtype and writes y. Results are deterministic, and the
+// workspace needs no initial contents.
 //
 // Every mbarrier wait is bounded in time; on an expiry the CTA stops working,
-// still waits (bounded) for every copy it issued, counts the expiry
-// (bnbq_wait_timeouts) and leaves y and the row-block counters it touched
-// unfinished: the caller then clears the workspace before reusing it.
+// still waits (bounded) for every copy it issued and counts the expiry
+// (bnbq_wait_timeouts); y is then wrong.
 //
-// Programmatic dependent launch: the producer starts streaming codes before
-// the previous kernel on the stream has finished (the weight is an input that
-// kernel does not write); x, the workspace and y are touched only after
+// Programmatic dependent launch: the producers start streaming codes, and
+// the consumers load the double-quantization constants, before the previous
+// kernel on the stream has finished (the weight is an input that kernel does
+// not write); x, the workspace and y are touched only after
 // griddepcontrol.wait.
 #include <cuda.h>
 #include <cudaTypedefs.h>
@@ -75,7 +75,6 @@ constexpr int kRows = 32;               // weight rows per unit (one per lane)
 constexpr int kMaxStages = 56;
 constexpr int kProducers = 2;  // producer warps per CTA (TMA issue is per-thread latency-bound)
 constexpr int kMaxDevices = 64;
-constexpr int kMaxFinish = 512;  // row blocks one CTA can complete (at most its units)
 
 template <int M>
 struct Cfg {
@@ -96,7 +95,6 @@ struct XtabArgs {
   const float* code2;
   const float* offset;
   void* y;
-  uint32_t* counters;  // [row_blocks], zero between calls
   float* partial;      // [row_blocks][groups][M][32]
   int64_t n_rows, ldy, block0, units;
   int k, log2_bs, log2_bs2, groups, row_blocks;
@@ -396,44 +394,42 @@ __device__ __forceinline__ void unit_dot(const uint32_t (&cw)[NB][Walk<M, NB>::W
   }
 }
 
-// Row block rb, once all its groups are in: sum its partials (fixed order),
-// round, store.
+// The reduction of the split-K partials: y[m, r] = round(sum over groups, in
+// order, of partial[rb][g][m][r % 32]). A CTA of kRedThreads threads takes one
+// row block and one row of x: thread t adds the groups g = t / 32, t / 32 + 8,
+// ... of row t % 32, and the eight warps' sums are added in warp order.
+constexpr int kRedThreads = 256;
+
 template <typename XT, int M>
-__device__ __forceinline__ void finish_row_block(const XtabArgs& a, int64_t rb, int lane) {
-  const float* part = a.partial + rb * int64_t(a.groups) * M * kRows;
-  const int nf4 = a.groups * M * 8;  // float4 pieces of the row block
-  float4 s = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
-  constexpr int kBatch = 16;
-  for (int t0 = lane; t0 < nf4; t0 += 32 * kBatch) {
-    float4 v[kBatch];
+__global__ void __launch_bounds__(kRedThreads) gemv_xtab_reduce_kernel(const float* partial, int groups,
+                                                                       int row_blocks, int64_t n_rows, void* y,
+                                                                       int64_t ldy) {
+  __shared__ float s_sum[kRedThreads / 32][kRows];
+  asm volatile("griddepcontrol.launch_dependents;");
+  asm volatile("griddepcontrol.wait;" ::: "memory");  // every partial of the GEMV kernel is visible
+  const int rb = int(blockIdx.x) / M, m = int(blockIdx.x) % M;
+  const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+  const float* p = partial + (int64_t(rb) * groups * M + m) * kRows + lane;
+  constexpr int kBatch = 8;
+  float sum = 0.0f;
+  for (int g0 = w; g0 < groups; g0 += 8 * kBatch) {
+    float v[kBatch];
 #pragma unroll
     for (int b = 0; b < kBatch; ++b) {
-      const int f = t0 + 32 * b;
-      v[b] = f < nf4 ? ldcg4(part + 4 * f) : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+      const int g = g0 + 8 * b;
+      v[b] = g < groups ? __ldcg(p + int64_t(g) * M * kRows) : 0.0f;
     }
 #pragma unroll
-    for (int b = 0; b < kBatch; ++b) {
-      s.x += v[b].x;
-      s.y += v[b].y;
-      s.z += v[b].z;
-      s.w += v[b].w;
-    }
+    for (int b = 0; b < kBatch; ++b) sum += v[b];
   }
-  // lanes with the same (x row, 4 weight rows) hold partial sums of different groups
+  s_sum[w][lane] = sum;
+  __syncthreads();
+  if (w == 0) {
+    float t = s_sum[0][lane];
 #pragma unroll
-  for (int d = 8 * M; d < 32; d <<= 1) {
-    s.x += __shfl_xor_sync(0xffffffffu, s.x, d);
-    s.y += __shfl_xor_sync(0xffffffffu, s.y, d);
-    s.z += __shfl_xor_sync(0xffffffffu, s.z, d);
-    s.w += __shfl_xor_sync(0xffffffffu, s.w, d);
-  }
-  if (lane < 8 * M) {
-    const int m = (lane >> 3) % M;
-    const int64_t r0 = rb * kRows + 4 * (lane & 7);
-    const float vals[4] = {s.x, s.y, s.z, s.w};
-#pragma unroll
-    for (int e = 0; e < 4; ++e)
-      if (r0 + e < a.n_rows) store_y<XT>(a.y, int64_t(m) * a.ldy + r0 + e, vals[e]);
+    for (int i = 1; i < kRedThreads / 32; ++i) t += s_sum[i][lane];
+    const int64_t r = int64_t(rb) * kRows + lane;
+    if (r < n_rows) store_y<XT>(y, int64_t(m) * ldy + r, t);
   }
 }
 
@@ -490,8 +486,6 @@ __global__ void __launch_bounds__((Cfg<M>::kConsumers + kProducers) * 32, 1)
   __shared__ __align__(8) uint64_t s_bar[2 * kMaxStages];
   __shared__ volatile int s_abort;
   __shared__ volatile int s_next[kProducers];
-  __shared__ int s_fin[kMaxFinish];  // row blocks this CTA completed
-  __shared__ int s_nfin;
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int ncw = int(blockDim.x >> 5) - kProducers;  // consumer warps; the last kProducers warps produce
@@ -513,7 +507,6 @@ __global__ void __launch_bounds__((Cfg<M>::kConsumers + kProducers) * 32, 1)
   if (threadIdx.x == 0) {
     s_abort = S < Cfg<M>::kRound || dyn0 + a.dyn_bytes < tab + kTabBytes;  // (the host sizes the launch for this)
     for (int q = 0; q < kProducers; ++q) s_next[q] = -1;  // set by producer q when it stops
-    s_nfin = 0;
     for (int s = 0; s < S; ++s) {
       mbar_init(full0 + 8u * s, 1);   // the producer's arrival (plus the copy's bytes)
       mbar_init(empty0 + 8u * s, 1);  // the one consumer warp that took the unit
@@ -572,13 +565,13 @@ __global__ void __launch_bounds__((Cfg<M>::kConsumers + kProducers) * 32, 1)
   }
 
   // ---------------------------------------------------------------- consumers
-  asm volatile("griddepcontrol.wait;" ::: "memory");  // x, workspace and y: after the previous kernel
   const int ncons = ncw * 32;
   float offset = 0.0f;
-  if constexpr (NESTED) {
+  if constexpr (NESTED) {  // constants of the weight: before waiting for the previous kernel
     for (int i = threadIdx.x; i < 256; i += ncons) s_code2[i] = a.code2[i];
     offset = *a.offset;
   }
+  asm volatile("griddepcontrol.wait;" ::: "memory");  // x and the workspace: after the previous kernel
   const Walk<M, NB> wk(lane);
   // word (p, s): code at row_codes + cb[p] + co[s]; table base tp[p] + to[s]
   uint32_t cb[NB], co[WB], tp[NB], to[WB];
@@ -666,30 +659,6 @@ __global__ void __launch_bounds__((Cfg<M>::kConsumers + kProducers) * 32, 1)
     seg = seg_end;
   }
 
-  // Count this warp's units in, lane t taking its t-th unit: a release atomic
-  // per unit (the warp barrier orders every lane's partial stores before it).
-  // The units that complete a row block put it on the CTA's list; after a
-  // barrier, the CTA's consumer warps finish the listed row blocks in parallel.
-  // Every consumer warp reaches the barrier below, aborted or not.
-  __syncwarp();
-  if (!s_abort) {
-    for (int t = lane; warp + t * ncw < n_units; t += 32) {
-      int ug, urb;
-      ord.at(uint32_t(warp + t * ncw), ug, urb);
-      uint32_t old;
-      asm volatile("atom.release.gpu.global.add.u32 %0, [%1], 1;" : "=r"(old) : "l"(a.counters + urb) : "memory");
-      if (old == uint32_t(a.groups - 1)) s_fin[atomicAdd(&s_nfin, 1)] = urb;
-    }
-  }
-  named_bar_sync(1, ncons);
-  if (s_abort) return;  // final by now: the producers have stopped
-  const int nfin = s_nfin;
-  if (warp < nfin) asm volatile("fence.acq_rel.gpu;" ::: "memory");
-  for (int f = warp; f < nfin; f += ncw) {
-    finish_row_block<XT, M>(a, s_fin[f], lane);
-    __syncwarp();
-    if (lane == 0) a.counters[s_fin[f]] = 0u;
-  }
 }
 
 // --------------------------------------------------------------- host side
@@ -707,17 +676,15 @@ PFN_cuTensorMapEncodeTiled_v12000 encoder() {
   return fn;
 }
 
-// Workspace: a fixed region of row-block counters (which must stay zero
-// between calls, whatever shapes share the workspace), then the partials.
-constexpr int64_t kMaxRowBlocks = 16384;  // n_rows <= 524288
-constexpr int64_t kCounterBytes = kMaxRowBlocks * 4;
+// Workspace: the partials of the split K (any initial contents).
+constexpr int64_t kMaxRowBlocks = int64_t(1) << 24;
 
 int64_t workspace_bytes_for(int m, int k, int64_t n_rows) {
   const int gk = m == 1 ? Cfg<1>::kGroupK : Cfg<2>::kGroupK;
   const int mm = m == 1 ? 1 : 2;
   const int64_t rbs = (n_rows + kRows - 1) / kRows;
   const int64_t groups = k / gk;
-  return kCounterBytes + rbs * groups * mm * kRows * 4;
+  return rbs * groups * mm * kRows * 4;
 }
 
 // Dynamic shared memory of a launch: all the block may have, less its static
@@ -755,7 +722,6 @@ int launch_t(const CUtensorMap& map, const XtabArgs& a0, const DeviceInfo& di, c
   }
   int64_t grid = di.sm_count;
   if (grid > a.units) grid = a.units;
-  if ((a.units + grid - 1) / grid > kMaxFinish) return BNBQ_ERR_UNSUPPORTED;  // a CTA lists its completions
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(unsigned(grid));
   cfg.blockDim = dim3(unsigned(nwarps * 32));
@@ -767,6 +733,14 @@ int launch_t(const CUtensorMap& map, const XtabArgs& a0, const DeviceInfo& di, c
   cfg.attrs = attr;
   cfg.numAttrs = 1;
   if (cudaLaunchKernelEx(&cfg, kern, map, a) != cudaSuccess) return BNBQ_ERR_CUDA;
+  // the reduction, behind it on the stream
+  cudaLaunchConfig_t rc = cfg;
+  rc.gridDim = dim3(unsigned(int64_t(a.row_blocks) * M));
+  rc.blockDim = dim3(kRedThreads);
+  rc.dynamicSmemBytes = 0;
+  if (cudaLaunchKernelEx(&rc, gemv_xtab_reduce_kernel<XT, M>, static_cast<const float*>(a.partial), a.groups,
+                         a.row_blocks, a.n_rows, a.y, a.ldy) != cudaSuccess)
+    return BNBQ_ERR_CUDA;
   return launch_status();
 }
 
@@ -794,7 +768,7 @@ int launch_rows(int mm, const XtabArgs& base, const uint8_t* w, bool nested, con
   a.groups = base.k / gk;
   a.row_blocks = int((base.n_rows + kRows - 1) / kRows);
   a.units = int64_t(a.groups) * a.row_blocks;
-  a.partial = reinterpret_cast<float*>(reinterpret_cast<char*>(a.counters) + kCounterBytes);
+
   auto encode = encoder();
   if (!encode) return BNBQ_ERR_CUDA;
   CUtensorMap map;
@@ -857,7 +831,7 @@ int gemv_xtab_launch(int dtype, const void* x, int m, int k, const uint8_t* w, i
   a.absmax2 = absmax2;
   a.code2 = code2;
   a.offset = offset;
-  a.counters = static_cast<uint32_t*>(workspace);
+  a.partial = static_cast<float*>(workspace);
   a.n_rows = n_rows;
   a.ldy = ldy;
   a.block0 = absmax2_block0;

@@ -152,19 +152,16 @@ BNBQ_API int bnbq_matmul_nf4(int dtype, const void* x, int32_t m, int32_t k,
 
 /* bnbq_gemv_nf4 / bnbq_matmul_nf4 with a workspace: device memory the caller
  * allocates once (bnbq_gemv_workspace_bytes gives its size for a shape; one
- * buffer as large as the largest serves every shape), zero-filled before its
- * first use, and passes to every call; each call that completes leaves the
- * part that must start at zero (its first 64 KB) zero again. With it,
- * 1 <= m <= 4 (and n_rows <= 524288) runs the
- * shared-memory pair-table GEMV, whose split of K across SMs adds its
- * partial sums there (a fixed order: the results are deterministic); other
- * shapes, or a workspace that is NULL or too small, run the kernels of
- * bnbq_gemv_nf4. Calls that share a workspace must be ordered on one stream.
- * After a bounded device wait has expired (bnbq_wait_timeouts), clear the
- * workspace before its next use. Same numerics contract and one-hot exactness
- * as bnbq_gemv_nf4. The weight codes and scales are read before the kernel
- * waits for the preceding kernel on the stream (programmatic dependent
- * launch); x is read and y written after it. */
+ * buffer as large as the largest serves every shape; its contents need no
+ * initial value) and passes to every call. With it, 1 <= m <= 4 runs the
+ * shared-memory pair-table GEMV, which splits K across the SMs and writes
+ * its partial sums there; a second kernel adds them in a fixed order (the
+ * results are deterministic). Other shapes, or a workspace that is NULL or
+ * too small, run the kernels of bnbq_gemv_nf4. Calls that share a workspace
+ * must be ordered on one stream. Same numerics contract and one-hot
+ * exactness as bnbq_gemv_nf4. The weight codes and scales are read before
+ * the kernel waits for the preceding kernel on the stream (programmatic
+ * dependent launch); x is read and y written after it. */
 BNBQ_API int bnbq_gemv_nf4_ws(int dtype, const void* x, int32_t m, int32_t k,
                      const uint8_t* w, int64_t n_rows, int32_t blocksize,
                      const float* absmax, const uint8_t* absmax_q, const float* absmax2,

@@ -3,9 +3,9 @@ multiple of 256) on the B200: one-hot x returns the dequantized weights
 bitwise at every blocksize, plain and double-quantized scales, both x dtypes;
 random x matches the oracle's float64 product within the stated tolerance and
 the workspace-free kernels' results within it too; results are deterministic
-(bitwise equal across calls) and the workspace is left reusable (zero
-counters) by every call, eagerly and from a CUDA graph; partial row blocks,
-row shards of a double-quantized weight and a wider output buffer."""
+(bitwise equal across calls) and do not depend on the workspace's earlier
+contents, eagerly and from a CUDA graph; partial row blocks, row shards of a
+double-quantized weight and a wider output buffer."""
 from __future__ import annotations
 
 import ctypes as C
@@ -53,14 +53,10 @@ def call(entry, x, w, n, ws=None, out=None, block0=0, data=None, scales=None):
 
 
 def new_ws(m, k, n):
+    """A workspace full of garbage (the kernels need no initial contents)."""
     nb = _lib.gemv_workspace_bytes(m, k, n)
     assert nb > 0
-    return torch.zeros(nb, dtype=torch.uint8, device="cuda")
-
-
-def counters_zero(ws, n):
-    rbs = -(-n // 32)
-    return bool((ws[: 4 * rbs] == 0).all())
+    return torch.full((nb,), 0xA5, dtype=torch.uint8, device="cuda")
 
 
 @pytest.mark.parametrize("double_quant", [False, True])
@@ -78,7 +74,6 @@ def test_table_gemv_one_hot_bitwise(cuda, blocksize, double_quant):
             y = call("bnbq_gemv_nf4_ws", x, w, n, ws)
             torch.cuda.synchronize()
             assert torch.equal(y, dense[:, cols].T), (dtype, m)
-            assert counters_zero(ws, n)
 
 
 @pytest.mark.parametrize("m", [1, 2, 3, 4])
@@ -100,7 +95,6 @@ def test_table_gemv_tolerance_against_oracle(cuda, shape, m):
     # the workspace-free kernels agree within the same tolerance
     y_old = O.bf16_to_f32(to_host(call("bnbq_gemv_nf4", x, w, n))).reshape(m, n).astype(np.float64)
     assert np.all(np.abs(yd - y_old) <= 2 * GEMV_RTOL * np.abs(y64) + 2 * GEMV_ATOL * yabs)
-    assert counters_zero(ws, n)
 
 
 def test_table_gemv_takes_the_benchmark_shapes(cuda):
@@ -119,7 +113,7 @@ def test_table_gemv_takes_the_benchmark_shapes(cuda):
 
 def test_table_gemv_deterministic_and_reusable(cuda):
     """Bitwise equal results over repeated calls on one workspace (the fixed
-    summation order), and every call leaves the counters at zero."""
+    summation order)."""
     n, k = 4096, 14336
     w = weight(n, k, seed=5)
     x = torch.randn(1, k, device="cuda").to(torch.bfloat16)
@@ -127,8 +121,6 @@ def test_table_gemv_deterministic_and_reusable(cuda):
     first = call("bnbq_gemv_nf4_ws", x, w, n, ws).clone()
     for _ in range(5):
         assert torch.equal(call("bnbq_gemv_nf4_ws", x, w, n, ws), first)
-    torch.cuda.synchronize()
-    assert counters_zero(ws, n)
 
 
 def test_table_gemv_in_cuda_graph(cuda):
@@ -152,7 +144,6 @@ def test_table_gemv_in_cuda_graph(cuda):
         for o, ref in zip(outs, want):
             assert torch.equal(o, ref)
     del graph
-    assert counters_zero(ws, n)
 
 
 def test_table_gemv_row_shard_and_wide_output(cuda):
@@ -177,11 +168,10 @@ def test_table_gemv_row_shard_and_wide_output(cuda):
 
 
 def test_table_gemv_one_workspace_many_shapes(cuda):
-    """One workspace shared by calls of different shapes (the partial sums of
-    one shape land where another shape's row-block counts are not)."""
+    """One workspace shared by calls of different shapes, in turn."""
     shapes = [(160, 512), (4096, 14336), (1000, 4096), (14336, 4096), (33, 256)]
     nbytes = max(_lib.gemv_workspace_bytes(m, k, n) for n, k in shapes for m in (1, 2, 4))
-    ws = torch.zeros(nbytes, dtype=torch.uint8, device="cuda")
+    ws = torch.full((nbytes,), 0x5A, dtype=torch.uint8, device="cuda")
     for rep in range(2):
         for i, (n, k) in enumerate(shapes):
             w = weight(n, k, seed=30 + i)
