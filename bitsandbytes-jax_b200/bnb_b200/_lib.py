@@ -36,6 +36,7 @@ _SIGNATURES = {
     "bnbq_matmul_nf4_ws": "iPiiPliPPPPPilPlPlP",
     "bnbq_gemv_workspace_bytes": "iilP",
     "bnbq_gemv_route": "iiliPiPlP",
+    "bnbq_set_gemv_policy": "i",
     "bnbq_rcp_approx_ftz": "PPlP",
     "bnbq_version": "",
     "bnbq_wait_timeouts": "P",
@@ -161,6 +162,12 @@ def gemv_workspace_bytes(m: int, k: int, n_rows: int) -> int:
 
 
 ROUTE_TABLE_GEMV, ROUTE_GEMV, ROUTE_GEMM = 1, 2, 3
+POLICY_AUTO, POLICY_TABLE, POLICY_NO_TABLE = 0, 1, 2
+
+
+def set_gemv_policy(policy: int) -> None:
+    """Which GEMV the workspace entry points use where both apply (POLICY_*)."""
+    check(lib().bnbq_set_gemv_policy(int(policy)), "bnbq_set_gemv_policy")
 
 
 def gemv_route(m: int, k: int, n_rows: int, blocksize: int, absmax_q_ptr, blocksize2: int, ws_ptr, ws_bytes: int) -> int:

@@ -1186,6 +1186,12 @@ int gemv_xtab_applies(int m, int k, int64_t n_rows, int blocksize, const uint8_t
                       const void* workspace, int64_t workspace_bytes);
 }  // namespace bnbq
 
+namespace bnbq {
+int gemv_xtab_set_policy(int policy);
+}  // namespace bnbq
+
+extern "C" int bnbq_set_gemv_policy(int32_t policy) { return gemv_xtab_set_policy(policy); }
+
 extern "C" int bnbq_gemv_route(int32_t m, int32_t k, int64_t n_rows, int32_t blocksize, const uint8_t* absmax_q,
                                int32_t blocksize2, const void* workspace, int64_t workspace_bytes, int32_t* route) {
   if (!route || m < 1 || k < 1 || n_rows < 1) return BNBQ_ERR_INVALID;

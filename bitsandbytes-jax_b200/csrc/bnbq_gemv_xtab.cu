@@ -76,12 +76,15 @@ constexpr int kMaxStages = 56;
 constexpr int kProducers = 2;  // producer warps per CTA (TMA issue is per-thread latency-bound)
 constexpr int kMaxDevices = 64;
 
+constexpr int gcd(int a, int b) { return b == 0 ? a : gcd(b, a % b); }
+constexpr int lcm(int a, int b) { return a / gcd(a, b) * b; }
+
 template <int M>
 struct Cfg {
   // consumer warps; the ring is a whole number of rounds of them, so a slot is
   // always taken by the same consumer warp and filled by the same producer
   static constexpr int kConsumers = M == 1 ? 11 : 14;
-  static constexpr int kRound = kConsumers * kProducers / (kConsumers % kProducers == 0 ? kProducers : 1);
+  static constexpr int kRound = lcm(kConsumers, kProducers);
   static constexpr int kGroupK = M == 1 ? 256 : 128;          // elements of K per table
   static constexpr int kWords = kGroupK / 8;                   // 32-bit code words per row and group
   static constexpr uint32_t kStageBytes = kRows * kWords * 4;  // 4 KB / 2 KB of codes per unit
@@ -224,12 +227,15 @@ __device__ __forceinline__ void build_table(uint32_t tab, const float (&xs)[M][8
   const int jq = M == 1 ? lane : (lane & 15);
   const int slot = M == 1 ? cw : 2 * cw + (lane >> 4);
   const int nslots = M == 1 ? ncw : 2 * ncw;
+  const float t_lane = kNF4Table[lane & 15];
 #pragma unroll
   for (int jl = 0; jl < 4; ++jl) {
     for (int hi = ((slot - 16 * jl) % nslots + nslots) % nslots; hi < 16; hi += nslots) {
+      // (one row of x: hi is the same across the warp; two rows: the halves may differ)
+      const float thi = M == 1 ? __shfl_sync(0xffffffffu, t_lane, hi) : kNF4Table[hi];
       float u[M];
 #pragma unroll
-      for (int m = 0; m < M; ++m) u[m] = __fmul_rn(kNF4Table[hi], xs[m][2 * jl]);
+      for (int m = 0; m < M; ++m) u[m] = __fmul_rn(thi, xs[m][2 * jl]);
       const uint32_t base = tab + entry_offset<M>(4 * jq + jl, hi * 16);
 #pragma unroll
       for (int lo = 0; lo < 16; ++lo) {
@@ -348,7 +354,9 @@ __device__ __forceinline__ void unit_dot(const uint32_t (&cw)[NB][Walk<M, NB>::W
                                          float (&acc)[M]) {
   constexpr int WB = Walk<M, NB>::WB;
   constexpr int kBatch = WB < 8 ? WB : 8;
-  constexpr int kOff1 = 1 << 7, kOff2 = 1 << 16, kOff3 = (1 << 16) | (1 << 7);  // pairs j & 3 = 1, 2, 3
+  // pairs j & 3 = 1, 2, 3: entry offsets 128, 64 K, 64 K + 128 from pair 0's; the 64 K is
+  // added to the base (a second base register) rather than to the load
+  constexpr int kOff1 = 1 << 7, kOff3 = 1 << 7;
 #pragma unroll
   for (int p = 0; p < NB; ++p) {
     float2 ps[M];
@@ -361,11 +369,11 @@ __device__ __forceinline__ void unit_dot(const uint32_t (&cw)[NB][Walk<M, NB>::W
 #pragma unroll
         for (int j = 0; j < kBatch; ++j) {
           const uint32_t c = cw[p][s0 + j];
-          const uint32_t tw = tp[p] + to[s0 + j];
+          const uint32_t tw = tp[p] + to[s0 + j], tw2 = tw + (1u << 16);
           v[j][0] = lds_f32<0>(__byte_perm(c, tw, 0x7604));
           v[j][1] = lds_f32<kOff1>(__byte_perm(c, tw, 0x7614));
-          v[j][2] = lds_f32<kOff2>(__byte_perm(c, tw, 0x7624));
-          v[j][3] = lds_f32<kOff3>(__byte_perm(c, tw, 0x7634));
+          v[j][2] = lds_f32<0>(__byte_perm(c, tw2, 0x7624));
+          v[j][3] = lds_f32<kOff3>(__byte_perm(c, tw2, 0x7634));
         }
 #pragma unroll
         for (int j = 0; j < kBatch; ++j)
@@ -375,11 +383,11 @@ __device__ __forceinline__ void unit_dot(const uint32_t (&cw)[NB][Walk<M, NB>::W
 #pragma unroll
         for (int j = 0; j < kBatch; ++j) {
           const uint32_t c = cw[p][s0 + j];
-          const uint32_t tw = tp[p] + to[s0 + j];
+          const uint32_t tw = tp[p] + to[s0 + j], tw2 = tw + (1u << 16);
           v[j][0] = lds_f32x2<0>(__byte_perm(c, tw, 0x7604));
           v[j][1] = lds_f32x2<kOff1>(__byte_perm(c, tw, 0x7614));
-          v[j][2] = lds_f32x2<kOff2>(__byte_perm(c, tw, 0x7624));
-          v[j][3] = lds_f32x2<kOff3>(__byte_perm(c, tw, 0x7634));
+          v[j][2] = lds_f32x2<0>(__byte_perm(c, tw2, 0x7624));
+          v[j][3] = lds_f32x2<kOff3>(__byte_perm(c, tw2, 0x7634));
         }
 #pragma unroll
         for (int j = 0; j < kBatch; ++j) {
@@ -643,7 +651,7 @@ __global__ void __launch_bounds__((Cfg<M>::kConsumers + kProducers) * 32, 1)
       decode_scales<NB, NESTED>(a_rot, sw, a, s_code2, offset, wk.al);
       const int gc = g, rbc = rb;
       if (i + ncw < n_units) {
-        ord.at(uint32_t(i + ncw), g, rb);
+        ord.advance(uint32_t(i), uint32_t(ncw), g, rb);
         fetch_scales<M, NB, NESTED>(sw, a, g, rb, lane);
       }
       if (ok) {
@@ -787,6 +795,12 @@ int launch_rows(int mm, const XtabArgs& base, const uint8_t* w, bool nested, con
 
 }  // namespace
 
+int gemv_xtab_set_policy(int policy) {
+  if (policy < 0 || policy > 2) return BNBQ_ERR_INVALID;
+  g_table_policy.store(policy, std::memory_order_relaxed);
+  return BNBQ_OK;
+}
+
 // Bytes of workspace the table GEMV needs for m rows of x (0 when it does not
 // apply to m).
 int64_t gemv_xtab_workspace_bytes(int m, int k, int64_t n_rows) {
@@ -796,11 +810,19 @@ int64_t gemv_xtab_workspace_bytes(int m, int k, int64_t n_rows) {
 
 // BNBQ_ERR_UNSUPPORTED when the table GEMV does not take this call (the caller
 // then uses the other GEMV kernels).
+// Which GEMV a call with a workspace gets: 0 automatic -- the table GEMV when
+// the weight has at least 1.5 output rows per element of K (wide weights:
+// there it measured faster; the streaming row kernels win on long rows) --,
+// 1 the table GEMV whenever it applies, 2 never.
+std::atomic<int> g_table_policy{0};
+
 // BNBQ_OK when the table GEMV takes a call of this shape (with a workspace of
 // workspace_bytes at `workspace`), else BNBQ_ERR_UNSUPPORTED (or a device error).
 int gemv_xtab_applies(int m, int k, int64_t n_rows, int blocksize, const uint8_t* absmax_q, int blocksize2,
                       const void* workspace, int64_t workspace_bytes) {
   if (m < 1 || m > 4 || !workspace || n_rows < 1 || n_rows > kMaxRowBlocks * kRows) return BNBQ_ERR_UNSUPPORTED;
+  const int policy = g_table_policy.load(std::memory_order_relaxed);
+  if (policy == 2 || (policy == 0 && 2 * n_rows < 3 * int64_t(k))) return BNBQ_ERR_UNSUPPORTED;
   if (k % Cfg<1>::kGroupK != 0) return BNBQ_ERR_UNSUPPORTED;  // (covers the two-row group too)
   const int l2 = log2_exact(blocksize);
   if (l2 < 5) return BNBQ_ERR_UNSUPPORTED;

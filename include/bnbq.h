@@ -184,6 +184,13 @@ enum bnbq_route { BNBQ_ROUTE_TABLE_GEMV = 1, BNBQ_ROUTE_GEMV = 2, BNBQ_ROUTE_GEM
 BNBQ_API int bnbq_gemv_route(int32_t m, int32_t k, int64_t n_rows, int32_t blocksize, const uint8_t* absmax_q,
                              int32_t blocksize2, const void* workspace, int64_t workspace_bytes, int32_t* route);
 
+/* Which GEMV bnbq_gemv_nf4_ws / bnbq_matmul_nf4_ws use when both apply:
+ * 0 (default) by shape -- the pair-table GEMV for weights with at least 1.5
+ * output rows per element of K, the streaming row kernels otherwise --, 1 the
+ * pair-table GEMV whenever it applies, 2 never. Process-wide; for tests and
+ * tuning. No counterpart in the reference. */
+BNBQ_API int bnbq_set_gemv_policy(int32_t policy);
+
 /* Workspace bytes bnbq_gemv_nf4_ws / bnbq_matmul_nf4_ws use for an (m x k) x
  * and an n_rows x k weight (0: that shape needs none). */
 BNBQ_API int bnbq_gemv_workspace_bytes(int32_t m, int32_t k, int64_t n_rows, int64_t* bytes);

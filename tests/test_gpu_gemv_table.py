@@ -19,7 +19,15 @@ from bnb_b200 import _lib
 from helpers import GEMV_ATOL, GEMV_RTOL, to_host
 from oracle import oracle as O
 
-pytestmark = [pytest.mark.gpu, pytest.mark.usefixtures("timeouts_at_start")]
+pytestmark = [pytest.mark.gpu, pytest.mark.usefixtures("timeouts_at_start", "table_policy")]
+
+
+@pytest.fixture(scope="module")
+def table_policy(cuda):
+    """This module tests the table GEMV at every shape it applies to."""
+    _lib.set_gemv_policy(_lib.POLICY_TABLE)
+    yield
+    _lib.set_gemv_policy(_lib.POLICY_AUTO)
 
 
 def weight(n, k, blocksize=64, double_quant=True, seed=0, std=0.02):
@@ -109,6 +117,15 @@ def test_table_gemv_takes_the_benchmark_shapes(cuda):
                 assert route == _lib.ROUTE_TABLE_GEMV, (n, k, m, dq, route)
     assert _lib.gemv_route(5, 14336, 4096, 64, None, 0, None, 0) == _lib.ROUTE_GEMV
     assert _lib.gemv_route(21, 14336, 4096, 64, None, 0, None, 0) == _lib.ROUTE_GEMM
+    # the automatic policy: wide weights take the table GEMV, long rows the streaming kernels
+    _lib.set_gemv_policy(_lib.POLICY_AUTO)
+    try:
+        ws = new_ws(1, 4096, 14336)
+        assert _lib.gemv_route(1, 4096, 14336, 64, None, 256, ws.data_ptr(), ws.numel()) == _lib.ROUTE_TABLE_GEMV
+        ws = new_ws(1, 14336, 4096)
+        assert _lib.gemv_route(1, 14336, 4096, 64, None, 256, ws.data_ptr(), ws.numel()) == _lib.ROUTE_GEMV
+    finally:
+        _lib.set_gemv_policy(_lib.POLICY_TABLE)
 
 
 def test_table_gemv_deterministic_and_reusable(cuda):
