@@ -76,6 +76,13 @@ constexpr int kMaxStages = 56;
 constexpr int kProducers = 2;  // producer warps per CTA (TMA issue is per-thread latency-bound)
 constexpr int kMaxDevices = 64;
 
+// Which GEMV a call with a workspace gets: 0 automatic -- the table GEMV when
+// the weight has at least 1.5 output rows per element of K (wide weights:
+// there it measured faster; the streaming row kernels win on long rows) --,
+// 1 the table GEMV whenever it applies, 2 never.
+std::atomic<int> g_table_policy{0};
+
+
 constexpr int gcd(int a, int b) { return b == 0 ? a : gcd(b, a % b); }
 constexpr int lcm(int a, int b) { return a / gcd(a, b) * b; }
 
@@ -810,12 +817,6 @@ int64_t gemv_xtab_workspace_bytes(int m, int k, int64_t n_rows) {
 
 // BNBQ_ERR_UNSUPPORTED when the table GEMV does not take this call (the caller
 // then uses the other GEMV kernels).
-// Which GEMV a call with a workspace gets: 0 automatic -- the table GEMV when
-// the weight has at least 1.5 output rows per element of K (wide weights:
-// there it measured faster; the streaming row kernels win on long rows) --,
-// 1 the table GEMV whenever it applies, 2 never.
-std::atomic<int> g_table_policy{0};
-
 // BNBQ_OK when the table GEMV takes a call of this shape (with a workspace of
 // workspace_bytes at `workspace`), else BNBQ_ERR_UNSUPPORTED (or a device error).
 int gemv_xtab_applies(int m, int k, int64_t n_rows, int blocksize, const uint8_t* absmax_q, int blocksize2,
