@@ -19,7 +19,8 @@ back every step. `m_sweep` repeats the device timing at M = 2..20.
 Multi-GPU (torchrun, one process per GPU): the north star's split. The
 weight is partitioned by output rows (row_partition, whole nested blocks per
 rank); a step is every rank's fused GEMV on its rows followed by the NVLink
-all-gather of y (PeerGather: one kernel, peer stores, bounded handshakes), so
+all-gather of y (PeerGather: one kernel that stores {value, epoch} words into
+every peer's inbox over NVLink and polls its own inbox, bounded), so
 every rank holds the full (M, 4096) product when the step ends -- strong
 scaling of one call. Each rank rotates 8 x N copies of its shard (242 MB per
 rank whatever N is, more than L2). Before timing, every rank checks the
@@ -46,7 +47,8 @@ quantize and dequantize of 2^28+37 elements, f32/f16/bf16, blocksizes 256 and
 the Llama-3-70B MLP shapes at M = 64, 512, 2048, beside dequantize + matmul).
 `--workload llama` is config 4: a Llama-3-8B decode stack (32 layers x q, k,
 v, o, gate, up, down; NF4 bs 64 double-quantized) with every GEMV sharded by
-output rows across the torchrun ranks and its y all-gathered (NCCL); one
+output rows across the torchrun ranks and its y all-gathered (PeerGather, or
+NCCL with --gather nccl); one
 step is one pass over the 224 matrices, captured in a CUDA graph.
 
 `--impl reference` times the reference's arithmetic on the host cores: the
@@ -236,7 +238,6 @@ def time_device(torch, step, steps: int, warmup: int, device, dist=None):
 def make_step(torch, shards, x, ranges, rank, world, pg):
     """One call: the fused GEMV on this rank's rows (+ the all-gather of y)."""
     from bnb_b200.kernels import gemv_nf4
-    from bnb_b200.parallel import matmul_rows
     m = x.shape[0]
     copies = len(shards)
     if world == 1:
@@ -251,13 +252,8 @@ def make_step(torch, shards, x, ranges, rank, world, pg):
             gemv_nf4(x, d, aq, N_ROWS, BS, nested=nested, out=ys[i % copies])
             return ys[i % copies]
         return step
-    col0 = ranges[rank][0]
-    n_local = ranges[rank][1] - col0
-    ys = [torch.empty(m, n_local, dtype=torch.bfloat16, device=x.device) for _ in range(2)]
-
-    def step(i):
-        y = matmul_rows(x, shards[i % copies].rs, out=ys[i % 2])
-        return pg.gather(y, col0)
+    def step(i):  # the rank's rows and the exchange in one call
+        return pg.matmul(x, shards[i % copies].rs)
     return step
 
 
@@ -376,11 +372,8 @@ def run_ours(args, dist, rank, world, local_rank):
         def e2e_call(xd, i):
             return bnb.matmul(xd, shards[i % copies].full)
     else:
-        from bnb_b200.parallel import matmul_rows
-        n_local = ranges[rank][1] - ranges[rank][0]
-
         def e2e_call(xd, i):
-            return pg.gather(matmul_rows(xd, shards[i % copies].rs), ranges[rank][0])
+            return pg.matmul(xd, shards[i % copies].rs)
     e2e_ms, h2d, d2h = time_e2e(torch, e2e_call, device, args.m, e2e_steps, args.warmup, dist)
 
     extras = {}
@@ -428,7 +421,7 @@ def run_ours(args, dist, rank, world, local_rank):
         "e2e": {"value": round(algo_bytes(args.m) * e2e_steps / (e2e_ms * 1e-3) / 1e9, 2), "unit": "GB/s",
                 "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
                 "us_per_step": round(e2e_ms / e2e_steps * 1e3, 3)},
-        "gpu_launches": args.steps * (2 if world > 1 else 1),
+        "gpu_launches": args.steps * launches_per_call(args.m, route, world),
         "clocks": clocks.summary(),
     }
     if sweep:
@@ -440,6 +433,18 @@ def run_ours(args, dist, rank, world, local_rank):
 
 
 GEMV_MAX_ROWS = 20
+
+
+def launches_per_call(m: int, route: int, world: int) -> int:
+    """Kernels one timed call launches: the table GEMV is two (partials, then
+    their reduction), the streaming GEMV and the GEMM one; M = 3, 4 take two
+    passes; at N > 1 the exchange rides in the GEMV's epilogue for M <= 2 and
+    is one more kernel otherwise."""
+    from bnb_b200 import _lib
+    per = 2 if route == _lib.ROUTE_TABLE_GEMV else 1
+    if route != _lib.ROUTE_GEMM and 3 <= m <= 4:
+        per *= 2
+    return per + (1 if world > 1 and m > 2 else 0)
 
 
 def roofline_entry(m, per_call_ms, peak, peak_kind, world, kernel):
@@ -596,20 +601,25 @@ def run_gemm_workload(args, local_rank):
 
 
 LLAMA8B = [(4096, 4096), (1024, 4096), (1024, 4096), (4096, 4096), (14336, 4096), (14336, 4096), (4096, 14336)]
+# the same weights with q/k/v stacked into one matrix and gate/up into another
+# (one GEMV and one exchange for each group): 4 matrices a layer
+LLAMA8B_GROUPED = [(6144, 4096), (4096, 4096), (28672, 4096), (4096, 14336)]
 
 
-def llama_pass(args, dist, rank, world, local_rank, m: int = 1, gather: str = "peer"):
+def llama_pass(args, dist, rank, world, local_rank, m: int = 1, gather: str = "peer", grouped: bool = True):
     """Config 4: device time of one pass over a Llama-3-8B decode stack (32
-    layers x 7 NF4 matrices), every GEMV row-sharded over the ranks and its y
-    all-gathered. Max over ranks; every rank returns the same dict."""
+    layers of q, k, v, o, gate, up, down; q/k/v and gate/up stacked into one
+    NF4 matrix each when `grouped`), every GEMV row-sharded over the ranks and
+    its y all-gathered. Max over ranks; every rank returns the same dict."""
     import torch
     from bnb_b200.parallel import PeerGather, all_gather_rows, matmul_rows, quantize_shard, row_partition, shard_rows
     device = torch.device("cuda", local_rank)
     layers = 32
     shards, plans = [], []
     weight_bytes = 0
-    for i in range(layers * len(LLAMA8B)):
-        n, k = LLAMA8B[i % len(LLAMA8B)]
+    mats = LLAMA8B_GROUPED if grouped else LLAMA8B
+    for i in range(layers * len(mats)):
+        n, k = mats[i % len(mats)]
         ranges = row_partition(n, k, BS * BS2, world)  # whole nested blocks per rank
         a, b = ranges[rank]
         g = torch.Generator(device).manual_seed(1000 + i)  # the same full weight on every rank
@@ -626,16 +636,16 @@ def llama_pass(args, dist, rank, world, local_rank, m: int = 1, gather: str = "p
     g = torch.Generator(device).manual_seed(5)
     xs = {k: torch.randn(m, k, device=device, generator=g).to(torch.bfloat16) for k in (4096, 14336)}
     peer = gather == "peer" and world > 1
-    pgs = {n: PeerGather(m, n, torch.bfloat16, device) for n in sorted({n for n, _ in LLAMA8B})} if peer else {}
+    pgs = {n: PeerGather(m, n, torch.bfloat16, device) for n in sorted({n for n, _ in mats})} if peer else {}
 
     def step():
         for sh, ranges in zip(shards, plans):
+            if peer:  # the rank's rows and the exchange in one call
+                pgs[sh.n_rows_total].matmul(xs[sh.k], sh)
+                continue
             y = matmul_rows(xs[sh.k], sh)
             if world > 1:
-                if peer:
-                    pgs[sh.n_rows_total].gather(y, sh.start)
-                else:
-                    all_gather_rows(y, ranges)
+                all_gather_rows(y, ranges)
 
     for _ in range(3):
         step()
@@ -675,7 +685,8 @@ def llama_pass(args, dist, rank, world, local_rank, m: int = 1, gather: str = "p
     per = float(ms_t.item()) / steps
     del shards, xs
     torch.cuda.empty_cache()
-    return {"workload": "Llama-3-8B decode stack, 32 layers x 7 NF4 matrices (bs64 nested), M=%d" % m,
+    shape = ("4 NF4 matrices (q|k|v and gate|up stacked)" if grouped else "7 NF4 matrices")
+    return {"workload": f"Llama-3-8B decode stack, 32 layers x {shape} (bs64 nested), M={m}",
             "ms_per_pass": round(per, 4), "weight_gbs": round(weight_bytes / (per * 1e-3) / 1e9, 1),
             "weight_bytes_per_pass": weight_bytes, "n_gpus": world,
             "exchange": "NVLink peer stores" if peer else ("NCCL" if world > 1 else "none"),
@@ -686,7 +697,7 @@ def run_llama_workload(args, dist, rank, world, local_rank):
     import torch
     torch.cuda.set_device(local_rank)
     with ClockSampler(local_rank) as clocks:
-        c4 = llama_pass(args, dist, rank, world, local_rank, args.m, args.gather)
+        c4 = llama_pass(args, dist, rank, world, local_rank, args.m, args.gather, not args.ungrouped)
     if rank != 0:
         return None
     return {"metric": "Llama-3-8B NF4 decode stack: effective weight GB/s, every GEMV row-sharded + all-gathered (config 4)",
@@ -750,6 +761,7 @@ def main():
     ap.add_argument("--no-extras", action="store_true", help="skip the config 1/3/4/5 keys")
     ap.add_argument("--workload", choices=["gemv", "quant", "gemm", "llama"], default="gemv")
     ap.add_argument("--gather", choices=["peer", "nccl"], default="peer", help="config 4 all-gather")
+    ap.add_argument("--ungrouped", action="store_true", help="config 4 with q/k/v and gate/up as separate GEMVs")
     args = ap.parse_args()
 
     world = int(os.environ.get("WORLD_SIZE", "1"))

@@ -34,14 +34,15 @@ _SIGNATURES = {
     "bnbq_matmul_nf4": "iPiiPliPPPPPilPlP",
     "bnbq_gemv_nf4_ws": "iPiiPliPPPPPilPlPlP",
     "bnbq_matmul_nf4_ws": "iPiiPliPPPPPilPlPlP",
+    "bnbq_matmul_nf4_allgather": "iPiiPliPPPPPilPlllPlPiiPlP",
     "bnbq_gemv_workspace_bytes": "iilP",
     "bnbq_gemv_route": "iiliPiPlP",
     "bnbq_set_gemv_policy": "i",
     "bnbq_rcp_approx_ftz": "PPlP",
     "bnbq_version": "",
     "bnbq_wait_timeouts": "P",
-    "bnbq_peer_allgather_rows": "iPillllPPPiiP",
-    "bnbq_peer_allgather_rows_noalloc": "iPillllPPiiiP",
+    "bnbq_peer_allgather_rows": "iPilllPllPlPiiP",
+    "bnbq_peer_allgather_rows_noalloc": "iPilllPllPliiiP",
     "bnbq_peer_allgather_noalloc_setup": "",
     "bnbq_peer_allgather_noalloc_reset": "iP",
     "bnbq_set_wait_limit_ns": "u",

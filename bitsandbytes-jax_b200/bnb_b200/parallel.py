@@ -185,17 +185,18 @@ def _ipc_close(device: torch.device, handle: bytes) -> None:
 class PeerGather:
     """All-gather of row-sharded outputs through NVLink peer memory.
 
-    Every rank allocates a full output buffer (``max_rows`` x ``n_total``), a
-    flag array and a small state word; the buffers are shared with the other
-    ranks through CUDA IPC (torch's tensor reduction, handles exchanged with
-    ``all_gather_object``). :meth:`gather` then enqueues ONE kernel
-    (``bnbq_peer_allgather_rows``) that stores this rank's slice into every
-    rank's buffer and waits, bounded, for the peers' slices -- no NCCL call on
-    the data path. Construct it on every rank of ``group`` (a collective).
-    The returned tensor is a view of this rank's buffer. It stays valid until
-    this rank's next :meth:`gather` runs on the stream: a peer stores into it
-    only after this rank's next gather kernel has started, so work enqueued
-    in between may read it."""
+    Every rank allocates an inbox of ``2 * max_rows * n_total`` 8-byte words
+    (zeroed), shared with the other ranks through CUDA IPC (handles exchanged
+    with ``all_gather_object``), a full output buffer that only it writes, and
+    a small state word. :meth:`gather` then enqueues ONE kernel
+    (``bnbq_peer_allgather_rows``): it stores this rank's slice into every
+    peer's inbox as {value, epoch} words, copies it into the output, and fills
+    the other columns from this rank's own inbox as the peers' words arrive
+    (bounded waits) -- no NCCL call and no handshake on the data path.
+    Construct it on every rank of ``group`` (a collective), and call
+    :meth:`gather` on every rank in the same order. The returned tensor (a
+    view of this rank's buffer, or ``out``) stays valid until this rank's
+    next :meth:`gather` on the stream."""
 
     def __init__(self, max_rows: int, n_total: int, dtype: torch.dtype, device: torch.device, group=None):
         import ctypes as C
@@ -207,7 +208,7 @@ class PeerGather:
         self.dtype = dtype
         self.device = torch.device(device)
         self.y_full = torch.zeros((max_rows, n_total), dtype=dtype, device=device)
-        self.flags = torch.zeros(2 * self.world, dtype=torch.int32, device=device)  # done | ready epochs
+        self.inbox = torch.zeros(2 * max_rows * n_total, dtype=torch.int64, device=device)
         self.state = torch.zeros(2, dtype=torch.int32, device=device)
         torch.cuda.synchronize(device)
 
@@ -218,44 +219,83 @@ class PeerGather:
                 _lib.call("bnbq_ipc_handle", t.data_ptr(), C.cast(h, C.c_void_p), C.addressof(off))
             return h.raw, off.value
 
-        mine = (export(self.y_full), export(self.flags))
         objs: list = [None] * self.world
-        dist.all_gather_object(objs, mine, group=group)
+        dist.all_gather_object(objs, export(self.inbox), group=group)
         self._opened: list[bytes] = []  # the peers' handles mapped here
-        y_ptrs, f_ptrs = [], []
-        for r, ((hy, oy), (hf, of)) in enumerate(objs):
+        ptrs = []
+        for r, (h, off) in enumerate(objs):
             if r == self.rank:
-                y_ptrs.append(self.y_full.data_ptr())
-                f_ptrs.append(self.flags.data_ptr())
+                ptrs.append(self.inbox.data_ptr())
                 continue
-            y_ptrs.append(_ipc_open(self.device, hy) + oy)
-            f_ptrs.append(_ipc_open(self.device, hf) + of)
-            self._opened += [hy, hf]
-        self.y_ptrs = torch.tensor(y_ptrs, dtype=torch.int64, device=device)
-        self.f_ptrs = torch.tensor(f_ptrs, dtype=torch.int64, device=device)
+            ptrs.append(_ipc_open(self.device, h) + off)
+            self._opened.append(h)
+        self.inbox_ptrs = torch.tensor(ptrs, dtype=torch.int64, device=device)
         dist.barrier(group=group)
 
     def close(self) -> None:
-        """Unmap the peers' buffers (every rank, after its last gather has completed)."""
+        """Unmap the peers' inboxes (every rank, after its last gather has completed)."""
         torch.cuda.synchronize(self.device)
         for handle in self._opened:
             _ipc_close(self.device, handle)
         self._opened = []
 
-    def gather(self, y_local: torch.Tensor, col0: int) -> torch.Tensor:
+    def _out(self, m: int, dtype, out):
+        if m > self.max_rows or dtype != self.dtype:
+            raise ValueError(f"{m} rows of {dtype} do not fit this gather ({self.max_rows} rows, {self.dtype})")
+        if out is None:
+            return self.y_full[:m]
+        if out.shape != (m, self.n_total) or out.dtype != self.dtype or out.stride(1) != 1:
+            raise ValueError(f"out {tuple(out.shape)} {out.dtype} is not an ({m}, {self.n_total}) {self.dtype} "
+                             "matrix with unit column stride")
+        return out
+
+    def matmul(self, x: torch.Tensor, shard: RowShard, out: torch.Tensor | None = None) -> torch.Tensor:
+        """``x @ W.T`` in full on every rank: this rank's rows of W (``shard``)
+        and the exchange in one call (``bnbq_matmul_nf4_allgather``). For
+        M <= 2 the matmul kernel itself stores its rows into the peers'
+        inboxes and collects theirs (no separate exchange kernel). Bitwise
+        :func:`matmul_rows` on every rank's rows, gathered."""
+        from . import _lib
+        from .kernels.gemv import GEMV_MAX_M, _prepare
+        if x.dim() != 2 or x.shape[1] != shard.k or shard.n_rows_total != self.n_total:
+            raise ValueError(f"x {tuple(x.shape)} and a ({shard.n_rows_total}, {shard.k}) weight do not match "
+                             f"this gather's {self.n_total} columns")
+        m, k = x.shape
+        out = self._out(m, x.dtype, out)
+        n = shard.n_rows
+        ptrs = (None,) * 6
+        bs2 = 0
+        xs = x
+        if n > 0:
+            xs, w, (a, aq, a2, c2, off, bs2) = _prepare(x, shard.data, shard.absmax, n, shard.blocksize,
+                                                         shard.nested, "matmul")
+            ptrs = (w, a, aq, a2, c2, off)
+        stream = _lib.stream_of(xs)
+        wsb = _lib.gemv_workspace_bytes(m, k, n) if n > 0 and m <= GEMV_MAX_M else 0
+        ws = _lib.workspace(x.device, stream, wsb) if wsb else None
+        w, a, aq, a2, c2, off = (_lib.ptr(t) for t in ptrs)
+        with torch.cuda.device(x.device):
+            _lib.call("bnbq_matmul_nf4_allgather", _lib.DTYPE_CODE[x.dtype], xs.data_ptr(), m, k, w, n,
+                      shard.blocksize, a, aq, a2, c2, off, bs2, shard.block0, out.data_ptr(), self.n_total,
+                      out.stride(0), shard.start, self.inbox_ptrs.data_ptr(), self.inbox.numel(),
+                      self.state.data_ptr(), self.world, self.rank, _lib.ptr(ws), 0 if ws is None else ws.numel(),
+                      stream)
+        return out
+
+    def gather(self, y_local: torch.Tensor, col0: int, out: torch.Tensor | None = None) -> torch.Tensor:
         """Columns [col0, col0 + y_local.shape[1]) from this rank, the rest
-        from the peers: the full (m, n_total) output."""
+        from the peers: the full (m, n_total) output, in ``out`` if given (an
+        (m, n_total) tensor of y's dtype with unit column stride)."""
         from . import _lib
         m, n_local = y_local.shape
-        if m > self.max_rows or y_local.dtype != self.dtype:
-            raise ValueError(f"y {tuple(y_local.shape)} {y_local.dtype} does not fit this gather "
-                             f"({self.max_rows} rows, {self.dtype})")
+        out = self._out(m, y_local.dtype, out)
         assert y_local.stride(1) == 1
         with torch.cuda.device(y_local.device):
             _lib.call("bnbq_peer_allgather_rows", _lib.DTYPE_CODE[y_local.dtype], y_local.data_ptr(), m, n_local,
-                      y_local.stride(0), col0, self.n_total, self.y_ptrs.data_ptr(), self.f_ptrs.data_ptr(),
-                      self.state.data_ptr(), self.world, self.rank, _lib.stream_of(y_local))
-        return self.y_full[:m]
+                      y_local.stride(0), col0, out.data_ptr(), self.n_total, out.stride(0),
+                      self.inbox_ptrs.data_ptr(), self.inbox.numel(), self.state.data_ptr(), self.world, self.rank,
+                      _lib.stream_of(y_local))
+        return out
 
 
 def matmul_sharded(x: torch.Tensor, shard: RowShard, ranges: list[tuple[int, int]] | None = None,

@@ -16,9 +16,11 @@ int gemv_launch(int dtype, const void* x, int32_t m, int32_t k, const uint8_t* w
 int gemv_wait_timeouts(unsigned int* out);
 int gemm_wait_timeouts(unsigned int* out);
 int peer_wait_timeouts(unsigned int* out);
+int xtab_wait_timeouts(unsigned int* out);
 int gemv_set_wait_limit(uint64_t ns);
 int gemm_set_wait_limit(uint64_t ns);
 int peer_set_wait_limit(uint64_t ns);
+int xtab_set_wait_limit(uint64_t ns);
 int gemm_launch(int dtype, const void* x, int32_t m, int32_t k, const uint8_t* w, int64_t n_rows,
                 int32_t blocksize, const float* absmax, const uint8_t* absmax_q,
                 const float* absmax2, const float* code2, const float* offset, int32_t blocksize2,
@@ -112,10 +114,12 @@ extern "C" int bnbq_wait_timeouts(unsigned int* count) {
   if (!count) return BNBQ_ERR_INVALID;
   DeviceInfo di;
   if (int st = device_info(&di)) return st;
-  unsigned int g = 0, h = 0, p = 0;
-  if (gemv_wait_timeouts(&g) != 0 || gemm_wait_timeouts(&h) != 0 || peer_wait_timeouts(&p) != 0)
+  // one counter per source file with bounded waits (each has its own copy)
+  unsigned int g = 0, h = 0, p = 0, t = 0;
+  if (gemv_wait_timeouts(&g) != 0 || gemm_wait_timeouts(&h) != 0 || peer_wait_timeouts(&p) != 0 ||
+      xtab_wait_timeouts(&t) != 0)
     return BNBQ_ERR_CUDA;
-  *count = g + h + p;
+  *count = g + h + p + t;
   return BNBQ_OK;
 }
 
@@ -137,7 +141,8 @@ extern "C" int bnbq_enable_peer_access(int peer_device) {
 extern "C" int bnbq_set_wait_limit_ns(uint64_t ns) {
   DeviceInfo di;
   if (int st = device_info(&di)) return st;
-  if (gemv_set_wait_limit(ns) != 0 || gemm_set_wait_limit(ns) != 0 || peer_set_wait_limit(ns) != 0)
+  if (gemv_set_wait_limit(ns) != 0 || gemm_set_wait_limit(ns) != 0 || peer_set_wait_limit(ns) != 0 ||
+      xtab_set_wait_limit(ns) != 0)
     return BNBQ_ERR_CUDA;
   return BNBQ_OK;
 }

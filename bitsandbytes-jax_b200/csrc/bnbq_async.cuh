@@ -32,9 +32,17 @@ constexpr uint64_t kWaitLimitNs = BNBQ_WAIT_LIMIT_DEFAULT_NS;
 // shorten it to make a wait expire on purpose; 0 restores the default.
 static __device__ uint64_t g_bnbq_wait_limit_ns = kWaitLimitNs;
 
+// Waits for another GPU (the row-shard exchange) get a longer limit: a peer
+// may legitimately start a call much later than this rank.
+constexpr uint64_t kPeerWaitLimitNs = 10000000000ull;  // 10 s: a peer that is this late has failed
+static __device__ uint64_t g_bnbq_peer_wait_limit_ns = kPeerWaitLimitNs;
+
+// Sets both limits (ns for each; 0 restores the defaults).
 static inline int write_wait_limit(uint64_t ns) {
   const uint64_t v = ns ? ns : kWaitLimitNs;
-  return cudaMemcpyToSymbol(g_bnbq_wait_limit_ns, &v, sizeof(v)) == cudaSuccess ? 0 : -1;
+  const uint64_t vp = ns ? ns : kPeerWaitLimitNs;
+  if (cudaMemcpyToSymbol(g_bnbq_wait_limit_ns, &v, sizeof(v)) != cudaSuccess) return -1;
+  return cudaMemcpyToSymbol(g_bnbq_peer_wait_limit_ns, &vp, sizeof(vp)) == cudaSuccess ? 0 : -1;
 }
 
 __device__ __forceinline__ uint64_t global_ns() {

@@ -22,6 +22,7 @@
 // bitwise the value QuantizedArray.dequantize produces (array.py:95-108).
 #include "bnbq_async.cuh"
 #include "bnbq_common.cuh"
+#include "bnbq_peer.cuh"
 
 namespace bnbq {
 namespace {
@@ -41,6 +42,7 @@ struct GemvArgs {
   int k;
   int log2_bs;
   int log2_bs2;
+  PeerOut px;  // exchange mode (the bulk kernel only) when px.inbox != nullptr
 };
 
 template <typename XT>
@@ -53,6 +55,13 @@ template <typename XT>
 __device__ __forceinline__ void store_y(void* y, int64_t i, float v) {
   if constexpr (Elem<XT>::kDtype == BNBQ_BF16) static_cast<__nv_bfloat16*>(y)[i] = __float2bfloat16_rn(v);
   else static_cast<__half*>(y)[i] = __float2half_rn(v);
+}
+
+// v rounded to XT, as its 16 bits
+template <typename XT>
+__device__ __forceinline__ uint16_t bits_of(float v) {
+  if constexpr (Elem<XT>::kDtype == BNBQ_BF16) return __bfloat16_as_ushort(__float2bfloat16_rn(v));
+  else return __half_as_ushort(__float2half_rn(v));
 }
 
 constexpr int kMaxWarps = 16;
@@ -476,22 +485,32 @@ constexpr int kMaxStages = 8;
 constexpr int kMaxGroupsPerFlush = 32;  // partial sums held in shared memory between flushes
 
 // SIS: the block scales travel with the stage (a compile-time choice, so that
-// the other layout's registers and code drop out).
-template <typename XT, int M, int R, bool NESTED, int SLOTS, bool SIS>
+// the other layout's registers and code drop out). RG: the consumer warps form
+// RG equal groups, group i taking rows [i R/RG, (i + 1) R/RG) of every stage
+// (short rows: more warps than one row's chunks could keep busy).
+template <typename XT, int M, int R, bool NESTED, int SLOTS, bool SIS, int RG>
 __global__ void __launch_bounds__(kMaxWarps * 32, 1)
 gemv_bulk_kernel(GemvArgs a, int n_groups, int n_stages, uint32_t stage_bytes) {
+  static_assert(R % RG == 0, "row groups split the stage's rows evenly");
+  constexpr int RT = R / RG;  // rows of a stage per consumer thread
   constexpr bool scales_in_stage = SIS;
   __shared__ __align__(16) float s_code2[256];
   __shared__ float s_part[kMaxGroupsPerFlush][kMaxWarps - 1][M * R];
   __shared__ __align__(8) uint64_t s_tbl_bar;
   __shared__ __align__(8) uint64_t s_done_bar;
   __shared__ volatile int s_abort;  // set by any thread whose wait expired
+  __shared__ volatile int s_rx_expired;  // exchange mode: a wait for a peer expired
   char* stages = reinterpret_cast<char*>(s_pair) + kPairTableBytes;
   uint64_t* bars = reinterpret_cast<uint64_t*>(stages + size_t(n_stages) * stage_bytes);
   const int tid = threadIdx.x;
   const int lane = tid & 31, warp = tid >> 5;
   const int ncw = (blockDim.x >> 5) - 1;  // consumer warps; the last warp produces
   const int ncons = ncw * 32;
+  const int wpg = ncw / RG;        // warps per row group (the host makes ncw a multiple of RG)
+  const int gthreads = wpg * 32;   // threads per row group
+  const int rgi = tid / gthreads;  // this thread's row group (consumers)
+  const int lt = tid - rgi * gthreads;
+  const int r0 = rgi * RT;         // its first row of a stage
   const int cpr = a.k >> 5;
   const uint32_t row_bytes = uint32_t(a.k) >> 1;
   const int spr = a.k >> a.log2_bs;  // scales per row (when K % bs == 0)
@@ -504,6 +523,7 @@ gemv_bulk_kernel(GemvArgs a, int n_groups, int n_stages, uint32_t stage_bytes) {
   if (warp == ncw) {  // ------------------------------------------- producer
     if (lane == 0) {
       s_abort = 0;
+      s_rx_expired = 0;
       mbar_init(smem_u32(&s_tbl_bar), 1);
       mbar_init(smem_u32(&s_done_bar), uint32_t(ncw));
       for (int st = 0; st < n_stages; ++st) {
@@ -564,15 +584,15 @@ gemv_bulk_kernel(GemvArgs a, int n_groups, int n_stages, uint32_t stage_bytes) {
   // first block (K % bs == 0), or its global block for group g (otherwise)
   int cofs[SLOTS];
 #pragma unroll
-  for (int sl = 0; sl < SLOTS; ++sl) cofs[sl] = min(tid + sl * ncons, cpr - 1) * 32;
+  for (int sl = 0; sl < SLOTS; ++sl) cofs[sl] = min(lt + sl * gthreads, cpr - 1) * 32;
   auto block_of = [&](int g, int sl, int r) -> int64_t {
     const int64_t row = min(int64_t(g) * R + r, a.n_rows - 1);
     return (row * a.k + cofs[sl]) >> a.log2_bs;
   };
   // second-level scales (nested) two groups ahead; whole scales when they do
   // not travel with the stage
-  float pre0[SLOTS][R], pre1[SLOTS][R];
-  int preq0[SLOTS][R], preq1[SLOTS][R];
+  float pre0[SLOTS][RT], pre1[SLOTS][RT];
+  int preq0[SLOTS][RT], preq1[SLOTS][RT];
   // nested scales travelling with the stage: second-level scale of (slot,
   // row) = absmax2[(block0 + (g R + r) spr + bir[slot]) >> log2_bs2], in
   // 32-bit block numbers (the host checks that they fit)
@@ -580,32 +600,32 @@ gemv_bulk_kernel(GemvArgs a, int n_groups, int n_stages, uint32_t stage_bytes) {
 #pragma unroll
   for (int sl = 0; sl < SLOTS; ++sl) bir[sl] = cofs[sl] >> a.log2_bs;
   const int last_row_blk = int((a.n_rows - 1) * int64_t(spr));
-  auto prefetch = [&](int g, float (&p)[SLOTS][R], int (&q)[SLOTS][R]) {
+  auto prefetch = [&](int g, float (&p)[SLOTS][RT], int (&q)[SLOTS][RT]) {
     if (NESTED && scales_in_stage) {
       const int gb = g * (R * spr);  // the group's first block
 #pragma unroll
       for (int sl = 0; sl < SLOTS; ++sl)
 #pragma unroll
-        for (int r = 0; r < R; ++r) {
-          q[sl][r] = 0;
-          const int rb = min(gb + r * spr, last_row_blk);  // clamped rows: results dropped
-          p[sl][r] = g < n_groups ? __ldg(a.absmax2 + ((int(a.block0) + rb + bir[sl]) >> a.log2_bs2)) : 0.0f;
+        for (int rr = 0; rr < RT; ++rr) {
+          q[sl][rr] = 0;
+          const int rb = min(gb + (r0 + rr) * spr, last_row_blk);  // clamped rows: results dropped
+          p[sl][rr] = g < n_groups ? __ldg(a.absmax2 + ((int(a.block0) + rb + bir[sl]) >> a.log2_bs2)) : 0.0f;
         }
       return;
     }
 #pragma unroll
     for (int sl = 0; sl < SLOTS; ++sl)
 #pragma unroll
-      for (int r = 0; r < R; ++r) {
-        p[sl][r] = 0.0f;
-        q[sl][r] = 0;
+      for (int rr = 0; rr < RT; ++rr) {
+        p[sl][rr] = 0.0f;
+        q[sl][rr] = 0;
         if (g < n_groups && (NESTED || !scales_in_stage)) {
-          const int64_t blk = block_of(g, sl, r);
+          const int64_t blk = block_of(g, sl, r0 + rr);
           if constexpr (NESTED) {
-            p[sl][r] = __ldg(a.absmax2 + ((a.block0 + blk) >> a.log2_bs2));
-            if (!scales_in_stage) q[sl][r] = __ldg(a.absmax_q + blk);
+            p[sl][rr] = __ldg(a.absmax2 + ((a.block0 + blk) >> a.log2_bs2));
+            if (!scales_in_stage) q[sl][rr] = __ldg(a.absmax_q + blk);
           } else {
-            p[sl][r] = __ldg(a.absmax + blk);
+            p[sl][rr] = __ldg(a.absmax + blk);
           }
         }
       }
@@ -637,8 +657,8 @@ gemv_bulk_kernel(GemvArgs a, int n_groups, int n_stages, uint32_t stage_bytes) {
   bool ok = mbar_wait(smem_u32(&s_tbl_bar), 0);
   if (!ok) s_abort = 1;
 
-  constexpr int kBits = (M * R >= 8) ? 3 : (M * R >= 4 ? 2 : (M * R >= 2 ? 1 : 0));
-  // lanes whose low bits are zero hold one of the M*R warp sums after warp_reduce_many
+  constexpr int kBits = (M * RT >= 8) ? 3 : (M * RT >= 4 ? 2 : (M * RT >= 2 ? 1 : 0));
+  // lanes whose low bits are zero hold one of the M*RT warp sums after warp_reduce_many
   const bool holder = (lane & ((32 >> kBits) - 1)) == 0;
   const int hidx = lane >> (5 - kBits);
 
@@ -652,30 +672,30 @@ gemv_bulk_kernel(GemvArgs a, int n_groups, int n_stages, uint32_t stage_bytes) {
     const char* stage = stages + size_t(st) * stage_bytes;
 
     // a row's block scale, decoded where it is used (fewer live registers)
-    auto scale_of = [&](int sl, int r) -> float {
+    auto scale_of = [&](int sl, int rr) -> float {
       if (scales_in_stage) {
-        const int si = sidx0[sl] + r * spr;
+        const int si = sidx0[sl] + (r0 + rr) * spr;
         if constexpr (NESTED) {
           const int q2 = reinterpret_cast<const uint8_t*>(stage + codes_bytes)[si];
-          return add_rn(mul_ftz(s_code2[q2], pre0[sl][r]), offset);
+          return add_rn(mul_ftz(s_code2[q2], pre0[sl][rr]), offset);
         } else {
           return reinterpret_cast<const float*>(stage + codes_bytes)[si];
         }
       } else {
-        return NESTED ? add_rn(mul_ftz(s_code2[preq0[sl][r]], pre0[sl][r]), offset) : pre0[sl][r];
+        return NESTED ? add_rn(mul_ftz(s_code2[preq0[sl][rr]], pre0[sl][rr]), offset) : pre0[sl][rr];
       }
     };
 
-    float acc[M * R];
+    float acc[M * RT];
 #pragma unroll
-    for (int e = 0; e < M * R; ++e) acc[e] = 0.0f;
+    for (int e = 0; e < M * RT; ++e) acc[e] = 0.0f;
 #pragma unroll
     for (int sl = 0; sl < SLOTS; ++sl) {
-      const int c = tid + sl * ncons;
+      const int c = lt + sl * gthreads;
       if (c < cpr) {
 #pragma unroll
-        for (int r = 0; r < R; ++r) {
-          const uint4 cw = *reinterpret_cast<const uint4*>(stage + r * row_bytes + c * 16);
+        for (int r = 0; r < RT; ++r) {
+          const uint4 cw = *reinterpret_cast<const uint4*>(stage + (r0 + r) * row_bytes + c * 16);
           const uint32_t words[4] = {cw.x, cw.y, cw.z, cw.w};
           float2 t[M][4];
 #pragma unroll
@@ -696,9 +716,8 @@ gemv_bulk_kernel(GemvArgs a, int n_groups, int n_stages, uint32_t stage_bytes) {
           }
 #pragma unroll
           for (int m = 0; m < M; ++m) {
-            if (false) {}
             const float2 u = __fadd2_rn(__fadd2_rn(t[m][0], t[m][1]), __fadd2_rn(t[m][2], t[m][3]));
-            acc[m * R + r] = __fmaf_rn(scale_of(sl, r), u.x + u.y, acc[m * R + r]);
+            acc[m * RT + r] = __fmaf_rn(scale_of(sl, r), u.x + u.y, acc[m * RT + r]);
           }
         }
       }
@@ -708,24 +727,40 @@ gemv_bulk_kernel(GemvArgs a, int n_groups, int n_stages, uint32_t stage_bytes) {
     if (lane == 0) mbar_arrive(smem_u32(bars + n_stages + st));  // stage consumed
     if (++st == n_stages) { st = 0; phase ^= 1u; }
 
-    const float vs = warp_reduce_many<M * R>(acc, lane);
-    if (holder && hidx < M * R) s_part[gl][warp][hidx] = vs;
+    const float vs = warp_reduce_many<M * RT>(acc, lane);
+    if (holder && hidx < M * RT) s_part[gl][warp][hidx] = vs;
   }
 
   // Final sums: every consumer warp arrives on s_done (aborted or not); warp
-  // 0 waits for all of them (bounded) and stores y.
+  // 0 waits for all of them (bounded) and stores y. Row r of a stage is the
+  // sum, in warp order, of its row group's warps' entries m * RT + r % RT.
+  // Exchange mode: warp 0 also stores each value into the peers' inboxes;
+  // then every consumer thread polls its share of the other ranks' columns
+  // (the host launches at most one CTA per SM, so all CTAs are resident) and
+  // the CTA reports that it has finished the call.
   __syncwarp();
   if (lane == 0) mbar_arrive(smem_u32(&s_done_bar));
-  if (warp != 0) return;
-  if (!mbar_wait(smem_u32(&s_done_bar), 0) || s_abort) return;
-  for (int e = lane; e < gl * M * R; e += 32) {
-    const int gi = e / (M * R), idx = e % (M * R);
-    float v = 0.0f;
-    for (int w = 0; w < ncw; ++w) v += s_part[gi][w][idx];
-    const int m = idx / R, r = idx % R;
-    const int64_t row = (int64_t(blockIdx.x) + int64_t(gi) * gridDim.x) * R + r;
-    if (row < a.n_rows) store_y<XT>(a.y, int64_t(m) * a.ldy + row, v);
+  const bool exchange = a.px.inbox != nullptr;
+  const uint32_t epoch = exchange ? peer_epoch(a.px) : 0u;  // after griddepcontrol.wait
+  if (warp == 0 && mbar_wait(smem_u32(&s_done_bar), 0) && !s_abort) {
+    for (int e = lane; e < gl * M * R; e += 32) {
+      const int gi = e / (M * R), idx = e % (M * R);
+      const int m = idx / R, r = idx % R;
+      const int w0 = (r / RT) * wpg, pi = m * RT + r % RT;
+      float v = 0.0f;
+      for (int w = w0; w < w0 + wpg; ++w) v += s_part[gi][w][pi];
+      const int64_t row = (int64_t(blockIdx.x) + int64_t(gi) * gridDim.x) * R + r;
+      if (row < a.n_rows) {
+        store_y<XT>(a.y, int64_t(m) * a.ldy + row, v);
+        if (exchange) peer_send(a.px, epoch, m, row, bits_of<XT>(v));
+      }
+    }
   }
+  if (!exchange) return;
+  if (!peer_receive(a.px, epoch, M, a.n_rows, int64_t(blockIdx.x) * ncons + tid, int64_t(gridDim.x) * ncons))
+    s_rx_expired = 1;
+  named_bar_sync(2, ncons);
+  if (tid == 0) peer_finish_cta(a.px, epoch, s_rx_expired != 0);
 }
 
 struct BulkPlan {
@@ -733,27 +768,39 @@ struct BulkPlan {
   int ncw = 0;      // consumer warps
   int slots = 0;    // chunks per consumer thread and row
   int rows = 0;     // R
+  int groups = 1;   // RG: row groups of consumer warps
   uint32_t stage_bytes = 0;
 };
 
-// Chooses consumer warps (fewest idle lanes), rows per group and whether the
-// scales travel with the codes; stages are sized at launch.
+// Chooses the consumer warps -- RG row groups of W warps, each thread owning
+// `slots` 32-element chunks of its group's rows -- for the most lanes with
+// work (at least 3/4 of the lanes busy; ties: fewer slots, then fewer warps),
+// the rows per stage and whether the scales travel with the codes; stages are
+// sized at launch. Row groups split a 4-row stage (RG = 2, 4) or a 3-row one
+// (RG = 3).
 bool plan_bulk(int m, int k, int log2_bs, bool nested, int smem_optin, BulkPlan* p) {
   const int cpr = k >> 5;
-  double best_eff = -1.0;
-  for (int w = kMaxWarps - 1; w >= 4; --w) {
-    const int slots = (cpr + 32 * w - 1) / (32 * w);
-    if (slots * m > 2) continue;
-    const double eff = double(cpr) / double(slots * 32 * w);
-    if (eff > best_eff + 1e-9) { best_eff = eff; p->ncw = w; p->slots = slots; }
+  double best_busy = -1.0;
+  for (int rg = 1; rg <= 4; ++rg) {
+    for (int w = 2; w * rg <= kMaxWarps - 1; ++w) {
+      const int slots = (cpr + 32 * w - 1) / (32 * w);
+      if (slots * m > 2) continue;
+      const double eff = double(cpr) / double(slots * 32 * w);
+      if (eff < 0.75 || w * rg < 4 || (rg > 1 && slots > 1)) continue;
+      const double busy = eff * w * rg;
+      const bool better = busy > best_busy + 1e-9 ||
+                          (busy > best_busy - 1e-9 && (slots < p->slots || (slots == p->slots && w * rg < p->ncw)));
+      if (better) { best_busy = busy; p->ncw = w * rg; p->slots = slots; p->groups = rg; }
+    }
   }
-  if (p->ncw == 0 || best_eff < 0.75) return false;
+  if (p->ncw == 0) return false;
   const uint32_t row_bytes = uint32_t(k) >> 1;
   const bool whole_blocks = (k & ((1 << log2_bs) - 1)) == 0;
   const uint32_t srb = whole_blocks ? uint32_t(k >> log2_bs) * (nested ? 1u : 4u) : 0u;
   p->scales_in_stage = whole_blocks && (srb % 16 == 0);
   const size_t room = size_t(smem_optin) - size_t(kPairTableBytes) - 24 * 1024;  // static smem margin
-  for (int R : {4, 2, 1}) {
+  for (int R : {4, 3, 2, 1}) {
+    if (p->groups == 1 ? R == 3 : (p->groups == 3 ? R != 3 : R != 4)) continue;
     const uint32_t sb = uint32_t(R) * (row_bytes + (p->scales_in_stage ? srb : 0u));
     if (room / (sb + 16) >= 4) {
       p->rows = R;
@@ -764,10 +811,10 @@ bool plan_bulk(int m, int k, int log2_bs, bool nested, int smem_optin, BulkPlan*
   return false;
 }
 
-template <typename XT, int M, int R, bool NESTED, int SLOTS>
+template <typename XT, int M, int R, bool NESTED, int SLOTS, int RG = 1>
 int launch_bulk_t(const GemvArgs& a, const BulkPlan& p, const DeviceInfo& di, cudaStream_t s) {
-  auto kern = p.scales_in_stage ? gemv_bulk_kernel<XT, M, R, NESTED, SLOTS, true>
-                                : gemv_bulk_kernel<XT, M, R, NESTED, SLOTS, false>;
+  auto kern = p.scales_in_stage ? gemv_bulk_kernel<XT, M, R, NESTED, SLOTS, true, RG>
+                                : gemv_bulk_kernel<XT, M, R, NESTED, SLOTS, false, RG>;
   cudaFuncAttributes fa;
   if (cudaFuncGetAttributes(&fa, kern) != cudaSuccess) return BNBQ_ERR_CUDA;
   const size_t room = size_t(di.smem_optin) - size_t(kPairTableBytes) - fa.sharedSizeBytes - 1024;
@@ -785,6 +832,8 @@ int launch_bulk_t(const GemvArgs& a, const BulkPlan& p, const DeviceInfo& di, cu
   int64_t grid = n_groups < di.sm_count ? n_groups : di.sm_count;
   const int64_t min_grid = (n_groups + kMaxGroupsPerFlush - 1) / kMaxGroupsPerFlush;  // <= 32 groups per CTA
   if (grid < min_grid) grid = min_grid;
+  // the exchange polls for peers from every CTA: all of them must be resident
+  if (a.px.inbox && grid > di.sm_count) return BNBQ_ERR_UNSUPPORTED;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(unsigned(grid));
   cfg.blockDim = dim3((p.ncw + 1) * 32);
@@ -803,6 +852,15 @@ int launch_bulk_t(const GemvArgs& a, const BulkPlan& p, const DeviceInfo& di, cu
 template <typename XT, int M, bool NESTED>
 int launch_bulk(const GemvArgs& a, const BulkPlan& p, const DeviceInfo& di, cudaStream_t s) {
   if constexpr (M <= 2) {
+    if (p.groups > 1) {  // short rows: one chunk per thread, row groups over a 4- or 3-row stage
+      if (p.slots != 1) return BNBQ_ERR_UNSUPPORTED;
+      switch (p.groups) {
+        case 2: return launch_bulk_t<XT, M, 4, NESTED, 1, 2>(a, p, di, s);
+        case 3: return launch_bulk_t<XT, M, 3, NESTED, 1, 3>(a, p, di, s);
+        case 4: return launch_bulk_t<XT, M, 4, NESTED, 1, 4>(a, p, di, s);
+        default: return BNBQ_ERR_UNSUPPORTED;
+      }
+    }
     if (p.slots == 1) {
       switch (p.rows) {
         case 4: return launch_bulk_t<XT, M, 4, NESTED, 1>(a, p, di, s);
@@ -1175,10 +1233,43 @@ using namespace bnbq;
 
 namespace bnbq {
 int64_t gemv_xtab_workspace_bytes(int m, int k, int64_t n_rows);
+// The streaming kernel with the exchange in its epilogue (M <= 2, one pass),
+// y = px.y_full's own columns; BNBQ_ERR_UNSUPPORTED where that kernel does not
+// apply (the caller then runs the matmul and the standalone exchange).
+int gemv_exchange_launch(int dtype, const void* x, int32_t m, int32_t k, const uint8_t* w, int64_t n_rows,
+                         int32_t blocksize, const float* absmax, const uint8_t* absmax_q, const float* absmax2,
+                         const float* code2, const float* offset, int32_t blocksize2, int64_t absmax2_block0,
+                         const PeerOut& px, cudaStream_t s) {
+  if (m < 1 || m > 2) return BNBQ_ERR_UNSUPPORTED;
+  DeviceInfo di;
+  if (int st = device_info(&di)) return st;
+  GemvArgs a{};
+  a.x = x; a.w = w; a.absmax = absmax; a.absmax_q = absmax_q; a.absmax2 = absmax2;
+  a.code2 = code2; a.offset = offset; a.n_rows = n_rows;
+  a.y = static_cast<char*>(px.y_full) + size_t(px.col0) * 2;
+  a.ldy = px.ldf;
+  a.block0 = absmax2_block0; a.k = k; a.log2_bs = log2_exact(blocksize);
+  a.log2_bs2 = absmax_q ? log2_exact(blocksize2) : 0;
+  a.px = px;
+  const bool nested = absmax_q != nullptr;
+  if (nested && !aligned(code2, 16)) return BNBQ_ERR_UNSUPPORTED;
+  BulkPlan p;
+  if (!plan_bulk(m, k, a.log2_bs, nested, di.smem_optin, &p)) return BNBQ_ERR_UNSUPPORTED;
+  if (p.scales_in_stage &&
+      !aligned(nested ? static_cast<const void*>(absmax_q) : static_cast<const void*>(absmax), 16))
+    p.scales_in_stage = 0;
+  if (dtype == BNBQ_BF16) {
+    if (m == 1) return nested ? launch_bulk<__nv_bfloat16, 1, true>(a, p, di, s) : launch_bulk<__nv_bfloat16, 1, false>(a, p, di, s);
+    return nested ? launch_bulk<__nv_bfloat16, 2, true>(a, p, di, s) : launch_bulk<__nv_bfloat16, 2, false>(a, p, di, s);
+  }
+  if (m == 1) return nested ? launch_bulk<__half, 1, true>(a, p, di, s) : launch_bulk<__half, 1, false>(a, p, di, s);
+  return nested ? launch_bulk<__half, 2, true>(a, p, di, s) : launch_bulk<__half, 2, false>(a, p, di, s);
+}
+
 int gemv_xtab_launch(int dtype, const void* x, int m, int k, const uint8_t* w, int64_t n_rows, int blocksize,
                      const float* absmax, const uint8_t* absmax_q, const float* absmax2, const float* code2,
                      const float* offset, int blocksize2, int64_t absmax2_block0, void* y, int64_t ldy,
-                     void* workspace, int64_t workspace_bytes, cudaStream_t s);
+                     void* workspace, int64_t workspace_bytes, cudaStream_t s, const PeerOut* px = nullptr);
 }  // namespace bnbq
 
 namespace bnbq {
@@ -1226,6 +1317,60 @@ extern "C" int bnbq_gemv_nf4_ws(int dtype, const void* x, int32_t m, int32_t k, 
   if (st != BNBQ_ERR_UNSUPPORTED) return st;
   return gemv_launch(dtype, x, m, k, w, n_rows, blocksize, absmax, absmax_q, absmax2, code2, offset,
                      blocksize2, absmax2_block0, y, ldy, s);
+}
+
+namespace bnbq {
+int peer_make(int dtype, int32_t m, int64_t n_local, int64_t col0, void* y_full, int64_t n_total, int64_t ldy,
+              uint64_t* const* inbox, int64_t inbox_words, uint32_t* state, int32_t world, int32_t rank,
+              PeerOut* px);
+int peer_allgather_launch(const void* y_local, int32_t m, int64_t n_local, int64_t ld_local, const PeerOut& px,
+                          cudaStream_t stream);
+}  // namespace bnbq
+
+// The row-sharded matmul and its exchange in one call: M <= 2 runs ONE kernel
+// chain that computes this rank's rows and, in its epilogue, stores them into
+// the peers' inboxes and collects the other ranks' columns (the table GEMV's
+// reduction or the streaming GEMV); other shapes run the matmul into y_full's
+// own columns and then the standalone exchange kernel on them. The results
+// are those of bnbq_matmul_nf4_ws on the rank's rows, bitwise.
+extern "C" int bnbq_matmul_nf4_allgather(int dtype, const void* x, int32_t m, int32_t k, const uint8_t* w,
+                                         int64_t n_local, int32_t blocksize, const float* absmax,
+                                         const uint8_t* absmax_q, const float* absmax2, const float* code2,
+                                         const float* offset, int32_t blocksize2, int64_t absmax2_block0,
+                                         void* y_full, int64_t n_total, int64_t ldy, int64_t col0,
+                                         uint64_t* const* inbox, int64_t inbox_words, uint32_t* state,
+                                         int32_t world, int32_t rank, void* workspace, int64_t workspace_bytes,
+                                         void* stream) {
+  PeerOut px;
+  if (int st = peer_make(dtype, m, n_local, col0, y_full, n_total, ldy, inbox, inbox_words, state, world, rank, &px))
+    return st;
+  if (m < 1 || workspace_bytes < 0 || (workspace_bytes > 0 && !workspace)) return BNBQ_ERR_INVALID;
+  void* y_own = static_cast<char*>(y_full) + size_t(col0) * 2;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (n_local > 0) {
+    if (int st = gemv_validate(dtype, x, m, k, w, n_local, blocksize, absmax, absmax_q, absmax2, code2, offset,
+                               blocksize2, y_own, ldy))
+      return st;
+    if (world == 1)  // nothing to exchange
+      return bnbq_matmul_nf4_ws(dtype, x, m, k, w, n_local, blocksize, absmax, absmax_q, absmax2, code2, offset,
+                                blocksize2, absmax2_block0, y_own, ldy, workspace, workspace_bytes, stream);
+    if (m <= 2) {  // the kernel the plain call would run, in its exchange mode, when it has one
+      const int table = gemv_xtab_applies(m, k, n_local, blocksize, absmax_q, blocksize2, workspace,
+                                          workspace_bytes);
+      if (table != BNBQ_OK && table != BNBQ_ERR_UNSUPPORTED) return table;
+      const int st = table == BNBQ_OK
+                         ? gemv_xtab_launch(dtype, x, m, k, w, n_local, blocksize, absmax, absmax_q, absmax2, code2,
+                                            offset, blocksize2, absmax2_block0, y_own, ldy, workspace,
+                                            workspace_bytes, s, &px)
+                         : gemv_exchange_launch(dtype, x, m, k, w, n_local, blocksize, absmax, absmax_q, absmax2,
+                                                code2, offset, blocksize2, absmax2_block0, px, s);
+      if (st != BNBQ_ERR_UNSUPPORTED) return st;
+    }
+    if (int st = bnbq_matmul_nf4_ws(dtype, x, m, k, w, n_local, blocksize, absmax, absmax_q, absmax2, code2, offset,
+                                    blocksize2, absmax2_block0, y_own, ldy, workspace, workspace_bytes, stream))
+      return st;
+  }
+  return peer_allgather_launch(y_own, m, n_local, ldy, px, s);
 }
 
 extern "C" int bnbq_gemv_nf4(int dtype, const void* x, int32_t m, int32_t k, const uint8_t* w,

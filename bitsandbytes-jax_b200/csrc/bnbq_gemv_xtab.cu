@@ -36,10 +36,11 @@
 // split evenly over one CTA per SM, so a CTA's units span one group or two (the
 // table is rebuilt between them, all consumer warps at a barrier). Each CTA
 // processes its units starting from its first row block 0, so that all CTAs
-// walk the row blocks together and read whole rows of W at a time. A producer
-// warp streams each unit's 32 x GK/2 code bytes with one TMA load into a ring
-// of shared-memory stages placed around the table (mbarrier full/empty
-// pairs); the consumer warps take the units round-robin, copy a unit's codes
+// walk the row blocks together and read whole rows of W at a time. Two
+// producer warps, taking turns, stream each unit's 32 x GK/2 code bytes with
+// one TMA load into a ring of shared-memory stages placed around the table
+// (mbarrier full/empty pairs); the consumer warps take the units round-robin,
+// copy a unit's codes
 // into registers (releasing the stage at once) and fetch their row's scale
 // words one unit ahead. Every unit's 32 (x M) float32 results go to the
 // caller's workspace. A second, small kernel (launched right behind, waiting
@@ -65,6 +66,7 @@
 
 #include "bnbq_async.cuh"
 #include "bnbq_common.cuh"
+#include "bnbq_peer.cuh"
 
 namespace bnbq {
 namespace {
@@ -108,6 +110,7 @@ struct XtabArgs {
   float* partial;      // [row_blocks][groups][M][32]
   int64_t n_rows, ldy, block0, units;
   int k, log2_bs, log2_bs2, groups, row_blocks;
+  PeerOut px;  // exchange mode of the reduction (px.inbox != nullptr)
   uint32_t dyn_bytes;  // dynamic shared memory of the launch
 };
 
@@ -413,12 +416,16 @@ __device__ __forceinline__ void unit_dot(const uint32_t (&cw)[NB][Walk<M, NB>::W
 // order, of partial[rb][g][m][r % 32]). A CTA of kRedThreads threads takes one
 // row block and one row of x: thread t adds the groups g = t / 32, t / 32 + 8,
 // ... of row t % 32, and the eight warps' sums are added in warp order.
+// Exchange mode (px.inbox != nullptr; the host has checked that every CTA can
+// be resident at once): the rows are also stored into the peers' inboxes,
+// then every thread polls its share of the other ranks' columns into
+// px.y_full and the CTA reports that it has finished the call.
 constexpr int kRedThreads = 256;
 
 template <typename XT, int M>
 __global__ void __launch_bounds__(kRedThreads) gemv_xtab_reduce_kernel(const float* partial, int groups,
                                                                        int row_blocks, int64_t n_rows, void* y,
-                                                                       int64_t ldy) {
+                                                                       int64_t ldy, PeerOut px) {
   __shared__ float s_sum[kRedThreads / 32][kRows];
   asm volatile("griddepcontrol.launch_dependents;");
   asm volatile("griddepcontrol.wait;" ::: "memory");  // every partial of the GEMV kernel is visible
@@ -439,13 +446,26 @@ __global__ void __launch_bounds__(kRedThreads) gemv_xtab_reduce_kernel(const flo
   }
   s_sum[w][lane] = sum;
   __syncthreads();
+  const bool exchange = px.inbox != nullptr;
+  const uint32_t epoch = exchange ? peer_epoch(px) : 0u;  // after griddepcontrol.wait
   if (w == 0) {
     float t = s_sum[0][lane];
 #pragma unroll
     for (int i = 1; i < kRedThreads / 32; ++i) t += s_sum[i][lane];
     const int64_t r = int64_t(rb) * kRows + lane;
-    if (r < n_rows) store_y<XT>(y, int64_t(m) * ldy + r, t);
+    if (r < n_rows) {
+      store_y<XT>(y, int64_t(m) * ldy + r, t);
+      if (exchange) {
+        if constexpr (Elem<XT>::kDtype == BNBQ_BF16) peer_send(px, epoch, m, r, __bfloat16_as_ushort(__float2bfloat16_rn(t)));
+        else peer_send(px, epoch, m, r, __half_as_ushort(__float2half_rn(t)));
+      }
+    }
   }
+  if (!exchange) return;
+  const bool ok = peer_receive(px, epoch, M, n_rows, int64_t(blockIdx.x) * kRedThreads + threadIdx.x,
+                               int64_t(gridDim.x) * kRedThreads);
+  const int expired = __syncthreads_or(!ok);
+  if (threadIdx.x == 0) peer_finish_cta(px, epoch, expired != 0);
 }
 
 // A CTA's units [u0, u1) (group-major numbering) in processing order: from
@@ -727,6 +747,13 @@ int launch_t(const CUtensorMap& map, const XtabArgs& a0, const DeviceInfo& di, c
   const int dyn = dyn_bytes(di);
   if (!fits<M>(dyn)) return BNBQ_ERR_UNSUPPORTED;
   a.dyn_bytes = uint32_t(dyn);
+  if (a.px.inbox) {  // the exchange polls for peers from every reduction CTA: all must be resident
+    int per_sm = 0;
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, gemv_xtab_reduce_kernel<XT, M>, kRedThreads, 0) !=
+        cudaSuccess)
+      return BNBQ_ERR_CUDA;
+    if (int64_t(a.row_blocks) * M > int64_t(per_sm) * di.sm_count) return BNBQ_ERR_UNSUPPORTED;
+  }
   static std::atomic<int> attr_set[kMaxDevices];  // per device: the attribute is set once
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return BNBQ_ERR_CUDA;
@@ -754,7 +781,7 @@ int launch_t(const CUtensorMap& map, const XtabArgs& a0, const DeviceInfo& di, c
   rc.blockDim = dim3(kRedThreads);
   rc.dynamicSmemBytes = 0;
   if (cudaLaunchKernelEx(&rc, gemv_xtab_reduce_kernel<XT, M>, static_cast<const float*>(a.partial), a.groups,
-                         a.row_blocks, a.n_rows, a.y, a.ldy) != cudaSuccess)
+                         a.row_blocks, a.n_rows, a.y, a.ldy, a.px) != cudaSuccess)
     return BNBQ_ERR_CUDA;
   return launch_status();
 }
@@ -802,6 +829,9 @@ int launch_rows(int mm, const XtabArgs& base, const uint8_t* w, bool nested, con
 
 }  // namespace
 
+int xtab_wait_timeouts(unsigned int* out) { return read_wait_timeouts(out); }
+int xtab_set_wait_limit(uint64_t ns) { return write_wait_limit(ns); }
+
 int gemv_xtab_set_policy(int policy) {
   if (policy < 0 || policy > 2) return BNBQ_ERR_INVALID;
   g_table_policy.store(policy, std::memory_order_relaxed);
@@ -839,12 +869,19 @@ int gemv_xtab_applies(int m, int k, int64_t n_rows, int blocksize, const uint8_t
   return BNBQ_OK;
 }
 
+// px != nullptr: the exchange mode (one pass, M <= 2), y = px->y_full's own
+// columns; y and ldy are then ignored.
 int gemv_xtab_launch(int dtype, const void* x, int m, int k, const uint8_t* w, int64_t n_rows, int blocksize,
                      const float* absmax, const uint8_t* absmax_q, const float* absmax2, const float* code2,
                      const float* offset, int blocksize2, int64_t absmax2_block0, void* y, int64_t ldy,
-                     void* workspace, int64_t workspace_bytes, cudaStream_t s) {
+                     void* workspace, int64_t workspace_bytes, cudaStream_t s, const PeerOut* px) {
   if (int st = gemv_xtab_applies(m, k, n_rows, blocksize, absmax_q, blocksize2, workspace, workspace_bytes))
     return st;
+  if (px) {
+    if (m > 2) return BNBQ_ERR_UNSUPPORTED;
+    y = static_cast<char*>(px->y_full) + size_t(px->col0) * 2;
+    ldy = px->ldf;
+  }
   const int l2 = log2_exact(blocksize);
   DeviceInfo di;
   if (int st = device_info(&di)) return st;
@@ -861,6 +898,7 @@ int gemv_xtab_launch(int dtype, const void* x, int m, int k, const uint8_t* w, i
   a.k = k;
   a.log2_bs = l2;
   a.log2_bs2 = absmax_q ? log2_exact(blocksize2) : 0;
+  if (px) a.px = *px;
   const size_t es = dtype == BNBQ_F32 ? 4 : 2;
   const bool nested = absmax_q != nullptr;
   // passes of two rows, then one of one row (m = 1, 3)

@@ -4,106 +4,86 @@
 // Every rank computes y[:, col0 : col0 + n_local] with the fused kernels and
 // then launches bnbq_peer_allgather_rows on the same stream (programmatic
 // dependent launch: it starts while the matmul drains and waits for it with
-// griddepcontrol.wait). Its CTAs store the rank's slice into the full-y buffer
-// of EVERY rank with plain stores to peer memory (CUDA IPC mappings over
-// NVLink; no multicast, no TMA).
+// griddepcontrol.wait).
 //
-// Two handshakes per call e (the epoch, kept in device memory in state[1] and
-// advanced once per call, so replays of a captured CUDA graph stay in step):
-//   ready -- once the kernel runs (after griddepcontrol.wait), everything
-//            before it on this rank's stream has completed, including whatever
-//            consumed the previous call's output. CTA 0 then publishes
-//            ready = e in every rank's flag array, and no CTA stores into rank
-//            d's buffer before rank d's ready has reached e. A fast peer can
-//            therefore never overwrite a result this rank is still reading.
-//   done  -- the last CTA to finish (a local arrival counter it resets) makes
-//            the stores visible system-wide, publishes done = e in every
-//            rank's flag array and waits until every peer's done has reached
-//            e: on return every slice is in this rank's buffer.
-// flags[d] is rank d's uint32[2 * world]: [0, world) done epochs by source
-// rank, [world, 2 * world) ready epochs. Every wait is bounded in time; on
-// expiry the kernel counts a timeout (bnbq_wait_timeouts), skips what waited
-// and returns with the output incomplete.
-#define BNBQ_WAIT_LIMIT_DEFAULT_NS 10000000000ull  // 10 s: a peer that is this late has failed
-#include "bnbq_async.cuh"
+// Protocol (device side in bnbq_peer.cuh): tagged words in a double-buffered
+// inbox, one per rank.
+//   * Rank d's inbox is a uint64 array of `inbox_words` words (zeroed once),
+//     shared with the peers through CUDA IPC. Its two halves alternate by the
+//     parity of the call's epoch e (kept in device memory in state[1] and
+//     advanced once per call, so replays of a captured CUDA graph stay in
+//     step). Word r * n_total + c of a half holds output element (r, c) as
+//     value | e << 32 in one 8-byte store.
+//   * Each CTA stores its share of this rank's slice into every peer's inbox
+//     (plain relaxed system-scope stores over NVLink; no multicast, no TMA,
+//     no fences) and straight into this rank's own output, then polls its
+//     share of the other columns in its OWN inbox (local memory) until each
+//     word carries epoch e, and unpacks it into the output. Peers never write
+//     the output itself, so it stays valid until this rank's next call on
+//     the stream.
+//   * No handshake guards the inbox: a peer can store call e + 2 into the
+//     half this rank reads for call e only after the peer finished call e + 1,
+//     which needed this rank's call-(e + 1) slice, which this rank sends only
+//     after its call-e kernel (and the matmul between them) has completed.
+//   * A word can be mistaken for a current one only if it was written exactly
+//     a multiple of 2^32 calls earlier and never since.
+// The last CTA (a local arrival counter in state[0], which it resets) stores
+// the epoch. Every wait is bounded in time from the start of the receive
+// phase (10 s by default); on expiry the CTA counts a timeout
+// (bnbq_wait_timeouts), leaves the words it did not receive unwritten in the
+// output and returns.
+//
+// The matmul kernels that can finish with the exchange themselves (M <= 2,
+// every CTA resident at once) take the same PeerOut and do both halves in
+// their epilogue; bnbq_matmul_nf4_allgather picks them and falls back to the
+// matmul plus this kernel.
 #include "bnbq_common.cuh"
+#include "bnbq_peer.cuh"
 
 namespace bnbq {
 namespace {
 
-__device__ __forceinline__ void st_release_sys(uint32_t* p, uint32_t v) {
-  asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
-}
-__device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* p) {
-  uint32_t v;
-  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
-  return v;
-}
+constexpr int kPeerMaxWorld = 64;
+constexpr int kPeerThreads = 256;
+constexpr int kPeerBatch = 4;  // words per thread with their loads in flight together
 
-// Wait (one thread) until *p has reached `epoch` (wrap-around safe), at most
-// the wait limit from t0; false on expiry (counted).
-__device__ __forceinline__ bool wait_epoch(const uint32_t* p, uint32_t epoch, uint64_t t0) {
-  const uint64_t limit = g_bnbq_wait_limit_ns;
-  while (int32_t(ld_acquire_sys(p) - epoch) < 0) {
-    if (global_ns() - t0 > limit) {
-      atomicAdd(&g_bnbq_wait_timeouts, 1u);
-      return false;
-    }
-    __nanosleep(128);
-  }
-  return true;
-}
-
-// y_local: m x n_local (row stride ld_local) 16-bit values; y_full[d]: rank d's
-// m x ldy buffer; flags[d]: rank d's uint32[2 * world]; state: this rank's
-// {arrived CTAs, epoch}.
-__global__ void __launch_bounds__(256) peer_allgather_kernel(const uint16_t* y_local, int m, int64_t n_local,
-                                                             int64_t ld_local, int64_t col0, int64_t ldy,
-                                                             uint16_t* const* y_full, uint32_t* const* flags,
-                                                             uint32_t* state, int world, int rank, int vec) {
-  __shared__ uint32_t s_ready;  // bit d: rank d may be written
+// y_local: m x n_local (row stride ld_local) 16-bit values; px: the exchange
+// (its y_full is this rank's m x n_total output).
+__global__ void __launch_bounds__(kPeerThreads) peer_allgather_kernel(const uint16_t* y_local, int m,
+                                                                      int64_t n_local, int64_t ld_local, PeerOut px) {
+  asm volatile("griddepcontrol.launch_dependents;");
   asm volatile("griddepcontrol.wait;" ::: "memory");  // the matmul that wrote y_local has completed
-  const uint32_t epoch = state[1] + 1u;  // read before any CTA can advance it (advanced by the last CTA only)
-  const uint32_t* mine = flags[rank];
-  if (threadIdx.x == 0) {
-    if (blockIdx.x == 0)
-      for (int d = 0; d < world; ++d) st_release_sys(flags[d] + world + rank, epoch);
-    uint32_t ok = 0;
-    const uint64_t t0 = global_ns();
-    for (int d = 0; d < world; ++d)
-      if (wait_epoch(mine + world + d, epoch, t0)) ok |= 1u << d;
-    s_ready = ok;
-  }
-  __syncthreads();
-  const uint32_t ready = s_ready;
-  const int64_t per_row = vec ? n_local / 8 : n_local;  // 16-byte pieces or single values
-  const int64_t total = int64_t(m) * per_row;
-  for (int64_t i = int64_t(blockIdx.x) * blockDim.x + threadIdx.x; i < total; i += int64_t(gridDim.x) * blockDim.x) {
-    const int64_t r = i / per_row, c = i - r * per_row;
-    if (vec) {
-      const uint4 v = *reinterpret_cast<const uint4*>(y_local + r * ld_local + 8 * c);
-      for (int d = 0; d < world; ++d)
-        if (ready >> d & 1u) *reinterpret_cast<uint4*>(y_full[d] + r * ldy + col0 + 8 * c) = v;
-    } else {
-      const uint16_t v = y_local[r * ld_local + c];
-      for (int d = 0; d < world; ++d)
-        if (ready >> d & 1u) y_full[d][r * ldy + col0 + c] = v;
+  // every thread reads the epoch (stored by the last CTA only, once every
+  // thread of the launch has read it and passed the final barrier)
+  const uint32_t epoch = peer_epoch(px);
+  const int64_t step = int64_t(gridDim.x) * kPeerThreads;
+  const int64_t tid = int64_t(blockIdx.x) * kPeerThreads + threadIdx.x;
+  uint16_t* y_full = static_cast<uint16_t*>(px.y_full);
+
+  // send: this rank's slice into every peer's inbox and its own output
+  const int64_t sends = int64_t(m) * n_local;
+  for (int64_t i0 = tid; i0 < sends; i0 += kPeerBatch * step) {
+    uint16_t v[kPeerBatch];
+    int64_t r[kPeerBatch], c[kPeerBatch];
+#pragma unroll
+    for (int j = 0; j < kPeerBatch; ++j) {
+      const int64_t i = i0 + j * step;
+      r[j] = i / n_local;
+      c[j] = i - r[j] * n_local;
+      if (i < sends) v[j] = y_local[r[j] * ld_local + c[j]];
+    }
+#pragma unroll
+    for (int j = 0; j < kPeerBatch; ++j) {
+      if (i0 + j * step >= sends) break;
+      peer_send(px, epoch, r[j], c[j], v[j]);
+      y_full[r[j] * px.ldf + px.col0 + c[j]] = v[j];
     }
   }
-  __threadfence_system();  // this thread's peer stores, before the CTA reports
-  __syncthreads();
-  __shared__ int s_last;
-  if (threadIdx.x == 0) s_last = atomicAdd(&state[0], 1u) == gridDim.x - 1;
-  __syncthreads();
-  if (!s_last || threadIdx.x != 0) return;
-  // last CTA of this rank: every CTA's stores are fenced (they fenced before arriving)
-  state[0] = 0;  // no CTA of this launch touches the counter again
-  __threadfence_system();
-  for (int d = 0; d < world; ++d) st_release_sys(flags[d] + rank, epoch);
-  const uint64_t t0 = global_ns();
-  for (int src = 0; src < world; ++src)
-    if (!wait_epoch(mine + src, epoch, t0)) break;
-  state[1] = epoch;  // also after an expiry: stay in step with the peers that did publish
+
+  // receive: the other ranks' columns from this rank's own inbox
+  const bool ok = peer_receive(px, epoch, m, n_local, tid, step);
+  const int expired = __syncthreads_or(!ok);
+  if (threadIdx.x == 0) peer_finish_cta(px, epoch, expired != 0);
 }
 
 }  // namespace
@@ -167,39 +147,70 @@ extern "C" int bnbq_ipc_close(void* base) {
   return cudaIpcCloseMemHandle(base) == cudaSuccess ? BNBQ_OK : BNBQ_ERR_CUDA;
 }
 
-extern "C" int bnbq_peer_allgather_rows(int dtype, const void* y_local, int32_t m, int64_t n_local, int64_t ld_local,
-                                        int64_t col0, int64_t ldy, void* const* y_full, uint32_t* const* flags,
-                                        uint32_t* state, int32_t world, int32_t rank, void* stream) {
+namespace bnbq {
+
+// Checks the exchange arguments shared by the standalone all-gather and the
+// matmuls that end with it, and fills *px.
+int peer_make(int dtype, int32_t m, int64_t n_local, int64_t col0, void* y_full, int64_t n_total, int64_t ldy,
+              uint64_t* const* inbox, int64_t inbox_words, uint32_t* state, int32_t world, int32_t rank,
+              PeerOut* px) {
   if (dtype != BNBQ_F16 && dtype != BNBQ_BF16) return BNBQ_ERR_UNSUPPORTED;
-  if (m < 0 || n_local < 0 || world < 1 || world > 32 || rank < 0 || rank >= world || ld_local < n_local ||
-      col0 < 0 || ldy < col0 + n_local)
+  if (m < 0 || n_local < 0 || world < 1 || world > kPeerMaxWorld || rank < 0 || rank >= world || col0 < 0 ||
+      n_total < col0 + n_local || ldy < n_total || inbox_words < 0)
     return BNBQ_ERR_INVALID;
-  if (!y_full || !flags || !state || (m > 0 && n_local > 0 && !y_local)) return BNBQ_ERR_INVALID;
-  if (!aligned(y_local, 2) || !aligned(state, 4) || !aligned(y_full, 8) || !aligned(flags, 8))
-    return BNBQ_ERR_MISALIGNED;
+  if (world == 1 && (col0 != 0 || n_local != n_total)) return BNBQ_ERR_INVALID;  // no one else owns a column
+  if (int64_t(m) * n_total > inbox_words / 2) return BNBQ_ERR_TOO_LARGE;
+  if (!inbox || !state || (m > 0 && n_total > 0 && !y_full)) return BNBQ_ERR_INVALID;
+  if (!aligned(y_full, 2) || !aligned(state, 4) || !aligned(inbox, 8)) return BNBQ_ERR_MISALIGNED;
+  px->inbox = inbox;
+  px->state = state;
+  px->y_full = y_full;
+  px->n_total = n_total;
+  px->ldf = ldy;
+  px->col0 = col0;
+  px->half = inbox_words / 2;
+  px->world = world;
+  px->rank = rank;
+  return BNBQ_OK;
+}
+
+// The standalone exchange kernel behind the matmul that wrote y_local.
+int peer_allgather_launch(const void* y_local, int32_t m, int64_t n_local, int64_t ld_local, const PeerOut& px,
+                          cudaStream_t stream) {
   DeviceInfo di;
   if (int st = device_info(&di)) return st;
-  // 16-byte pieces when every row start on both sides is 16-byte aligned (the
-  // full-y buffers themselves are 16-byte aligned allocations)
-  const int vec = (n_local % 8 == 0 && col0 % 8 == 0 && ldy % 8 == 0 && ld_local % 8 == 0 && aligned(y_local, 16)) ? 1 : 0;
-  const int64_t work = int64_t(m) * (vec ? n_local / 8 : n_local);
-  int64_t grid = (work + 255) / 256;
+  // one word per thread and pass, at most four CTAs per SM (all resident)
+  const int64_t work = int64_t(m) * (n_local > px.n_total - n_local ? n_local : px.n_total - n_local);
+  int64_t grid = (work + kPeerThreads - 1) / kPeerThreads;
   if (grid < 1) grid = 1;
-  if (grid > int64_t(di.sm_count)) grid = di.sm_count;
+  if (grid > 4 * int64_t(di.sm_count)) grid = 4 * int64_t(di.sm_count);
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(unsigned(grid));
-  cfg.blockDim = dim3(256);
-  cfg.stream = static_cast<cudaStream_t>(stream);
+  cfg.blockDim = dim3(kPeerThreads);
+  cfg.stream = stream;
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
   if (cudaLaunchKernelEx(&cfg, peer_allgather_kernel, static_cast<const uint16_t*>(y_local), int(m), n_local,
-                         ld_local, col0, ldy, reinterpret_cast<uint16_t* const*>(y_full), flags, state, int(world),
-                         int(rank), vec) != cudaSuccess)
+                         ld_local, px) != cudaSuccess)
     return BNBQ_ERR_CUDA;
   return launch_status();
+}
+
+}  // namespace bnbq
+
+extern "C" int bnbq_peer_allgather_rows(int dtype, const void* y_local, int32_t m, int64_t n_local, int64_t ld_local,
+                                        int64_t col0, void* y_full, int64_t n_total, int64_t ldy,
+                                        uint64_t* const* inbox, int64_t inbox_words, uint32_t* state, int32_t world,
+                                        int32_t rank, void* stream) {
+  PeerOut px;
+  if (int st = peer_make(dtype, m, n_local, col0, y_full, n_total, ldy, inbox, inbox_words, state, world, rank, &px))
+    return st;
+  if (ld_local < n_local || (m > 0 && n_local > 0 && !y_local)) return BNBQ_ERR_INVALID;
+  if (!aligned(y_local, 2)) return BNBQ_ERR_MISALIGNED;
+  return peer_allgather_launch(y_local, m, n_local, ld_local, px, static_cast<cudaStream_t>(stream));
 }
 
 // ---------------------------------------------------------------------------
@@ -213,14 +224,14 @@ extern "C" int bnbq_peer_allgather_rows(int dtype, const void* y_local, int32_t 
 // there can fail, and it would synchronise the device), or a serving loop held
 // to a fixed memory plan. The state words must outlive every call (the epoch
 // advances once per call, in step with the peers) and start at zero, so such
-// a caller has nowhere to keep them. The flag arrays and full-y buffers are
-// shared with the peers and are still the caller's (created once, with the
+// a caller has nowhere to keep them. The inboxes (shared with the peers) and
+// the output are still the caller's (the inboxes are created once, with the
 // group, by code that may allocate).
 //
 // Here the state lives in a fixed 256-byte array per device, held by every
 // device that loads this library until the process exits: one {arrived CTAs,
 // epoch} pair per exchange slot, kNoAllocExchanges (32) slots. A slot stands
-// for one group's sequence of exchanges with one set of zeroed flag arrays;
+// for one group's sequence of exchanges with one set of zeroed inboxes;
 // every rank of the group names the same slot on every call. Slots at or
 // beyond 32 return BNBQ_ERR_TOO_LARGE.
 namespace bnbq {
@@ -270,7 +281,7 @@ extern "C" int bnbq_peer_allgather_noalloc_setup(void) {
 
 // Puts slot `exchange` back to zero on `stream` (stream-ordered, no host
 // synchronisation): for a slot taken over by another group or by a group with
-// new, zeroed flag arrays. Every rank of the group resets the slot before its
+// new, zeroed inboxes. Every rank of the group resets the slot before its
 // first exchange through it.
 extern "C" int bnbq_peer_allgather_noalloc_reset(int32_t exchange, void* stream) {
   if (exchange < 0) return BNBQ_ERR_INVALID;
@@ -286,14 +297,14 @@ extern "C" int bnbq_peer_allgather_noalloc_reset(int32_t exchange, void* stream)
 // Calls on one device share the array: two calls whose kernels overlap on
 // the GPU with the same slot race on its counter and epoch.
 extern "C" int bnbq_peer_allgather_rows_noalloc(int dtype, const void* y_local, int32_t m, int64_t n_local,
-                                                int64_t ld_local, int64_t col0, int64_t ldy, void* const* y_full,
-                                                uint32_t* const* flags, int32_t exchange, int32_t world,
-                                                int32_t rank, void* stream) {
+                                                int64_t ld_local, int64_t col0, void* y_full, int64_t n_total,
+                                                int64_t ldy, uint64_t* const* inbox, int64_t inbox_words,
+                                                int32_t exchange, int32_t world, int32_t rank, void* stream) {
   if (exchange < 0) return BNBQ_ERR_INVALID;
   if (exchange >= kNoAllocExchanges) return BNBQ_ERR_TOO_LARGE;
   if (dtype != BNBQ_F16 && dtype != BNBQ_BF16) return BNBQ_ERR_UNSUPPORTED;
   uint32_t* state = nullptr;
   if (int st = noalloc_state(&state)) return st;
-  return bnbq_peer_allgather_rows(dtype, y_local, m, n_local, ld_local, col0, ldy, y_full, flags,
-                                  state + 2 * exchange, world, rank, stream);
+  return bnbq_peer_allgather_rows(dtype, y_local, m, n_local, ld_local, col0, y_full, n_total, ldy, inbox,
+                                  inbox_words, state + 2 * exchange, world, rank, stream);
 }

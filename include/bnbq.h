@@ -201,19 +201,23 @@ BNBQ_API int bnbq_gemv_workspace_bytes(int32_t m, int32_t k, int64_t n_rows, int
  * exchange of the N-sharded GEMV/GEMM; the reference has no counterpart -- it
  * runs on one device -- and NCCL's all-gather is the portable alternative).
  * y_local: this rank's m x n_local slice (row stride ld_local, dtype F16/BF16),
- * destined for columns [col0, col0 + n_local) of every rank's full output.
- * y_full: device array of `world` pointers, rank d's m x ldy buffer (IPC-mapped
- * peer memory; 16-byte aligned allocations). flags: device array of `world`
- * pointers to each rank's uint32[2 * world] flag array (zero-initialised once).
- * state: this rank's uint32[2] (zero-initialised once; the kernel keeps it).
- * 1 <= world <= 32. Enqueued on `stream` after the matmul that wrote y_local
- * (it waits for it); on return of the kernel every rank's slice is in this
- * rank's y_full. Every rank must make the same sequence of calls. A rank's
- * y_full stays unchanged until its next call on `stream` starts: no peer
- * stores into it before this rank's kernel of that next call has begun
- * (a "ready" handshake), so anything enqueued in between may read it. The
- * waits for peers are bounded (10 s by default); an expiry is counted by
- * bnbq_wait_timeouts and leaves the output incomplete. */
+ * columns [col0, col0 + n_local) of the m x n_total output (the ranks'
+ * slices tile [0, n_total); with world 1, col0 = 0 and n_local = n_total,
+ * else BNBQ_ERR_INVALID). y_full: this
+ * rank's output (row stride ldy >= n_total; written only by this rank).
+ * inbox: device array of `world` pointers, rank d's inbox of inbox_words
+ * uint64 words (IPC-mapped peer memory for d != rank; 8-byte aligned; zeroed
+ * once before the first call; the same inbox_words on every rank, at least
+ * 2 * m * n_total, else BNBQ_ERR_TOO_LARGE). state: this rank's uint32[2]
+ * (zeroed once; the kernel keeps it). 1 <= world <= 64. Enqueued on `stream`
+ * after the matmul that wrote y_local (it waits for it): it stores the slice
+ * into every peer's inbox as words {value, epoch} (one 8-byte store each,
+ * halves alternating by call), copies it into y_full, and fills the other
+ * columns of y_full from this rank's own inbox once their words carry the
+ * call's epoch. Every rank must make the same sequence of calls with the same
+ * n_total. y_full stays unchanged until this rank's next call on `stream`.
+ * The waits for peers are bounded (10 s by default); an expiry is counted by
+ * bnbq_wait_timeouts and leaves those columns of y_full unwritten. */
 /* CUDA IPC of the buffers the peer all-gather writes (no counterpart in the
  * reference). bnbq_ipc_handle exports the allocation containing `ptr`: 64
  * bytes into handle_out and ptr's offset from the allocation base.
@@ -232,8 +236,28 @@ BNBQ_API int bnbq_ipc_close(void* base);
 BNBQ_API int bnbq_enable_peer_access(int peer_device);
 
 BNBQ_API int bnbq_peer_allgather_rows(int dtype, const void* y_local, int32_t m, int64_t n_local, int64_t ld_local,
-                                      int64_t col0, int64_t ldy, void* const* y_full, uint32_t* const* flags,
-                                      uint32_t* state, int32_t world, int32_t rank, void* stream);
+                                      int64_t col0, void* y_full, int64_t n_total, int64_t ldy,
+                                      uint64_t* const* inbox, int64_t inbox_words, uint32_t* state, int32_t world,
+                                      int32_t rank, void* stream);
+
+/* The row-sharded matmul and its all-gather in one call (no counterpart in
+ * the reference, which runs on one device): y_full[:, col0 : col0 + n_local]
+ * = x @ W_rank.T for this rank's n_local rows of the weight (the arguments of
+ * bnbq_matmul_nf4_ws, with n_rows = n_local), and the other columns from the
+ * peers, as bnbq_peer_allgather_rows would assemble them (same inbox, state,
+ * world and rank arguments; one call per rank in the same order). For M <= 2
+ * the matmul kernel itself stores its rows into the peers' inboxes and
+ * collects theirs in its epilogue (one kernel chain, no separate exchange
+ * launch); other shapes run the matmul, then the exchange kernel. A rank
+ * with n_local = 0 only collects. Results bitwise those of
+ * bnbq_matmul_nf4_ws on the rank's rows. */
+BNBQ_API int bnbq_matmul_nf4_allgather(int dtype, const void* x, int32_t m, int32_t k, const uint8_t* w,
+                                       int64_t n_local, int32_t blocksize, const float* absmax,
+                                       const uint8_t* absmax_q, const float* absmax2, const float* code2,
+                                       const float* offset, int32_t blocksize2, int64_t absmax2_block0,
+                                       void* y_full, int64_t n_total, int64_t ldy, int64_t col0,
+                                       uint64_t* const* inbox, int64_t inbox_words, uint32_t* state, int32_t world,
+                                       int32_t rank, void* workspace, int64_t workspace_bytes, void* stream);
 
 /* bnbq_peer_allgather_rows for a caller that may not allocate device memory:
  * code that runs the exchange inside a compiled program whose runtime owns
@@ -246,7 +270,7 @@ BNBQ_API int bnbq_peer_allgather_rows(int dtype, const void* y_local, int32_t m,
  * exits) with one state pair per exchange slot. Every rank of a group names
  * the same `exchange` slot on every call; limit 32 slots (0..31), a larger
  * slot returns BNBQ_ERR_TOO_LARGE. A slot belongs to one group and one set of
- * zeroed flag arrays: before another group (or new flag arrays) uses it,
+ * zeroed inboxes: before another group (or new inboxes) uses it,
  * every rank calls bnbq_peer_allgather_noalloc_reset. The other arguments and
  * the result are bnbq_peer_allgather_rows's. The first call on a device looks
  * up the array's device address (bnbq_peer_allgather_noalloc_setup does only
@@ -255,9 +279,9 @@ BNBQ_API int bnbq_peer_allgather_rows(int dtype, const void* y_local, int32_t m,
  * cudaDeviceReset. Calls whose kernels overlap on one device with the same
  * slot race. No counterpart in the reference. */
 BNBQ_API int bnbq_peer_allgather_rows_noalloc(int dtype, const void* y_local, int32_t m, int64_t n_local,
-                                              int64_t ld_local, int64_t col0, int64_t ldy, void* const* y_full,
-                                              uint32_t* const* flags, int32_t exchange, int32_t world,
-                                              int32_t rank, void* stream);
+                                              int64_t ld_local, int64_t col0, void* y_full, int64_t n_total,
+                                              int64_t ldy, uint64_t* const* inbox, int64_t inbox_words,
+                                              int32_t exchange, int32_t world, int32_t rank, void* stream);
 
 /* The no-allocation exchange's set-up for the current device (the device
  * address of the library's state array), with no exchange; BNBQ_OK when done.

@@ -1,9 +1,9 @@
 """Generate the golden vectors that pin the CPU oracle to the reference.
 
-Run in the development container, where the reference source tree is mounted
-(default ``/root/reference``; override with ``BNBQ_REFERENCE``)::
+Run where the reference source tree (bnb_jax 0.2.0) is available, giving its
+root directory (the one that holds ``src/bnb_jax``)::
 
-    python tests/golden/make_golden.py
+    python tests/golden/make_golden.py <reference-root>
 
 The reference (bnb_jax 0.2.0) is pure Python over JAX, cutejax and the CUTLASS
 DSL, none of which can run here. Its host-side functions, however, are plain
@@ -27,7 +27,6 @@ stored in ``reference_golden.npz`` and checked against the oracle by
 from __future__ import annotations
 
 import importlib
-import os
 import sys
 import types
 from pathlib import Path
@@ -35,7 +34,6 @@ from pathlib import Path
 import numpy as np
 
 HERE = Path(__file__).resolve().parent
-REFERENCE = Path(os.environ.get("BNBQ_REFERENCE", "/root/reference"))
 
 
 def _install_stubs() -> None:
@@ -98,9 +96,11 @@ def _install_stubs() -> None:
     })
 
 
-def _load_reference():
+def _load_reference(root: Path):
+    if not (root / "src" / "bnb_jax" / "kernels" / "quantize.py").is_file():
+        raise SystemExit(f"{root} is not the reference's root (no src/bnb_jax/kernels/quantize.py)")
     _install_stubs()
-    sys.path.insert(0, str(REFERENCE / "src"))
+    sys.path.insert(0, str(root / "src"))
     q = importlib.import_module("bnb_jax.kernels.quantize")
     d = importlib.import_module("bnb_jax.kernels.dequantize")
     g = importlib.import_module("bnb_jax.kernels.gemv")
@@ -118,8 +118,10 @@ def _ulp_neighbours(vals: np.ndarray, k: int) -> np.ndarray:
     return np.concatenate(out).astype(np.float32)
 
 
-def main() -> None:
-    q, d, g = _load_reference()
+def main(argv: list[str]) -> None:
+    if len(argv) != 1:
+        raise SystemExit("usage: python tests/golden/make_golden.py <reference-root>")
+    q, d, g = _load_reference(Path(argv[0]))
     rng = np.random.default_rng(20261201)
 
     thresholds = np.array(q._NF4_THRESHOLDS, np.float32)
@@ -188,4 +190,4 @@ def main() -> None:
 
 
 if __name__ == "__main__":
-    main()
+    main(sys.argv[1:])

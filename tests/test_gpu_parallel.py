@@ -72,6 +72,38 @@ def _worker(rank, world, port, queue):
             torch.cuda.synchronize()
             for i, (xi, got) in enumerate(zip(xs, consumed)):
                 assert torch.equal(got, bnb.matmul(xi, w).float()), ("back-to-back", i)
+            # the matmul and the exchange in one call (the GEMV's own epilogue
+            # exchanges for M <= 2), eagerly and from a CUDA graph; a wide
+            # weight takes the table GEMV's route
+            for m in (1, 2, 3, 7, 20):
+                x = torch.randn(m, k, device=dev, generator=g).to(torch.bfloat16)
+                assert torch.equal(pg.matmul(x, shard).clone(), bnb.matmul(x, w)), ("fused", m)
+            w2 = bnb.quantize((torch.randn(4096, 1024, device=dev, generator=g) * 0.02).to(torch.bfloat16), "nf4",
+                              64, double_quant=True)
+            r2 = row_partition(4096, 1024, 64, world)
+            sh2 = shard_rows(w2, *r2[rank])
+            pg2 = PeerGather(2, 4096, torch.bfloat16, dev)
+            for m in (1, 2, 1):
+                x = torch.randn(m, 1024, device=dev, generator=g).to(torch.bfloat16)
+                assert torch.equal(pg2.matmul(x, sh2).clone(), bnb.matmul(x, w2)), ("fused table", m)
+            xs2 = [torch.randn(1, 1024, device=dev, generator=g).to(torch.bfloat16) for _ in range(4)]
+            outs = [torch.empty(1, 4096, dtype=torch.bfloat16, device=dev) for _ in xs2]
+            graph = torch.cuda.CUDAGraph()
+            with torch.cuda.stream(stream):
+                with torch.cuda.graph(graph, stream=stream):
+                    for xi, o in zip(xs2, outs):
+                        pg2.matmul(xi, sh2, out=o)
+            for _ in range(3):
+                for o in outs:
+                    o.zero_()
+                graph.replay()
+                torch.cuda.synchronize()
+                for xi, o in zip(xs2, outs):
+                    assert torch.equal(o, bnb.matmul(xi, w2)), "fused graph replay"
+            del graph
+            torch.cuda.synchronize()
+            dist.barrier()
+            pg2.close()
             from bnb_b200 import _lib
             assert _lib.wait_timeouts() == 0
             # block-sharded quantize == the whole tensor's codes and absmax

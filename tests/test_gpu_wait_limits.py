@@ -1,12 +1,12 @@
 """Failure detection of the bounded device-side waits, on one GPU and without
 a fault: the peer all-gather is run as rank 0 of a group of two whose "rank
-1" is a pair of local buffers nobody ever publishes to. The waits for rank 1
-must run out after the (shortened) limit, the kernel must return, the expiry
-must be counted by bnbq_wait_timeouts, and the device must stay usable for a
+1" is a local inbox nobody ever sends to. The waits for rank 1's columns must
+run out after the (shortened) limit, the kernel must return, the expiry must
+be counted by bnbq_wait_timeouts, and the device must stay usable for a
 normal exchange right after.
 
 Nothing here reaches another GPU's memory or waits on another kernel: the
-flags rank 0 waits on are local, zero, and written by no one."""
+inbox words rank 0 polls are local, zero, and written by no one."""
 from __future__ import annotations
 
 import time
@@ -19,31 +19,33 @@ from bnb_b200 import _lib
 pytestmark = pytest.mark.gpu
 
 
-def _group(world, m, ldy, dev):
-    """y_full / flags of `world` ranks, all local buffers of this device."""
-    ys = [torch.full((m, ldy), 3.0, dtype=torch.bfloat16, device=dev) for _ in range(world)]
-    flags = [torch.zeros(2 * world, dtype=torch.int32, device=dev) for _ in range(world)]
-    y_ptrs = torch.tensor([y.data_ptr() for y in ys], dtype=torch.int64, device=dev)
-    f_ptrs = torch.tensor([f.data_ptr() for f in flags], dtype=torch.int64, device=dev)
-    return ys, flags, y_ptrs, f_ptrs
+class Group:
+    """The inboxes of `world` ranks, all local buffers of this device, and
+    rank 0's output and state."""
 
+    def __init__(self, world, m, n_total, dev):
+        self.inboxes = [torch.zeros(2 * m * n_total, dtype=torch.int64, device=dev) for _ in range(world)]
+        self.ptrs = torch.tensor([b.data_ptr() for b in self.inboxes], dtype=torch.int64, device=dev)
+        self.y = torch.full((m, n_total), 3.0, dtype=torch.bfloat16, device=dev)
+        self.state = torch.zeros(2, dtype=torch.int32, device=dev)
+        self.world = world
 
-def _gather(y_local, col0, ldy, y_ptrs, f_ptrs, state, world, rank):
-    _lib.call("bnbq_peer_allgather_rows", _lib.BF16, y_local.data_ptr(), y_local.shape[0], y_local.shape[1],
-              y_local.stride(0), col0, ldy, y_ptrs.data_ptr(), f_ptrs.data_ptr(), state.data_ptr(), world, rank,
-              _lib.stream_of(y_local))
+    def gather(self, y_local, col0, rank=0):
+        _lib.call("bnbq_peer_allgather_rows", _lib.BF16, y_local.data_ptr(), y_local.shape[0], y_local.shape[1],
+                  y_local.stride(0), col0, self.y.data_ptr(), self.y.shape[1], self.y.stride(0),
+                  self.ptrs.data_ptr(), self.inboxes[0].numel(), self.state.data_ptr(), self.world, rank,
+                  _lib.stream_of(y_local))
 
 
 def test_peer_wait_expires_and_is_counted(cuda):
-    m, n_local, ldy = 2, 512, 1024
+    m, n_local, n_total = 2, 512, 1024
     y_local = torch.randn(m, n_local, device=cuda).to(torch.bfloat16)
-    ys, flags, y_ptrs, f_ptrs = _group(2, m, ldy, cuda)
-    state = torch.zeros(2, dtype=torch.int32, device=cuda)
+    grp = Group(2, m, n_total, cuda)
     before = _lib.wait_timeouts()
     _lib.set_wait_limit_ns(5_000_000)  # 5 ms
     try:
         t0 = time.perf_counter()
-        _gather(y_local, 0, ldy, y_ptrs, f_ptrs, state, 2, 0)
+        grp.gather(y_local, 0)
         torch.cuda.synchronize()
         elapsed = time.perf_counter() - t0
     finally:
@@ -51,31 +53,42 @@ def test_peer_wait_expires_and_is_counted(cuda):
     after = _lib.wait_timeouts()
     assert after > before, "the wait for the silent rank did not expire"
     assert elapsed < 5.0, f"the kernel took {elapsed:.2f} s to give up"
-    # rank 0 published its own ready and done epochs (1) in both ranks' flags
-    assert flags[0][0].item() == 1 and flags[1][0].item() == 1  # done[0]
-    assert flags[0][2].item() == 1 and flags[1][2].item() == 1  # ready[0]
-    # its own slice still reached its own buffer; the silent rank's did not
-    assert torch.equal(ys[0][:, :n_local], y_local)
-    assert bool((ys[1] == 3.0).all()), "stored into a rank that never said ready"
-    assert state[1].item() == 1 and state[0].item() == 0
+    # rank 0's own slice reached its output; the silent rank's columns were left alone
+    assert torch.equal(grp.y[:, :n_local], y_local)
+    assert bool((grp.y[:, n_local:] == 3.0).all()), "wrote columns that never arrived"
+    # rank 0 sent its slice to rank 1 as {value, epoch 1} words in the odd half
+    words = grp.inboxes[1].reshape(2, m, n_total)[1, :, :n_local]
+    assert bool((words >> 32 == 1).all())
+    low = words & 0xFFFF
+    assert torch.equal((low - ((low & 0x8000) << 1)).to(torch.int16).view(torch.bfloat16), y_local)
+    assert bool((grp.inboxes[1].reshape(2, m, n_total)[:, :, n_local:] == 0).all())
+    assert grp.state.tolist() == [0, 1]
     # the device is still usable: a normal exchange (a group of one) works
-    ys1, _, y1, f1 = _group(1, m, ldy, cuda)
-    state1 = torch.zeros(2, dtype=torch.int32, device=cuda)
-    _gather(y_local, 100, ldy, y1, f1, state1, 1, 0)
+    one = Group(1, m, n_local, cuda)
+    one.gather(y_local, 0)
     torch.cuda.synchronize()
-    assert torch.equal(ys1[0][:, 100:100 + n_local], y_local)
+    assert torch.equal(one.y, y_local)
     assert _lib.wait_timeouts() == after, "a normal exchange counted a timeout"
 
 
 def test_wait_limit_restores_default(cuda):
-    """After set_wait_limit_ns(0), a normal exchange takes no time-outs."""
+    """After set_wait_limit_ns(0), exchanges whose peer words are already
+    there take no time-outs: rank 0 of two, with rank 1's words for epochs 1
+    to 3 written into rank 0's inbox beforehand."""
     _lib.set_wait_limit_ns(0)
-    y_local = torch.randn(4, 64, device=cuda).to(torch.bfloat16)
-    ys, _, y_ptrs, f_ptrs = _group(1, 4, 64, cuda)
-    state = torch.zeros(2, dtype=torch.int32, device=cuda)
+    m, n_total = 4, 64
+    grp = Group(2, m, n_total, cuda)
+    y_local = torch.randn(m, 32, device=cuda).to(torch.bfloat16)
+    peer = torch.randn(3, m, 32, device=cuda).to(torch.bfloat16)
     before = _lib.wait_timeouts()
-    for _ in range(3):
-        _gather(y_local, 0, 64, y_ptrs, f_ptrs, state, 1, 0)
-    torch.cuda.synchronize()
+    halves = grp.inboxes[0].reshape(2, m, n_total)
+    for call in range(3):
+        epoch = call + 1
+        bits = peer[call].view(torch.int16).to(torch.int64) & 0xFFFF
+        halves[epoch & 1, :, 32:] = bits | (epoch << 32)
+        grp.gather(y_local, 0)
+        torch.cuda.synchronize()
+        assert torch.equal(grp.y[:, :32], y_local)
+        assert torch.equal(grp.y[:, 32:], peer[call]), f"call {call}"
     assert _lib.wait_timeouts() == before
-    assert state[1].item() == 3
+    assert grp.state.tolist() == [0, 3]
