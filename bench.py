@@ -552,6 +552,51 @@ def run_quant_workload(args, local_rank):
             "config1": c1, "config3": c3, "clocks": clocks.summary()}
 
 
+def run_quant_profile(args, local_rank):
+    """The driver of the 8-bit quantize profile (an ncu target, not a
+    measurement): four eager quantize_blockwise calls with the dynamic map on
+    2^27 N(0, 1) values of --qdtype at --qbs. Captured with, e.g.,
+    ncu --set full --clock-control none -k regex:quant_8bit -s 2 -c 1 ...
+    python bench.py --workload quant-profile --qdtype f16 --qbs 256"""
+    import torch
+    from bnb_b200.kernels import create_dynamic_map, quantize_blockwise
+    device = torch.device("cuda", local_rank)
+    torch.cuda.set_device(device)
+    dt = {"f32": torch.float32, "f16": torch.float16, "bf16": torch.bfloat16}[args.qdtype]
+    g = torch.Generator(device).manual_seed(0)
+    x = torch.randn(1 << 27, device=device, generator=g).to(dt)
+    code = create_dynamic_map().to(device)
+    for _ in range(4):
+        q, a = quantize_blockwise(x, code, args.qbs)
+    torch.cuda.synchronize()
+    return {"workload": "quant-profile", "dtype": args.qdtype, "blocksize": args.qbs, "n": x.numel(),
+            "calls": 4, "codes_checksum": int(q[:4096].to(torch.int64).sum().item())}
+
+
+def run_matmul_profile(args, local_rank):
+    """The driver of a matmul profile (an ncu target, not a measurement): four
+    eager bnb.matmul calls at M = --rows on one (--pn, --pk) NF4 bs64
+    double-quantized weight of N(0, 0.02^2) entries, with the kernels the
+    router picks (reported as "route")."""
+    import torch
+    import bnb_b200 as bnb
+    from bnb_b200 import _lib
+    device = torch.device("cuda", local_rank)
+    torch.cuda.set_device(device)
+    g = torch.Generator(device).manual_seed(0)
+    w = bnb.quantize((torch.randn(args.pn, args.pk, device=device, generator=g) * 0.02).to(torch.bfloat16), "nf4",
+                     BS, double_quant=True)
+    x = torch.randn(args.m, args.pk, device=device, generator=g).to(torch.bfloat16)
+    for _ in range(4):
+        y = bnb.matmul(x, w)
+    torch.cuda.synchronize()
+    nb = _lib.gemv_workspace_bytes(args.m, args.pk, args.pn) if args.m <= 20 else 0
+    ws = torch.empty(max(nb, 16), dtype=torch.uint8, device=device)
+    route = _lib.gemv_route(args.m, args.pk, args.pn, BS, w.absmax.data.data_ptr(), BS2, ws.data_ptr(), nb)
+    return {"workload": "matmul-profile", "n": args.pn, "k": args.pk, "m": args.m, "calls": 4, "route": route,
+            "y_checksum": float(y.float().sum().item())}
+
+
 def gemm_cases(torch, bnb, device, ms=(64, 512, 2048)):
     """Config 5: the fused NF4 dequantize-GEMM on the Llama-3-70B MLP shapes,
     beside the reference's fallback (dequantize + matmul)."""
@@ -759,7 +804,12 @@ def main():
     ap.add_argument("--no-sweep", dest="sweep", action="store_false")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-extras", action="store_true", help="skip the config 1/3/4/5 keys")
-    ap.add_argument("--workload", choices=["gemv", "quant", "gemm", "llama"], default="gemv")
+    ap.add_argument("--workload", choices=["gemv", "quant", "gemm", "llama", "quant-profile", "matmul-profile"],
+                    default="gemv")
+    ap.add_argument("--pn", type=int, default=14336, help="matmul-profile weight rows")
+    ap.add_argument("--pk", type=int, default=4096, help="matmul-profile weight columns (K)")
+    ap.add_argument("--qdtype", choices=["f32", "f16", "bf16"], default="f16", help="quant-profile input type")
+    ap.add_argument("--qbs", type=int, default=256, help="quant-profile blocksize")
     ap.add_argument("--gather", choices=["peer", "nccl"], default="peer", help="config 4 all-gather")
     ap.add_argument("--ungrouped", action="store_true", help="config 4 with q/k/v and gate/up as separate GEMVs")
     args = ap.parse_args()
@@ -774,6 +824,12 @@ def main():
         line = run_reference(args, rank)
         if line is not None:
             print(json.dumps(line), flush=True)
+        return
+
+    if args.workload in ("quant-profile", "matmul-profile"):
+        if rank == 0:
+            fn = run_quant_profile if args.workload == "quant-profile" else run_matmul_profile
+            print(json.dumps(fn(args, local_rank)), flush=True)
         return
 
     if args.workload in ("quant", "gemm"):

@@ -32,12 +32,13 @@ def matmul(x: torch.Tensor, w: QuantizedArray) -> torch.Tensor:
     n, k = w.shape
     if x.shape[-1] != k:
         raise ValueError(f"contraction mismatch: x {tuple(x.shape)} @ w.T {w.shape[::-1]}")
-    xm = x.reshape(-1, k)
+    flat = x.dim() == 2  # the common (M, K) case needs no reshapes (host time per call)
+    xm = x if flat else x.reshape(-1, k)
     if torch.is_grad_enabled() and xm.requires_grad:
         out = _Matmul2d.apply(xm, w)
-    else:  # no gradient wanted: skip the autograd node (host time per call)
+    else:  # no gradient wanted: skip the autograd node
         out = _forward(xm, w)
-    return out.reshape(*x.shape[:-1], n)
+    return out if flat else out.reshape(*x.shape[:-1], n)
 
 
 def _fused_args(w: QuantizedArray):

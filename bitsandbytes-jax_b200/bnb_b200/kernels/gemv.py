@@ -174,26 +174,28 @@ class FusedPlan:
 
     def run(self, x: torch.Tensor) -> torch.Tensor:
         m = x.shape[0]
-        dev = x.device
-        if not x.is_contiguous() or x.data_ptr() % 16:
+        xp = x.data_ptr()
+        if xp % 16 or not x.is_contiguous():
             x = _lib.aligned(x)
-        out = torch.empty((m, self.n), dtype=x.dtype, device=dev)
-        stream = torch._C._cuda_getCurrentRawStream(dev.index)
+            xp = x.data_ptr()
+        out = x.new_empty((m, self.n))
+        di = x.get_device()
+        stream = torch._C._cuda_getCurrentRawStream(di)
         ws_ptr, ws_n = None, 0
         if m <= GEMV_MAX_M:
             nb = self._ws_bytes.get(m)
             if nb is None:
                 nb = self._ws_bytes[m] = _lib.gemv_workspace_bytes(m, self.k, self.n)
             if nb:
-                ws = _lib.workspace(dev, stream, nb)
+                ws = _lib.workspace(x.device, stream, nb)
                 ws_ptr, ws_n = ws.data_ptr(), ws.numel()
         wp, ap, aqp, a2p, c2p, offp = self.ptrs
-        args = (_lib.DTYPE_CODE[x.dtype], x.data_ptr(), m, self.k, wp, self.n, self.bs, ap, aqp, a2p, c2p, offp,
+        args = (_lib.DTYPE_CODE[x.dtype], xp, m, self.k, wp, self.n, self.bs, ap, aqp, a2p, c2p, offp,
                 self.bs2, 0, out.data_ptr(), self.n, ws_ptr, ws_n, stream)
-        if torch._C._cuda_getDevice() == dev.index:
+        if torch._C._cuda_getDevice() == di:
             st = _lib.lib().bnbq_matmul_nf4_ws(*args)
         else:
-            with torch.cuda.device(dev):
+            with torch.cuda.device(di):
                 st = _lib.lib().bnbq_matmul_nf4_ws(*args)
         if st:
             _lib.check(st, "bnbq_matmul_nf4_ws")

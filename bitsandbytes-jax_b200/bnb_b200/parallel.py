@@ -256,30 +256,35 @@ class PeerGather:
         inboxes and collects theirs (no separate exchange kernel). Bitwise
         :func:`matmul_rows` on every rank's rows, gathered."""
         from . import _lib
-        from .kernels.gemv import GEMV_MAX_M, _prepare
         if x.dim() != 2 or x.shape[1] != shard.k or shard.n_rows_total != self.n_total:
             raise ValueError(f"x {tuple(x.shape)} and a ({shard.n_rows_total}, {shard.k}) weight do not match "
                              f"this gather's {self.n_total} columns")
+        if x.dtype not in (torch.bfloat16, torch.float16):
+            raise NotImplementedError(f"matmul of {x.dtype} x is not implemented")
         m, k = x.shape
         out = self._out(m, x.dtype, out)
-        n = shard.n_rows
-        ptrs = (None,) * 6
-        bs2 = 0
-        xs = x
-        if n > 0:
-            xs, w, (a, aq, a2, c2, off, bs2) = _prepare(x, shard.data, shard.absmax, n, shard.blocksize,
-                                                         shard.nested, "matmul")
-            ptrs = (w, a, aq, a2, c2, off)
-        stream = _lib.stream_of(xs)
-        wsb = _lib.gemv_workspace_bytes(m, k, n) if n > 0 and m <= GEMV_MAX_M else 0
-        ws = _lib.workspace(x.device, stream, wsb) if wsb else None
-        w, a, aq, a2, c2, off = (_lib.ptr(t) for t in ptrs)
-        with torch.cuda.device(x.device):
-            _lib.call("bnbq_matmul_nf4_allgather", _lib.DTYPE_CODE[x.dtype], xs.data_ptr(), m, k, w, n,
-                      shard.blocksize, a, aq, a2, c2, off, bs2, shard.block0, out.data_ptr(), self.n_total,
-                      out.stride(0), shard.start, self.inbox_ptrs.data_ptr(), self.inbox.numel(),
-                      self.state.data_ptr(), self.world, self.rank, _lib.ptr(ws), 0 if ws is None else ws.numel(),
-                      stream)
+        if not x.is_contiguous() or x.data_ptr() % 16:
+            x = _lib.aligned(x)
+        dev = x.device
+        plan = _shard_plan(shard, dev)
+        stream = torch._C._cuda_getCurrentRawStream(dev.index)
+        ws_ptr, ws_n = None, 0
+        nb = plan.ws_bytes(m)
+        if nb:
+            ws = _lib.workspace(dev, stream, nb)
+            ws_ptr, ws_n = ws.data_ptr(), ws.numel()
+        w, a, aq, a2, c2, off = plan.ptrs
+        args = (_lib.DTYPE_CODE[x.dtype], x.data_ptr(), m, k, w, shard.n_rows, shard.blocksize, a, aq, a2, c2, off,
+                plan.bs2, shard.block0, out.data_ptr(), self.n_total, out.stride(0), shard.start,
+                self.inbox_ptrs.data_ptr(), self.inbox.numel(), self.state.data_ptr(), self.world, self.rank,
+                ws_ptr, ws_n, stream)
+        if torch._C._cuda_getDevice() == dev.index:
+            st = _lib.lib().bnbq_matmul_nf4_allgather(*args)
+        else:
+            with torch.cuda.device(dev):
+                st = _lib.lib().bnbq_matmul_nf4_allgather(*args)
+        if st:
+            _lib.check(st, "bnbq_matmul_nf4_allgather")
         return out
 
     def gather(self, y_local: torch.Tensor, col0: int, out: torch.Tensor | None = None) -> torch.Tensor:
@@ -296,6 +301,60 @@ class PeerGather:
                       self.inbox_ptrs.data_ptr(), self.inbox.numel(), self.state.data_ptr(), self.world, self.rank,
                       _lib.stream_of(y_local))
         return out
+
+
+class _ShardPlan:
+    """A RowShard's C-ABI arguments, prepared once (aligned device tensors
+    and their addresses) and cached on the shard."""
+
+    __slots__ = ("data", "absmax", "device", "ptrs", "bs2", "keep", "k", "n", "_ws")
+
+    def __init__(self, shard: RowShard, device):
+        from . import _lib
+        from .kernels.gemv import _CHUNK, _f32_on
+        from .kernels.dequantize import _log2_blocksize
+        self.data, self.absmax, self.device = shard.data, shard.absmax, device
+        self.k, self.n = shard.k, shard.n_rows
+        self._ws: dict[int, int] = {}
+        if shard.k % _CHUNK:
+            raise ValueError(f"K must be a multiple of {_CHUNK}, got {shard.k}")
+        _log2_blocksize(shard.blocksize)
+        if self.n == 0:
+            self.ptrs, self.bs2, self.keep = (None,) * 6, 0, ()
+            return
+        _lib.require_cuda(shard.data, shard.absmax)
+        w = _lib.aligned(shard.data.reshape(-1))
+        if shard.nested is None:
+            a = _lib.aligned(shard.absmax.reshape(-1), 4)
+            self.keep = (w, a)
+            self.ptrs = (w.data_ptr(), a.data_ptr(), None, None, None, None)
+            self.bs2 = 0
+        else:
+            absmax2, code2, offset, bs2 = shard.nested
+            _log2_blocksize(bs2)
+            aq = _lib.aligned(shard.absmax.reshape(-1))
+            a2 = _lib.aligned(_f32_on(absmax2, device).reshape(-1), 4)
+            c2 = _lib.aligned(_f32_on(code2, device).reshape(-1), 4)
+            off = _lib.aligned(_f32_on(offset, device).reshape(1), 4)
+            self.keep = (w, aq, a2, c2, off)
+            self.ptrs = (w.data_ptr(), None, aq.data_ptr(), a2.data_ptr(), c2.data_ptr(), off.data_ptr())
+            self.bs2 = bs2
+
+    def ws_bytes(self, m: int) -> int:
+        from . import _lib
+        from .kernels.gemv import GEMV_MAX_M
+        nb = self._ws.get(m)
+        if nb is None:
+            nb = self._ws[m] = _lib.gemv_workspace_bytes(m, self.k, self.n) if self.n and m <= GEMV_MAX_M else 0
+        return nb
+
+
+def _shard_plan(shard: RowShard, device) -> _ShardPlan:
+    plan = shard.__dict__.get("_bnbq_plan")
+    if plan is None or plan.data is not shard.data or plan.absmax is not shard.absmax or plan.device != device:
+        plan = _ShardPlan(shard, device)
+        shard.__dict__["_bnbq_plan"] = plan
+    return plan
 
 
 def matmul_sharded(x: torch.Tensor, shard: RowShard, ranges: list[tuple[int, int]] | None = None,

@@ -488,7 +488,7 @@ constexpr int kMaxGroupsPerFlush = 32;  // partial sums held in shared memory be
 // the other layout's registers and code drop out). RG: the consumer warps form
 // RG equal groups, group i taking rows [i R/RG, (i + 1) R/RG) of every stage
 // (short rows: more warps than one row's chunks could keep busy).
-template <typename XT, int M, int R, bool NESTED, int SLOTS, bool SIS, int RG>
+template <typename XT, int M, int R, bool NESTED, int SLOTS, bool SIS, int RG, bool PX>
 __global__ void __launch_bounds__(kMaxWarps * 32, 1)
 gemv_bulk_kernel(GemvArgs a, int n_groups, int n_stages, uint32_t stage_bytes) {
   static_assert(R % RG == 0, "row groups split the stage's rows evenly");
@@ -508,7 +508,7 @@ gemv_bulk_kernel(GemvArgs a, int n_groups, int n_stages, uint32_t stage_bytes) {
   const int ncons = ncw * 32;
   const int wpg = ncw / RG;        // warps per row group (the host makes ncw a multiple of RG)
   const int gthreads = wpg * 32;   // threads per row group
-  const int rgi = tid / gthreads;  // this thread's row group (consumers)
+  const int rgi = RG == 1 ? 0 : tid / gthreads;  // this thread's row group (consumers); constant for RG = 1
   const int lt = tid - rgi * gthreads;
   const int r0 = rgi * RT;         // its first row of a stage
   const int cpr = a.k >> 5;
@@ -740,7 +740,7 @@ gemv_bulk_kernel(GemvArgs a, int n_groups, int n_stages, uint32_t stage_bytes) {
   // the CTA reports that it has finished the call.
   __syncwarp();
   if (lane == 0) mbar_arrive(smem_u32(&s_done_bar));
-  const bool exchange = a.px.inbox != nullptr;
+  constexpr bool exchange = PX;  // a compile-time variant: the plain kernel carries no exchange code
   const uint32_t epoch = exchange ? peer_epoch(a.px) : 0u;  // after griddepcontrol.wait
   if (warp == 0 && mbar_wait(smem_u32(&s_done_bar), 0) && !s_abort) {
     for (int e = lane; e < gl * M * R; e += 32) {
@@ -756,11 +756,12 @@ gemv_bulk_kernel(GemvArgs a, int n_groups, int n_stages, uint32_t stage_bytes) {
       }
     }
   }
-  if (!exchange) return;
-  if (!peer_receive(a.px, epoch, M, a.n_rows, int64_t(blockIdx.x) * ncons + tid, int64_t(gridDim.x) * ncons))
-    s_rx_expired = 1;
-  named_bar_sync(2, ncons);
-  if (tid == 0) peer_finish_cta(a.px, epoch, s_rx_expired != 0);
+  if constexpr (exchange) {
+    if (!peer_receive(a.px, epoch, M, a.n_rows, int64_t(blockIdx.x) * ncons + tid, int64_t(gridDim.x) * ncons))
+      s_rx_expired = 1;
+    named_bar_sync(2, ncons);
+    if (tid == 0) peer_finish_cta(a.px, epoch, s_rx_expired != 0);
+  }
 }
 
 struct BulkPlan {
@@ -786,7 +787,9 @@ bool plan_bulk(int m, int k, int log2_bs, bool nested, int smem_optin, BulkPlan*
       const int slots = (cpr + 32 * w - 1) / (32 * w);
       if (slots * m > 2) continue;
       const double eff = double(cpr) / double(slots * 32 * w);
-      if (eff < 0.75 || w * rg < 4 || (rg > 1 && slots > 1)) continue;
+      // row groups only for rows of >= 128 chunks (K >= 4096, measured); shorter rows
+      // keep the flat kernel
+      if (eff < 0.75 || w * rg < 4 || (rg > 1 && (slots > 1 || cpr < 128))) continue;
       const double busy = eff * w * rg;
       const bool better = busy > best_busy + 1e-9 ||
                           (busy > best_busy - 1e-9 && (slots < p->slots || (slots == p->slots && w * rg < p->ncw)));
@@ -813,8 +816,11 @@ bool plan_bulk(int m, int k, int log2_bs, bool nested, int smem_optin, BulkPlan*
 
 template <typename XT, int M, int R, bool NESTED, int SLOTS, int RG = 1>
 int launch_bulk_t(const GemvArgs& a, const BulkPlan& p, const DeviceInfo& di, cudaStream_t s) {
-  auto kern = p.scales_in_stage ? gemv_bulk_kernel<XT, M, R, NESTED, SLOTS, true, RG>
-                                : gemv_bulk_kernel<XT, M, R, NESTED, SLOTS, false, RG>;
+  const bool px = a.px.inbox != nullptr;
+  auto kern = p.scales_in_stage ? (px ? gemv_bulk_kernel<XT, M, R, NESTED, SLOTS, true, RG, true>
+                                      : gemv_bulk_kernel<XT, M, R, NESTED, SLOTS, true, RG, false>)
+                                : (px ? gemv_bulk_kernel<XT, M, R, NESTED, SLOTS, false, RG, true>
+                                      : gemv_bulk_kernel<XT, M, R, NESTED, SLOTS, false, RG, false>);
   cudaFuncAttributes fa;
   if (cudaFuncGetAttributes(&fa, kern) != cudaSuccess) return BNBQ_ERR_CUDA;
   const size_t room = size_t(di.smem_optin) - size_t(kPairTableBytes) - fa.sharedSizeBytes - 1024;

@@ -6,10 +6,12 @@ another GPU.
 
 Checked for each route -- the streaming GEMV and the table GEMV with the
 exchange in their epilogue (M = 1, 2), and the matmul followed by the
-standalone exchange kernel (M = 3, 8) -- bitwise against bnb.matmul on the
-rank's rows: rank 0's columns of the output, the words it sent to rank 1
-(its values tagged with the call's epoch, in the epoch's half), the columns
-it received, and the state (epoch advanced once per call, counter reset).
+standalone exchange kernel (M = 3, 8) -- bitwise against matmul_rows (the
+same kernels on the rank's rows): rank 0's columns of the output, the words
+it sent to rank 1 (its values tagged with the call's epoch, in the epoch's
+half), the columns it received, and the state (epoch advanced once per call,
+counter reset). On the GEMV routes the rank's rows also equal the whole
+weight's product bitwise.
 Then a peer that never sends: the fused kernel's bounded wait expires, is
 counted, and the device stays usable."""
 from __future__ import annotations
@@ -19,7 +21,7 @@ import torch
 
 import bnb_b200
 from bnb_b200 import _lib
-from bnb_b200.parallel import row_partition, shard_rows
+from bnb_b200.parallel import matmul_rows, row_partition, shard_rows
 
 pytestmark = [pytest.mark.gpu, pytest.mark.usefixtures("timeouts_at_start")]
 
@@ -63,7 +65,6 @@ def test_fused_exchange_rank0_of_two(cuda, shape):
     w = _weight(n, k, seed=n)
     (a0, b0), (a1, b1) = row_partition(n, k, 64 * 256, 2)
     sh = shard_rows(w, a0, b0)
-    full = None
     epoch = 0
     for m in (1, 2, 3, 8):
         r0 = Rank0(m, n, cuda)
@@ -71,14 +72,18 @@ def test_fused_exchange_rank0_of_two(cuda, shape):
         for rep in range(2):
             epoch += 1
             x = torch.randn(m, k, device=cuda).to(torch.bfloat16)
-            full = bnb_b200.matmul(x, w)
-            r0.half(0, epoch)[:, a1:b1] = _bits64(full[:, a1:b1]) | (epoch << 32)  # rank 1's words
+            mine = matmul_rows(x, sh)
+            peer = torch.randn(m, b1 - a1, device=cuda).to(torch.bfloat16)
+            r0.half(0, epoch)[:, a1:b1] = _bits64(peer) | (epoch << 32)  # rank 1's words
             r0.call(x, sh)
             torch.cuda.synchronize()
-            assert torch.equal(r0.y, full), (m, rep)
+            assert torch.equal(r0.y[:, a0:b0], mine), (m, rep)
+            assert torch.equal(r0.y[:, a1:b1], peer), (m, rep)
+            if m <= 4:
+                assert torch.equal(mine, bnb_b200.matmul(x, w)[:, a0:b0]), (m, rep)
             sent = r0.half(1, epoch)[:, a0:b0]
             assert bool((sent >> 32 == epoch).all()), (m, rep)
-            assert torch.equal(sent & 0xFFFF, _bits64(full[:, a0:b0])), (m, rep)
+            assert torch.equal(sent & 0xFFFF, _bits64(mine)), (m, rep)
             assert r0.state.tolist() == [0, epoch], (m, rep)
 
 

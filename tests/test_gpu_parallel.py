@@ -75,9 +75,9 @@ def _worker(rank, world, port, queue):
             # the matmul and the exchange in one call (the GEMV's own epilogue
             # exchanges for M <= 2), eagerly and from a CUDA graph; a wide
             # weight takes the table GEMV's route
-            for m in (1, 2, 3, 7, 20):
+            for m in (1, 2, 3, 7, 20):  # the same kernels on each rank's rows, gathered by NCCL
                 x = torch.randn(m, k, device=dev, generator=g).to(torch.bfloat16)
-                assert torch.equal(pg.matmul(x, shard).clone(), bnb.matmul(x, w)), ("fused", m)
+                assert torch.equal(pg.matmul(x, shard).clone(), matmul_sharded(x, shard, ranges)), ("fused", m)
             w2 = bnb.quantize((torch.randn(4096, 1024, device=dev, generator=g) * 0.02).to(torch.bfloat16), "nf4",
                               64, double_quant=True)
             r2 = row_partition(4096, 1024, 64, world)
@@ -85,7 +85,9 @@ def _worker(rank, world, port, queue):
             pg2 = PeerGather(2, 4096, torch.bfloat16, dev)
             for m in (1, 2, 1):
                 x = torch.randn(m, 1024, device=dev, generator=g).to(torch.bfloat16)
-                assert torch.equal(pg2.matmul(x, sh2).clone(), bnb.matmul(x, w2)), ("fused table", m)
+                want = matmul_sharded(x, sh2, r2)
+                assert torch.equal(pg2.matmul(x, sh2).clone(), want), ("fused table", m)
+                assert torch.equal(want, bnb.matmul(x, w2)), ("table rows vs whole", m)
             xs2 = [torch.randn(1, 1024, device=dev, generator=g).to(torch.bfloat16) for _ in range(4)]
             outs = [torch.empty(1, 4096, dtype=torch.bfloat16, device=dev) for _ in xs2]
             graph = torch.cuda.CUDAGraph()
