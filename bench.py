@@ -553,23 +553,31 @@ def run_quant_workload(args, local_rank):
 
 
 def run_quant_profile(args, local_rank):
-    """The driver of the 8-bit quantize profile (an ncu target, not a
-    measurement): four eager quantize_blockwise calls with the dynamic map on
-    2^27 N(0, 1) values of --qdtype at --qbs. Captured with, e.g.,
+    """The driver of a quantize profile (an ncu target, not a measurement):
+    four eager calls on 2^27 N(0, 1) values of --qdtype at --qbs --
+    quantize_blockwise with the dynamic map (--qtype 8bit), or quantize_nf4
+    on the 4096 x 4096 N(0, 0.02^2) tensor of config 1 (--qtype nf4).
+    Captured with, e.g.,
     ncu --set full --clock-control none -k regex:quant_8bit -s 2 -c 1 ...
     python bench.py --workload quant-profile --qdtype f16 --qbs 256"""
     import torch
-    from bnb_b200.kernels import create_dynamic_map, quantize_blockwise
+    from bnb_b200.kernels import create_dynamic_map, quantize_blockwise, quantize_nf4
     device = torch.device("cuda", local_rank)
     torch.cuda.set_device(device)
     dt = {"f32": torch.float32, "f16": torch.float16, "bf16": torch.bfloat16}[args.qdtype]
     g = torch.Generator(device).manual_seed(0)
-    x = torch.randn(1 << 27, device=device, generator=g).to(dt)
-    code = create_dynamic_map().to(device)
-    for _ in range(4):
-        q, a = quantize_blockwise(x, code, args.qbs)
+    if args.qtype == "nf4":
+        x = (torch.randn(4096 * 4096, device=device, generator=g) * 0.02).to(dt)
+        for _ in range(4):
+            q, a = quantize_nf4(x, args.qbs)
+    else:
+        x = torch.randn(1 << 27, device=device, generator=g).to(dt)
+        code = create_dynamic_map().to(device)
+        for _ in range(4):
+            q, a = quantize_blockwise(x, code, args.qbs)
     torch.cuda.synchronize()
-    return {"workload": "quant-profile", "dtype": args.qdtype, "blocksize": args.qbs, "n": x.numel(),
+    return {"workload": "quant-profile", "qtype": args.qtype, "dtype": args.qdtype, "blocksize": args.qbs,
+            "n": x.numel(),
             "calls": 4, "codes_checksum": int(q[:4096].to(torch.int64).sum().item())}
 
 
@@ -810,6 +818,7 @@ def main():
     ap.add_argument("--pk", type=int, default=4096, help="matmul-profile weight columns (K)")
     ap.add_argument("--qdtype", choices=["f32", "f16", "bf16"], default="f16", help="quant-profile input type")
     ap.add_argument("--qbs", type=int, default=256, help="quant-profile blocksize")
+    ap.add_argument("--qtype", choices=["8bit", "nf4"], default="8bit", help="quant-profile quantization")
     ap.add_argument("--gather", choices=["peer", "nccl"], default="peer", help="config 4 all-gather")
     ap.add_argument("--ungrouped", action="store_true", help="config 4 with q/k/v and gate/up as separate GEMVs")
     args = ap.parse_args()

@@ -54,25 +54,28 @@ def _dtype_name(dtype: torch.dtype) -> str:
 
 @dataclass
 class QuantizedArray:
-    """A blockwise-quantized tensor: codes, per-block scales, and the metadata
-    to decode them.
+    """Codes of a flattened tensor, the scale of each block of ``blocksize``
+    codes, and what it takes to turn them back into values.
 
-    Element ``i`` decodes as ``table[code_i] * absmax[i // blocksize] + offset``,
-    with ``table`` the NF4 table or the 8-bit codebook ``code``.
+    Decoding element ``i``: look its code up (the built-in NF4 table, or the
+    256-entry ``code`` of an 8-bit array), multiply by its block's scale
+    ``absmax[i // blocksize]``, and add ``offset`` when there is one.
 
-    Attributes:
-        data: uint8 codes for the flattened tensor: ``ceil(size / 2)`` bytes
-            for ``"nf4"`` (high nibble first), ``size`` for ``"8bit"``.
-        absmax: float32 scale per block, or itself a ``"8bit"``
-            QuantizedArray when double-quantized.
-        code: the 256-entry float32 codebook (``"8bit"`` only).
-        offset: float32 scalar added after decoding. Only set on the absmax
-            of a double-quantized array, which is quantized around its mean.
+    Fields:
+        data: the uint8 codes. NF4 packs two per byte, the even element in
+            the high nibble (``ceil(size / 2)`` bytes); 8-bit uses one byte
+            per element.
+        absmax: the block scales, float32 -- or, for a double-quantized
+            array, an 8-bit QuantizedArray that holds them.
+        code: an 8-bit array's float32 codebook; None for NF4.
+        offset: a float32 scalar added after decoding; only the nested absmax
+            of a double-quantized array has one (its values were centred on
+            their mean before quantizing).
         qtype: ``"nf4"`` or ``"8bit"``.
-        blocksize: elements per absmax block.
-        shape: shape of the decoded tensor.
-        dtype: default dtype :meth:`dequantize` decodes to.
-    (reference array.py:35-68)
+        blocksize: codes per scale.
+        shape: the decoded tensor's shape.
+        dtype: what :meth:`dequantize` returns unless told otherwise.
+    Same fields and meaning as the reference's dataclass (array.py:35-68).
     """
 
     data: torch.Tensor
@@ -153,21 +156,23 @@ class QuantizedArray:
 
     @classmethod
     def from_dict(cls, weight: torch.Tensor, qs_dict: dict[str, Any]) -> QuantizedArray:
-        """Wrap a weight from a HuggingFace bnb-4bit state dict.
+        """A QuantizedArray over a 4-bit weight saved by HuggingFace with
+        bitsandbytes (keys as the reference reads them, array.py:116-163).
 
-        ``weight`` is the packed uint8 tensor; ``qs_dict`` its quant state
-        entries with the weight's key prefix stripped (``absmax``,
-        ``quant_map``, ``nested_*``, and either the unpacked metadata or the
-        packed ``quant_state.bitsandbytes__nf4`` JSON tensor).
-        (reference array.py:116-163)
+        ``weight``: the uint8 tensor of packed codes. ``qs_dict``: the entries
+        stored next to it, keyed by what follows the weight's name --
+        ``absmax``, ``quant_map``, the ``nested_*`` entries of a
+        double-quantized weight, and the metadata, given either as separate
+        keys or packed into one ``quant_state.bitsandbytes__nf4`` tensor of
+        JSON bytes.
         """
-        qs_dict = dict(qs_dict)  # make a copy to avoid mutating input
+        qs_dict = dict(qs_dict)  # the caller's dict is left as it was
         packed = [k for k, v in qs_dict.items() if "quant_state" in k and isinstance(v, torch.Tensor)]
         if "quant_type" not in qs_dict:
             if len(packed) != 1:
                 raise ValueError(f"expected exactly one packed quant_state item, found {packed}")
             qs_dict.update(_unpack_tensor_to_dict(qs_dict.pop(packed[0])))
-        qs_dict = {k.split(".")[-1]: v for k, v in qs_dict.items()}  # strip prefixes
+        qs_dict = {k.split(".")[-1]: v for k, v in qs_dict.items()}  # keep the last dotted part of each key
 
         if qs_dict["quant_type"] != "nf4":
             raise NotImplementedError(f"quant_type {qs_dict['quant_type']!r} is not supported")
@@ -189,8 +194,8 @@ class QuantizedArray:
         else:
             absmax = absmax.reshape(-1)
 
-        # quant_map, the NF4 table, is not kept: like bitsandbytes' kernel,
-        # dequantization uses the built-in one
+        # the saved quant_map is not stored: decoding always uses the NF4
+        # table built into the kernels (so does bitsandbytes)
         return cls(
             data=weight.reshape(-1),
             absmax=absmax,
@@ -234,20 +239,23 @@ def quantize(
     double_quant: bool = False,
     dtype=None,
 ) -> QuantizedArray:
-    """Quantize a tensor, bitwise as bitsandbytes does.
+    """Blockwise quantization with bitsandbytes' codes and scales, bit for bit
+    (same arguments as the reference's ``quantize``, array.py:166-213).
 
     Args:
-        array: float16, bfloat16 or float32 CUDA tensor, any shape.
-        qtype: ``"nf4"`` (``quantize_4bit``) or ``"8bit"`` (``quantize_blockwise``).
-        blocksize: power of two; bitsandbytes supports 32-4096 for nf4 and
-            64-4096 for 8bit.
-        code: the codebook for ``"8bit"`` (default :func:`create_dynamic_map`).
-        double_quant: also quantize the absmax values, as bitsandbytes'
-            ``compress_statistics=True``. The offset is their mean, whose float32
-            rounding can differ from torch's, so this part is close to
-            bitsandbytes but not bitwise.
-        dtype: default dequantization dtype (default: ``array.dtype``).
-    (reference array.py:166-213)
+        array: the values (a CUDA tensor of float16, bfloat16 or float32, any
+            shape), quantized as one flat run.
+        qtype: ``"nf4"`` (bitsandbytes' ``quantize_4bit``) or ``"8bit"``
+            (``quantize_blockwise``).
+        blocksize: a power of two (bitsandbytes accepts 32..4096 for NF4 and
+            64..4096 for 8-bit).
+        code: the 8-bit codebook; the dynamic map when omitted.
+        double_quant: quantize the block scales as well, 8-bit in blocks of
+            256 around their mean (bitsandbytes' ``compress_statistics``).
+            That mean is a float32 rounding of its own, which may differ from
+            torch's in the last bit, so this one value is not bitwise.
+        dtype: the result's default decoding dtype (``array.dtype`` when
+            omitted).
     """
     x = array.reshape(-1)
     if qtype == "nf4":

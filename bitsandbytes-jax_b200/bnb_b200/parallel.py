@@ -43,6 +43,7 @@ __all__ = [
     "matmul_sharded",
     "quantize_shard",
     "row_partition",
+    "shard_from_dict",
     "shard_rows",
 ]
 
@@ -123,6 +124,28 @@ def shard_rows(w: QuantizedArray, start: int, stop: int) -> RowShard:
         nested = None
         scales = absmax.reshape(-1)[b0:b1]
     return RowShard(data, scales, nested, bs, b0, start, stop, n, k)
+
+
+def shard_from_dict(weight: torch.Tensor, qs_dict: dict, rank: int, world: int,
+                    device: torch.device | str | None = None) -> RowShard:
+    """This rank's rows of a 4-bit weight saved by HuggingFace with
+    bitsandbytes, loaded straight into ``device``: the arguments of
+    :meth:`QuantizedArray.from_dict` (``weight`` and ``qs_dict`` may stay in
+    host memory, e.g. from a safetensors file), the row range from
+    :func:`row_partition` (whole nested blocks when double-quantized, so the
+    scale codes split cleanly), and only that range's codes and scales --
+    plus the small second-level arrays -- are copied to the device. The full
+    weight never lands on any GPU."""
+    w = QuantizedArray.from_dict(weight, qs_dict)
+    if w.ndim != 2:
+        raise ValueError(f"row shards are of 2-D weights, got shape {w.shape}")
+    n, k = w.shape
+    unit = w.blocksize
+    if isinstance(w.absmax, QuantizedArray):
+        unit *= w.absmax.blocksize
+    start, stop = row_partition(n, k, unit, world)[rank]
+    shard = shard_rows(w, start, stop)
+    return shard if device is None else shard.to(device)
 
 
 def matmul_rows(x: torch.Tensor, shard: RowShard, out: torch.Tensor | None = None) -> torch.Tensor:

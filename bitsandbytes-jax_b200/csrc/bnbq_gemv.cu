@@ -42,7 +42,6 @@ struct GemvArgs {
   int k;
   int log2_bs;
   int log2_bs2;
-  PeerOut px;  // exchange mode (the bulk kernel only) when px.inbox != nullptr
 };
 
 template <typename XT>
@@ -490,7 +489,7 @@ constexpr int kMaxGroupsPerFlush = 32;  // partial sums held in shared memory be
 // (short rows: more warps than one row's chunks could keep busy).
 template <typename XT, int M, int R, bool NESTED, int SLOTS, bool SIS, int RG, bool PX>
 __global__ void __launch_bounds__(kMaxWarps * 32, 1)
-gemv_bulk_kernel(GemvArgs a, int n_groups, int n_stages, uint32_t stage_bytes) {
+gemv_bulk_kernel(GemvArgs a, int n_groups, int n_stages, uint32_t stage_bytes, PeerOut px) {
   static_assert(R % RG == 0, "row groups split the stage's rows evenly");
   constexpr int RT = R / RG;  // rows of a stage per consumer thread
   constexpr bool scales_in_stage = SIS;
@@ -506,8 +505,8 @@ gemv_bulk_kernel(GemvArgs a, int n_groups, int n_stages, uint32_t stage_bytes) {
   const int lane = tid & 31, warp = tid >> 5;
   const int ncw = (blockDim.x >> 5) - 1;  // consumer warps; the last warp produces
   const int ncons = ncw * 32;
-  const int wpg = ncw / RG;        // warps per row group (the host makes ncw a multiple of RG)
-  const int gthreads = wpg * 32;   // threads per row group
+  const int wpg = RG == 1 ? ncw : ncw / RG;  // warps per row group (the host makes ncw a multiple of RG)
+  const int gthreads = RG == 1 ? ncons : wpg * 32;  // threads per row group
   const int rgi = RG == 1 ? 0 : tid / gthreads;  // this thread's row group (consumers); constant for RG = 1
   const int lt = tid - rgi * gthreads;
   const int r0 = rgi * RT;         // its first row of a stage
@@ -740,8 +739,26 @@ gemv_bulk_kernel(GemvArgs a, int n_groups, int n_stages, uint32_t stage_bytes) {
   // the CTA reports that it has finished the call.
   __syncwarp();
   if (lane == 0) mbar_arrive(smem_u32(&s_done_bar));
-  constexpr bool exchange = PX;  // a compile-time variant: the plain kernel carries no exchange code
-  const uint32_t epoch = exchange ? peer_epoch(a.px) : 0u;  // after griddepcontrol.wait
+  if constexpr (!PX) {  // the plain kernel: warp 0 alone finishes
+    if (warp != 0) return;
+    if (!mbar_wait(smem_u32(&s_done_bar), 0) || s_abort) return;
+    for (int e = lane; e < gl * M * R; e += 32) {
+      const int gi = e / (M * R), idx = e % (M * R);
+      const int m = idx / R, r = idx % R;
+      float v = 0.0f;
+      if constexpr (RG == 1) {
+        for (int w = 0; w < ncw; ++w) v += s_part[gi][w][idx];
+      } else {
+        const int w0 = (r / RT) * wpg, pi = m * RT + r % RT;
+        for (int w = w0; w < w0 + wpg; ++w) v += s_part[gi][w][pi];
+      }
+      const int64_t row = (int64_t(blockIdx.x) + int64_t(gi) * gridDim.x) * R + r;
+      if (row < a.n_rows) store_y<XT>(a.y, int64_t(m) * a.ldy + row, v);
+    }
+    return;
+  }
+  constexpr bool exchange = PX;
+  const uint32_t epoch = exchange ? peer_epoch(px) : 0u;  // after griddepcontrol.wait
   if (warp == 0 && mbar_wait(smem_u32(&s_done_bar), 0) && !s_abort) {
     for (int e = lane; e < gl * M * R; e += 32) {
       const int gi = e / (M * R), idx = e % (M * R);
@@ -752,15 +769,15 @@ gemv_bulk_kernel(GemvArgs a, int n_groups, int n_stages, uint32_t stage_bytes) {
       const int64_t row = (int64_t(blockIdx.x) + int64_t(gi) * gridDim.x) * R + r;
       if (row < a.n_rows) {
         store_y<XT>(a.y, int64_t(m) * a.ldy + row, v);
-        if (exchange) peer_send(a.px, epoch, m, row, bits_of<XT>(v));
+        if (exchange) peer_send(px, epoch, m, row, bits_of<XT>(v));
       }
     }
   }
   if constexpr (exchange) {
-    if (!peer_receive(a.px, epoch, M, a.n_rows, int64_t(blockIdx.x) * ncons + tid, int64_t(gridDim.x) * ncons))
+    if (!peer_receive(px, epoch, M, a.n_rows, int64_t(blockIdx.x) * ncons + tid, int64_t(gridDim.x) * ncons))
       s_rx_expired = 1;
     named_bar_sync(2, ncons);
-    if (tid == 0) peer_finish_cta(a.px, epoch, s_rx_expired != 0);
+    if (tid == 0) peer_finish_cta(px, epoch, s_rx_expired != 0);
   }
 }
 
@@ -814,9 +831,11 @@ bool plan_bulk(int m, int k, int log2_bs, bool nested, int smem_optin, BulkPlan*
   return false;
 }
 
+// px: the exchange mode (nullptr: none).
 template <typename XT, int M, int R, bool NESTED, int SLOTS, int RG = 1>
-int launch_bulk_t(const GemvArgs& a, const BulkPlan& p, const DeviceInfo& di, cudaStream_t s) {
-  const bool px = a.px.inbox != nullptr;
+int launch_bulk_t(const GemvArgs& a, const BulkPlan& p, const DeviceInfo& di, cudaStream_t s,
+                  const PeerOut* xp = nullptr) {
+  const bool px = xp != nullptr;
   auto kern = p.scales_in_stage ? (px ? gemv_bulk_kernel<XT, M, R, NESTED, SLOTS, true, RG, true>
                                       : gemv_bulk_kernel<XT, M, R, NESTED, SLOTS, true, RG, false>)
                                 : (px ? gemv_bulk_kernel<XT, M, R, NESTED, SLOTS, false, RG, true>
@@ -839,7 +858,7 @@ int launch_bulk_t(const GemvArgs& a, const BulkPlan& p, const DeviceInfo& di, cu
   const int64_t min_grid = (n_groups + kMaxGroupsPerFlush - 1) / kMaxGroupsPerFlush;  // <= 32 groups per CTA
   if (grid < min_grid) grid = min_grid;
   // the exchange polls for peers from every CTA: all of them must be resident
-  if (a.px.inbox && grid > di.sm_count) return BNBQ_ERR_UNSUPPORTED;
+  if (px && grid > di.sm_count) return BNBQ_ERR_UNSUPPORTED;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(unsigned(grid));
   cfg.blockDim = dim3((p.ncw + 1) * 32);
@@ -850,35 +869,36 @@ int launch_bulk_t(const GemvArgs& a, const BulkPlan& p, const DeviceInfo& di, cu
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  if (cudaLaunchKernelEx(&cfg, kern, a, int(n_groups), stages, p.stage_bytes) != cudaSuccess)
+  if (cudaLaunchKernelEx(&cfg, kern, a, int(n_groups), stages, p.stage_bytes, px ? *xp : PeerOut{}) != cudaSuccess)
     return BNBQ_ERR_CUDA;
   return launch_status();
 }
 
 template <typename XT, int M, bool NESTED>
-int launch_bulk(const GemvArgs& a, const BulkPlan& p, const DeviceInfo& di, cudaStream_t s) {
+int launch_bulk(const GemvArgs& a, const BulkPlan& p, const DeviceInfo& di, cudaStream_t s,
+                const PeerOut* xp = nullptr) {
   if constexpr (M <= 2) {
     if (p.groups > 1) {  // short rows: one chunk per thread, row groups over a 4- or 3-row stage
       if (p.slots != 1) return BNBQ_ERR_UNSUPPORTED;
       switch (p.groups) {
-        case 2: return launch_bulk_t<XT, M, 4, NESTED, 1, 2>(a, p, di, s);
-        case 3: return launch_bulk_t<XT, M, 3, NESTED, 1, 3>(a, p, di, s);
-        case 4: return launch_bulk_t<XT, M, 4, NESTED, 1, 4>(a, p, di, s);
+        case 2: return launch_bulk_t<XT, M, 4, NESTED, 1, 2>(a, p, di, s, xp);
+        case 3: return launch_bulk_t<XT, M, 3, NESTED, 1, 3>(a, p, di, s, xp);
+        case 4: return launch_bulk_t<XT, M, 4, NESTED, 1, 4>(a, p, di, s, xp);
         default: return BNBQ_ERR_UNSUPPORTED;
       }
     }
     if (p.slots == 1) {
       switch (p.rows) {
-        case 4: return launch_bulk_t<XT, M, 4, NESTED, 1>(a, p, di, s);
-        case 2: return launch_bulk_t<XT, M, 2, NESTED, 1>(a, p, di, s);
-        default: return launch_bulk_t<XT, M, 1, NESTED, 1>(a, p, di, s);
+        case 4: return launch_bulk_t<XT, M, 4, NESTED, 1>(a, p, di, s, xp);
+        case 2: return launch_bulk_t<XT, M, 2, NESTED, 1>(a, p, di, s, xp);
+        default: return launch_bulk_t<XT, M, 1, NESTED, 1>(a, p, di, s, xp);
       }
     }
     if constexpr (M == 1) {
       switch (p.rows) {
-        case 4: return launch_bulk_t<XT, 1, 4, NESTED, 2>(a, p, di, s);
-        case 2: return launch_bulk_t<XT, 1, 2, NESTED, 2>(a, p, di, s);
-        default: return launch_bulk_t<XT, 1, 1, NESTED, 2>(a, p, di, s);
+        case 4: return launch_bulk_t<XT, 1, 4, NESTED, 2>(a, p, di, s, xp);
+        case 2: return launch_bulk_t<XT, 1, 2, NESTED, 2>(a, p, di, s, xp);
+        default: return launch_bulk_t<XT, 1, 1, NESTED, 2>(a, p, di, s, xp);
       }
     }
   }
@@ -1256,7 +1276,6 @@ int gemv_exchange_launch(int dtype, const void* x, int32_t m, int32_t k, const u
   a.ldy = px.ldf;
   a.block0 = absmax2_block0; a.k = k; a.log2_bs = log2_exact(blocksize);
   a.log2_bs2 = absmax_q ? log2_exact(blocksize2) : 0;
-  a.px = px;
   const bool nested = absmax_q != nullptr;
   if (nested && !aligned(code2, 16)) return BNBQ_ERR_UNSUPPORTED;
   BulkPlan p;
@@ -1264,12 +1283,17 @@ int gemv_exchange_launch(int dtype, const void* x, int32_t m, int32_t k, const u
   if (p.scales_in_stage &&
       !aligned(nested ? static_cast<const void*>(absmax_q) : static_cast<const void*>(absmax), 16))
     p.scales_in_stage = 0;
+  const PeerOut* xp = &px;
   if (dtype == BNBQ_BF16) {
-    if (m == 1) return nested ? launch_bulk<__nv_bfloat16, 1, true>(a, p, di, s) : launch_bulk<__nv_bfloat16, 1, false>(a, p, di, s);
-    return nested ? launch_bulk<__nv_bfloat16, 2, true>(a, p, di, s) : launch_bulk<__nv_bfloat16, 2, false>(a, p, di, s);
+    if (m == 1)
+      return nested ? launch_bulk<__nv_bfloat16, 1, true>(a, p, di, s, xp)
+                    : launch_bulk<__nv_bfloat16, 1, false>(a, p, di, s, xp);
+    return nested ? launch_bulk<__nv_bfloat16, 2, true>(a, p, di, s, xp)
+                  : launch_bulk<__nv_bfloat16, 2, false>(a, p, di, s, xp);
   }
-  if (m == 1) return nested ? launch_bulk<__half, 1, true>(a, p, di, s) : launch_bulk<__half, 1, false>(a, p, di, s);
-  return nested ? launch_bulk<__half, 2, true>(a, p, di, s) : launch_bulk<__half, 2, false>(a, p, di, s);
+  if (m == 1)
+    return nested ? launch_bulk<__half, 1, true>(a, p, di, s, xp) : launch_bulk<__half, 1, false>(a, p, di, s, xp);
+  return nested ? launch_bulk<__half, 2, true>(a, p, di, s, xp) : launch_bulk<__half, 2, false>(a, p, di, s, xp);
 }
 
 int gemv_xtab_launch(int dtype, const void* x, int m, int k, const uint8_t* w, int64_t n_rows, int blocksize,

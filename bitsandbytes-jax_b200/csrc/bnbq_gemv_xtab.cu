@@ -110,7 +110,6 @@ struct XtabArgs {
   float* partial;      // [row_blocks][groups][M][32]
   int64_t n_rows, ldy, block0, units;
   int k, log2_bs, log2_bs2, groups, row_blocks;
-  PeerOut px;  // exchange mode of the reduction (px.inbox != nullptr)
   uint32_t dyn_bytes;  // dynamic shared memory of the launch
 };
 
@@ -733,7 +732,7 @@ bool fits(int dyn) {
 }
 
 template <typename XT, int M, int NB, bool NESTED>
-int launch_t(const CUtensorMap& map, const XtabArgs& a0, const DeviceInfo& di, cudaStream_t s) {
+int launch_t(const CUtensorMap& map, const XtabArgs& a0, const DeviceInfo& di, cudaStream_t s, const PeerOut* xp) {
   constexpr uint32_t kStage = Cfg<M>::kStageBytes;
   auto kern = gemv_xtab_kernel<XT, M, NB, NESTED>;
   XtabArgs a = a0;
@@ -747,7 +746,7 @@ int launch_t(const CUtensorMap& map, const XtabArgs& a0, const DeviceInfo& di, c
   const int dyn = dyn_bytes(di);
   if (!fits<M>(dyn)) return BNBQ_ERR_UNSUPPORTED;
   a.dyn_bytes = uint32_t(dyn);
-  if (a.px.inbox) {  // the exchange polls for peers from every reduction CTA: all must be resident
+  if (xp) {  // the exchange polls for peers from every reduction CTA: all must be resident
     int per_sm = 0;
     if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, gemv_xtab_reduce_kernel<XT, M>, kRedThreads, 0) !=
         cudaSuccess)
@@ -781,19 +780,20 @@ int launch_t(const CUtensorMap& map, const XtabArgs& a0, const DeviceInfo& di, c
   rc.blockDim = dim3(kRedThreads);
   rc.dynamicSmemBytes = 0;
   if (cudaLaunchKernelEx(&rc, gemv_xtab_reduce_kernel<XT, M>, static_cast<const float*>(a.partial), a.groups,
-                         a.row_blocks, a.n_rows, a.y, a.ldy, a.px) != cudaSuccess)
+                         a.row_blocks, a.n_rows, a.y, a.ldy, xp ? *xp : PeerOut{}) != cudaSuccess)
     return BNBQ_ERR_CUDA;
   return launch_status();
 }
 
 template <typename XT, int M, bool NESTED>
-int launch_nb(int nb, const CUtensorMap& map, const XtabArgs& a, const DeviceInfo& di, cudaStream_t s) {
+int launch_nb(int nb, const CUtensorMap& map, const XtabArgs& a, const DeviceInfo& di, cudaStream_t s,
+              const PeerOut* xp) {
   switch (nb) {
-    case 1: return launch_t<XT, M, 1, NESTED>(map, a, di, s);
-    case 2: return launch_t<XT, M, 2, NESTED>(map, a, di, s);
-    case 4: return launch_t<XT, M, 4, NESTED>(map, a, di, s);
+    case 1: return launch_t<XT, M, 1, NESTED>(map, a, di, s, xp);
+    case 2: return launch_t<XT, M, 2, NESTED>(map, a, di, s, xp);
+    case 4: return launch_t<XT, M, 4, NESTED>(map, a, di, s, xp);
     case 8:
-      if constexpr (M == 1) return launch_t<XT, M, 8, NESTED>(map, a, di, s);
+      if constexpr (M == 1) return launch_t<XT, M, 8, NESTED>(map, a, di, s, xp);
       else return BNBQ_ERR_UNSUPPORTED;
     default: return BNBQ_ERR_UNSUPPORTED;
   }
@@ -801,7 +801,7 @@ int launch_nb(int nb, const CUtensorMap& map, const XtabArgs& a, const DeviceInf
 
 // One pass over rows [m0, m0 + mm) of x (mm = 1 or 2).
 template <typename XT>
-int launch_rows(int mm, const XtabArgs& base, const uint8_t* w, bool nested, const DeviceInfo& di,
+int launch_rows(int mm, const XtabArgs& base, const uint8_t* w, bool nested, const DeviceInfo& di, const PeerOut* xp,
                 cudaStream_t s) {
   const int gk = mm == 1 ? Cfg<1>::kGroupK : Cfg<2>::kGroupK;
   const int bs = 1 << base.log2_bs;
@@ -823,8 +823,8 @@ int launch_rows(int mm, const XtabArgs& base, const uint8_t* w, bool nested, con
              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
     return BNBQ_ERR_UNSUPPORTED;
   if (mm == 1)
-    return nested ? launch_nb<XT, 1, true>(nb, map, a, di, s) : launch_nb<XT, 1, false>(nb, map, a, di, s);
-  return nested ? launch_nb<XT, 2, true>(nb, map, a, di, s) : launch_nb<XT, 2, false>(nb, map, a, di, s);
+    return nested ? launch_nb<XT, 1, true>(nb, map, a, di, s, xp) : launch_nb<XT, 1, false>(nb, map, a, di, s, xp);
+  return nested ? launch_nb<XT, 2, true>(nb, map, a, di, s, xp) : launch_nb<XT, 2, false>(nb, map, a, di, s, xp);
 }
 
 }  // namespace
@@ -898,7 +898,6 @@ int gemv_xtab_launch(int dtype, const void* x, int m, int k, const uint8_t* w, i
   a.k = k;
   a.log2_bs = l2;
   a.log2_bs2 = absmax_q ? log2_exact(blocksize2) : 0;
-  if (px) a.px = *px;
   const size_t es = dtype == BNBQ_F32 ? 4 : 2;
   const bool nested = absmax_q != nullptr;
   // passes of two rows, then one of one row (m = 1, 3)
@@ -907,8 +906,8 @@ int gemv_xtab_launch(int dtype, const void* x, int m, int k, const uint8_t* w, i
     a.x = static_cast<const char*>(x) + size_t(m0) * size_t(k) * es;
     a.y = static_cast<char*>(y) + size_t(m0) * size_t(ldy) * es;
     int st;
-    if (dtype == BNBQ_BF16) st = launch_rows<__nv_bfloat16>(mm, a, w, nested, di, s);
-    else if (dtype == BNBQ_F16) st = launch_rows<__half>(mm, a, w, nested, di, s);
+    if (dtype == BNBQ_BF16) st = launch_rows<__nv_bfloat16>(mm, a, w, nested, di, px, s);
+    else if (dtype == BNBQ_F16) st = launch_rows<__half>(mm, a, w, nested, di, px, s);
     else return BNBQ_ERR_UNSUPPORTED;
     if (st != BNBQ_OK) return st;
     m0 += mm;

@@ -87,8 +87,10 @@ def _worker(rank, world, port, queue):
                 x = torch.randn(m, 1024, device=dev, generator=g).to(torch.bfloat16)
                 want = matmul_sharded(x, sh2, r2)
                 assert torch.equal(pg2.matmul(x, sh2).clone(), want), ("fused table", m)
-                assert torch.equal(want, bnb.matmul(x, w2)), ("table rows vs whole", m)
+                if world == 2:  # 2048-row shards take the table GEMV, as the whole weight does
+                    assert torch.equal(want, bnb.matmul(x, w2)), ("table rows vs whole", m)
             xs2 = [torch.randn(1, 1024, device=dev, generator=g).to(torch.bfloat16) for _ in range(4)]
+            wants = [matmul_sharded(xi, sh2, r2) for xi in xs2]
             outs = [torch.empty(1, 4096, dtype=torch.bfloat16, device=dev) for _ in xs2]
             graph = torch.cuda.CUDAGraph()
             with torch.cuda.stream(stream):
@@ -100,8 +102,8 @@ def _worker(rank, world, port, queue):
                     o.zero_()
                 graph.replay()
                 torch.cuda.synchronize()
-                for xi, o in zip(xs2, outs):
-                    assert torch.equal(o, bnb.matmul(xi, w2)), "fused graph replay"
+                for want, o in zip(wants, outs):
+                    assert torch.equal(o, want), "fused graph replay"
             del graph
             torch.cuda.synchronize()
             dist.barrier()
@@ -135,16 +137,19 @@ def _worker(rank, world, port, queue):
 
 @pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device_count() < 2, reason="needs 2 GPUs")
 def test_two_gpu_row_shards_and_block_shards():
+    """Run on 2 GPUs, or on 4 when the box has them (the exchange then has
+    three peers per rank)."""
     import multiprocessing as mp
+    world = 4 if torch.cuda.device_count() >= 4 else 2
     ctx = mp.get_context("spawn")
     queue = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_worker, args=(r, 2, port, queue)) for r in range(2)]
+    procs = [ctx.Process(target=_worker, args=(r, world, port, queue)) for r in range(world)]
     for p in procs:
         p.start()
     errs = []
     try:
-        for _ in range(2):
+        for _ in range(world):
             rank, err = queue.get(timeout=240)
             if err:
                 errs.append(f"rank {rank}:\n{err}")

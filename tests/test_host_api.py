@@ -137,3 +137,39 @@ def test_matmul_shape_errors_before_any_compute():
     w1 = _qa((512 * 64,))
     with pytest.raises(ValueError, match="2-D"):
         bnb_b200.matmul(torch.zeros(1, 512, dtype=torch.bfloat16), w1)
+
+
+@pytest.mark.parametrize("compress", [True, False])
+def test_shard_from_dict_takes_only_the_rank_rows(compress):
+    """parallel.shard_from_dict: each rank's codes and scales are exactly its
+    rows' slices of the whole weight's (host tensors here; the device copy is
+    the shard's .to()), the ranks tile the rows, and a nested weight keeps
+    the whole second level with the shard's first global block."""
+    from bnb_b200.parallel import shard_from_dict
+    n, k = 1024, 512  # 8192 blocks of 64; nested blocks of 256 -> row unit 32
+    g = torch.Generator().manual_seed(1)
+    weight = torch.randint(0, 256, (n * k // 2,), dtype=torch.uint8, generator=g)
+    nb = n * k // 64
+    qs = {"quant_map": torch.zeros(16), "quant_type": "nf4", "blocksize": 64, "dtype": "bfloat16", "shape": [n, k]}
+    if compress:
+        qs.update({"absmax": torch.randint(0, 256, (nb,), dtype=torch.uint8, generator=g),
+                   "nested_absmax": torch.rand(nb // 256, generator=g), "nested_quant_map": bnb_b200.create_dynamic_map(),
+                   "nested_blocksize": 256, "nested_offset": 0.02, "nested_dtype": "float32"})
+    else:
+        qs["absmax"] = torch.rand(nb, generator=g)
+    world, covered = 3, 0
+    for rank in range(world):
+        sh = shard_from_dict(weight, qs, rank, world)
+        assert sh.start == covered and sh.n_rows_total == n and sh.k == k
+        covered = sh.stop
+        assert torch.equal(sh.data, weight[sh.start * k // 2:sh.stop * k // 2])
+        b0, b1 = sh.start * k // 64, sh.stop * k // 64
+        assert sh.block0 == b0
+        assert torch.equal(sh.absmax, qs["absmax"][b0:b1])
+        if compress:
+            assert sh.start % 32 == 0  # whole nested blocks per rank
+            a2, c2, off, bs2 = sh.nested
+            assert torch.equal(a2, qs["nested_absmax"]) and bs2 == 256 and abs(float(off) - 0.02) < 1e-7
+        else:
+            assert sh.nested is None
+    assert covered == n
