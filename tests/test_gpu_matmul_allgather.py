@@ -10,8 +10,8 @@ standalone exchange kernel (M = 3, 8) -- bitwise against matmul_rows (the
 same kernels on the rank's rows): rank 0's columns of the output, the words
 it sent to rank 1 (its values tagged with the call's epoch, in the epoch's
 half), the columns it received, and the state (epoch advanced once per call,
-counter reset). On the GEMV routes the rank's rows also equal the whole
-weight's product bitwise.
+counter reset). For M <= 2 the rank's rows also equal the whole weight's
+product bitwise.
 Then a peer that never sends: the fused kernel's bounded wait expires, is
 counted, and the device stays usable."""
 from __future__ import annotations
@@ -79,7 +79,7 @@ def test_fused_exchange_rank0_of_two(cuda, shape):
             torch.cuda.synchronize()
             assert torch.equal(r0.y[:, a0:b0], mine), (m, rep)
             assert torch.equal(r0.y[:, a1:b1], peer), (m, rep)
-            if m <= 4:
+            if m <= 2:  # the row kernels: a row's result does not depend on how many rows run
                 assert torch.equal(mine, bnb_b200.matmul(x, w)[:, a0:b0]), (m, rep)
             sent = r0.half(1, epoch)[:, a0:b0]
             assert bool((sent >> 32 == epoch).all()), (m, rep)
