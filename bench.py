@@ -607,7 +607,8 @@ def run_matmul_profile(args, local_rank):
 
 def gemm_cases(torch, bnb, device, ms=(64, 512, 2048)):
     """Config 5: the fused NF4 dequantize-GEMM on the Llama-3-70B MLP shapes,
-    beside the reference's fallback (dequantize + matmul)."""
+    beside the reference's fallback (dequantize + matmul) and bnb_b200.matmul
+    (the router: fused up to 512 rows of x, the fallback above)."""
     from bnb_b200.kernels.gemv import matmul_nf4
     out = {}
     peak_tf = 1669.8
@@ -626,8 +627,9 @@ def gemm_cases(torch, bnb, device, ms=(64, 512, 2048)):
             tf = time_graph(torch, lambda i: matmul_nf4(x, w.data, a.data, n, 64, nested=nested),
                             s5, 2, device) / s5
             tr = time_graph(torch, lambda i: x @ w.dequantize(torch.bfloat16).T, s5, 2, device) / s5
+            tm = time_graph(torch, lambda i: bnb.matmul(x, w), s5, 2, device) / s5  # the router's choice
             fl = 2.0 * m * n * k
-            out[f"{n}x{k}_m{m}"] = {"fused_us": round(tf * 1e3, 1),
+            out[f"{n}x{k}_m{m}"] = {"matmul_us": round(tm * 1e3, 1), "fused_us": round(tf * 1e3, 1),
                                     "fused_tflops": round(fl / (tf * 1e-3) / 1e12, 1),
                                     "dequant_matmul_us": round(tr * 1e3, 1),
                                     "speedup_vs_dequant_matmul": round(tr / tf, 2),

@@ -6,11 +6,15 @@ signature, shape checks and errors, and the same custom backward
 kept for the backward pass).
 
 Routing. An NF4 weight with a bfloat16/float16 x, K % 32 == 0 and blocksize >=
-32 never materializes: up to GEMV_MAX_M rows of x run the fused GEMV (float32
-weights, closer to the exact product than the fallback), more rows run the
-fused tcgen05 dequantize-GEMM (weights decoded to x's dtype in tensor memory,
-the fallback's precision, float32 accumulation). Everything else is ``x @ w.dequantize(x.dtype).T``
-with the dequantize on the sm_100a kernels.
+32: up to GEMV_MAX_M rows of x run the fused GEMV (float32 weights, closer to
+the exact product than the fallback), up to FUSED_GEMM_MAX_M rows the fused
+tcgen05 dequantize-GEMM (weights decoded to x's dtype in tensor memory, the
+fallback's precision, float32 accumulation), where the weight never
+materializes. Above that, and for everything else, ``x @ w.dequantize(x.dtype).T``
+with the dequantize on the sm_100a kernels and the product on cuBLAS: measured
+on a B200, the fused GEMM wins up to M = 512 (1.03-1.75x on the Llama-3-8B
+and -70B MLP shapes) and loses from M = 768 on (0.67-0.95x at 768-2048),
+because each 128-row weight tile is decoded once per 256 rows of x.
 """
 from __future__ import annotations
 
@@ -20,6 +24,8 @@ from .array import QuantizedArray
 from .kernels.gemv import _CHUNK, plan_for
 
 __all__ = ["matmul"]
+
+FUSED_GEMM_MAX_M = 512  # rows of x up to which the fused GEMM beats dequantize + cuBLAS (B200, measured)
 
 def matmul(x: torch.Tensor, w: QuantizedArray) -> torch.Tensor:
     """``x @ w.T`` for a 2-D quantized weight ``w`` (N, K).
@@ -51,7 +57,7 @@ def _fused_args(w: QuantizedArray):
 
 
 def _forward(xm: torch.Tensor, w: QuantizedArray) -> torch.Tensor:
-    if _fused_applies(xm, w):
+    if xm.shape[0] <= FUSED_GEMM_MAX_M and _fused_applies(xm, w):
         plan = w.__dict__.get("_bnbq_plan")
         if plan is None or plan.data is not w.data or plan.absmax is not w.absmax or plan.device != xm.device:
             scales, nested = _fused_args(w)

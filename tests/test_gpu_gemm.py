@@ -180,3 +180,18 @@ def test_gemm_no_wait_timeouts(cuda, timeouts_at_start):
     from bnb_b200 import _lib
     torch.cuda.synchronize()
     assert _lib.wait_timeouts() == timeouts_at_start
+
+
+def test_large_m_routes_to_the_fallback(cuda):
+    """Above FUSED_GEMM_MAX_M rows of x (the measured crossover), matmul is the
+    reference's fallback: dequantize on the sm_100a kernels, then a dense
+    matmul; up to it, the fused GEMM."""
+    from bnb_b200._matmul import FUSED_GEMM_MAX_M
+    n, k = 256, 1024
+    w = weight(n, k, seed=7)
+    x = x_rand(FUSED_GEMM_MAX_M + 1, k, torch.bfloat16, 7)
+    assert torch.equal(bnb_b200.matmul(x, w), x @ w.dequantize(torch.bfloat16).T)
+    xs = x[:FUSED_GEMM_MAX_M]
+    a = w.absmax
+    fused = matmul_nf4(xs, w.data, a.data, n, 64, nested=(a.absmax, a.code, a.offset, a.blocksize))
+    assert torch.equal(bnb_b200.matmul(xs, w), fused)
