@@ -18,6 +18,7 @@ LIB_PATH = Path(__file__).resolve().parent / "libbnbq.so"
 F32, F16, BF16 = 0, 1, 2
 OK, ERR_INVALID, ERR_UNSUPPORTED, ERR_MISALIGNED, ERR_CUDA, ERR_DEVICE, ERR_TOO_LARGE = 0, -1, -2, -3, -4, -5, -6
 GEMV_MAX_M = 20
+GEMV8_MAX_M = 4  # BNBQ_GEMV8_MAX_M
 
 DTYPE_CODE = {torch.float32: F32, torch.float16: F16, torch.bfloat16: BF16}
 
@@ -36,6 +37,8 @@ _SIGNATURES = {
     "bnbq_matmul_nf4_ws": "iPiiPliPPPPPilPlPlP",
     "bnbq_matmul_nf4_allgather": "iPiiPliPPPPPilPlllPlPiiPlP",
     "bnbq_gemv_workspace_bytes": "iilP",
+    "bnbq_gemv_blockwise_ws": "iPiiPliPPPPPPilPlPlP",
+    "bnbq_gemv_blockwise_workspace_bytes": "iilP",
     "bnbq_gemv_route": "iiliPiPlP",
     "bnbq_set_gemv_policy": "i",
     "bnbq_rcp_approx_ftz": "PPlP",
@@ -159,6 +162,12 @@ def workspace(device: torch.device, stream: int, nbytes: int) -> torch.Tensor:
 def gemv_workspace_bytes(m: int, k: int, n_rows: int) -> int:
     n = C.c_int64(0)
     check(lib().bnbq_gemv_workspace_bytes(m, k, n_rows, C.byref(n)), "bnbq_gemv_workspace_bytes")
+    return int(n.value)
+
+
+def gemv8_workspace_bytes(m: int, k: int, n_rows: int) -> int:
+    n = C.c_int64(0)
+    check(lib().bnbq_gemv_blockwise_workspace_bytes(m, k, n_rows, C.byref(n)), "bnbq_gemv_blockwise_workspace_bytes")
     return int(n.value)
 
 

@@ -21,7 +21,7 @@ from __future__ import annotations
 import torch
 
 from .array import QuantizedArray
-from .kernels.gemv import _CHUNK, plan_for
+from .kernels.gemv import _CHUNK, gemv_blockwise, gemv_blockwise_applies, plan_for
 
 __all__ = ["matmul"]
 
@@ -57,6 +57,9 @@ def _fused_args(w: QuantizedArray):
 
 
 def _forward(xm: torch.Tensor, w: QuantizedArray) -> torch.Tensor:
+    if w.qtype == "8bit" and _fused8_applies(xm, w):
+        scales, nested = _fused_args(w)
+        return gemv_blockwise(xm, w.data, scales, w.code, w.shape[0], w.blocksize, nested=nested)
     if xm.shape[0] <= FUSED_GEMM_MAX_M and _fused_applies(xm, w):
         plan = w.__dict__.get("_bnbq_plan")
         if plan is None or plan.data is not w.data or plan.absmax is not w.absmax or plan.device != xm.device:
@@ -86,3 +89,13 @@ def _fused_applies(xm: torch.Tensor, w: QuantizedArray) -> bool:
             and xm.shape[0] > 0
             and xm.shape[1] % _CHUNK == 0
             and w.blocksize >= _CHUNK)
+
+
+def _fused8_applies(xm: torch.Tensor, w: QuantizedArray) -> bool:
+    """An 8-bit weight with a 16-bit x of up to GEMV8_MAX_M rows: the fused
+    8-bit GEMV (the reference always takes the fallback for 8-bit weights,
+    _matmul.py:74-79)."""
+    return (xm.dtype in (torch.bfloat16, torch.float16)
+            and xm.is_cuda
+            and w.code is not None
+            and gemv_blockwise_applies(xm.shape[0], xm.shape[1], w.blocksize))

@@ -11,10 +11,11 @@ from .dequantize import (
     dequantize_nf4,
     dequantize_nf4_nested,
 )
-from .gemv import GEMV_MAX_M, gemv_nf4, matmul_nf4
+from .gemv import GEMV8_MAX_M, GEMV_MAX_M, gemv_blockwise, gemv_nf4, matmul_nf4
 from .quantize import absmax_mean, create_dynamic_map, quantize_blockwise, quantize_nf4
 
 __all__ = [
+    "GEMV8_MAX_M",
     "GEMV_MAX_M",
     "NF4_TABLE",
     "absmax_mean",
@@ -23,6 +24,7 @@ __all__ = [
     "dequantize_blockwise_nested",
     "dequantize_nf4",
     "dequantize_nf4_nested",
+    "gemv_blockwise",
     "gemv_nf4",
     "matmul_nf4",
     "quantize_blockwise",

@@ -18,6 +18,8 @@ from .dequantize import _log2_blocksize
 
 _CHUNK = 32
 GEMV_MAX_M = _lib.GEMV_MAX_M
+GEMV8_MAX_M = _lib.GEMV8_MAX_M  # rows of x the fused 8-bit-weight GEMV takes
+_GROUP8 = 128  # elements of K per unit of the 8-bit-weight GEMV (K must be a multiple)
 
 
 def _rows_per_warp(m: int) -> int:
@@ -216,3 +218,75 @@ def plan_for(w, scales, nested, device) -> FusedPlan:
         plan = FusedPlan(w.data, w.absmax, scales, n, k, w.blocksize, nested, device)
         w.__dict__["_bnbq_plan"] = plan
     return plan
+
+
+def gemv_blockwise_applies(m: int, k: int, blocksize: int) -> bool:
+    """Whether :func:`gemv_blockwise` takes an (m x k) x with this blocksize."""
+    return 1 <= m <= GEMV8_MAX_M and k % _GROUP8 == 0 and blocksize >= _CHUNK
+
+
+def gemv_blockwise(
+    x: torch.Tensor,
+    data: torch.Tensor,
+    absmax: torch.Tensor,
+    code: torch.Tensor,
+    n_rows: int,
+    blocksize: int,
+    *,
+    nested: tuple[torch.Tensor, torch.Tensor, torch.Tensor, int] | None = None,
+    absmax2_block0: int = 0,
+    out: torch.Tensor | None = None,
+) -> torch.Tensor:
+    """``x @ W.T`` for an 8-bit blockwise-quantized weight W (n_rows, K) with
+    codebook ``code``, never materialized (``bnbq_gemv_blockwise_ws``).
+
+    The reference has no such kernel: it computes ``x @ w.dequantize().T``
+    for 8-bit weights (_matmul.py:58-59, routed by _matmul.py:74-79). Same
+    arguments and numerics as :func:`gemv_nf4` (float32 products with the
+    exact codebook value, each block's scale applied once, one rounding), plus
+    the codebook; ``1 <= M <= GEMV8_MAX_M`` and ``K % 128 == 0``."""
+    if x.dim() != 2:
+        raise ValueError(f"x must be 2-D (M, K), got shape {tuple(x.shape)}")
+    m, k = x.shape
+    if not 0 < m <= GEMV8_MAX_M:
+        raise ValueError(f"gemv_blockwise takes 1..{GEMV8_MAX_M} rows of x, got {m}")
+    if x.dtype not in (torch.bfloat16, torch.float16):
+        raise NotImplementedError(f"gemv_blockwise of {x.dtype} x is not implemented")
+    if k % _GROUP8:
+        raise ValueError(f"K must be a multiple of {_GROUP8}, got {k}")
+    _log2_blocksize(blocksize)
+    if blocksize < _CHUNK:
+        raise ValueError(f"blocksize must be >= {_CHUNK}, got {blocksize}")
+    assert data.dtype == torch.uint8 and data.numel() == n_rows * k, (tuple(data.shape), n_rows, k)
+    _lib.require_cuda(x, data, absmax)
+    xs = _lib.aligned(x)
+    w = _lib.aligned(data.reshape(-1))
+    cb = _lib.aligned(_f32_on(code, x.device).reshape(-1), 4)
+    if cb.numel() != 256:
+        raise ValueError(f"code must have 256 entries, got {cb.numel()}")
+    if nested is None:
+        assert absmax.dtype == torch.float32, absmax.dtype
+        a, aq, a2, c2, off, bs2 = _lib.aligned(absmax.reshape(-1), 4), None, None, None, None, 0
+    else:
+        absmax2, code2, offset, bs2 = nested
+        assert absmax.dtype == torch.uint8, absmax.dtype
+        _log2_blocksize(bs2)
+        a = None
+        aq = _lib.aligned(absmax.reshape(-1))
+        a2 = _lib.aligned(_f32_on(absmax2, x.device).reshape(-1), 4)
+        c2 = _lib.aligned(_f32_on(code2, x.device).reshape(-1), 4)
+        off = _lib.aligned(_f32_on(offset, x.device).reshape(1), 4)
+    if out is None:
+        out = torch.empty((m, n_rows), dtype=x.dtype, device=x.device)
+    assert out.dtype == x.dtype and out.stride(1) == 1 and out.shape == (m, n_rows)
+    stream = _lib.stream_of(xs)
+    ws = _lib.workspace(x.device, stream, _lib.gemv8_workspace_bytes(m, k, n_rows))
+    args = ("bnbq_gemv_blockwise_ws", _lib.DTYPE_CODE[x.dtype], xs.data_ptr(), m, k, w.data_ptr(), n_rows,
+            blocksize, cb.data_ptr(), _lib.ptr(a), _lib.ptr(aq), _lib.ptr(a2), _lib.ptr(c2), _lib.ptr(off), bs2,
+            absmax2_block0, out.data_ptr(), out.stride(0), ws.data_ptr(), ws.numel(), stream)
+    if x.device.index == torch.cuda.current_device():
+        _lib.call(*args)
+    else:
+        with torch.cuda.device(x.device):
+            _lib.call(*args)
+    return out

@@ -1332,6 +1332,37 @@ extern "C" int bnbq_gemv_workspace_bytes(int32_t m, int32_t k, int64_t n_rows, i
   return BNBQ_OK;
 }
 
+namespace bnbq {
+int64_t gemv_code8_workspace_bytes(int m, int k, int64_t n_rows);
+int gemv_code8_launch(int dtype, const void* x, int m, int k, const uint8_t* w, int64_t n_rows, int blocksize,
+                      const float* code, const float* absmax, const uint8_t* absmax_q, const float* absmax2,
+                      const float* code2, const float* offset, int blocksize2, int64_t absmax2_block0, void* y,
+                      int64_t ldy, void* workspace, int64_t workspace_bytes, cudaStream_t s);
+}  // namespace bnbq
+
+extern "C" int bnbq_gemv_blockwise_workspace_bytes(int32_t m, int32_t k, int64_t n_rows, int64_t* bytes) {
+  if (!bytes || m < 1 || m > BNBQ_GEMV8_MAX_M || k < 1 || n_rows < 1) return BNBQ_ERR_INVALID;
+  if (k % 128) return BNBQ_ERR_UNSUPPORTED;
+  *bytes = gemv_code8_workspace_bytes(m, k, n_rows);
+  return *bytes > 0 ? BNBQ_OK : BNBQ_ERR_UNSUPPORTED;
+}
+
+extern "C" int bnbq_gemv_blockwise_ws(int dtype, const void* x, int32_t m, int32_t k, const uint8_t* w,
+                                      int64_t n_rows, int32_t blocksize, const float* code, const float* absmax,
+                                      const uint8_t* absmax_q, const float* absmax2, const float* code2,
+                                      const float* offset, int32_t blocksize2, int64_t absmax2_block0, void* y,
+                                      int64_t ldy, void* workspace, int64_t workspace_bytes, void* stream) {
+  if (int st = gemv_validate(dtype, x, m, k, w, n_rows, blocksize, absmax, absmax_q, absmax2, code2,
+                             offset, blocksize2, y, ldy))
+    return st;
+  if (m > BNBQ_GEMV8_MAX_M || !code || workspace_bytes < 0 || !workspace) return BNBQ_ERR_INVALID;
+  if (k % 128) return BNBQ_ERR_UNSUPPORTED;
+  if (!aligned(code, 4)) return BNBQ_ERR_MISALIGNED;
+  return gemv_code8_launch(dtype, x, m, k, w, n_rows, blocksize, code, absmax, absmax_q, absmax2, code2, offset,
+                           blocksize2, absmax2_block0, y, ldy, workspace, workspace_bytes,
+                           static_cast<cudaStream_t>(stream));
+}
+
 extern "C" int bnbq_gemv_nf4_ws(int dtype, const void* x, int32_t m, int32_t k, const uint8_t* w,
                                 int64_t n_rows, int32_t blocksize, const float* absmax,
                                 const uint8_t* absmax_q, const float* absmax2, const float* code2,

@@ -267,13 +267,13 @@ struct ScaleWords {
   bool valid;
 };
 
-template <int M, int NB, bool NESTED>
+template <int M, int NB, bool NESTED, int GK = Cfg<M>::kGroupK>
 __device__ __forceinline__ void fetch_scales(ScaleWords<NB, NESTED>& s, const XtabArgs& a, int g, int rb, int lane) {
   const int64_t row = int64_t(rb) * kRows + lane;
   s.valid = row < a.n_rows;
   if (!s.valid) return;
   const int64_t bpr = int64_t(a.k) >> a.log2_bs;  // blocks per row
-  s.gb0 = row * bpr + ((int64_t(g) * Cfg<M>::kGroupK) >> a.log2_bs);
+  s.gb0 = row * bpr + ((int64_t(g) * GK) >> a.log2_bs);
   if constexpr (NESTED) {
     if constexpr (NB == 8) {
       ldg_u32x2(a.absmax_q + s.gb0, s.q[0], s.q[1]);
@@ -695,6 +695,259 @@ __global__ void __launch_bounds__((Cfg<M>::kConsumers + kProducers) * 32, 1)
 
 }
 
+// ---------------------------------------------------------------------------
+// 8-bit codebook weights (quantize_blockwise: one code byte per element, a
+// 256-entry float32 codebook): gemv_code8_kernel, for 1 to 4 rows of x.
+// The reference has no fused path for them (its router sends them to
+// x @ dequantize(w).T, _matmul.py:74-79); the numerics here are those of the
+// NF4 GEMV: float32 products of x with the exact codebook value, block sums,
+// the block's scale applied once (acc = fma.rn.ftz(a, block sum, 0), a being
+// the float32 absmax or the double-quantized one decoded as
+// QuantizedArray.dequantize does), the blocks, then the groups, added in a
+// fixed order, one rounding to x's dtype. A one-hot x gives
+// mul.ftz(code[q], a) rounded once: the dequantized weight, bitwise.
+// Layout: units of (128 elements of K, 32 rows), streamed by the same
+// producers as the NF4 kernels (the unit is again 32 rows x 128 bytes); lane l
+// owns code word l -- elements 4l .. 4l + 3 -- of every row of its unit, with
+// x's 4 matching elements in registers. The codebook sits in shared memory
+// once per lane, entry (code c, lane l) at c << 8 | l << 2 of a 64 KB-aligned
+// table, so one byte permute forms each load's address and the 32 lanes'
+// loads always hit 32 distinct banks, whatever the codes are.
+// Row sums without selects: at slot s lane l takes row s ^ l of the unit
+// (its code-word loads hit bank l too). At the butterfly level with lane mask
+// m the lane adds its partner's slot s + m into its slot s (s & m == 0); both
+// hold the same row, because (s + m) ^ (l ^ m) = s ^ l. The levels inside a
+// block (m < 32 / NB lanes) run first, each block's sum then gets its scale
+// -- lane r decoded the NB scales of row r and hands the one a lane needs to
+// it with one shuffle --, and the remaining levels add a row's blocks,
+// leaving row l of the unit in lane l.
+constexpr int kGroupK8 = 128;         // elements of K per unit
+constexpr uint32_t kTab8Bytes = 65536;  // 256 codes x 256-byte rows (32 lanes used)
+
+template <int M>
+struct Cfg8 {
+  static constexpr int kConsumers = M >= 3 ? 8 : 16;  // (registers: 4 x M values per lane and row)
+  static constexpr int kRound = lcm(kConsumers, kProducers);
+};
+
+template <typename XT, int M, int NB, bool NESTED>
+__global__ void __launch_bounds__((Cfg8<M>::kConsumers + kProducers) * 32, 1)
+    gemv_code8_kernel(const __grid_constant__ CUtensorMap tmap, const XtabArgs a, const float* __restrict__ code) {
+  constexpr uint32_t kStage = kRows * kGroupK8;  // 4 KB
+  constexpr int LPB = 32 / NB;
+  static_assert(LPB >= 2, "two or more code words per block");
+  extern __shared__ __align__(1024) uint8_t smem[];
+  __shared__ float s_code2[256];
+  __shared__ __align__(8) uint64_t s_bar[2 * kMaxStages];
+  __shared__ volatile int s_abort;
+  __shared__ volatile int s_next[kProducers];
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int ncw = int(blockDim.x >> 5) - kProducers;
+  const int64_t u0 = int64_t(blockIdx.x) * a.units / gridDim.x;
+  const int64_t u1 = int64_t(blockIdx.x + 1) * a.units / gridDim.x;
+  const int n_units = int(u1 - u0);
+  const Order ord(u0, u1, a.row_blocks);
+  const uint32_t dyn0 = smem_u32(smem);
+  const uint32_t tab = (dyn0 + kTabAlign - 1) & ~(kTabAlign - 1);
+  const int s_lo = int((tab - dyn0) / kStage);
+  int S = s_lo + int((dyn0 + a.dyn_bytes - (tab + kTab8Bytes)) / kStage);
+  if (S > kMaxStages) S = kMaxStages;
+  S -= S % Cfg8<M>::kRound;
+  const uint32_t stage_hi = tab + kTab8Bytes;
+  const uint32_t full0 = smem_u32(s_bar), empty0 = full0 + 8u * kMaxStages;
+
+  if (threadIdx.x == 0) {
+    s_abort = S < Cfg8<M>::kRound || dyn0 + a.dyn_bytes < tab + kTab8Bytes;
+    for (int q = 0; q < kProducers; ++q) s_next[q] = -1;
+    for (int s = 0; s < S; ++s) {
+      mbar_init(full0 + 8u * s, 1);
+      mbar_init(empty0 + 8u * s, 1);
+    }
+    fence_mbar_init();
+  }
+  __syncthreads();
+  asm volatile("griddepcontrol.launch_dependents;");
+  if (s_abort) {
+    if (threadIdx.x == 0) atomicAdd(&g_bnbq_wait_timeouts, 1u);
+    return;
+  }
+  auto stage_addr = [&](int slot) -> uint32_t {
+    return slot < s_lo ? dyn0 + uint32_t(slot) * kStage : stage_hi + uint32_t(slot - s_lo) * kStage;
+  };
+
+  if (warp >= ncw) {  // ----------------------------------------------- producers
+    const int q = warp - ncw;
+    if (lane == 0 && q < n_units) {
+      if (q == 0) asm volatile("prefetch.tensormap [%0];" ::"l"(&tmap) : "memory");
+      int i = q, slot = q % S, g, rb;
+      uint32_t use = uint32_t(q / S);
+      ord.at(uint32_t(q), g, rb);
+      bool ok = true;
+      int unissued = 0x7fffffff;
+      while (true) {
+        if (use > 0) ok = mbar_wait(empty0 + 8u * slot, (use - 1u) & 1u);
+        if (!ok || s_abort) {
+          unissued = i;
+          break;
+        }
+        const uint32_t full = full0 + 8u * slot;
+        mbar_arrive_expect_tx(full, kStage);
+        tma_load_2d(stage_addr(slot), &tmap, g * kGroupK8, rb * kRows, full);
+        if (i + kProducers >= n_units) break;
+        ord.advance(uint32_t(i), kProducers, g, rb);
+        i += kProducers;
+        slot += kProducers;
+        if (slot >= S) {
+          slot -= S;
+          ++use;
+        }
+      }
+      if (!ok) {
+        __threadfence_block();
+        s_abort = 1;
+      }
+      s_next[q] = unissued;
+    } else if (lane == 0) {
+      s_next[q] = 0x7fffffff;
+    }
+    return;
+  }
+
+  // ---------------------------------------------------------------- consumers
+  const int ncons = ncw * 32;
+  // the codebook, one copy per lane (weight constants: before the wait)
+  for (int c = warp; c < 256; c += ncw) sts_f32(tab + (uint32_t(c) << 8) + uint32_t(lane) * 4u, __ldg(code + c));
+  float offset = 0.0f;
+  if constexpr (NESTED) {
+    for (int i = threadIdx.x; i < 256; i += ncons) s_code2[i] = a.code2[i];
+    offset = *a.offset;
+  }
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+  named_bar_sync(1, ncons);  // the codebook (and code2) are complete
+  const uint32_t base = tab + uint32_t(lane) * 4u;
+  const uint32_t word_ofs = uint32_t(lane) * 4u;
+  const int qs = lane / LPB;
+  const XT* xg = static_cast<const XT*>(a.x);
+
+  int g = 0, rb = 0;
+  ScaleWords<NB, NESTED> sw;
+  uint2 xw[M];  // x's 4 elements of this lane for the unit, per row of x
+  auto fetch_x = [&](int gg) {
+#pragma unroll
+    for (int m = 0; m < M; ++m)
+      xw[m] = __ldg(reinterpret_cast<const uint2*>(xg + int64_t(m) * a.k + int64_t(gg) * kGroupK8 + 4 * lane));
+  };
+  if (warp < n_units) {
+    ord.at(uint32_t(warp), g, rb);
+    fetch_scales<M, NB, NESTED, kGroupK8>(sw, a, g, rb, lane);
+    fetch_x(g);
+  }
+  int slot = warp % S;
+  uint32_t parity = uint32_t((warp / S) & 1);
+  for (int i = warp; i < n_units; i += ncw) {
+    bool ok;
+    if (s_abort) {
+      ok = false;
+      const int q = i % kProducers;
+      const uint64_t t0 = global_ns();
+      while (s_next[q] < 0 && global_ns() - t0 < g_bnbq_wait_limit_ns) {
+      }
+      if (i < s_next[q]) mbar_wait(full0 + 8u * slot, parity);
+    } else {
+      ok = mbar_wait(full0 + 8u * slot, parity);
+      ok = __shfl_sync(0xffffffffu, ok, 0);
+      if (!ok) s_abort = 1;
+    }
+    uint32_t cw[kRows];
+    if (ok) {
+      const uint32_t st = stage_addr(slot) + word_ofs;
+#pragma unroll
+      for (int s = 0; s < kRows; ++s) cw[s] = lds_code(st + (uint32_t(s ^ lane) << 7));
+    }
+    __syncwarp();
+    if (lane == 0) mbar_arrive(empty0 + 8u * slot);
+    slot += ncw;
+    if (slot >= S) {
+      slot -= S;
+      parity ^= 1u;
+    }
+    float a_own[NB];
+    decode_scales<NB, NESTED>(a_own, sw, a, s_code2, offset, 0);
+    float xv[M][4];
+#pragma unroll
+    for (int m = 0; m < M; ++m) {
+      float2 f0, f1;
+      if constexpr (Elem<XT>::kDtype == BNBQ_BF16) {
+        f0 = unpack2_bf16(xw[m].x);
+        f1 = unpack2_bf16(xw[m].y);
+      } else {
+        f0 = unpack2_f16(xw[m].x);
+        f1 = unpack2_f16(xw[m].y);
+      }
+      xv[m][0] = f0.x;
+      xv[m][1] = f0.y;
+      xv[m][2] = f1.x;
+      xv[m][3] = f1.y;
+    }
+    const int gc = g, rbc = rb;
+    if (i + ncw < n_units) {
+      ord.advance(uint32_t(i), uint32_t(ncw), g, rb);
+      fetch_scales<M, NB, NESTED, kGroupK8>(sw, a, g, rb, lane);
+      fetch_x(g);
+    }
+    if (ok) {
+      float acc[NB][M];
+#pragma unroll
+      for (int t = 0; t < NB; ++t) {
+        // this lane's 4 elements of row slot LPB t + k, per row of x
+        auto row_dot = [&](int k, float (&r)[M]) {
+          const uint32_t c = cw[LPB * t + k];
+          const float w0 = lds_f32<0>(__byte_perm(c, base, 0x7604));
+          const float w1 = lds_f32<0>(__byte_perm(c, base, 0x7614));
+          const float w2 = lds_f32<0>(__byte_perm(c, base, 0x7624));
+          const float w3 = lds_f32<0>(__byte_perm(c, base, 0x7634));
+#pragma unroll
+          for (int m = 0; m < M; ++m)
+            r[m] = __fmaf_rn(w3, xv[m][3], __fmaf_rn(w2, xv[m][2], __fmaf_rn(w1, xv[m][1], w0 * xv[m][0])));
+        };
+        // the first level as the slots are made (fewer live values)
+        float v[LPB / 2][M];
+#pragma unroll
+        for (int k = 0; k < LPB / 2; ++k) {
+          float hi[M];
+          row_dot(k, v[k]);
+          row_dot(k + LPB / 2, hi);
+#pragma unroll
+          for (int m = 0; m < M; ++m) v[k][m] += __shfl_xor_sync(0xffffffffu, hi[m], LPB / 2);
+        }
+#pragma unroll
+        for (int mk = LPB / 4; mk >= 1; mk >>= 1)
+#pragma unroll
+          for (int k = 0; k < mk; ++k)
+#pragma unroll
+            for (int m = 0; m < M; ++m) v[k][m] += __shfl_xor_sync(0xffffffffu, v[k + mk][m], mk);
+        float give = a_own[0];
+#pragma unroll
+        for (int p = 1; p < NB; ++p)
+          if ((qs ^ t) == p) give = a_own[p];
+        const float at = __shfl_xor_sync(0xffffffffu, give, LPB * t);
+#pragma unroll
+        for (int m = 0; m < M; ++m) acc[t][m] = fma_ftz(at, v[0][m], 0.0f);
+      }
+#pragma unroll
+      for (int mk = NB / 2; mk >= 1; mk >>= 1)
+#pragma unroll
+        for (int t = 0; t < mk; ++t)
+#pragma unroll
+          for (int m = 0; m < M; ++m) acc[t][m] += __shfl_xor_sync(0xffffffffu, acc[t + mk][m], LPB * mk);
+      float* part = a.partial + ((int64_t(rbc) * a.groups + gc) * M) * kRows + lane;
+#pragma unroll
+      for (int m = 0; m < M; ++m) __stcg(part + m * kRows, acc[0][m]);
+    }
+  }
+}
+
 // --------------------------------------------------------------- host side
 
 PFN_cuTensorMapEncodeTiled_v12000 encoder() {
@@ -827,6 +1080,70 @@ int launch_rows(int mm, const XtabArgs& base, const uint8_t* w, bool nested, con
   return nested ? launch_nb<XT, 2, true>(nb, map, a, di, s, xp) : launch_nb<XT, 2, false>(nb, map, a, di, s, xp);
 }
 
+// ---- 8-bit codebook weights
+int64_t code8_workspace_bytes(int m, int k, int64_t n_rows) {
+  const int64_t rbs = (n_rows + kRows - 1) / kRows;
+  return rbs * (k / kGroupK8) * m * kRows * 4;
+}
+
+template <typename XT, int M, int NB, bool NESTED>
+int launch_code8_t(const CUtensorMap& map, const XtabArgs& a0, const float* code, const DeviceInfo& di,
+                   cudaStream_t s) {
+  auto kern = gemv_code8_kernel<XT, M, NB, NESTED>;
+  XtabArgs a = a0;
+  const int dyn = dyn_bytes(di);
+  if (dyn < int(kTab8Bytes + kTabAlign) || (dyn - int(kTab8Bytes)) / (kRows * kGroupK8) - 1 < Cfg8<M>::kRound)
+    return BNBQ_ERR_UNSUPPORTED;
+  a.dyn_bytes = uint32_t(dyn);
+  static std::atomic<int> attr_set[kMaxDevices];
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return BNBQ_ERR_CUDA;
+  if (attr_set[dev].load(std::memory_order_acquire) != dyn) {
+    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, dyn) != cudaSuccess)
+      return BNBQ_ERR_CUDA;
+    attr_set[dev].store(dyn, std::memory_order_release);
+  }
+  int64_t grid = di.sm_count;
+  if (grid > a.units) grid = a.units;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(unsigned(grid));
+  cfg.blockDim = dim3(unsigned((Cfg8<M>::kConsumers + kProducers) * 32));
+  cfg.dynamicSmemBytes = size_t(dyn);
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  if (cudaLaunchKernelEx(&cfg, kern, map, a, code) != cudaSuccess) return BNBQ_ERR_CUDA;
+  cudaLaunchConfig_t rc = cfg;
+  rc.gridDim = dim3(unsigned(int64_t(a.row_blocks) * M));
+  rc.blockDim = dim3(kRedThreads);
+  rc.dynamicSmemBytes = 0;
+  if (cudaLaunchKernelEx(&rc, gemv_xtab_reduce_kernel<XT, M>, static_cast<const float*>(a.partial), a.groups,
+                         a.row_blocks, a.n_rows, a.y, a.ldy, PeerOut{}) != cudaSuccess)
+    return BNBQ_ERR_CUDA;
+  return launch_status();
+}
+
+template <typename XT, int M, bool NESTED>
+int launch_code8_nb(int nb, const CUtensorMap& map, const XtabArgs& a, const float* code, const DeviceInfo& di,
+                    cudaStream_t s) {
+  switch (nb) {
+    case 1: return launch_code8_t<XT, M, 1, NESTED>(map, a, code, di, s);
+    case 2: return launch_code8_t<XT, M, 2, NESTED>(map, a, code, di, s);
+    case 4: return launch_code8_t<XT, M, 4, NESTED>(map, a, code, di, s);
+    default: return BNBQ_ERR_UNSUPPORTED;
+  }
+}
+
+template <typename XT, int M>
+int launch_code8_m(int nb, bool nested, const CUtensorMap& map, const XtabArgs& a, const float* code,
+                   const DeviceInfo& di, cudaStream_t s) {
+  return nested ? launch_code8_nb<XT, M, true>(nb, map, a, code, di, s)
+                : launch_code8_nb<XT, M, false>(nb, map, a, code, di, s);
+}
+
 }  // namespace
 
 int xtab_wait_timeouts(unsigned int* out) { return read_wait_timeouts(out); }
@@ -913,6 +1230,79 @@ int gemv_xtab_launch(int dtype, const void* x, int m, int k, const uint8_t* w, i
     m0 += mm;
   }
   return BNBQ_OK;
+}
+
+
+// ---- 8-bit codebook weights: the fused GEMV (gemv_code8_kernel)
+int64_t gemv_code8_workspace_bytes(int m, int k, int64_t n_rows) {
+  if (m < 1 || m > 4 || k < kGroupK8 || k % kGroupK8 || n_rows < 1 || n_rows > kMaxRowBlocks * kRows) return 0;
+  return code8_workspace_bytes(m, k, n_rows);
+}
+
+int gemv_code8_launch(int dtype, const void* x, int m, int k, const uint8_t* w, int64_t n_rows, int blocksize,
+                      const float* code, const float* absmax, const uint8_t* absmax_q, const float* absmax2,
+                      const float* code2, const float* offset, int blocksize2, int64_t absmax2_block0, void* y,
+                      int64_t ldy, void* workspace, int64_t workspace_bytes, cudaStream_t s) {
+  if (m < 1 || m > 4 || k % kGroupK8 || n_rows < 1 || n_rows > kMaxRowBlocks * kRows) return BNBQ_ERR_UNSUPPORTED;
+  const int l2 = log2_exact(blocksize);
+  if (l2 < 5) return BNBQ_ERR_INVALID;
+  const int nb = blocksize >= kGroupK8 ? 1 : kGroupK8 / blocksize;
+  if (absmax_q) {
+    if (log2_exact(blocksize2) < 0 || blocksize2 < nb) return BNBQ_ERR_UNSUPPORTED;
+    if (!aligned(absmax_q, uint64_t(nb))) return BNBQ_ERR_MISALIGNED;
+  }
+  if (!workspace || workspace_bytes < gemv_code8_workspace_bytes(m, k, n_rows) || !aligned(workspace, 256))
+    return BNBQ_ERR_INVALID;
+  DeviceInfo di;
+  if (int st = device_info(&di)) return st;
+  auto encode = encoder();
+  if (!encode) return BNBQ_ERR_CUDA;
+  CUtensorMap map;
+  const cuuint64_t dims[2] = {cuuint64_t(k), cuuint64_t(n_rows)};
+  const cuuint64_t strides[1] = {cuuint64_t(k)};
+  const cuuint32_t box[2] = {cuuint32_t(kGroupK8), cuuint32_t(kRows)};
+  const cuuint32_t estr[2] = {1, 1};
+  if (encode(&map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<uint8_t*>(w), dims, strides, box, estr,
+             CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+    return BNBQ_ERR_UNSUPPORTED;
+  XtabArgs a{};
+  a.absmax = absmax;
+  a.absmax_q = absmax_q;
+  a.absmax2 = absmax2;
+  a.code2 = code2;
+  a.offset = offset;
+  a.partial = static_cast<float*>(workspace);
+  a.n_rows = n_rows;
+  a.ldy = ldy;
+  a.block0 = absmax2_block0;
+  a.k = k;
+  a.log2_bs = l2;
+  a.log2_bs2 = absmax_q ? log2_exact(blocksize2) : 0;
+  a.groups = k / kGroupK8;
+  a.row_blocks = int((n_rows + kRows - 1) / kRows);
+  a.units = int64_t(a.groups) * a.row_blocks;
+  const bool nested = absmax_q != nullptr;
+  // one pass over the weight for all m rows of x
+  a.x = x;
+  a.y = y;
+  if (dtype == BNBQ_BF16) {
+    switch (m) {
+      case 1: return launch_code8_m<__nv_bfloat16, 1>(nb, nested, map, a, code, di, s);
+      case 2: return launch_code8_m<__nv_bfloat16, 2>(nb, nested, map, a, code, di, s);
+      case 3: return launch_code8_m<__nv_bfloat16, 3>(nb, nested, map, a, code, di, s);
+      default: return launch_code8_m<__nv_bfloat16, 4>(nb, nested, map, a, code, di, s);
+    }
+  }
+  if (dtype == BNBQ_F16) {
+    switch (m) {
+      case 1: return launch_code8_m<__half, 1>(nb, nested, map, a, code, di, s);
+      case 2: return launch_code8_m<__half, 2>(nb, nested, map, a, code, di, s);
+      case 3: return launch_code8_m<__half, 3>(nb, nested, map, a, code, di, s);
+      default: return launch_code8_m<__half, 4>(nb, nested, map, a, code, di, s);
+    }
+  }
+  return BNBQ_ERR_UNSUPPORTED;
 }
 
 }  // namespace bnbq

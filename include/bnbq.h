@@ -195,6 +195,28 @@ BNBQ_API int bnbq_set_gemv_policy(int32_t policy);
  * and an n_rows x k weight (0: that shape needs none). */
 BNBQ_API int bnbq_gemv_workspace_bytes(int32_t m, int32_t k, int64_t n_rows, int64_t* bytes);
 
+/* y[m, j] = sum_k x[m, k] * W[j, k] for an 8-bit blockwise-quantized weight W
+ * (bnbq_quantize_blockwise's format: one code byte per element, row-major
+ * n_rows x k, decoded through the 256-float codebook `code`), never
+ * materialised, for 1 <= m <= BNBQ_GEMV8_MAX_M rows of x (F16 or BF16).
+ * Scales, absmax2 indexing, y's row stride, numerics (float32 products of x
+ * with code[q], the block's scale applied once per block, one rounding) and
+ * the one-hot exactness are those of bnbq_gemv_nf4. Requires k % 128 == 0
+ * and a power-of-two blocksize >= 32; the workspace (any contents, at least
+ * bnbq_gemv_blockwise_workspace_bytes, 256-byte aligned) takes the split-K
+ * partial sums, which a second kernel adds in a fixed order.
+ * The reference has no fused path for 8-bit weights: this replaces its
+ * fallback x @ w.dequantize(x.dtype).T for them (_matmul.py:58-59, chosen by
+ * _fused_applies, _matmul.py:74-79). */
+#define BNBQ_GEMV8_MAX_M 4
+BNBQ_API int bnbq_gemv_blockwise_ws(int dtype, const void* x, int32_t m, int32_t k,
+                                    const uint8_t* w, int64_t n_rows, int32_t blocksize, const float* code,
+                                    const float* absmax, const uint8_t* absmax_q, const float* absmax2,
+                                    const float* code2, const float* offset, int32_t blocksize2,
+                                    int64_t absmax2_block0, void* y, int64_t ldy,
+                                    void* workspace, int64_t workspace_bytes, void* stream);
+BNBQ_API int bnbq_gemv_blockwise_workspace_bytes(int32_t m, int32_t k, int64_t n_rows, int64_t* bytes);
+
 /* ------------------------------------------------------------ diagnostics */
 
 /* All-gather of a row-sharded matmul output over NVLink peer memory (the

@@ -70,3 +70,28 @@ def test_argument_errors_need_no_device(lib):
     assert g(*args) == -2                                     # float32 x
     args[0] = 2; args[2] = 21
     assert g(*args) == -1                                     # M above the GEMV limit
+
+
+def test_gemv_blockwise_host_checks(lib):
+    """The 8-bit-weight GEMV: workspace size and argument errors, no device."""
+    P = ctypes.c_void_p
+    n = ctypes.c_int64(0)
+    w = lib.bnbq_gemv_blockwise_workspace_bytes
+    w.argtypes = [ctypes.c_int32, ctypes.c_int32, ctypes.c_int64, P]
+    assert w(1, 14336, 4096, ctypes.byref(n)) == 0
+    assert n.value == 4096 // 32 * (14336 // 128) * 1 * 32 * 4  # one float per (unit, row, x row)
+    assert w(5, 14336, 4096, ctypes.byref(n)) == -1            # above BNBQ_GEMV8_MAX_M
+    assert w(1, 14336 + 32, 4096, ctypes.byref(n)) == -2       # K % 128 != 0
+    g = lib.bnbq_gemv_blockwise_ws
+    g.argtypes = [ctypes.c_int, P, ctypes.c_int32, ctypes.c_int32, P, ctypes.c_int64, ctypes.c_int32, P,
+                  P, P, P, P, P, ctypes.c_int32, ctypes.c_int64, P, ctypes.c_int64, P, ctypes.c_int64, P]
+    args = [2, P(256), 1, 256, P(256), 8, 64, P(256), P(256), None, None, None, None, 0, 0, P(256), 8,
+            P(256), 1 << 20, None]
+    args[2] = 5
+    assert g(*args) == -1                                      # M above the 8-bit GEMV limit
+    args[2] = 1; args[7] = None
+    assert g(*args) == -1                                      # no codebook
+    args[7] = P(258)
+    assert g(*args) == -3                                      # codebook not 4-byte aligned
+    args[7] = P(256); args[3] = 288
+    assert g(*args) == -2                                      # K % 128 != 0

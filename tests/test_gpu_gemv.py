@@ -10,7 +10,7 @@ import torch
 
 import bnb_b200
 from bnb_b200.kernels import gemv_nf4
-from bnb_b200.kernels.gemv import GEMV_MAX_M
+from bnb_b200.kernels.gemv import GEMV8_MAX_M, GEMV_MAX_M
 from helpers import GEMV_ATOL, GEMV_RTOL, TORCH_DTYPES, bits, to_host
 from oracle import oracle as O
 
@@ -112,10 +112,12 @@ def test_matmul_batch_dims(cuda):
 @pytest.mark.parametrize("case", ["8bit", "float32_x"])
 def test_matmul_fallback(cuda, case):
     """Where no fused kernel applies, x @ w.dequantize(x.dtype).T exactly
-    (reference test_matmul.py:55-67)."""
+    (reference test_matmul.py:55-67). 8-bit weights take the fallback above
+    GEMV8_MAX_M rows of x (below it, the fused 8-bit GEMV: test_gpu_gemv_8bit.py)."""
     m, dtype, qtype = 4, torch.bfloat16, "nf4"
     if case == "8bit":
         qtype = "8bit"
+        m = GEMV8_MAX_M + 1
     else:
         dtype = torch.float32
     w = weight(256, 512, qtype=qtype)
