@@ -14,7 +14,10 @@ A step is one GEMV call. `value` is the whole job's effective bandwidth
 inputs resident in HBM, timed with CUDA events around the replay of a CUDA
 graph that holds the K timed calls. `e2e` is the same metric through the
 public API (bnb_b200.matmul) with x copied from pinned host memory and y read
-back every step. `m_sweep` repeats the device timing at M = 2..20.
+back every step; on one GPU the steps alternate between two streams (each
+with its own buffers), so one step's copies overlap the other's call, and the
+one-stream time per step is reported beside it. `m_sweep` repeats the device
+timing at M = 2..20.
 
 Multi-GPU (torchrun, one process per GPU): the north star's split. The
 weight is partitioned by output rows (row_partition, whole nested blocks per
@@ -257,28 +260,45 @@ def make_step(torch, shards, x, ranges, rank, world, pg):
     return step
 
 
-def time_e2e(torch, step_fn, device, m: int, steps: int, warmup: int, dist=None):
-    """The public API with host buffers: pinned x -> device, the call, y -> host."""
+def time_e2e(torch, step_fn, device, m: int, steps: int, warmup: int, dist=None, lanes: int = 1):
+    """The public API with host buffers: pinned x -> device, the call, y -> host.
+
+    lanes = 1: every step on one stream, so a step's copies and call run
+    strictly after the previous step's (per-step latency). lanes = 2: steps
+    alternate between two streams with their own pinned and device buffers,
+    so the copies of one step overlap the call of the other (throughput of a
+    pipelined caller); every step still copies its x in and its y out."""
     g = torch.Generator().manual_seed(7)
-    xh = torch.randn(m, K_COLS, generator=g).to(torch.bfloat16).pin_memory()
-    yh = torch.empty(m, N_ROWS, dtype=torch.bfloat16).pin_memory()
-    xd = torch.empty(m, K_COLS, dtype=torch.bfloat16, device=device)
+    xh = [torch.randn(m, K_COLS, generator=g).to(torch.bfloat16).pin_memory() for _ in range(lanes)]
+    yh = [torch.empty(m, N_ROWS, dtype=torch.bfloat16).pin_memory() for _ in range(lanes)]
+    xd = [torch.empty(m, K_COLS, dtype=torch.bfloat16, device=device) for _ in range(lanes)]
+    main = torch.cuda.current_stream(device)
+    streams = [main] if lanes == 1 else [torch.cuda.Stream(device) for _ in range(lanes)]
 
     def one(i):
-        xd.copy_(xh, non_blocking=True)
-        y = step_fn(xd, i)
-        yh.copy_(y, non_blocking=True)
+        j = i % lanes
+        if lanes > 1:
+            torch.cuda.set_stream(streams[j])
+        xd[j].copy_(xh[j], non_blocking=True)
+        y = step_fn(xd[j], i)
+        yh[j].copy_(y, non_blocking=True)
 
     for i in range(max(warmup, 3)):
         one(i)
+    torch.cuda.set_stream(main)
     torch.cuda.synchronize()
     if dist is not None:
         dist.barrier()
     start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    start.record()
+    start.record(main)
+    for s in streams:
+        s.wait_event(start)
     for i in range(steps):
         one(i)
-    end.record()
+    torch.cuda.set_stream(main)
+    for s in streams:
+        main.wait_stream(s)
+    end.record(main)
     torch.cuda.synchronize()
     ms = start.elapsed_time(end)
     if dist is not None:
@@ -374,7 +394,13 @@ def run_ours(args, dist, rank, world, local_rank):
     else:
         def e2e_call(xd, i):
             return pg.matmul(xd, shards[i % copies].rs)
-    e2e_ms, h2d, d2h = time_e2e(torch, e2e_call, device, args.m, e2e_steps, args.warmup, dist)
+    # one GPU: two streams, steps overlapped (the throughput e2e), and one
+    # stream (per-step latency, reported beside it); several GPUs: one stream
+    # per rank (the peer exchange orders a rank's calls on its stream)
+    e2e_lanes = 2 if world == 1 else 1
+    e2e_ms, h2d, d2h = time_e2e(torch, e2e_call, device, args.m, e2e_steps, args.warmup, dist, e2e_lanes)
+    e2e_serial_ms = (time_e2e(torch, e2e_call, device, args.m, e2e_steps, args.warmup, dist, 1)[0]
+                     if e2e_lanes > 1 else e2e_ms)
 
     extras = {}
     if not args.no_extras:
@@ -420,7 +446,8 @@ def run_ours(args, dist, rank, world, local_rank):
         "roofline": roofline_entry(args.m, per_call_ms, peak, peak_kind, world, kernel),
         "e2e": {"value": round(algo_bytes(args.m) * e2e_steps / (e2e_ms * 1e-3) / 1e9, 2), "unit": "GB/s",
                 "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
-                "us_per_step": round(e2e_ms / e2e_steps * 1e3, 3)},
+                "us_per_step": round(e2e_ms / e2e_steps * 1e3, 3), "streams": e2e_lanes,
+                "one_stream_us_per_step": round(e2e_serial_ms / e2e_steps * 1e3, 3)},
         "gpu_launches": args.steps * launches_per_call(args.m, route, world),
         "clocks": clocks.summary(),
     }

@@ -150,12 +150,13 @@ class FusedPlan:
     x only (dtype, device, contiguity, alignment). Built by :func:`plan_for`
     and cached on the weight object."""
 
-    __slots__ = ("data", "absmax", "n", "k", "bs", "ptrs", "bs2", "keep", "device", "_ws_bytes")
+    __slots__ = ("data", "absmax", "n", "k", "bs", "ptrs", "bs2", "keep", "device", "_dev", "_ws", "_fn")
 
     def __init__(self, data, absmax, scales, n_rows, k, blocksize, nested, device):
         self.data, self.absmax = data, absmax  # the weight's own fields (identity checked on reuse)
         self.n, self.k, self.bs = n_rows, k, blocksize
         self.device = device
+        self._dev = device.index
         w = _lib.aligned(data.reshape(-1))
         if nested is None:
             a = _lib.aligned(scales.reshape(-1), 4)
@@ -172,33 +173,40 @@ class FusedPlan:
             self.keep = (w, aq, a2, c2, off)
             self.ptrs = (w.data_ptr(), None, aq.data_ptr(), a2.data_ptr(), c2.data_ptr(), off.data_ptr())
             self.bs2 = blocksize2
-        self._ws_bytes: dict[int, int] = {}
+        # (m, stream) -> (workspace pointer, bytes, the tensor: held, so that the
+        # pointer stays valid even if the shared workspace is later replaced)
+        self._ws: dict[tuple[int, int], tuple] = {}
+        self._fn = _lib.lib().bnbq_matmul_nf4_ws
+
+    def _workspace(self, m: int, stream: int) -> tuple:
+        if m > GEMV_MAX_M:
+            return None, 0, None
+        nb = _lib.gemv_workspace_bytes(m, self.k, self.n)
+        if not nb:
+            return None, 0, None
+        ws = _lib.workspace(self.device, stream, nb)
+        return ws.data_ptr(), ws.numel(), ws
 
     def run(self, x: torch.Tensor) -> torch.Tensor:
         m = x.shape[0]
         xp = x.data_ptr()
-        if xp % 16 or not x.is_contiguous():
+        if xp & 15 or not x.is_contiguous():
             x = _lib.aligned(x)
             xp = x.data_ptr()
         out = x.new_empty((m, self.n))
-        di = x.get_device()
+        di = self._dev
         stream = torch._C._cuda_getCurrentRawStream(di)
-        ws_ptr, ws_n = None, 0
-        if m <= GEMV_MAX_M:
-            nb = self._ws_bytes.get(m)
-            if nb is None:
-                nb = self._ws_bytes[m] = _lib.gemv_workspace_bytes(m, self.k, self.n)
-            if nb:
-                ws = _lib.workspace(x.device, stream, nb)
-                ws_ptr, ws_n = ws.data_ptr(), ws.numel()
+        ws = self._ws.get((m, stream))
+        if ws is None:
+            ws = self._ws[(m, stream)] = self._workspace(m, stream)
         wp, ap, aqp, a2p, c2p, offp = self.ptrs
         args = (_lib.DTYPE_CODE[x.dtype], xp, m, self.k, wp, self.n, self.bs, ap, aqp, a2p, c2p, offp,
-                self.bs2, 0, out.data_ptr(), self.n, ws_ptr, ws_n, stream)
+                self.bs2, 0, out.data_ptr(), self.n, ws[0], ws[1], stream)
         if torch._C._cuda_getDevice() == di:
-            st = _lib.lib().bnbq_matmul_nf4_ws(*args)
+            st = self._fn(*args)
         else:
             with torch.cuda.device(di):
-                st = _lib.lib().bnbq_matmul_nf4_ws(*args)
+                st = self._fn(*args)
         if st:
             _lib.check(st, "bnbq_matmul_nf4_ws")
         return out

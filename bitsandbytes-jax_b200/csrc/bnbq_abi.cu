@@ -1,5 +1,7 @@
 // bnbq_abi.cu -- device checks, status strings, diagnostics and the matmul router.
+#include <map>
 #include <mutex>
+#include <tuple>
 
 #include "bnbq_common.cuh"
 
@@ -40,6 +42,61 @@ __global__ void rcp_kernel(const float* in, float* out, int64_t n) {
 }  // namespace
 
 // Queried once per device; the kernels are built for sm_100a only.
+namespace {
+// (kernel, device) -> static shared memory and the dynamic shared memory
+// attribute set so far; (kernel, device, threads, dynamic bytes) -> blocks per SM
+struct FuncState {
+  int static_smem = -1;
+  int dyn_set = -1;
+};
+std::mutex g_func_mu;
+std::map<std::pair<const void*, int>, FuncState> g_func;
+std::map<std::tuple<const void*, int, int, size_t>, int> g_occ;
+}  // namespace
+
+int kernel_static_smem(const void* fn, int* bytes) {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return BNBQ_ERR_CUDA;
+  std::lock_guard<std::mutex> lk(g_func_mu);
+  FuncState& f = g_func[{fn, dev}];
+  if (f.static_smem < 0) {
+    cudaFuncAttributes fa;
+    if (cudaFuncGetAttributes(&fa, fn) != cudaSuccess) return BNBQ_ERR_CUDA;
+    f.static_smem = int(fa.sharedSizeBytes);
+  }
+  *bytes = f.static_smem;
+  return BNBQ_OK;
+}
+
+int kernel_reserve_smem(const void* fn, int bytes) {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return BNBQ_ERR_CUDA;
+  std::lock_guard<std::mutex> lk(g_func_mu);
+  FuncState& f = g_func[{fn, dev}];
+  if (bytes > f.dyn_set) {
+    if (cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes) != cudaSuccess)
+      return BNBQ_ERR_CUDA;
+    f.dyn_set = bytes;
+  }
+  return BNBQ_OK;
+}
+
+int kernel_occupancy(const void* fn, int threads, size_t dyn_bytes, int* per_sm) {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return BNBQ_ERR_CUDA;
+  std::lock_guard<std::mutex> lk(g_func_mu);
+  auto key = std::make_tuple(fn, dev, threads, dyn_bytes);
+  auto it = g_occ.find(key);
+  if (it == g_occ.end()) {
+    int n = 0;
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, fn, threads, dyn_bytes) != cudaSuccess)
+      return BNBQ_ERR_CUDA;
+    it = g_occ.emplace(key, n).first;
+  }
+  *per_sm = it->second;
+  return BNBQ_OK;
+}
+
 int device_info(DeviceInfo* out) {
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return BNBQ_ERR_CUDA;

@@ -148,6 +148,15 @@ struct DeviceInfo {
 // Per-device attributes, queried once per device (thread-safe).
 int device_info(DeviceInfo* out);
 
+// Kernel launch attributes on the current device, each CUDA query made once
+// per (kernel, device) and then served from a table (a launch then costs no
+// attribute round trips): the kernel's static shared memory; its maximum
+// dynamic shared memory raised to at least `bytes` (set only when it grows);
+// its resident blocks per SM for (threads, dynamic bytes).
+int kernel_static_smem(const void* fn, int* bytes);
+int kernel_reserve_smem(const void* fn, int bytes);
+int kernel_occupancy(const void* fn, int threads, size_t dyn_bytes, int* per_sm);
+
 inline bool aligned(const void* p, uintptr_t a) {
   return (reinterpret_cast<uintptr_t>(p) & (a - 1)) == 0;
 }

@@ -196,17 +196,10 @@ int launch_t(const DequantArgs& a, cudaStream_t s) {
   constexpr int EPV = Vec<OutT>::kEPV;
   auto kern = dequant_kernel<OutT, NF4, NESTED, POSTADD>;
   constexpr size_t smem = Smem<NF4, NESTED>::kBytes;
-  static bool configured[64] = {};
-  int dev = 0;
-  cudaGetDevice(&dev);
-  if (smem > 48 * 1024 && dev < 64 && !configured[dev]) {
-    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem)) != cudaSuccess)
-      return BNBQ_ERR_CUDA;
-    configured[dev] = true;
-  }
+  if (smem > 48 * 1024)
+    if (int st = kernel_reserve_smem(reinterpret_cast<const void*>(kern), int(smem))) return st;
   int per_sm = 0;
-  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, kThreads, smem) != cudaSuccess)
-    return BNBQ_ERR_CUDA;
+  if (int st = kernel_occupancy(reinterpret_cast<const void*>(kern), kThreads, smem, &per_sm)) return st;
   if (per_sm < 1) per_sm = 1;
   const int64_t nvec = a.n / EPV;
   constexpr int kUnroll = unroll_for<OutT, NF4>();

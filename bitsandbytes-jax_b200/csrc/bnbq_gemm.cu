@@ -623,13 +623,13 @@ int launch_t(GemmArgs a, const void* x, const uint8_t* w, const DeviceInfo& di, 
                  uint64_t(a.k / 2), kBK / 2, kBM, CU_TENSOR_MAP_SWIZZLE_NONE))
     return BNBQ_ERR_CUDA;
   auto kern = gemm_kernel<XT, BN, NESTED, PRECISE>;
-  cudaFuncAttributes fa;
-  if (cudaFuncGetAttributes(&fa, kern) != cudaSuccess) return BNBQ_ERR_CUDA;
+  int static_smem = 0;
+  if (int st = kernel_static_smem(reinterpret_cast<const void*>(kern), &static_smem)) return st;
   // Paired tiles take just under half of the SM's shared memory (so that no
   // third CTA becomes resident and waits in tcgen05.alloc) and at most 256
   // tensor-memory columns each.
-  const size_t smem_cap = T::kPair ? size_t(di.smem_optin) / 2 - fa.sharedSizeBytes - 1024
-                                   : size_t(di.smem_optin) - fa.sharedSizeBytes;
+  const size_t smem_cap = T::kPair ? size_t(di.smem_optin) / 2 - size_t(static_smem) - 1024
+                                   : size_t(di.smem_optin) - size_t(static_smem);
   int stages = int((smem_cap - 1024 - T::kTableBytes) / T::kStageBytes);
   stages = stages < kMaxStages ? stages : kMaxStages;
   const uint32_t tmem_budget = T::kPair ? 256u : 512u;
@@ -641,8 +641,7 @@ int launch_t(GemmArgs a, const void* x, const uint8_t* w, const DeviceInfo& di, 
   a.n_aslots = aslots;
   a.tmem_cols = pow2_at_least(uint32_t(BN) + uint32_t(aslots) * T::kACols);
   const size_t smem = T::kPair ? (smem_cap / 1024) * 1024 : size_t(stages) * T::kStageBytes + T::kTableBytes + 1024;
-  if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem)) != cudaSuccess)
-    return BNBQ_ERR_CUDA;
+  if (int st = kernel_reserve_smem(reinterpret_cast<const void*>(kern), int(smem))) return st;
   // K split across a cluster when the tiles alone leave SMs idle: about one CTA
   // per SM, at most 8 (portable cluster size), each with >= 2 K blocks, and
   // the partial tiles of ranks 1.. must fit in rank 0's ring.

@@ -840,15 +840,14 @@ int launch_bulk_t(const GemvArgs& a, const BulkPlan& p, const DeviceInfo& di, cu
                                       : gemv_bulk_kernel<XT, M, R, NESTED, SLOTS, true, RG, false>)
                                 : (px ? gemv_bulk_kernel<XT, M, R, NESTED, SLOTS, false, RG, true>
                                       : gemv_bulk_kernel<XT, M, R, NESTED, SLOTS, false, RG, false>);
-  cudaFuncAttributes fa;
-  if (cudaFuncGetAttributes(&fa, kern) != cudaSuccess) return BNBQ_ERR_CUDA;
-  const size_t room = size_t(di.smem_optin) - size_t(kPairTableBytes) - fa.sharedSizeBytes - 1024;
+  int static_smem = 0;
+  if (int st = kernel_static_smem(reinterpret_cast<const void*>(kern), &static_smem)) return st;
+  const size_t room = size_t(di.smem_optin) - size_t(kPairTableBytes) - size_t(static_smem) - 1024;
   int stages = int(room / (p.stage_bytes + 16));
   if (stages > kMaxStages) stages = kMaxStages;
   if (stages < 2) return BNBQ_ERR_UNSUPPORTED;
   const size_t smem = size_t(kPairTableBytes) + size_t(stages) * p.stage_bytes + size_t(2 * stages) * 8;
-  if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem)) != cudaSuccess)
-    return BNBQ_ERR_CUDA;
+  if (int st = kernel_reserve_smem(reinterpret_cast<const void*>(kern), int(smem))) return st;
   const int64_t n_groups = (a.n_rows + R - 1) / R;
   if (n_groups > INT32_MAX / 2) return BNBQ_ERR_UNSUPPORTED;
   // the kernel numbers blocks in 32 bits when the scales travel with the stage
@@ -947,11 +946,9 @@ int launch_m(const GemvArgs& a, cudaStream_t s) {
   const int threads = pick_threads(a.k >> 5, max_threads_for(M));
   const int64_t n_groups = (a.n_rows + R - 1) / R;
   auto kern = gemv_kernel<XT, M, R, NESTED>;
-  if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kPairTableBytes) != cudaSuccess)
-    return BNBQ_ERR_CUDA;
+  if (int st = kernel_reserve_smem(reinterpret_cast<const void*>(kern), kPairTableBytes)) return st;
   int per_sm = 0;
-  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, threads, kPairTableBytes) != cudaSuccess)
-    return BNBQ_ERR_CUDA;
+  if (int st = kernel_occupancy(reinterpret_cast<const void*>(kern), threads, kPairTableBytes, &per_sm)) return st;
   per_sm = per_sm < 1 ? 1 : (per_sm > 2 ? 2 : per_sm);
   // One CTA per SM when that balances the groups to within 2%, else two.
   int64_t grid = di.sm_count;
@@ -1153,11 +1150,10 @@ template <typename XT, int MT, bool NESTED>
 int launch_rows_t(int m, const GemvArgs& a, const DeviceInfo& di, cudaStream_t s) {
   using L = RowsLayout<MT>;
   auto kern = gemv_rows_kernel<XT, MT, NESTED>;
-  cudaFuncAttributes fa;
-  if (cudaFuncGetAttributes(&fa, kern) != cudaSuccess) return BNBQ_ERR_CUDA;
-  if (size_t(L::kDynamic) + fa.sharedSizeBytes > size_t(di.smem_optin)) return BNBQ_ERR_UNSUPPORTED;
-  if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, int(L::kDynamic)) != cudaSuccess)
-    return BNBQ_ERR_CUDA;
+  int static_smem = 0;
+  if (int st = kernel_static_smem(reinterpret_cast<const void*>(kern), &static_smem)) return st;
+  if (size_t(L::kDynamic) + size_t(static_smem) > size_t(di.smem_optin)) return BNBQ_ERR_UNSUPPORTED;
+  if (int st = kernel_reserve_smem(reinterpret_cast<const void*>(kern), int(L::kDynamic))) return st;
   int kw = (a.k + kRowsWarps - 1) / kRowsWarps;
   kw = (kw + 31) & ~31;
   cudaLaunchConfig_t cfg = {};

@@ -1001,9 +1001,9 @@ int launch_t(const CUtensorMap& map, const XtabArgs& a0, const DeviceInfo& di, c
   a.dyn_bytes = uint32_t(dyn);
   if (xp) {  // the exchange polls for peers from every reduction CTA: all must be resident
     int per_sm = 0;
-    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, gemv_xtab_reduce_kernel<XT, M>, kRedThreads, 0) !=
-        cudaSuccess)
-      return BNBQ_ERR_CUDA;
+    if (int st = kernel_occupancy(reinterpret_cast<const void*>(gemv_xtab_reduce_kernel<XT, M>), kRedThreads, 0,
+                                  &per_sm))
+      return st;
     if (int64_t(a.row_blocks) * M > int64_t(per_sm) * di.sm_count) return BNBQ_ERR_UNSUPPORTED;
   }
   static std::atomic<int> attr_set[kMaxDevices];  // per device: the attribute is set once

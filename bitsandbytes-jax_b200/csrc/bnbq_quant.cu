@@ -556,12 +556,10 @@ template <typename Kern>
 int launch_grid(Kern kern, size_t smem, int64_t work_warps, const QuantArgs& a, cudaStream_t s) {
   DeviceInfo di;
   if (int st = device_info(&di)) return st;
-  if (smem > 48 * 1024 &&
-      cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem)) != cudaSuccess)
-    return BNBQ_ERR_CUDA;
+  if (smem > 48 * 1024)
+    if (int st = kernel_reserve_smem(reinterpret_cast<const void*>(kern), int(smem))) return st;
   int per_sm = 0;
-  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, kThreads, smem) != cudaSuccess)
-    return BNBQ_ERR_CUDA;
+  if (int st = kernel_occupancy(reinterpret_cast<const void*>(kern), kThreads, smem, &per_sm)) return st;
   if (per_sm < 1) per_sm = 1;
   int64_t grid = int64_t(di.sm_count) * per_sm;
   const int64_t want = (work_warps + kWarps - 1) / kWarps;
