@@ -512,8 +512,8 @@ def time_graph(torch, call, steps: int, warmup: int, device):
 def quant_cases(torch, device, warmup: int, steps: int = 8):
     """Configs 1 and 3: blockwise quantize / dequantize bandwidth (device time
     per call, CUDA graph of `steps` calls); returns (config1, config3) dicts."""
-    from bnb_b200.kernels import (create_dynamic_map, dequantize_blockwise, dequantize_nf4,
-                                  quantize_blockwise, quantize_nf4)
+    from bnb_b200.kernels import (absmax_mean, create_dynamic_map, dequantize_blockwise, dequantize_nf4,
+                                  quantize_blockwise, quantize_nf4, quantize_nf4_dq)
     peak, _ = measured_peaks()
     # config 1: 4096 x 4096 bf16, NF4 bs 64, 8 rotated copies (256 MiB)
     n1 = 4096 * 4096
@@ -530,6 +530,17 @@ def quant_cases(torch, device, warmup: int, steps: int = 8):
           "quantize_frac": round(b1 / (tq * 1e-3) / 1e9 / peak, 3),
           "dequantize_us": round(td * 1e3, 2), "dequantize_gbs": round(b1 / (td * 1e-3) / 1e9, 1),
           "dequantize_frac": round(b1 / (td * 1e-3) / 1e9 / peak, 3)}
+    # double quantization (the weight format of config 2): one launch against the three-call chain
+    code2 = create_dynamic_map(device=device)
+
+    def dq_chain(i):
+        q, a = quantize_nf4(xs[i % 8], 64)
+        quantize_blockwise(a, code2, 256, offset=absmax_mean(a))
+
+    tdq = time_graph(torch, lambda i: quantize_nf4_dq(xs[i % 8], 64, code2), s1, warmup, device) / s1
+    tch = time_graph(torch, dq_chain, s1, warmup, device) / s1
+    c1["double_quant_us"] = round(tdq * 1e3, 2)
+    c1["double_quant_chain_us"] = round(tch * 1e3, 2)
     del xs, qs
     # config 3: 2^28 + 37 elements, 90% N(0,1) + 10% Laplace(0,8), 8-bit dynamic map
     n3 = (1 << 28) + 37

@@ -27,6 +27,8 @@ _SIGNATURES = {
     "bnbq_quantize_nf4": "ipliPPP",
     "bnbq_quantize_blockwise": "ipliPPPPP",
     "bnbq_absmax_mean": "PlPP",
+    "bnbq_quantize_nf4_dq": "ipliPiPPPPPPlP",
+    "bnbq_quantize_nf4_dq_workspace_bytes": "",
     "bnbq_dequantize_nf4": "iPPliPP",
     "bnbq_dequantize_blockwise": "iPPPliPPP",
     "bnbq_dequantize_nf4_nested": "iPPPPPliiPP",
@@ -77,6 +79,7 @@ def lib() -> C.CDLL:
                     fn = getattr(L, name)
                     fn.argtypes = [_KIND[c] for c in sig]
                     fn.restype = C.c_int32
+                L.bnbq_quantize_nf4_dq_workspace_bytes.restype = C.c_int64
                 L.bnbq_error_string.argtypes = [C.c_int32]
                 L.bnbq_error_string.restype = C.c_char_p
                 _lib = L

@@ -32,6 +32,7 @@ from .kernels import (
     dequantize_nf4_nested,
     quantize_blockwise,
     quantize_nf4,
+    quantize_nf4_dq,
 )
 
 __all__ = ["QType", "QuantizedArray", "quantize"]
@@ -258,6 +259,15 @@ def quantize(
             omitted).
     """
     x = array.reshape(-1)
+    if qtype == "nf4" and double_quant and x.numel() > 0:
+        # the three steps below in one launch (bnbq_quantize_nf4_dq), bitwise the same
+        code2 = create_dynamic_map(device=x.device)
+        data, absmax, q2, absmax2, offset = quantize_nf4_dq(x, blocksize, code2, _NESTED_BLOCKSIZE)
+        absmax = QuantizedArray(data=q2, absmax=absmax2, code=code2, offset=offset,
+                                qtype="8bit", blocksize=_NESTED_BLOCKSIZE, shape=tuple(absmax.shape),
+                                dtype=torch.float32)
+        return QuantizedArray(data=data, absmax=absmax, code=None, offset=None, qtype=qtype, blocksize=blocksize,
+                              shape=tuple(array.shape), dtype=array.dtype if dtype is None else dtype)
     if qtype == "nf4":
         data, absmax = quantize_nf4(x, blocksize=blocksize)
         code = None

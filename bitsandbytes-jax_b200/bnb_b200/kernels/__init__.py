@@ -12,7 +12,7 @@ from .dequantize import (
     dequantize_nf4_nested,
 )
 from .gemv import GEMV8_MAX_M, GEMV_MAX_M, gemv_blockwise, gemv_nf4, matmul_nf4
-from .quantize import absmax_mean, create_dynamic_map, quantize_blockwise, quantize_nf4
+from .quantize import absmax_mean, create_dynamic_map, quantize_blockwise, quantize_nf4, quantize_nf4_dq
 
 __all__ = [
     "GEMV8_MAX_M",
@@ -29,4 +29,5 @@ __all__ = [
     "matmul_nf4",
     "quantize_blockwise",
     "quantize_nf4",
+    "quantize_nf4_dq",
 ]

@@ -80,6 +80,39 @@ def quantize_nf4(input: torch.Tensor, blocksize: int = 64) -> tuple[torch.Tensor
     return q, absmax
 
 
+def quantize_nf4_dq(input: torch.Tensor, blocksize: int = 64, code2: torch.Tensor | None = None,
+                    blocksize2: int = 256):
+    """NF4 quantization with double-quantized scales in one kernel launch
+    (``bnbq_quantize_nf4_dq``).
+
+    Returns ``(q, absmax, absmax_q, absmax2, offset)``: the NF4 codes and the
+    float32 block maxima as :func:`quantize_nf4` gives them, then
+    ``offset = absmax_mean(absmax)`` and ``quantize_blockwise(absmax - offset,
+    code2, blocksize2)``, all bitwise the three separate calls (the reference's
+    ``quantize(..., double_quant=True)``, array.py:199-202). ``code2`` defaults
+    to the dynamic map; ``blocksize2 <= 256``."""
+    x = _check_input(input, blocksize)
+    n = x.numel()
+    if n == 0:
+        raise ValueError("nothing to quantize")
+    if code2 is None:
+        code2 = create_dynamic_map(device=x.device)
+    c2 = _lib.aligned(torch.as_tensor(code2, dtype=torch.float32).reshape(-1).to(x.device), 4)
+    nb = -(-n // blocksize)
+    q = torch.empty(-(-n // 2), dtype=torch.uint8, device=x.device)
+    absmax = torch.empty(nb, dtype=torch.float32, device=x.device)
+    absmax_q = torch.empty(nb, dtype=torch.uint8, device=x.device)
+    absmax2 = torch.empty(-(-nb // blocksize2), dtype=torch.float32, device=x.device)
+    offset = torch.empty((), dtype=torch.float32, device=x.device)
+    with torch.cuda.device(x.device):
+        stream = _lib.stream_of(x)
+        ws = _lib.workspace(x.device, stream, int(_lib.lib().bnbq_quantize_nf4_dq_workspace_bytes()))
+        _lib.call("bnbq_quantize_nf4_dq", _lib.DTYPE_CODE[x.dtype], x.data_ptr(), n, blocksize, c2.data_ptr(),
+                  blocksize2, q.data_ptr(), absmax.data_ptr(), absmax_q.data_ptr(), absmax2.data_ptr(),
+                  offset.data_ptr(), ws.data_ptr(), ws.numel(), stream)
+    return q, absmax, absmax_q, absmax2, offset
+
+
 def quantize_blockwise(input: torch.Tensor, code: torch.Tensor, blocksize: int = 64, *,
                        offset: torch.Tensor | None = None) -> tuple[torch.Tensor, torch.Tensor]:
     """Quantize with 8-bit blockwise quantization and codebook ``code``.

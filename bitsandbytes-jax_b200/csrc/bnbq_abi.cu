@@ -19,10 +19,12 @@ int gemv_wait_timeouts(unsigned int* out);
 int gemm_wait_timeouts(unsigned int* out);
 int peer_wait_timeouts(unsigned int* out);
 int xtab_wait_timeouts(unsigned int* out);
+int quant_wait_timeouts(unsigned int* out);
 int gemv_set_wait_limit(uint64_t ns);
 int gemm_set_wait_limit(uint64_t ns);
 int peer_set_wait_limit(uint64_t ns);
 int xtab_set_wait_limit(uint64_t ns);
+int quant_set_wait_limit(uint64_t ns);
 int gemm_launch(int dtype, const void* x, int32_t m, int32_t k, const uint8_t* w, int64_t n_rows,
                 int32_t blocksize, const float* absmax, const uint8_t* absmax_q,
                 const float* absmax2, const float* code2, const float* offset, int32_t blocksize2,
@@ -172,11 +174,11 @@ extern "C" int bnbq_wait_timeouts(unsigned int* count) {
   DeviceInfo di;
   if (int st = device_info(&di)) return st;
   // one counter per source file with bounded waits (each has its own copy)
-  unsigned int g = 0, h = 0, p = 0, t = 0;
+  unsigned int g = 0, h = 0, p = 0, t = 0, q = 0;
   if (gemv_wait_timeouts(&g) != 0 || gemm_wait_timeouts(&h) != 0 || peer_wait_timeouts(&p) != 0 ||
-      xtab_wait_timeouts(&t) != 0)
+      xtab_wait_timeouts(&t) != 0 || quant_wait_timeouts(&q) != 0)
     return BNBQ_ERR_CUDA;
-  *count = g + h + p + t;
+  *count = g + h + p + t + q;
   return BNBQ_OK;
 }
 
@@ -199,7 +201,7 @@ extern "C" int bnbq_set_wait_limit_ns(uint64_t ns) {
   DeviceInfo di;
   if (int st = device_info(&di)) return st;
   if (gemv_set_wait_limit(ns) != 0 || gemm_set_wait_limit(ns) != 0 || peer_set_wait_limit(ns) != 0 ||
-      xtab_set_wait_limit(ns) != 0)
+      xtab_set_wait_limit(ns) != 0 || quant_set_wait_limit(ns) != 0)
     return BNBQ_ERR_CUDA;
   return BNBQ_OK;
 }

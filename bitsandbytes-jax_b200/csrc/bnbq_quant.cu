@@ -44,6 +44,7 @@
 #include <float.h>
 #include <limits.h>
 
+#include "bnbq_async.cuh"
 #include "bnbq_common.cuh"
 
 namespace bnbq {
@@ -120,7 +121,13 @@ struct QuantArgs {
   const float* code;    // 8-bit only
   const float* offset;  // 8-bit only, nullable: x := fl32(x - offset)
   uint32_t two;         // 2, passed at run time (see gt01)
+  int offset_in_arg;    // the offset is offset_value (computed by the same kernel), not *offset
+  float offset_value;
 };
+
+__device__ __forceinline__ float offset_of(const QuantArgs& a) {
+  return a.offset ? (a.offset_in_arg ? a.offset_value : __ldg(a.offset)) : 0.0f;
+}
 
 // Shared memory of the 8-bit kernel.
 struct Q8Smem {
@@ -434,7 +441,7 @@ __device__ void quant_small(const QuantArgs& a, const Choose& choose) {
   const int64_t nseg = (a.n + 255) >> 8;
   const int64_t gw = (int64_t(blockIdx.x) * kThreads + threadIdx.x) >> 5;
   const int64_t tw = (int64_t(gridDim.x) * kThreads) >> 5;
-  const float off = a.offset ? __ldg(a.offset) : 0.0f;
+  const float off = offset_of(a);
   constexpr int U = sizeof(InT) == 4 ? 2 : 4;
   for (int64_t seg0 = gw; seg0 < nseg; seg0 += tw * U) {
     Raw8<InT> raw[U];
@@ -475,7 +482,7 @@ __device__ void quant_large(const QuantArgs& a, const Choose& choose) {
   const int P = 1 << (a.log2_bs - 8);
   const int64_t gw = (int64_t(blockIdx.x) * kThreads + threadIdx.x) >> 5;
   const int64_t tw = (int64_t(gridDim.x) * kThreads) >> 5;
-  const float off = a.offset ? __ldg(a.offset) : 0.0f;
+  const float off = offset_of(a);
   for (int64_t b = gw; b < a.nb; b += tw) {
     const int64_t base = b << a.log2_bs;
     float m = -FLT_MAX;
@@ -618,7 +625,128 @@ __global__ void __launch_bounds__(1024) mean_kernel(const float* a, int64_t n, f
   }
 }
 
+// --------------------------------------------- NF4 + double quantization, one launch
+// quant_nf4_dq_kernel: the three steps of quantize(..., double_quant=True)
+// (array.py:199-202) in one cooperative launch (every CTA resident):
+//   1. NF4 codes and float32 absmax of x, exactly as quant_nf4_kernel;
+//   2. grid barrier; CTAs 0..7 form the float64 sums of absmax in mean_kernel's
+//      order (slot c*1024 + t sums elements c*1024 + t + j*8192 in order of j,
+//      then the 1024 slots of each c in mean_kernel's tree), store them to the
+//      workspace; grid barrier; every CTA adds the 8 sums in order, so every
+//      CTA holds offset = fl32(sum / nb), bitwise bnbq_absmax_mean's value;
+//   3. the 8-bit quantization of absmax - offset with code2 in blocks of
+//      blocksize2, exactly as quant_8bit_kernel with that offset.
+// The grid barriers count CTAs on a workspace word that the host zeroes on the
+// stream before the launch; each wait is bounded in time (an expiry is counted
+// in the wait-timeout counter and the CTA stops: the outputs are then wrong).
+struct DqWork {
+  unsigned int arrived;  // CTAs past barrier 1 (gridDim.x), then barrier 2 (2 gridDim.x)
+  unsigned int pad[3];
+  double sums[kMeanCtas];
+};
+
+__device__ __forceinline__ bool grid_barrier(unsigned int* arrived, unsigned int target, int* s_fail) {
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    __threadfence();  // this CTA's outputs before its arrival
+    atomicAdd(arrived, 1u);
+    const uint64_t t0 = global_ns();
+    const uint64_t limit = g_bnbq_wait_limit_ns;
+    unsigned int v;
+    while (true) {
+      asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(arrived) : "memory");
+      if (v >= target) break;
+      if (global_ns() - t0 > limit) {
+        atomicAdd(&g_bnbq_wait_timeouts, 1u);
+        *s_fail = 1;
+        break;
+      }
+      __nanosleep(64);
+    }
+  }
+  __syncthreads();
+  return *s_fail == 0;
+}
+
+template <typename InT, bool LARGE>
+__global__ void __launch_bounds__(kThreads) quant_nf4_dq_kernel(QuantArgs a4, QuantArgs a8, DqWork* work) {
+  extern __shared__ __align__(16) unsigned char smem_raw[];
+  Q8Smem& s8 = *reinterpret_cast<Q8Smem*>(smem_raw);
+  __shared__ NF4Smem s4;
+  __shared__ double part[1024];
+  __shared__ int s_fail;
+  if (threadIdx.x == 0) s_fail = 0;
+  build_nf4_tables(s4);
+  build_q8_tables(s8, a8.code);  // (ends with a CTA barrier)
+  __syncthreads();
+  // 1. NF4
+  quant_body<InT, true, LARGE>(a4, NF4Choose{&s4, a4.two});
+  if (!grid_barrier(&work->arrived, gridDim.x, &s_fail)) return;
+  // 2. the mean, in mean_kernel's summation order
+  const int64_t nb = a8.n;
+  if (blockIdx.x < kMeanCtas) {
+    const int c = int(blockIdx.x);
+    for (int t = threadIdx.x; t < 1024; t += kThreads) {
+      double sum = 0.0;
+      for (int64_t i = int64_t(c) * 1024 + t; i < nb; i += int64_t(kMeanCtas) * 1024)
+        sum += double(__ldcg(static_cast<const float*>(a8.x) + i));
+      part[t] = sum;
+    }
+    __syncthreads();
+    for (int w = 512; w > 0; w >>= 1) {
+      for (int t = threadIdx.x; t < w; t += kThreads) part[t] += part[t + w];
+      __syncthreads();
+    }
+    if (threadIdx.x == 0) __stcg(&work->sums[c], part[0]);
+  }
+  if (!grid_barrier(&work->arrived, 2u * gridDim.x, &s_fail)) return;
+  double total = 0.0;
+  for (int c = 0; c < kMeanCtas; ++c) total += __ldcg(&work->sums[c]);
+  const float off = float(total / double(nb));
+  if (blockIdx.x == 0 && threadIdx.x == 0) *const_cast<float*>(a8.offset) = off;
+  // 3. 8-bit quantization of absmax - offset
+  QuantArgs b = a8;
+  b.offset_in_arg = 1;
+  b.offset_value = off;
+  if (s8.mode > 0 && !s8.map.ex) quant_body<float, false, false>(b, Q8Choose<0>{&s8, s8.map});
+  else if (s8.mode > 0) quant_body<float, false, false>(b, Q8Choose<1>{&s8, s8.map});
+  else quant_body<float, false, false>(b, Q8Choose<-1>{&s8, Q8Map{}});
+}
+
+template <typename InT, bool LARGE>
+int launch_dq(const QuantArgs& a4, const QuantArgs& a8, DqWork* work, cudaStream_t s) {
+  auto kern = quant_nf4_dq_kernel<InT, LARGE>;
+  DeviceInfo di;
+  if (int st = device_info(&di)) return st;
+  const size_t smem = sizeof(Q8Smem);
+  if (int st = kernel_reserve_smem(reinterpret_cast<const void*>(kern), int(smem))) return st;
+  int per_sm = 0;
+  if (int st = kernel_occupancy(reinterpret_cast<const void*>(kern), kThreads, smem, &per_sm)) return st;
+  if (per_sm < 1) return BNBQ_ERR_UNSUPPORTED;
+  int64_t grid = int64_t(di.sm_count) * per_sm;  // every CTA resident (cooperative launch)
+  const int64_t want = (work_warps(a4) + kWarps - 1) / kWarps;
+  if (want < grid) grid = want;
+  if (grid < kMeanCtas) grid = kMeanCtas;
+  if (grid > int64_t(di.sm_count) * per_sm) return BNBQ_ERR_UNSUPPORTED;
+  if (cudaMemsetAsync(work, 0, sizeof(DqWork), s) != cudaSuccess) return BNBQ_ERR_CUDA;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(unsigned(grid));
+  cfg.blockDim = dim3(kThreads);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeCooperative;
+  attr[0].val.cooperative = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  if (cudaLaunchKernelEx(&cfg, kern, a4, a8, work) != cudaSuccess) return BNBQ_ERR_CUDA;
+  return launch_status();
+}
+
 }  // namespace
+
+int quant_wait_timeouts(unsigned int* out) { return read_wait_timeouts(out); }
+int quant_set_wait_limit(uint64_t ns) { return write_wait_limit(ns); }
 }  // namespace bnbq
 
 using namespace bnbq;
@@ -668,6 +796,38 @@ extern "C" int bnbq_quantize_blockwise(int dtype, const void* x, int64_t n, int3
                            : launch_grid(quant_8bit_kernel<__nv_bfloat16, false>, smem, ww, a, s);
   }
 }
+
+extern "C" int bnbq_quantize_nf4_dq(int dtype, const void* x, int64_t n, int32_t blocksize, const float* code2,
+                                    int32_t blocksize2, uint8_t* q, float* absmax, uint8_t* absmax_q,
+                                    float* absmax2, float* offset, void* workspace, int64_t workspace_bytes,
+                                    void* stream) {
+  QuantArgs a4{};
+  if (int st = check_quant(dtype, x, n, blocksize, q, absmax, &a4)) return st;
+  if (n == 0 || !code2 || !absmax_q || !absmax2 || !offset || !workspace) return BNBQ_ERR_INVALID;
+  if (workspace_bytes < int64_t(sizeof(DqWork))) return BNBQ_ERR_INVALID;
+  if (!aligned(code2, 4) || !aligned(absmax2, 4) || !aligned(offset, 4) || !aligned(absmax_q, 16) ||
+      !aligned(workspace, 16))
+    return BNBQ_ERR_MISALIGNED;
+  QuantArgs a8{};
+  if (int st = check_quant(BNBQ_F32, absmax, a4.nb, blocksize2, absmax_q, absmax2, &a8)) return st;
+  if (a8.log2_bs > 8) return BNBQ_ERR_UNSUPPORTED;  // the nested pass takes blocks of up to 256
+  a8.code = code2;
+  a8.offset = offset;
+  if (!aligned(absmax, 16)) return BNBQ_ERR_MISALIGNED;  // (the nested pass reads it as 16-byte vectors)
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  DqWork* w = static_cast<DqWork*>(workspace);
+  switch (dtype) {
+    case BNBQ_F32:
+      return a4.log2_bs > 8 ? launch_dq<float, true>(a4, a8, w, s) : launch_dq<float, false>(a4, a8, w, s);
+    case BNBQ_F16:
+      return a4.log2_bs > 8 ? launch_dq<__half, true>(a4, a8, w, s) : launch_dq<__half, false>(a4, a8, w, s);
+    default:
+      return a4.log2_bs > 8 ? launch_dq<__nv_bfloat16, true>(a4, a8, w, s)
+                            : launch_dq<__nv_bfloat16, false>(a4, a8, w, s);
+  }
+}
+
+extern "C" int64_t bnbq_quantize_nf4_dq_workspace_bytes(void) { return int64_t(sizeof(DqWork)); }
 
 extern "C" int bnbq_absmax_mean(const float* absmax, int64_t nb, float* offset, void* stream) {
   if (nb <= 0 || !absmax || !offset) return BNBQ_ERR_INVALID;

@@ -82,6 +82,27 @@ BNBQ_API int bnbq_quantize_blockwise(int dtype, const void* x, int64_t n, int32_
  * deterministic). Replaces the XLA reduction `jnp.mean(absmax)` at array.py:200. */
 BNBQ_API int bnbq_absmax_mean(const float* absmax, int64_t nb, float* offset, void* stream);
 
+/* NF4 quantization with double-quantized scales in ONE kernel launch (plus a
+ * 16-byte memset of the workspace): bitwise the chain
+ *   bnbq_quantize_nf4(x -> q, absmax);
+ *   bnbq_absmax_mean(absmax -> offset);
+ *   bnbq_quantize_blockwise(absmax with *offset subtracted, code2, blocksize2
+ *                           -> absmax_q, absmax2).
+ * absmax (ceil(n/blocksize) floats, 16-byte aligned) is written too: it is the
+ * nested pass's input. blocksize2: power of two, 8..256 (the format's 256).
+ * workspace: at least bnbq_quantize_nf4_dq_workspace_bytes() bytes, 16-byte
+ * aligned, any contents (the call clears it on the stream); calls sharing it
+ * must be ordered on one stream. The kernel is a cooperative launch whose two
+ * grid-wide barriers are bounded in time (an expiry is counted by
+ * bnbq_wait_timeouts and leaves the outputs wrong). n must be > 0.
+ * Replaces: quantize(x, "nf4", bs, double_quant=True) at array.py:199-202
+ * (quantize_nf4, then jnp.mean, then quantize_blockwise: three launches). */
+BNBQ_API int bnbq_quantize_nf4_dq(int dtype, const void* x, int64_t n, int32_t blocksize,
+                                  const float* code2, int32_t blocksize2, uint8_t* q, float* absmax,
+                                  uint8_t* absmax_q, float* absmax2, float* offset,
+                                  void* workspace, int64_t workspace_bytes, void* stream);
+BNBQ_API int64_t bnbq_quantize_nf4_dq_workspace_bytes(void);
+
 /* -------------------------------------------------------------- dequantize */
 
 /* out[i] = dtype(mul.ftz(NF4_TABLE[nibble_i], absmax[i / bs])), i < n.

@@ -95,3 +95,27 @@ def test_gemv_blockwise_host_checks(lib):
     assert g(*args) == -3                                      # codebook not 4-byte aligned
     args[7] = P(256); args[3] = 288
     assert g(*args) == -2                                      # K % 128 != 0
+
+
+def test_quantize_nf4_dq_host_checks(lib):
+    """The single-pass NF4 + double quantization: workspace size and argument
+    errors, no device."""
+    P = ctypes.c_void_p
+    lib.bnbq_quantize_nf4_dq_workspace_bytes.restype = ctypes.c_int64
+    assert 16 <= lib.bnbq_quantize_nf4_dq_workspace_bytes() <= 4096
+    f = lib.bnbq_quantize_nf4_dq
+    f.argtypes = [ctypes.c_int, P, ctypes.c_int64, ctypes.c_int32, P, ctypes.c_int32, P, P, P, P, P, P,
+                  ctypes.c_int64, P]
+    ok = [2, P(256), 1024, 64, P(256), 256, P(256), P(256), P(256), P(256), P(256), P(256), 4096, None]
+    args = list(ok); args[0] = 7
+    assert f(*args) == -2                                      # unknown dtype
+    args = list(ok); args[2] = 0
+    assert f(*args) == -1                                      # nothing to quantize
+    args = list(ok); args[11] = None
+    assert f(*args) == -1                                      # no workspace
+    args = list(ok); args[12] = 8
+    assert f(*args) == -1                                      # workspace too small
+    args = list(ok); args[5] = 512
+    assert f(*args) == -2                                      # nested blocks above 256
+    args = list(ok); args[11] = P(264)
+    assert f(*args) == -3                                      # workspace not 16-byte aligned
