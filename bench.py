@@ -594,17 +594,22 @@ def run_quant_profile(args, local_rank):
     """The driver of a quantize profile (an ncu target, not a measurement):
     four eager calls on 2^27 N(0, 1) values of --qdtype at --qbs --
     quantize_blockwise with the dynamic map (--qtype 8bit), or quantize_nf4
-    on the 4096 x 4096 N(0, 0.02^2) tensor of config 1 (--qtype nf4).
+    on the 4096 x 4096 N(0, 0.02^2) tensor of config 1 (--qtype nf4), or the
+    single-launch NF4 + double quantization of that tensor (--qtype nf4dq).
     Captured with, e.g.,
     ncu --set full --clock-control none -k regex:quant_8bit -s 2 -c 1 ...
     python bench.py --workload quant-profile --qdtype f16 --qbs 256"""
     import torch
-    from bnb_b200.kernels import create_dynamic_map, quantize_blockwise, quantize_nf4
+    from bnb_b200.kernels import create_dynamic_map, quantize_blockwise, quantize_nf4, quantize_nf4_dq
     device = torch.device("cuda", local_rank)
     torch.cuda.set_device(device)
     dt = {"f32": torch.float32, "f16": torch.float16, "bf16": torch.bfloat16}[args.qdtype]
     g = torch.Generator(device).manual_seed(0)
-    if args.qtype == "nf4":
+    if args.qtype == "nf4dq":
+        x = (torch.randn(4096 * 4096, device=device, generator=g) * 0.02).to(dt)
+        for _ in range(4):
+            q = quantize_nf4_dq(x, args.qbs)[0]
+    elif args.qtype == "nf4":
         x = (torch.randn(4096 * 4096, device=device, generator=g) * 0.02).to(dt)
         for _ in range(4):
             q, a = quantize_nf4(x, args.qbs)
@@ -621,16 +626,16 @@ def run_quant_profile(args, local_rank):
 
 def run_matmul_profile(args, local_rank):
     """The driver of a matmul profile (an ncu target, not a measurement): four
-    eager bnb.matmul calls at M = --rows on one (--pn, --pk) NF4 bs64
-    double-quantized weight of N(0, 0.02^2) entries, with the kernels the
-    router picks (reported as "route")."""
+    eager bnb.matmul calls at M = --rows on one (--pn, --pk) NF4 (--wq nf4) or
+    8-bit (--wq 8bit) bs64 double-quantized weight of N(0, 0.02^2) entries,
+    with the kernels the router picks (reported as "route")."""
     import torch
     import bnb_b200 as bnb
     from bnb_b200 import _lib
     device = torch.device("cuda", local_rank)
     torch.cuda.set_device(device)
     g = torch.Generator(device).manual_seed(0)
-    w = bnb.quantize((torch.randn(args.pn, args.pk, device=device, generator=g) * 0.02).to(torch.bfloat16), "nf4",
+    w = bnb.quantize((torch.randn(args.pn, args.pk, device=device, generator=g) * 0.02).to(torch.bfloat16), args.wq,
                      BS, double_quant=True)
     x = torch.randn(args.m, args.pk, device=device, generator=g).to(torch.bfloat16)
     for _ in range(4):
@@ -638,8 +643,10 @@ def run_matmul_profile(args, local_rank):
     torch.cuda.synchronize()
     nb = _lib.gemv_workspace_bytes(args.m, args.pk, args.pn) if args.m <= 20 else 0
     ws = torch.empty(max(nb, 16), dtype=torch.uint8, device=device)
-    route = _lib.gemv_route(args.m, args.pk, args.pn, BS, w.absmax.data.data_ptr(), BS2, ws.data_ptr(), nb)
-    return {"workload": "matmul-profile", "n": args.pn, "k": args.pk, "m": args.m, "calls": 4, "route": route,
+    route = (_lib.gemv_route(args.m, args.pk, args.pn, BS, w.absmax.data.data_ptr(), BS2, ws.data_ptr(), nb)
+             if args.wq == "nf4" else "8-bit GEMV" if args.m <= _lib.GEMV8_MAX_M else "dequantize + matmul")
+    return {"workload": "matmul-profile", "weight": args.wq, "n": args.pn, "k": args.pk, "m": args.m, "calls": 4,
+            "route": route,
             "y_checksum": float(y.float().sum().item())}
 
 
@@ -858,7 +865,9 @@ def main():
     ap.add_argument("--pk", type=int, default=4096, help="matmul-profile weight columns (K)")
     ap.add_argument("--qdtype", choices=["f32", "f16", "bf16"], default="f16", help="quant-profile input type")
     ap.add_argument("--qbs", type=int, default=256, help="quant-profile blocksize")
-    ap.add_argument("--qtype", choices=["8bit", "nf4"], default="8bit", help="quant-profile quantization")
+    ap.add_argument("--qtype", choices=["8bit", "nf4", "nf4dq"], default="8bit",
+                    help="quant-profile quantization (nf4dq: NF4 with double quantization, one launch)")
+    ap.add_argument("--wq", choices=["nf4", "8bit"], default="nf4", help="matmul-profile weight quantization")
     ap.add_argument("--gather", choices=["peer", "nccl"], default="peer", help="config 4 all-gather")
     ap.add_argument("--ungrouped", action="store_true", help="config 4 with q/k/v and gate/up as separate GEMVs")
     args = ap.parse_args()

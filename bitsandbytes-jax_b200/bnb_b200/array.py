@@ -45,6 +45,12 @@ QType = Literal["nf4", "8bit"]
 # bitsandbytes' double quantization: absmax is itself 8-bit quantized in
 # blocks of this size, around its mean (reference array.py:30).
 _NESTED_BLOCKSIZE = 256
+# Largest tensor that double-quantizes in the single launch: measured on a
+# B200, the one-launch kernel matches the three launches at 2^24 elements
+# (35.3 vs 35.8 us) and falls behind above (90 vs 78 us at 4096 x 14336): its
+# NF4 pass runs with the occupancy of the whole kernel and without the CTAs
+# that do the nested pass.
+_SINGLE_PASS_MAX = 1 << 24
 
 _DTYPES = {"float16": torch.float16, "bfloat16": torch.bfloat16, "float32": torch.float32}
 
@@ -259,7 +265,7 @@ def quantize(
             omitted).
     """
     x = array.reshape(-1)
-    if qtype == "nf4" and double_quant and x.numel() > 0:
+    if qtype == "nf4" and double_quant and 0 < x.numel() <= _SINGLE_PASS_MAX:
         # the three steps below in one launch (bnbq_quantize_nf4_dq), bitwise the same
         code2 = create_dynamic_map(device=x.device)
         data, absmax, q2, absmax2, offset = quantize_nf4_dq(x, blocksize, code2, _NESTED_BLOCKSIZE)

@@ -123,7 +123,15 @@ struct QuantArgs {
   uint32_t two;         // 2, passed at run time (see gt01)
   int offset_in_arg;    // the offset is offset_value (computed by the same kernel), not *offset
   float offset_value;
+  int cta0, ctas;       // the CTAs [cta0, cta0 + ctas) share the work (ctas == 0: the whole grid)
 };
+
+// This thread's warp among the working CTAs, and the number of their warps.
+__device__ __forceinline__ void work_warp(const QuantArgs& a, int64_t& gw, int64_t& tw) {
+  const int64_t ctas = a.ctas ? a.ctas : gridDim.x;
+  gw = ((int64_t(blockIdx.x) - a.cta0) * kThreads + threadIdx.x) >> 5;
+  tw = (ctas * kThreads) >> 5;
+}
 
 __device__ __forceinline__ float offset_of(const QuantArgs& a) {
   return a.offset ? (a.offset_in_arg ? a.offset_value : __ldg(a.offset)) : 0.0f;
@@ -439,8 +447,8 @@ __device__ void quant_small(const QuantArgs& a, const Choose& choose) {
   const int lane = threadIdx.x & 31;
   const int L = 1 << (a.log2_bs - 3);
   const int64_t nseg = (a.n + 255) >> 8;
-  const int64_t gw = (int64_t(blockIdx.x) * kThreads + threadIdx.x) >> 5;
-  const int64_t tw = (int64_t(gridDim.x) * kThreads) >> 5;
+  int64_t gw, tw;
+  work_warp(a, gw, tw);
   const float off = offset_of(a);
   constexpr int U = sizeof(InT) == 4 ? 2 : 4;
   for (int64_t seg0 = gw; seg0 < nseg; seg0 += tw * U) {
@@ -480,8 +488,8 @@ __device__ void quant_large(const QuantArgs& a, const Choose& choose) {
   const InT* x = static_cast<const InT*>(a.x);
   const int lane = threadIdx.x & 31;
   const int P = 1 << (a.log2_bs - 8);
-  const int64_t gw = (int64_t(blockIdx.x) * kThreads + threadIdx.x) >> 5;
-  const int64_t tw = (int64_t(gridDim.x) * kThreads) >> 5;
+  int64_t gw, tw;
+  work_warp(a, gw, tw);
   const float off = offset_of(a);
   for (int64_t b = gw; b < a.nb; b += tw) {
     const int64_t base = b << a.log2_bs;
@@ -627,29 +635,42 @@ __global__ void __launch_bounds__(1024) mean_kernel(const float* a, int64_t n, f
 
 // --------------------------------------------- NF4 + double quantization, one launch
 // quant_nf4_dq_kernel: the three steps of quantize(..., double_quant=True)
-// (array.py:199-202) in one cooperative launch (every CTA resident):
-//   1. NF4 codes and float32 absmax of x, exactly as quant_nf4_kernel;
-//   2. grid barrier; CTAs 0..7 form the float64 sums of absmax in mean_kernel's
-//      order (slot c*1024 + t sums elements c*1024 + t + j*8192 in order of j,
-//      then the 1024 slots of each c in mean_kernel's tree), store them to the
-//      workspace; grid barrier; every CTA adds the 8 sums in order, so every
-//      CTA holds offset = fl32(sum / nb), bitwise bnbq_absmax_mean's value;
-//   3. the 8-bit quantization of absmax - offset with code2 in blocks of
-//      blocksize2, exactly as quant_8bit_kernel with that offset.
-// The grid barriers count CTAs on a workspace word that the host zeroes on the
-// stream before the launch; each wait is bounded in time (an expiry is counted
-// in the wait-timeout counter and the CTA stops: the outputs are then wrong).
+// (array.py:199-202) in one cooperative launch (every CTA resident). The grid
+// is split: the first CTAs quantize x, the last a8.ctas CTAs -- as many as the
+// nested pass fills -- build that pass's code tables meanwhile.
+//   1. NF4 codes and float32 absmax of x, exactly as quant_nf4_kernel, by the
+//      first CTAs, which then arrive on barrier 1.
+//   2. The float64 mean of absmax in mean_kernel's summation order: CTAs
+//      0 .. 31 wait for barrier 1; thread s of them forms mean_kernel's slot
+//      sum s (elements s + j*8192 in order of j, 16 loads in flight) into the
+//      workspace and arrives on barrier 2; CTA c < 8 waits for it, adds the
+//      1024 slots of its c in mean_kernel's tree, stores the sum and arrives on
+//      barrier 3.
+//   3. The nested CTAs wait for barrier 3, add the 8 sums in order, so that
+//      each holds offset = fl32(sum / nb), bitwise bnbq_absmax_mean's value,
+//      and quantize absmax - offset with code2 in blocks of blocksize2,
+//      exactly as quant_8bit_kernel with that offset.
+// The barriers count arrivals on three workspace words that the host zeroes on
+// the stream before the launch; only the CTAs that need a barrier wait on it,
+// each wait bounded in time (an expiry is counted in the wait-timeout counter
+// and the CTA stops: the outputs are then wrong).
 struct DqWork {
-  unsigned int arrived;  // CTAs past barrier 1 (gridDim.x), then barrier 2 (2 gridDim.x)
-  unsigned int pad[3];
+  unsigned int arrived[3];  // CTAs that reached barrier 1, 2, 3
+  unsigned int pad;
   double sums[kMeanCtas];
+  double slots[kMeanCtas * 1024];
 };
 
-__device__ __forceinline__ bool grid_barrier(unsigned int* arrived, unsigned int target, int* s_fail) {
+__device__ __forceinline__ void grid_arrive(unsigned int* arrived) {
   __syncthreads();
   if (threadIdx.x == 0) {
     __threadfence();  // this CTA's outputs before its arrival
     atomicAdd(arrived, 1u);
+  }
+}
+
+__device__ __forceinline__ bool grid_wait(const unsigned int* arrived, unsigned int target, int* s_fail) {
+  if (threadIdx.x == 0) {
     const uint64_t t0 = global_ns();
     const uint64_t limit = g_bnbq_wait_limit_ns;
     unsigned int v;
@@ -676,35 +697,54 @@ __global__ void __launch_bounds__(kThreads) quant_nf4_dq_kernel(QuantArgs a4, Qu
   __shared__ double part[1024];
   __shared__ int s_fail;
   if (threadIdx.x == 0) s_fail = 0;
-  build_nf4_tables(s4);
-  build_q8_tables(s8, a8.code);  // (ends with a CTA barrier)
-  __syncthreads();
-  // 1. NF4
-  quant_body<InT, true, LARGE>(a4, NF4Choose{&s4, a4.two});
-  if (!grid_barrier(&work->arrived, gridDim.x, &s_fail)) return;
-  // 2. the mean, in mean_kernel's summation order
-  const int64_t nb = a8.n;
-  if (blockIdx.x < kMeanCtas) {
-    const int c = int(blockIdx.x);
-    for (int t = threadIdx.x; t < 1024; t += kThreads) {
+  if (int(blockIdx.x) < a8.cta0) {  // ------------------------- 1. NF4 (and 2. the mean)
+    build_nf4_tables(s4);
+    __syncthreads();
+    quant_body<InT, true, LARGE>(a4, NF4Choose{&s4, a4.two});
+    grid_arrive(&work->arrived[0]);
+    constexpr int64_t kSlots = int64_t(kMeanCtas) * 1024;
+    constexpr int kSlotCtas = int(kSlots / kThreads);  // one slot per thread
+    if (int(blockIdx.x) >= kSlotCtas) return;
+    if (!grid_wait(&work->arrived[0], unsigned(a8.cta0), &s_fail)) return;
+    {  // slot s sums elements s + j*8192 in order of j, 16 loads in flight
+      const int64_t nb = a8.n;
+      const float* am = static_cast<const float*>(a8.x);
+      const int64_t slot = int64_t(blockIdx.x) * kThreads + threadIdx.x;
       double sum = 0.0;
-      for (int64_t i = int64_t(c) * 1024 + t; i < nb; i += int64_t(kMeanCtas) * 1024)
-        sum += double(__ldcg(static_cast<const float*>(a8.x) + i));
-      part[t] = sum;
+      for (int64_t j0 = 0; slot + j0 * kSlots < nb; j0 += 16) {
+        float v[16];
+#pragma unroll
+        for (int u = 0; u < 16; ++u) {
+          const int64_t i = slot + (j0 + u) * kSlots;
+          v[u] = i < nb ? __ldcg(am + i) : 0.0f;
+        }
+#pragma unroll
+        for (int u = 0; u < 16; ++u)
+          if (slot + (j0 + u) * kSlots < nb) sum += double(v[u]);
+      }
+      __stcg(&work->slots[slot], sum);
     }
+    grid_arrive(&work->arrived[1]);
+    if (blockIdx.x >= kMeanCtas) return;
+    if (!grid_wait(&work->arrived[1], unsigned(kSlotCtas), &s_fail)) return;
+    const int c = int(blockIdx.x);
+    for (int t = threadIdx.x; t < 1024; t += kThreads) part[t] = __ldcg(&work->slots[c * 1024 + t]);
     __syncthreads();
     for (int w = 512; w > 0; w >>= 1) {
       for (int t = threadIdx.x; t < w; t += kThreads) part[t] += part[t + w];
       __syncthreads();
     }
     if (threadIdx.x == 0) __stcg(&work->sums[c], part[0]);
+    grid_arrive(&work->arrived[2]);
+    return;
   }
-  if (!grid_barrier(&work->arrived, 2u * gridDim.x, &s_fail)) return;
+  // ------------------------------------------------------------------ 3. nested
+  build_q8_tables(s8, a8.code);  // (ends with a CTA barrier)
+  if (!grid_wait(&work->arrived[2], kMeanCtas, &s_fail)) return;
   double total = 0.0;
   for (int c = 0; c < kMeanCtas; ++c) total += __ldcg(&work->sums[c]);
-  const float off = float(total / double(nb));
-  if (blockIdx.x == 0 && threadIdx.x == 0) *const_cast<float*>(a8.offset) = off;
-  // 3. 8-bit quantization of absmax - offset
+  const float off = float(total / double(a8.n));
+  if (int(blockIdx.x) == a8.cta0 && threadIdx.x == 0) *const_cast<float*>(a8.offset) = off;
   QuantArgs b = a8;
   b.offset_in_arg = 1;
   b.offset_value = off;
@@ -726,9 +766,22 @@ int launch_dq(const QuantArgs& a4, const QuantArgs& a8, DqWork* work, cudaStream
   int64_t grid = int64_t(di.sm_count) * per_sm;  // every CTA resident (cooperative launch)
   const int64_t want = (work_warps(a4) + kWarps - 1) / kWarps;
   if (want < grid) grid = want;
-  if (grid < kMeanCtas) grid = kMeanCtas;
+  if (grid < 64) grid = 64;  // 32 CTAs for the mean's slots, and the nested pass
   if (grid > int64_t(di.sm_count) * per_sm) return BNBQ_ERR_UNSUPPORTED;
-  if (cudaMemsetAsync(work, 0, sizeof(DqWork), s) != cudaSuccess) return BNBQ_ERR_CUDA;
+  // the nested pass (1/64 of the NF4 pass's elements for blocksize 64) on the
+  // last CTAs of the grid: as many as its work fills, at most 1/16 of the grid
+  // (measured: the NF4 pass slows in proportion to the CTAs it loses); the
+  // NF4 pass, and the mean, on the others
+  static_assert(1024 % kThreads == 0, "whole CTAs per mean slot group");
+  const int64_t cap3 = grid / 16 > 8 ? grid / 16 : 8;
+  int64_t ctas3 = (work_warps(a8) + kWarps - 1) / kWarps;
+  ctas3 = ctas3 < 1 ? 1 : (ctas3 > cap3 ? cap3 : ctas3);
+  QuantArgs a = a4, b = a8;
+  a.cta0 = 0;
+  a.ctas = int(grid - ctas3);
+  b.cta0 = int(grid - ctas3);
+  b.ctas = int(ctas3);
+  if (cudaMemsetAsync(work->arrived, 0, sizeof(work->arrived), s) != cudaSuccess) return BNBQ_ERR_CUDA;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(unsigned(grid));
   cfg.blockDim = dim3(kThreads);
@@ -739,7 +792,7 @@ int launch_dq(const QuantArgs& a4, const QuantArgs& a8, DqWork* work, cudaStream
   attr[0].val.cooperative = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  if (cudaLaunchKernelEx(&cfg, kern, a4, a8, work) != cudaSuccess) return BNBQ_ERR_CUDA;
+  if (cudaLaunchKernelEx(&cfg, kern, a, b, work) != cudaSuccess) return BNBQ_ERR_CUDA;
   return launch_status();
 }
 

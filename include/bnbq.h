@@ -83,7 +83,7 @@ BNBQ_API int bnbq_quantize_blockwise(int dtype, const void* x, int64_t n, int32_
 BNBQ_API int bnbq_absmax_mean(const float* absmax, int64_t nb, float* offset, void* stream);
 
 /* NF4 quantization with double-quantized scales in ONE kernel launch (plus a
- * 16-byte memset of the workspace): bitwise the chain
+ * 12-byte memset of the workspace's barrier counters): bitwise the chain
  *   bnbq_quantize_nf4(x -> q, absmax);
  *   bnbq_absmax_mean(absmax -> offset);
  *   bnbq_quantize_blockwise(absmax with *offset subtracted, code2, blocksize2
