@@ -41,6 +41,8 @@ _SIGNATURES = {
     "bnbq_gemv_workspace_bytes": "iilP",
     "bnbq_gemv_blockwise_ws": "iPiiPliPPPPPPilPlPlP",
     "bnbq_gemv_blockwise_workspace_bytes": "iilP",
+    "bnbq_gemv_t_nf4_ws": "iPillipiPPPPPilPlPlP",
+    "bnbq_gemv_t_nf4_workspace_bytes": "iilP",
     "bnbq_gemv_route": "iiliPiPlP",
     "bnbq_set_gemv_policy": "i",
     "bnbq_rcp_approx_ftz": "PPlP",
@@ -171,6 +173,12 @@ def gemv_workspace_bytes(m: int, k: int, n_rows: int) -> int:
 def gemv8_workspace_bytes(m: int, k: int, n_rows: int) -> int:
     n = C.c_int64(0)
     check(lib().bnbq_gemv_blockwise_workspace_bytes(m, k, n_rows, C.byref(n)), "bnbq_gemv_blockwise_workspace_bytes")
+    return int(n.value)
+
+
+def gemv_t_workspace_bytes(m: int, k: int, n_rows: int) -> int:
+    n = C.c_int64(0)
+    check(lib().bnbq_gemv_t_nf4_workspace_bytes(m, k, n_rows, C.byref(n)), "bnbq_gemv_t_nf4_workspace_bytes")
     return int(n.value)
 
 

@@ -11,12 +11,13 @@ from .dequantize import (
     dequantize_nf4,
     dequantize_nf4_nested,
 )
-from .gemv import GEMV8_MAX_M, GEMV_MAX_M, gemv_blockwise, gemv_nf4, matmul_nf4
+from .gemv import GEMV8_MAX_M, GEMV_MAX_M, GEMV_T_MAX_M, gemv_blockwise, gemv_nf4, gemv_t_nf4, matmul_nf4
 from .quantize import absmax_mean, create_dynamic_map, quantize_blockwise, quantize_nf4, quantize_nf4_dq
 
 __all__ = [
     "GEMV8_MAX_M",
     "GEMV_MAX_M",
+    "GEMV_T_MAX_M",
     "NF4_TABLE",
     "absmax_mean",
     "create_dynamic_map",
@@ -26,6 +27,7 @@ __all__ = [
     "dequantize_nf4_nested",
     "gemv_blockwise",
     "gemv_nf4",
+    "gemv_t_nf4",
     "matmul_nf4",
     "quantize_blockwise",
     "quantize_nf4",

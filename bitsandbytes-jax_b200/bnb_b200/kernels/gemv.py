@@ -298,3 +298,66 @@ def gemv_blockwise(
         with torch.cuda.device(x.device):
             _lib.call(*args)
     return out
+
+
+GEMV_T_MAX_M = 4  # rows of g the fused backward takes
+
+
+def gemv_t_applies(m: int, k: int, n_rows: int) -> bool:
+    """Whether :func:`gemv_t_nf4` takes this shape."""
+    return 1 <= m <= GEMV_T_MAX_M and k % 256 == 0 and n_rows <= 512 * 256
+
+
+def gemv_t_nf4(
+    g: torch.Tensor,
+    data: torch.Tensor,
+    absmax: torch.Tensor,
+    n_rows: int,
+    k: int,
+    blocksize: int,
+    *,
+    nested: tuple[torch.Tensor, torch.Tensor, torch.Tensor, int] | None = None,
+    absmax2_block0: int = 0,
+) -> torch.Tensor:
+    """``g @ W`` for an NF4 weight W (n_rows, k), never materialized
+    (``bnbq_gemv_t_nf4_ws``): the backward of :func:`bnb_b200.matmul` for up to
+    GEMV_T_MAX_M rows of g. The reference computes ``g @ w.dequantize(g.dtype)``
+    (_matmul.py:67-68); here every weight is its exact float32 dequantized
+    value, accumulated in float32 and rounded once, so a one-hot g returns the
+    dequantized weight row bitwise."""
+    if g.dim() != 2 or g.shape[1] != n_rows:
+        raise ValueError(f"g must be (M, {n_rows}), got {tuple(g.shape)}")
+    m = g.shape[0]
+    if g.dtype not in (torch.bfloat16, torch.float16):
+        raise NotImplementedError(f"gemv_t_nf4 of {g.dtype} g is not implemented")
+    if not gemv_t_applies(m, k, n_rows):
+        raise ValueError(f"gemv_t_nf4 takes 1..{GEMV_T_MAX_M} rows, K % 256 == 0, got M={m}, K={k}")
+    _log2_blocksize(blocksize)
+    assert data.dtype == torch.uint8 and data.numel() * 2 == n_rows * k, (tuple(data.shape), n_rows, k)
+    _lib.require_cuda(g, data, absmax)
+    gs = g if g.stride(1) == 1 and g.data_ptr() % 2 == 0 else g.contiguous()
+    w = _lib.aligned(data.reshape(-1))
+    if nested is None:
+        assert absmax.dtype == torch.float32, absmax.dtype
+        a, aq, a2, c2, off, bs2 = _lib.aligned(absmax.reshape(-1), 4), None, None, None, None, 0
+    else:
+        absmax2, code2, offset, bs2 = nested
+        assert absmax.dtype == torch.uint8, absmax.dtype
+        _log2_blocksize(bs2)
+        a = None
+        aq = _lib.aligned(absmax.reshape(-1))
+        a2 = _lib.aligned(_f32_on(absmax2, g.device).reshape(-1), 4)
+        c2 = _lib.aligned(_f32_on(code2, g.device).reshape(-1), 4)
+        off = _lib.aligned(_f32_on(offset, g.device).reshape(1), 4)
+    out = torch.empty((m, k), dtype=g.dtype, device=g.device)
+    stream = _lib.stream_of(gs)
+    ws = _lib.workspace(g.device, stream, _lib.gemv_t_workspace_bytes(m, k, n_rows))
+    args = ("bnbq_gemv_t_nf4_ws", _lib.DTYPE_CODE[g.dtype], gs.data_ptr(), m, n_rows, gs.stride(0), k, w.data_ptr(),
+            blocksize, _lib.ptr(a), _lib.ptr(aq), _lib.ptr(a2), _lib.ptr(c2), _lib.ptr(off), bs2, absmax2_block0,
+            out.data_ptr(), k, ws.data_ptr(), ws.numel(), stream)
+    if g.device.index == torch.cuda.current_device():
+        _lib.call(*args)
+    else:
+        with torch.cuda.device(g.device):
+            _lib.call(*args)
+    return out
