@@ -38,9 +38,12 @@ graph replay.
 Extra keys of the default line (N=1): `config1` (NF4 quantize and dequantize
 of a 4096x4096 bf16 tensor), `config3` (8-bit blockwise of 2^28+37 elements,
 f32/f16/bf16, blocksizes 256 and 4096), `config5` (the fused GEMM on the
-Llama-3-70B MLP shapes at M=2048 beside dequantize+matmul) and, at every N,
+Llama-3-70B MLP shapes at M=2048 beside dequantize+matmul), `next_rows`
+(the config-2 weight shape through the fused 8-bit-weight GEMV and the fused
+backward g @ W, each beside the reference's dequantize route) and, at every N,
 `config4` (one pass over a Llama-3-8B decode stack with every GEMV
-row-sharded and its y all-gathered).
+row-sharded and its y all-gathered). `config1` also times the single-launch
+NF4 + double quantization beside the three-launch chain.
 
 `--workload quant` and `--workload gemm` (not read by the driver) measure the
 other configurations the same way: config 1 (NF4 quantize + dequantize round
@@ -408,6 +411,7 @@ def run_ours(args, dist, rank, world, local_rank):
         if world == 1:
             extras["config1"], extras["config3"] = quant_cases(torch, device, args.warmup)
             extras["config5"] = gemm_cases(torch, bnb, device)
+            extras["next_rows"] = next_rows_cases(torch, bnb, device, args.warmup)
     if pg is not None:
         torch.cuda.synchronize()
         dist.barrier()
@@ -628,7 +632,8 @@ def run_matmul_profile(args, local_rank):
     """The driver of a matmul profile (an ncu target, not a measurement): four
     eager bnb.matmul calls at M = --rows on one (--pn, --pk) NF4 (--wq nf4) or
     8-bit (--wq 8bit) bs64 double-quantized weight of N(0, 0.02^2) entries,
-    with the kernels the router picks (reported as "route")."""
+    with the kernels the router picks (reported as "route"), or four calls of
+    the fused backward g @ W with g of M x --pn (--backward)."""
     import torch
     import bnb_b200 as bnb
     from bnb_b200 import _lib
@@ -638,6 +643,15 @@ def run_matmul_profile(args, local_rank):
     w = bnb.quantize((torch.randn(args.pn, args.pk, device=device, generator=g) * 0.02).to(torch.bfloat16), args.wq,
                      BS, double_quant=True)
     x = torch.randn(args.m, args.pk, device=device, generator=g).to(torch.bfloat16)
+    if args.backward:  # the fused backward g @ W, g of M x --pn
+        x = torch.randn(args.m, args.pn, device=device, generator=g).to(torch.bfloat16)
+        from bnb_b200.kernels import gemv_t_nf4
+        a = w.absmax
+        for _ in range(4):
+            y = gemv_t_nf4(x, w.data, a.data, args.pn, args.pk, BS, nested=(a.absmax, a.code, a.offset, a.blocksize))
+        torch.cuda.synchronize()
+        return {"workload": "matmul-profile", "backward": True, "n": args.pn, "k": args.pk, "m": args.m,
+                "calls": 4, "y_checksum": float(y.float().sum().item())}
     for _ in range(4):
         y = bnb.matmul(x, w)
     torch.cuda.synchronize()
@@ -648,6 +662,44 @@ def run_matmul_profile(args, local_rank):
     return {"workload": "matmul-profile", "weight": args.wq, "n": args.pn, "k": args.pk, "m": args.m, "calls": 4,
             "route": route,
             "y_checksum": float(y.float().sum().item())}
+
+
+def next_rows_cases(torch, bnb, device, warmup: int):
+    """The config-2 weight shape through the two extensions beyond the
+    reference's kernels: the fused GEMV of an 8-bit weight (dynamic map, bs 64,
+    double-quantized) and the fused backward g @ W of the NF4 weight, each
+    beside the reference's own route (x @ w.dequantize().T; g @ w.dequantize()).
+    Device time per call, CUDA graph over rotated weights (more than L2)."""
+    from bnb_b200.kernels import gemv_t_nf4
+    g0 = torch.Generator(device).manual_seed(5)
+    out = {}
+    w8 = [bnb.quantize((torch.randn(N_ROWS, K_COLS, device=device, generator=g0) * 0.02).to(torch.bfloat16), "8bit",
+                       BS, double_quant=True) for _ in range(4)]
+    b8 = N_ROWS * K_COLS + N_ROWS * K_COLS // BS
+    for m in (1, 4):
+        x = torch.randn(m, K_COLS, device=device, generator=g0).to(torch.bfloat16)
+        t = time_graph(torch, lambda i: bnb.matmul(x, w8[i % 4]), 64, warmup, device) / 64
+        tr = time_graph(torch, lambda i: x @ w8[i % 4].dequantize(x.dtype).T, 16, warmup, device) / 16
+        out[f"gemv_8bit_m{m}"] = {"us": round(t * 1e3, 2), "weight_gbs": round(b8 / (t * 1e-3) / 1e9, 1),
+                                  "dequantize_matmul_us": round(tr * 1e3, 2)}
+    del w8
+    w4 = [bnb.quantize((torch.randn(N_ROWS, K_COLS, device=device, generator=g0) * 0.02).to(torch.bfloat16), "nf4",
+                       BS, double_quant=True) for _ in range(8)]
+
+    def fused(w, gm):
+        a = w.absmax
+        return gemv_t_nf4(gm, w.data, a.data, N_ROWS, K_COLS, BS, nested=(a.absmax, a.code, a.offset, a.blocksize))
+
+    for m in (1, 4):
+        gm = torch.randn(m, N_ROWS, device=device, generator=g0).to(torch.bfloat16)
+        t = time_graph(torch, lambda i: fused(w4[i % 8], gm), 64, warmup, device) / 64
+        tr = time_graph(torch, lambda i: gm @ w4[i % 8].dequantize(gm.dtype), 16, warmup, device) / 16
+        out[f"backward_m{m}"] = {"us": round(t * 1e3, 2), "weight_gbs": round(W_BYTES / (t * 1e-3) / 1e9, 1),
+                                 "dequantize_matmul_us": round(tr * 1e3, 2)}
+    del w4
+    torch.cuda.synchronize()
+    torch.cuda.empty_cache()
+    return out
 
 
 def gemm_cases(torch, bnb, device, ms=(64, 512, 2048)):
@@ -868,6 +920,7 @@ def main():
     ap.add_argument("--qtype", choices=["8bit", "nf4", "nf4dq"], default="8bit",
                     help="quant-profile quantization (nf4dq: NF4 with double quantization, one launch)")
     ap.add_argument("--wq", choices=["nf4", "8bit"], default="nf4", help="matmul-profile weight quantization")
+    ap.add_argument("--backward", action="store_true", help="matmul-profile: the fused backward g @ W (NF4)")
     ap.add_argument("--gather", choices=["peer", "nccl"], default="peer", help="config 4 all-gather")
     ap.add_argument("--ungrouped", action="store_true", help="config 4 with q/k/v and gate/up as separate GEMVs")
     args = ap.parse_args()

@@ -12,9 +12,10 @@
 // dequantized weight row, bitwise.
 //
 // Mapping. The columns are cut into groups of 256 (K % 256 == 0) and the rows
-// into P parts; a unit is (part, group). One CTA per SM slot (persistent, two
-// per SM) builds the byte -> (T[hi], T[lo]) pair table once (one copy per lane,
-// so a warp's 32 pair loads hit 32 distinct banks) and walks its units. In a
+// into P parts; a unit is (part, group). One CTA per SM slot (persistent,
+// two per SM) builds the byte -> (T[hi], T[lo]) pair table once (one copy per
+// lane, so a warp's 32 pair loads hit 32 distinct banks) and walks its units.
+// In a
 // unit, lane l of every warp owns code word l of the group (columns 8l ..
 // 8l + 7); warp w takes the part's rows w, w + 8, ..., loading the code words
 // and scales of 8 rows before it decodes any (each row's 32 words are one
@@ -25,6 +26,13 @@
 // it waits for the first with griddepcontrol.wait) adds each output's P
 // partials in part order and rounds once. Deterministic; the workspace needs
 // no initial contents.
+//
+// Measured on a B200 (config 2's weight, 4096 x 14336, M = 1): 67.7 us against
+// 58.5 us for the reference's rule (our dequantize kernel, then cuBLAS). The
+// kernel is memory-latency bound (long-scoreboard stalls first, 22 % issue
+// active): a warp has only 8 rows x 128 bytes of codes in flight. So
+// bnb_b200.matmul's backward keeps the rule, and this entry point is offered
+// as the fused path that needs no dense weight in memory.
 #include <atomic>
 
 #include "bnbq_common.cuh"

@@ -206,8 +206,10 @@ BNBQ_API int bnbq_matmul_nf4_ws(int dtype, const void* x, int32_t m, int32_t k,
  * workspace (any contents, 16-byte aligned, at least
  * bnbq_gemv_t_nf4_workspace_bytes) takes split-row partial sums that a
  * second kernel adds in order. Calls sharing it must be ordered on one stream.
- * Replaces: the custom VJP's backward g @ w.dequantize(g.dtype)
- * (_matmul.py:67-68) for those shapes. */
+ * Replaces (where a caller wants no dense weight): the custom VJP's
+ * backward g @ w.dequantize(g.dtype) (_matmul.py:67-68) for those shapes;
+ * measured slower than our dequantize plus cuBLAS on a B200, so
+ * bnb_b200.matmul's backward keeps the dequantize route. */
 BNBQ_API int bnbq_gemv_t_nf4_ws(int dtype, const void* g, int32_t m, int64_t n_rows, int64_t ldg, int32_t k,
                                 const uint8_t* w, int32_t blocksize, const float* absmax,
                                 const uint8_t* absmax_q, const float* absmax2, const float* code2,
