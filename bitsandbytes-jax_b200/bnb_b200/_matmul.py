@@ -3,7 +3,8 @@
 Mirrors the reference's ``bnb_jax._matmul`` (_matmul.py): same ``matmul``
 signature, shape checks and errors, and the same custom backward
 (``g @ w.dequantize(g.dtype)``, no gradient to ``w``, only the quantized weight
-kept for the backward pass).
+kept for the backward pass); for up to 4 rows of g (an NF4 weight, K % 256 ==
+0) that product runs fused, the weight never materialized.
 
 Routing. An NF4 weight with a bfloat16/float16 x, K % 32 == 0 and blocksize >=
 32: up to GEMV_MAX_M rows of x run the fused GEMV (float32 weights, closer to
@@ -21,7 +22,7 @@ from __future__ import annotations
 import torch
 
 from .array import QuantizedArray
-from .kernels.gemv import _CHUNK, gemv_blockwise, gemv_blockwise_applies, plan_for
+from .kernels.gemv import _CHUNK, gemv_blockwise, gemv_blockwise_applies, gemv_t_applies, gemv_t_nf4, plan_for
 
 __all__ = ["matmul"]
 
@@ -79,11 +80,14 @@ class _Matmul2d(torch.autograd.Function):
 
     @staticmethod
     def backward(ctx, g: torch.Tensor):
-        # The reference's rule. (kernels.gemv_t_nf4 computes it without a
-        # dense weight for up to 4 rows of g, but measured slower on a B200
-        # than our dequantize kernel plus cuBLAS: 67.7 vs 58.5 us on config 2's
-        # weight at M = 1.)
-        return g @ ctx.w.dequantize(g.dtype), None
+        w = ctx.w
+        if (w.qtype == "nf4" and g.dtype in (torch.bfloat16, torch.float16) and g.is_cuda
+                and w.blocksize >= _CHUNK and gemv_t_applies(g.shape[0], w.shape[1], w.shape[0])):
+            # the reference's rule with the weight kept NF4 (measured on a B200:
+            # 23.8 us against 58.0 us for dequantize + cuBLAS on config 2's weight)
+            scales, nested = _fused_args(w)
+            return gemv_t_nf4(g, w.data, scales, w.shape[0], w.shape[1], w.blocksize, nested=nested), None
+        return g @ w.dequantize(g.dtype), None
 
 
 def _fused_applies(xm: torch.Tensor, w: QuantizedArray) -> bool:

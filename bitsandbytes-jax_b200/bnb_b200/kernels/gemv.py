@@ -305,7 +305,7 @@ GEMV_T_MAX_M = 4  # rows of g the fused backward takes
 
 def gemv_t_applies(m: int, k: int, n_rows: int) -> bool:
     """Whether :func:`gemv_t_nf4` takes this shape."""
-    return 1 <= m <= GEMV_T_MAX_M and k % 256 == 0 and n_rows <= 512 * 256
+    return 1 <= m <= GEMV_T_MAX_M and k % 256 == 0 and n_rows <= (1 << 29)
 
 
 def gemv_t_nf4(
@@ -333,6 +333,8 @@ def gemv_t_nf4(
     if not gemv_t_applies(m, k, n_rows):
         raise ValueError(f"gemv_t_nf4 takes 1..{GEMV_T_MAX_M} rows, K % 256 == 0, got M={m}, K={k}")
     _log2_blocksize(blocksize)
+    if blocksize < _CHUNK:
+        raise ValueError(f"blocksize must be >= {_CHUNK}, got {blocksize}")
     assert data.dtype == torch.uint8 and data.numel() * 2 == n_rows * k, (tuple(data.shape), n_rows, k)
     _lib.require_cuda(g, data, absmax)
     gs = g if g.stride(1) == 1 and g.data_ptr() % 2 == 0 else g.contiguous()

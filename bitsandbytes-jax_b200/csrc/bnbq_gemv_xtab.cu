@@ -77,6 +77,7 @@ constexpr int kRows = 32;               // weight rows per unit (one per lane)
 constexpr int kMaxStages = 56;
 constexpr int kProducers = 2;  // producer warps per CTA (TMA issue is per-thread latency-bound)
 constexpr int kMaxDevices = 64;
+constexpr uint32_t kPairTableBytesT = 256 * 32 * 8;  // the backward's byte -> (T[hi], T[lo]) table, one copy per lane
 
 // Which GEMV a call with a workspace gets: 0 automatic -- the table GEMV when
 // the weight has at least 1.5 output rows per element of K (wide weights:
@@ -948,6 +949,264 @@ __global__ void __launch_bounds__((Cfg8<M>::kConsumers + kProducers) * 32, 1)
   }
 }
 
+// ---------------------------------------------------------------------------
+// The backward of the fused matmul for a few rows of g (gemv_t_kernel):
+// out[m, k] = sum_n g[m, n] * W[n, k], W NF4 (n_rows x K) never decoded to
+// memory; the reference computes g @ w.dequantize(g.dtype) (_matmul.py:67-68).
+// Units are the table GEMV's (256 columns x 32 rows, one TMA tile), taken in
+// plain unit order (column group major) from the same producers and ring.
+// Lane l owns code word l (columns 8l .. 8l + 7) of the group; for each row of
+// its unit it reads the row's word (the warp reads the row's 128 contiguous
+// bytes), the row's block scale (decoded by the lane that owns the row and
+// passed through a per-warp shared array) and g's values of the row, and
+// accumulates g * w, w = mul.ftz(T[q], a) exactly (the pair table gives T of
+// both nibbles), in float32, over every unit it takes of a column group. A
+// warp stores one partial per column group it touched (zeros for a group of
+// its CTA it had no unit of); a second kernel adds, per output, the partials
+// of the CTAs that covered its group, in CTA, group-segment and warp order,
+// and rounds once. A one-hot g returns the dequantized weight row bitwise.
+constexpr int kTConsumers = 12;
+constexpr int kTRound = lcm(kTConsumers, kProducers);
+
+struct GemvTArgs {
+  const void* g;   // M x n_rows, row stride ldg
+  float* partial;  // [grid][maxseg][kTConsumers][M][256]
+  XtabArgs x;      // the weight's scales, sizes and block numbering, as fetch_scales reads them
+  int64_t ldg, units;
+  int groups, row_blocks, maxseg;
+  uint32_t dyn_bytes;
+};
+
+template <typename XT, int M, int NB, bool NESTED>
+__global__ void __launch_bounds__((kTConsumers + kProducers) * 32, 1)
+    gemv_t_kernel(const __grid_constant__ CUtensorMap tmap, const GemvTArgs a) {
+  constexpr uint32_t kStage = kRows * 128;
+  constexpr int LPB = 32 / NB;  // lanes per block
+  extern __shared__ __align__(1024) uint8_t smem[];
+  __shared__ float s_code2[256];
+  __shared__ __align__(8) uint64_t s_bar[2 * kMaxStages];
+  __shared__ volatile int s_abort;
+  __shared__ volatile int s_next[kProducers];
+  __shared__ float s_a[kTConsumers][kRows][NB];
+  __shared__ float s_gv[kTConsumers][M][kRows];
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int ncw = kTConsumers;
+  const int64_t u0 = int64_t(blockIdx.x) * a.units / gridDim.x;
+  const int64_t u1 = int64_t(blockIdx.x + 1) * a.units / gridDim.x;
+  const int n_units = int(u1 - u0);
+  const int g_first = int(u0 / a.row_blocks);
+  float2* s_pair = reinterpret_cast<float2*>(smem);  // [256][32]
+  const uint32_t stage0 = smem_u32(smem) + kPairTableBytesT;
+  int S = int((a.dyn_bytes - kPairTableBytesT) / kStage);
+  if (S > kMaxStages) S = kMaxStages;
+  S -= S % kTRound;
+  const uint32_t full0 = smem_u32(s_bar), empty0 = full0 + 8u * kMaxStages;
+  if (threadIdx.x == 0) {
+    s_abort = S < kTRound;
+    for (int q = 0; q < kProducers; ++q) s_next[q] = -1;
+    for (int s = 0; s < S; ++s) {
+      mbar_init(full0 + 8u * s, 1);
+      mbar_init(empty0 + 8u * s, 1);
+    }
+    fence_mbar_init();
+  }
+  __syncthreads();
+  asm volatile("griddepcontrol.launch_dependents;");
+  if (s_abort) {
+    if (threadIdx.x == 0) atomicAdd(&g_bnbq_wait_timeouts, 1u);
+    return;
+  }
+  if (warp >= ncw) {  // ----------------------------------------------- producers
+    const int q = warp - ncw;
+    if (lane == 0 && q < n_units) {
+      if (q == 0) asm volatile("prefetch.tensormap [%0];" ::"l"(&tmap) : "memory");
+      int i = q, slot = q % S;
+      uint32_t use = uint32_t(q / S);
+      bool ok = true;
+      int unissued = 0x7fffffff;
+      while (true) {
+        if (use > 0) ok = mbar_wait(empty0 + 8u * slot, (use - 1u) & 1u);
+        if (!ok || s_abort) {
+          unissued = i;
+          break;
+        }
+        const int64_t u = u0 + i;
+        const int g = int(u / a.row_blocks), rb = int(u % a.row_blocks);
+        const uint32_t full = full0 + 8u * slot;
+        mbar_arrive_expect_tx(full, kStage);
+        tma_load_2d(stage0 + uint32_t(slot) * kStage, &tmap, g * 128, rb * kRows, full);
+        if (i + kProducers >= n_units) break;
+        i += kProducers;
+        slot += kProducers;
+        if (slot >= S) {
+          slot -= S;
+          ++use;
+        }
+      }
+      if (!ok) {
+        __threadfence_block();
+        s_abort = 1;
+      }
+      s_next[q] = unissued;
+    } else if (lane == 0) {
+      s_next[q] = 0x7fffffff;
+    }
+    return;
+  }
+
+  // ---------------------------------------------------------------- consumers
+  const int ncons = ncw * 32;
+  for (int b = warp; b < 256; b += ncw) s_pair[b * 32 + lane] = make_float2(kNF4Table[b >> 4], kNF4Table[b & 15]);
+  float offset = 0.0f;
+  if constexpr (NESTED) {
+    for (int i = threadIdx.x; i < 256; i += ncons) s_code2[i] = a.x.code2[i];
+    offset = *a.x.offset;
+  }
+  asm volatile("griddepcontrol.wait;" ::: "memory");  // g and the workspace: after the previous kernel
+  named_bar_sync(1, ncons);
+  const XT* gp = static_cast<const XT*>(a.g);
+  const int qs = lane / LPB;
+  const int nseg = int((u1 - 1) / a.row_blocks) - g_first + 1;
+  float* part_cta = a.partial + int64_t(blockIdx.x) * a.maxseg * ncw * M * 256;
+  auto flush = [&](int seg, const float2 (&acc)[M][4]) {
+#pragma unroll
+    for (int m = 0; m < M; ++m) {
+      float* dst = part_cta + ((int64_t(seg) * ncw + warp) * M + m) * 256 + 8 * lane;
+      __stcg(reinterpret_cast<float4*>(dst), make_float4(acc[m][0].x, acc[m][0].y, acc[m][1].x, acc[m][1].y));
+      __stcg(reinterpret_cast<float4*>(dst + 4), make_float4(acc[m][2].x, acc[m][2].y, acc[m][3].x, acc[m][3].y));
+    }
+  };
+  float2 acc[M][4];
+#pragma unroll
+  for (int m = 0; m < M; ++m)
+#pragma unroll
+    for (int j = 0; j < 4; ++j) acc[m][j] = make_float2(0.0f, 0.0f);
+  int cur = 0;  // the segment (column group - g_first) acc belongs to
+  ScaleWords<NB, NESTED> sw;
+  float gv[M];
+  auto fetch_g = [&](int rb) {
+    const int64_t row = int64_t(rb) * kRows + lane;
+#pragma unroll
+    for (int m = 0; m < M; ++m) gv[m] = row < a.x.n_rows ? Elem<XT>::to_f32(gp[int64_t(m) * a.ldg + row]) : 0.0f;
+  };
+  if (warp < n_units) {
+    const int64_t u = u0 + warp;
+    fetch_scales<1, NB, NESTED>(sw, a.x, int(u / a.row_blocks), int(u % a.row_blocks), lane);
+    fetch_g(int(u % a.row_blocks));
+  }
+  int slot = warp % S;
+  uint32_t parity = uint32_t((warp / S) & 1);
+  for (int i = warp; i < n_units; i += ncw) {
+    bool ok;
+    if (s_abort) {
+      ok = false;
+      const int q = i % kProducers;
+      const uint64_t t0 = global_ns();
+      while (s_next[q] < 0 && global_ns() - t0 < g_bnbq_wait_limit_ns) {
+      }
+      if (i < s_next[q]) mbar_wait(full0 + 8u * slot, parity);
+    } else {
+      ok = mbar_wait(full0 + 8u * slot, parity);
+      ok = __shfl_sync(0xffffffffu, ok, 0);
+      if (!ok) s_abort = 1;
+    }
+    uint32_t cw[kRows];
+    if (ok) {
+      const uint32_t st = stage0 + uint32_t(slot) * kStage + uint32_t(lane) * 4u;
+#pragma unroll
+      for (int r = 0; r < kRows; ++r) cw[r] = lds_code(st + uint32_t(r) * 128u);
+    }
+    __syncwarp();
+    if (lane == 0) mbar_arrive(empty0 + 8u * slot);
+    slot += ncw;
+    if (slot >= S) {
+      slot -= S;
+      parity ^= 1u;
+    }
+    const int64_t u = u0 + i;
+    const int seg = int(u / a.row_blocks) - g_first;
+    // this row's block scales and g values, for the warp's lanes to read
+    float a_own[NB];
+    decode_scales<NB, NESTED>(a_own, sw, a.x, s_code2, offset, 0);
+#pragma unroll
+    for (int p = 0; p < NB; ++p) s_a[warp][lane][p] = a_own[p];
+#pragma unroll
+    for (int m = 0; m < M; ++m) s_gv[warp][m][lane] = gv[m];
+    __syncwarp();
+    if (i + ncw < n_units) {
+      const int64_t un = u0 + i + ncw;
+      fetch_scales<1, NB, NESTED>(sw, a.x, int(un / a.row_blocks), int(un % a.row_blocks), lane);
+      fetch_g(int(un % a.row_blocks));
+    }
+    if (seg != cur) {  // a new column group: store the finished ones (zeros for skipped)
+      for (; cur < seg; ++cur) {
+        flush(cur, acc);
+#pragma unroll
+        for (int m = 0; m < M; ++m)
+#pragma unroll
+          for (int j = 0; j < 4; ++j) acc[m][j] = make_float2(0.0f, 0.0f);
+      }
+    }
+    if (ok) {
+#pragma unroll
+      for (int r = 0; r < kRows; ++r) {
+        const float sa = s_a[warp][r][qs];
+        float2 wv[4];
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          const uint32_t byte = (cw[r] >> (8 * j)) & 0xffu;
+          wv[j] = mul_ftz2(s_pair[byte * 32 + lane], make_float2(sa, sa));
+        }
+#pragma unroll
+        for (int m = 0; m < M; ++m) {
+          const float gr = s_gv[warp][m][r];
+#pragma unroll
+          for (int j = 0; j < 4; ++j) acc[m][j] = __ffma2_rn(wv[j], make_float2(gr, gr), acc[m][j]);
+        }
+      }
+    }
+    __syncwarp();  // s_a and s_gv are rewritten for the next unit
+  }
+  for (; cur < nseg; ++cur) {
+    flush(cur, acc);
+#pragma unroll
+    for (int m = 0; m < M; ++m)
+#pragma unroll
+      for (int j = 0; j < 4; ++j) acc[m][j] = make_float2(0.0f, 0.0f);
+  }
+}
+
+// The CTA of a grid of G over U units (CTA b: units [b U / G, (b + 1) U / G))
+// that holds unit u.
+__device__ __forceinline__ int64_t cta_of(int64_t u, int64_t units, int64_t grid) {
+  return ((u + 1) * grid + units - 1) / units - 1;
+}
+
+template <typename XT, int M>
+__global__ void __launch_bounds__(256) gemv_t_reduce_kernel(const float* partial, int64_t units, int64_t grid,
+                                                            int row_blocks, int maxseg, int k, void* out,
+                                                            int64_t ldo) {
+  asm volatile("griddepcontrol.launch_dependents;");
+  asm volatile("griddepcontrol.wait;" ::: "memory");  // every partial of the first kernel is visible
+  const int64_t total = int64_t(M) * k;
+  for (int64_t i = int64_t(blockIdx.x) * blockDim.x + threadIdx.x; i < total; i += int64_t(gridDim.x) * blockDim.x) {
+    const int m = int(i / k), c = int(i - int64_t(m) * k);
+    const int g = c >> 8, cc = c & 255;
+    const int64_t b_lo = cta_of(int64_t(g) * row_blocks, units, grid);
+    const int64_t b_hi = cta_of(int64_t(g + 1) * row_blocks - 1, units, grid);
+    float v = 0.0f;
+    for (int64_t b = b_lo; b <= b_hi; ++b) {
+      const int g0 = int((b * units / grid) / row_blocks);
+      const float* p = partial + ((b * maxseg + (g - g0)) * kTConsumers * M + m) * 256 + cc;
+      for (int w = 0; w < kTConsumers; ++w) v += __ldcg(p + int64_t(w) * M * 256);
+    }
+    XT* o = static_cast<XT*>(out);
+    if constexpr (Elem<XT>::kDtype == BNBQ_BF16) o[int64_t(m) * ldo + c] = __float2bfloat16_rn(v);
+    else o[int64_t(m) * ldo + c] = __float2half_rn(v);
+  }
+}
+
 // --------------------------------------------------------------- host side
 
 PFN_cuTensorMapEncodeTiled_v12000 encoder() {
@@ -1144,6 +1403,88 @@ int launch_code8_m(int nb, bool nested, const CUtensorMap& map, const XtabArgs& 
                 : launch_code8_nb<XT, M, false>(nb, map, a, code, di, s);
 }
 
+// ---- the backward (gemv_t_kernel)
+struct TPlan {
+  int64_t grid, units;
+  int maxseg;
+};
+
+TPlan plan_t(int64_t n_rows, int k, int sm_count) {
+  TPlan p;
+  const int rbs = int((n_rows + kRows - 1) / kRows);
+  p.units = int64_t(k / 256) * rbs;
+  p.grid = p.units < sm_count ? p.units : sm_count;
+  p.maxseg = 1;
+  for (int64_t b = 0; b < p.grid; ++b) {
+    const int64_t u0 = b * p.units / p.grid, u1 = (b + 1) * p.units / p.grid;
+    const int nseg = int((u1 - 1) / rbs - u0 / rbs + 1);
+    p.maxseg = nseg > p.maxseg ? nseg : p.maxseg;
+  }
+  return p;
+}
+
+int64_t t_workspace_bytes(int m, const TPlan& p) { return p.grid * p.maxseg * kTConsumers * m * 256 * 4; }
+
+template <typename XT, int M, int NB, bool NESTED>
+int launch_gemv_t(const CUtensorMap& map, const GemvTArgs& a0, const TPlan& p, void* out, int64_t ldo,
+                  const DeviceInfo& di, cudaStream_t s) {
+  auto kern = gemv_t_kernel<XT, M, NB, NESTED>;
+  GemvTArgs a = a0;
+  int static_smem = 0;
+  if (int st = kernel_static_smem(reinterpret_cast<const void*>(kern), &static_smem)) return st;
+  const int dyn = (di.smem_optin - static_smem - 1024) / 1024 * 1024;
+  if (dyn < int(kPairTableBytesT) + kTRound * kRows * 128) return BNBQ_ERR_UNSUPPORTED;
+  if (int st = kernel_reserve_smem(reinterpret_cast<const void*>(kern), dyn)) return st;
+  a.dyn_bytes = uint32_t(dyn);
+  a.units = p.units;
+  a.maxseg = p.maxseg;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(unsigned(p.grid));
+  cfg.blockDim = dim3(unsigned((kTConsumers + kProducers) * 32));
+  cfg.dynamicSmemBytes = size_t(dyn);
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  if (cudaLaunchKernelEx(&cfg, kern, map, a) != cudaSuccess) return BNBQ_ERR_CUDA;
+  cudaLaunchConfig_t rc = cfg;
+  const int64_t total = int64_t(M) * a.x.k;
+  int64_t rgrid = (total + 255) / 256;
+  if (rgrid > int64_t(di.sm_count) * 8) rgrid = int64_t(di.sm_count) * 8;
+  rc.gridDim = dim3(unsigned(rgrid));
+  rc.blockDim = dim3(256);
+  rc.dynamicSmemBytes = 0;
+  if (cudaLaunchKernelEx(&rc, gemv_t_reduce_kernel<XT, M>, static_cast<const float*>(a.partial), p.units, p.grid,
+                         a.row_blocks, p.maxseg, a.x.k, out, ldo) != cudaSuccess)
+    return BNBQ_ERR_CUDA;
+  return launch_status();
+}
+
+template <typename XT, int M, bool NESTED>
+int launch_gemv_t_nb(int nb, const CUtensorMap& map, const GemvTArgs& a, const TPlan& p, void* out, int64_t ldo,
+                     const DeviceInfo& di, cudaStream_t s) {
+  switch (nb) {
+    case 1: return launch_gemv_t<XT, M, 1, NESTED>(map, a, p, out, ldo, di, s);
+    case 2: return launch_gemv_t<XT, M, 2, NESTED>(map, a, p, out, ldo, di, s);
+    case 4: return launch_gemv_t<XT, M, 4, NESTED>(map, a, p, out, ldo, di, s);
+    case 8: return launch_gemv_t<XT, M, 8, NESTED>(map, a, p, out, ldo, di, s);
+    default: return BNBQ_ERR_UNSUPPORTED;
+  }
+}
+
+template <typename XT, bool NESTED>
+int launch_gemv_t_m(int m, int nb, const CUtensorMap& map, const GemvTArgs& a, const TPlan& p, void* out,
+                    int64_t ldo, const DeviceInfo& di, cudaStream_t s) {
+  switch (m) {
+    case 1: return launch_gemv_t_nb<XT, 1, NESTED>(nb, map, a, p, out, ldo, di, s);
+    case 2: return launch_gemv_t_nb<XT, 2, NESTED>(nb, map, a, p, out, ldo, di, s);
+    case 3: return launch_gemv_t_nb<XT, 3, NESTED>(nb, map, a, p, out, ldo, di, s);
+    default: return launch_gemv_t_nb<XT, 4, NESTED>(nb, map, a, p, out, ldo, di, s);
+  }
+}
+
 }  // namespace
 
 int xtab_wait_timeouts(unsigned int* out) { return read_wait_timeouts(out); }
@@ -1306,3 +1647,75 @@ int gemv_code8_launch(int dtype, const void* x, int m, int k, const uint8_t* w, 
 }
 
 }  // namespace bnbq
+
+using namespace bnbq;
+
+extern "C" int bnbq_gemv_t_nf4_workspace_bytes(int32_t m, int32_t k, int64_t n_rows, int64_t* bytes) {
+  if (!bytes || m < 1 || m > 4 || k < 1 || n_rows < 1) return BNBQ_ERR_INVALID;
+  if (k % 256 || n_rows > kMaxRowBlocks * kRows) return BNBQ_ERR_UNSUPPORTED;
+  DeviceInfo di;
+  if (int st = device_info(&di)) return st;
+  *bytes = t_workspace_bytes(m, plan_t(n_rows, k, di.sm_count));
+  return BNBQ_OK;
+}
+
+extern "C" int bnbq_gemv_t_nf4_ws(int dtype, const void* g, int32_t m, int64_t n_rows, int64_t ldg, int32_t k,
+                                  const uint8_t* w, int32_t blocksize, const float* absmax, const uint8_t* absmax_q,
+                                  const float* absmax2, const float* code2, const float* offset, int32_t blocksize2,
+                                  int64_t absmax2_block0, void* out, int64_t ldo, void* workspace,
+                                  int64_t workspace_bytes, void* stream) {
+  if (dtype != BNBQ_F16 && dtype != BNBQ_BF16) return BNBQ_ERR_UNSUPPORTED;
+  if (m < 1 || m > 4 || n_rows < 1 || k < 1 || ldg < n_rows || ldo < k) return BNBQ_ERR_INVALID;
+  if (k % 256 || n_rows > kMaxRowBlocks * kRows) return BNBQ_ERR_UNSUPPORTED;
+  const int l2 = log2_exact(blocksize);
+  if (l2 < 5 || !g || !w || !out || !workspace) return BNBQ_ERR_INVALID;
+  const int nb = blocksize >= 256 ? 1 : 256 / blocksize;
+  if (absmax_q) {
+    if (!absmax2 || !code2 || !offset || log2_exact(blocksize2) < 0) return BNBQ_ERR_INVALID;
+    if (blocksize2 < nb) return BNBQ_ERR_UNSUPPORTED;
+    if (!aligned(absmax2, 4) || !aligned(code2, 4) || !aligned(offset, 4) || !aligned(absmax_q, uint64_t(nb)))
+      return BNBQ_ERR_MISALIGNED;
+  } else {
+    if (!absmax) return BNBQ_ERR_INVALID;
+    if (!aligned(absmax, 4)) return BNBQ_ERR_MISALIGNED;
+  }
+  if (!aligned(g, 2) || !aligned(w, 16) || !aligned(out, 2) || !aligned(workspace, 16)) return BNBQ_ERR_MISALIGNED;
+  DeviceInfo di;
+  if (int st = device_info(&di)) return st;
+  const TPlan p = plan_t(n_rows, k, di.sm_count);
+  if (workspace_bytes < t_workspace_bytes(m, p)) return BNBQ_ERR_INVALID;
+  auto encode = encoder();
+  if (!encode) return BNBQ_ERR_CUDA;
+  CUtensorMap map;
+  const cuuint64_t dims[2] = {cuuint64_t(k / 2), cuuint64_t(n_rows)};
+  const cuuint64_t strides[1] = {cuuint64_t(k / 2)};
+  const cuuint32_t box[2] = {128u, cuuint32_t(kRows)};
+  const cuuint32_t estr[2] = {1, 1};
+  if (encode(&map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<uint8_t*>(w), dims, strides, box, estr,
+             CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+    return BNBQ_ERR_UNSUPPORTED;
+  GemvTArgs a{};
+  a.g = g;
+  a.partial = static_cast<float*>(workspace);
+  a.ldg = ldg;
+  a.row_blocks = int((n_rows + kRows - 1) / kRows);
+  a.groups = k / 256;
+  a.x.absmax = absmax;
+  a.x.absmax_q = absmax_q;
+  a.x.absmax2 = absmax2;
+  a.x.code2 = code2;
+  a.x.offset = offset;
+  a.x.n_rows = n_rows;
+  a.x.block0 = absmax2_block0;
+  a.x.k = k;
+  a.x.log2_bs = l2;
+  a.x.log2_bs2 = absmax_q ? log2_exact(blocksize2) : 0;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const bool nested = absmax_q != nullptr;
+  if (dtype == BNBQ_BF16)
+    return nested ? launch_gemv_t_m<__nv_bfloat16, true>(m, nb, map, a, p, out, ldo, di, s)
+                  : launch_gemv_t_m<__nv_bfloat16, false>(m, nb, map, a, p, out, ldo, di, s);
+  return nested ? launch_gemv_t_m<__half, true>(m, nb, map, a, p, out, ldo, di, s)
+                : launch_gemv_t_m<__half, false>(m, nb, map, a, p, out, ldo, di, s);
+}

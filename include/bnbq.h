@@ -198,18 +198,17 @@ BNBQ_API int bnbq_matmul_nf4_ws(int dtype, const void* x, int32_t m, int32_t k,
 
 /* The backward of the fused matmul for a few rows of g: out[m, k] =
  * sum_n g[m, n] * W[n, k] for an NF4 weight W (n_rows x k), never
- * materialised, 1 <= m <= 4, k % 256 == 0, n_rows <= 131072. g: m x n_rows
+ * materialised, 1 <= m <= 4, k % 256 == 0, blocksize >= 32. g: m x n_rows
  * (row stride ldg elements), out: m x k (row stride ldo), both F16 or BF16;
  * scales and absmax2 indexing as bnbq_gemv_nf4. Every weight is its exact
  * dequantized float32 value, times g in float32, summed in a fixed order and
  * rounded once: a one-hot g returns the dequantized weight row bitwise. The
  * workspace (any contents, 16-byte aligned, at least
- * bnbq_gemv_t_nf4_workspace_bytes) takes split-row partial sums that a
- * second kernel adds in order. Calls sharing it must be ordered on one stream.
- * Replaces (where a caller wants no dense weight): the custom VJP's
- * backward g @ w.dequantize(g.dtype) (_matmul.py:67-68) for those shapes;
- * measured slower than our dequantize plus cuBLAS on a B200, so
- * bnb_b200.matmul's backward keeps the dequantize route. */
+ * bnbq_gemv_t_nf4_workspace_bytes for that m, k and n_rows on this device)
+ * takes per-warp partial sums of each column group that a second kernel adds
+ * in a fixed order. Calls sharing it must be ordered on one stream.
+ * Replaces: the custom VJP's backward g @ w.dequantize(g.dtype)
+ * (_matmul.py:67-68) for those shapes. */
 BNBQ_API int bnbq_gemv_t_nf4_ws(int dtype, const void* g, int32_t m, int64_t n_rows, int64_t ldg, int32_t k,
                                 const uint8_t* w, int32_t blocksize, const float* absmax,
                                 const uint8_t* absmax_q, const float* absmax2, const float* code2,

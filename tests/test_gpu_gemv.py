@@ -10,7 +10,7 @@ import torch
 
 import bnb_b200
 from bnb_b200.kernels import gemv_nf4
-from bnb_b200.kernels.gemv import GEMV8_MAX_M, GEMV_MAX_M
+from bnb_b200.kernels.gemv import GEMV8_MAX_M, GEMV_MAX_M, GEMV_T_MAX_M
 from helpers import GEMV_ATOL, GEMV_RTOL, TORCH_DTYPES, bits, to_host
 from oracle import oracle as O
 
@@ -138,8 +138,10 @@ def test_matmul_large_m(cuda):
 
 @pytest.mark.parametrize("m", [1, GEMV_MAX_M + 1])
 def test_matmul_grad(cuda, m):
-    """Gradient in x through either route equals the fallback's own gradient
-    bitwise (reference test_matmul.py:70-79)."""
+    """Gradient in x (reference test_matmul.py:70-79). More than GEMV_T_MAX_M
+    rows of g: the reference's rule g @ w.dequantize(g.dtype), bitwise. Up to
+    it: the fused backward (exact float32 weights), within the GEMV tolerance
+    of the float64 product and closer to it than the rule."""
     w = weight(256, 512)
     x = x_rand(2 * m, 512, torch.bfloat16, 4).reshape(2, m, 512).requires_grad_(True)
     bnb_b200.matmul(x, w).float().sum().backward()
@@ -147,7 +149,15 @@ def test_matmul_grad(cuda, m):
     x.grad = None
     (x @ w.dequantize(x.dtype).T).float().sum().backward()
     assert g.dtype == torch.bfloat16
-    assert torch.equal(g, x.grad)
+    if 2 * m > GEMV_T_MAX_M:
+        assert torch.equal(g, x.grad)
+        return
+    wd = w.dequantize(torch.float32).double()
+    exact = torch.ones(2 * m, 256, dtype=torch.float64, device="cuda") @ wd
+    bound = GEMV_RTOL * exact.abs() + GEMV_ATOL * wd.abs().sum(0, keepdim=True)
+    got = g.reshape(2 * m, 512).double()
+    assert torch.all((got - exact).abs() <= bound)
+    assert (got - exact).abs().mean() <= (x.grad.reshape(2 * m, 512).double() - exact).abs().mean()
 
 
 def test_matmul_saves_no_dense_weight(cuda):

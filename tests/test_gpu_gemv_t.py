@@ -3,7 +3,7 @@ out = g @ W with W kept NF4. The reference computes g @ w.dequantize(g.dtype)
 (_matmul.py:67-68); here a one-hot g returns the dequantized weight rows
 bitwise, a random g is within the GEMV tolerance of the float64 product with
 the dequantized float32 weight (which the dequantize tests pin to the oracle)
-and closer to it than the reference's rule."""
+and closer to it than the reference's rule, and autograd uses it."""
 from __future__ import annotations
 
 import pytest
@@ -89,6 +89,16 @@ def test_strided_g_and_repeat(cuda):
     b = call(g.contiguous(), w)
     assert torch.equal(a, b)
     check_tolerance(g, w, a)
+
+
+def test_autograd_uses_it(cuda):
+    w = weight(256, 512, 64, True, seed=2)
+    x = torch.randn(3, 512, device="cuda", generator=torch.Generator("cuda").manual_seed(2)).to(torch.bfloat16)
+    x.requires_grad_(True)
+    y = bnb_b200.matmul(x, w)
+    gy = torch.randn_like(y)
+    y.backward(gy)
+    assert torch.equal(x.grad, call(gy, w))
 
 
 def test_errors(cuda):
