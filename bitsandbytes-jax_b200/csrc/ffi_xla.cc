@@ -5,6 +5,10 @@
 //   kernels/dequantize.py:110-116  (nf4 / 8-bit)          -> BnbqDequantizeNf4 / BnbqDequantizeBlockwise
 //   array.py:95-108                (nested decode chain)  -> BnbqDequantizeNf4Nested / BnbqDequantizeBlockwiseNested
 //   kernels/gemv.py:195-204 and _matmul.py:46-60 (GEMV, and the M > 20 route) -> BnbqMatmulNf4
+// and three with no cutejax.call of their own in the reference:
+//   _matmul.py:74-79 -> 58-59  (8-bit weights: the dequantize fallback)   -> BnbqGemvBlockwise
+//   _matmul.py:67-68           (the custom VJP's g @ w.dequantize())      -> BnbqGemvTNf4
+//   array.py:199-202           (quantize_nf4, jnp.mean, quantize_blockwise) -> BnbqQuantizeNf4Dq
 //
 // Built by build.py only where jaxlib's FFI headers are found
 // (jax.ffi.include_dir(), or the BNBQ_XLA_FFI_INCLUDE environment variable),
@@ -158,6 +162,69 @@ ffi::Error MatmulNf4(cudaStream_t s, ffi::AnyBuffer x, ffi::Buffer<ffi::U8> w, f
                "matmul_nf4");
 }
 
+// y (M, n_rows) = x (M, K) @ W.T for an 8-bit blockwise weight with codebook
+// `code`; scales as MatmulNf4. `workspace`: a uint8 result of
+// bnbq_gemv_blockwise_workspace_bytes(M, K, n_rows) bytes.
+ffi::Error GemvBlockwise(cudaStream_t s, ffi::AnyBuffer x, ffi::Buffer<ffi::U8> w, ffi::Buffer<ffi::F32> code,
+                         ffi::AnyBuffer absmax, ffi::Buffer<ffi::F32> absmax2, ffi::Buffer<ffi::F32> code2,
+                         ffi::Buffer<ffi::F32> offset, ffi::Result<ffi::AnyBuffer> y,
+                         ffi::Result<ffi::Buffer<ffi::U8>> workspace, int64_t n_rows, int64_t blocksize,
+                         int64_t nested, int64_t blocksize2) {
+  const int dt = DtypeOf(x.element_type());
+  if (dt != BNBQ_F16 && dt != BNBQ_BF16) return BadType("gemv_blockwise");
+  const auto dims = x.dimensions();
+  if (dims.size() != 2) return ffi::Error(ffi::ErrorCode::kInvalidArgument, "gemv_blockwise: x must be (M, K)");
+  const int32_t m = int32_t(dims[0]), k = int32_t(dims[1]);
+  const float* a = nested ? nullptr : static_cast<const float*>(absmax.untyped_data());
+  const uint8_t* aq = nested ? static_cast<const uint8_t*>(absmax.untyped_data()) : nullptr;
+  return Check(bnbq_gemv_blockwise_ws(dt, x.untyped_data(), m, k, w.typed_data(), n_rows, int32_t(blocksize),
+                                      code.typed_data(), a, aq, nested ? absmax2.typed_data() : nullptr,
+                                      nested ? code2.typed_data() : nullptr, nested ? offset.typed_data() : nullptr,
+                                      nested ? int32_t(blocksize2) : 0, 0, y->untyped_data(), n_rows,
+                                      workspace->untyped_data(), int64_t(workspace->size_bytes()), s),
+               "gemv_blockwise");
+}
+
+// out (M, K) = g (M, n_rows) @ W for an NF4 weight of n_rows x K: the VJP's
+// backward for up to 4 rows of g. `workspace`: a uint8 result of
+// bnbq_gemv_t_nf4_workspace_bytes(M, K, n_rows) bytes.
+ffi::Error GemvTNf4(cudaStream_t s, ffi::AnyBuffer g, ffi::Buffer<ffi::U8> w, ffi::AnyBuffer absmax,
+                    ffi::Buffer<ffi::F32> absmax2, ffi::Buffer<ffi::F32> code2, ffi::Buffer<ffi::F32> offset,
+                    ffi::Result<ffi::AnyBuffer> out, ffi::Result<ffi::Buffer<ffi::U8>> workspace, int64_t k,
+                    int64_t blocksize, int64_t nested, int64_t blocksize2) {
+  const int dt = DtypeOf(g.element_type());
+  if (dt != BNBQ_F16 && dt != BNBQ_BF16) return BadType("gemv_t_nf4");
+  const auto dims = g.dimensions();
+  if (dims.size() != 2) return ffi::Error(ffi::ErrorCode::kInvalidArgument, "gemv_t_nf4: g must be (M, N)");
+  const int32_t m = int32_t(dims[0]);
+  const int64_t n_rows = dims[1];
+  const float* a = nested ? nullptr : static_cast<const float*>(absmax.untyped_data());
+  const uint8_t* aq = nested ? static_cast<const uint8_t*>(absmax.untyped_data()) : nullptr;
+  return Check(bnbq_gemv_t_nf4_ws(dt, g.untyped_data(), m, n_rows, n_rows, int32_t(k), w.typed_data(),
+                                  int32_t(blocksize), a, aq, nested ? absmax2.typed_data() : nullptr,
+                                  nested ? code2.typed_data() : nullptr, nested ? offset.typed_data() : nullptr,
+                                  nested ? int32_t(blocksize2) : 0, 0, out->untyped_data(), k,
+                                  workspace->untyped_data(), int64_t(workspace->size_bytes()), s),
+               "gemv_t_nf4");
+}
+
+// quantize(x, "nf4", blocksize, double_quant=True) in one launch: codes,
+// absmax, the nested codes and scales and the offset. `workspace`: a uint8
+// result of bnbq_quantize_nf4_dq_workspace_bytes() bytes.
+ffi::Error QuantizeNf4Dq(cudaStream_t s, ffi::AnyBuffer x, ffi::Buffer<ffi::F32> code2,
+                         ffi::Result<ffi::Buffer<ffi::U8>> q, ffi::Result<ffi::Buffer<ffi::F32>> absmax,
+                         ffi::Result<ffi::Buffer<ffi::U8>> absmax_q, ffi::Result<ffi::Buffer<ffi::F32>> absmax2,
+                         ffi::Result<ffi::Buffer<ffi::F32>> offset, ffi::Result<ffi::Buffer<ffi::U8>> workspace,
+                         int64_t blocksize, int64_t blocksize2) {
+  const int dt = DtypeOf(x.element_type());
+  if (dt < 0) return BadType("quantize_nf4_dq");
+  return Check(bnbq_quantize_nf4_dq(dt, x.untyped_data(), int64_t(x.element_count()), int32_t(blocksize),
+                                    code2.typed_data(), int32_t(blocksize2), q->typed_data(), absmax->typed_data(),
+                                    absmax_q->typed_data(), absmax2->typed_data(), offset->typed_data(),
+                                    workspace->untyped_data(), int64_t(workspace->size_bytes()), s),
+               "quantize_nf4_dq");
+}
+
 }  // namespace
 
 XLA_FFI_DEFINE_HANDLER_SYMBOL(bnbq_quantize_nf4_ffi, QuantizeNf4,
@@ -241,4 +308,51 @@ XLA_FFI_DEFINE_HANDLER_SYMBOL(bnbq_matmul_nf4_ffi, MatmulNf4,
                                   .Attr<int64_t>("n_rows")
                                   .Attr<int64_t>("blocksize")
                                   .Attr<int64_t>("nested")
+                                  .Attr<int64_t>("blocksize2"));
+
+XLA_FFI_DEFINE_HANDLER_SYMBOL(bnbq_gemv_blockwise_ffi, GemvBlockwise,
+                              ffi::Ffi::Bind()
+                                  .Ctx<ffi::PlatformStream<cudaStream_t>>()
+                                  .Arg<ffi::AnyBuffer>()
+                                  .Arg<ffi::Buffer<ffi::U8>>()
+                                  .Arg<ffi::Buffer<ffi::F32>>()
+                                  .Arg<ffi::AnyBuffer>()
+                                  .Arg<ffi::Buffer<ffi::F32>>()
+                                  .Arg<ffi::Buffer<ffi::F32>>()
+                                  .Arg<ffi::Buffer<ffi::F32>>()
+                                  .Ret<ffi::AnyBuffer>()
+                                  .Ret<ffi::Buffer<ffi::U8>>()
+                                  .Attr<int64_t>("n_rows")
+                                  .Attr<int64_t>("blocksize")
+                                  .Attr<int64_t>("nested")
+                                  .Attr<int64_t>("blocksize2"));
+
+XLA_FFI_DEFINE_HANDLER_SYMBOL(bnbq_gemv_t_nf4_ffi, GemvTNf4,
+                              ffi::Ffi::Bind()
+                                  .Ctx<ffi::PlatformStream<cudaStream_t>>()
+                                  .Arg<ffi::AnyBuffer>()
+                                  .Arg<ffi::Buffer<ffi::U8>>()
+                                  .Arg<ffi::AnyBuffer>()
+                                  .Arg<ffi::Buffer<ffi::F32>>()
+                                  .Arg<ffi::Buffer<ffi::F32>>()
+                                  .Arg<ffi::Buffer<ffi::F32>>()
+                                  .Ret<ffi::AnyBuffer>()
+                                  .Ret<ffi::Buffer<ffi::U8>>()
+                                  .Attr<int64_t>("k")
+                                  .Attr<int64_t>("blocksize")
+                                  .Attr<int64_t>("nested")
+                                  .Attr<int64_t>("blocksize2"));
+
+XLA_FFI_DEFINE_HANDLER_SYMBOL(bnbq_quantize_nf4_dq_ffi, QuantizeNf4Dq,
+                              ffi::Ffi::Bind()
+                                  .Ctx<ffi::PlatformStream<cudaStream_t>>()
+                                  .Arg<ffi::AnyBuffer>()
+                                  .Arg<ffi::Buffer<ffi::F32>>()
+                                  .Ret<ffi::Buffer<ffi::U8>>()
+                                  .Ret<ffi::Buffer<ffi::F32>>()
+                                  .Ret<ffi::Buffer<ffi::U8>>()
+                                  .Ret<ffi::Buffer<ffi::F32>>()
+                                  .Ret<ffi::Buffer<ffi::F32>>()
+                                  .Ret<ffi::Buffer<ffi::U8>>()
+                                  .Attr<int64_t>("blocksize")
                                   .Attr<int64_t>("blocksize2"));

@@ -33,5 +33,5 @@ def test_ffi_handlers_cover_every_reference_call_site():
     src = (ROOT / "bitsandbytes-jax_b200/csrc/ffi_xla.cc").read_text()
     for entry in ("bnbq_quantize_nf4(", "bnbq_quantize_blockwise(", "bnbq_absmax_mean(", "bnbq_dequantize_nf4(",
                   "bnbq_dequantize_blockwise(", "bnbq_dequantize_nf4_nested(", "bnbq_dequantize_blockwise_nested(",
-                  "bnbq_matmul_nf4_ws("):
+                  "bnbq_matmul_nf4_ws(", "bnbq_gemv_blockwise_ws(", "bnbq_gemv_t_nf4_ws(", "bnbq_quantize_nf4_dq("):
         assert entry in src, entry
