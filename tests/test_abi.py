@@ -119,3 +119,26 @@ def test_quantize_nf4_dq_host_checks(lib):
     assert f(*args) == -2                                      # nested blocks above 256
     args = list(ok); args[11] = P(264)
     assert f(*args) == -3                                      # workspace not 16-byte aligned
+
+
+def test_gemv_t_host_checks(lib):
+    """The fused backward's argument errors, before any device call."""
+    P = ctypes.c_void_p
+    f = lib.bnbq_gemv_t_nf4_ws
+    f.argtypes = [ctypes.c_int, P, ctypes.c_int32, ctypes.c_int64, ctypes.c_int64, ctypes.c_int32, P,
+                  ctypes.c_int32, P, P, P, P, P, ctypes.c_int32, ctypes.c_int64, P, ctypes.c_int64, P,
+                  ctypes.c_int64, P]
+    ok = [2, P(256), 1, 64, 64, 512, P(256), 64, P(256), None, None, None, None, 0, 0, P(256), 512,
+          P(256), 1 << 24, None]
+    args = list(ok); args[0] = 0
+    assert f(*args) == -2                                      # float32 g
+    args = list(ok); args[2] = 5
+    assert f(*args) == -1                                      # more than 4 rows of g
+    args = list(ok); args[16] = 256
+    assert f(*args) == -1                                      # ldo < k
+    args = list(ok); args[5] = 320; args[16] = 320
+    assert f(*args) == -2                                      # K % 256 != 0
+    args = list(ok); args[7] = 16
+    assert f(*args) == -1                                      # blocksize below 32
+    args = list(ok); args[8] = P(258)
+    assert f(*args) == -3                                      # absmax not 4-byte aligned
