@@ -86,7 +86,10 @@ class _Matmul2d(torch.autograd.Function):
             # the reference's rule with the weight kept NF4 (measured on a B200:
             # 23.8 us against 58.0 us for dequantize + cuBLAS on config 2's weight)
             scales, nested = _fused_args(w)
-            return gemv_t_nf4(g, w.data, scales, w.shape[0], w.shape[1], w.blocksize, nested=nested), None
+            try:
+                return gemv_t_nf4(g, w.data, scales, w.shape[0], w.shape[1], w.blocksize, nested=nested), None
+            except NotImplementedError:
+                pass  # the kernel declined this call (BNBQ_ERR_UNSUPPORTED): the rule below
         return g @ w.dequantize(g.dtype), None
 
 
