@@ -33,7 +33,7 @@ def cta_of(u: int, units: int, grid: int) -> int:
 
 
 @pytest.mark.parametrize("n_rows,k,sms", list(itertools.product(
-    [1, 31, 32, 33, 100, 1000, 4096, 14336, 28672], [256, 512, 4096, 14336], [148, 132, 7])))
+    [1, 31, 32, 33, 100, 256, 512, 777, 1000, 4096, 14336, 28672], [256, 512, 768, 4096, 14336], [148, 132, 7])))
 def test_backward_partials_cover_every_unit_once(n_rows, k, sms):
     rbs, units, grid, maxseg = plan_t(n_rows, k, sms)
     groups = k // 256
