@@ -173,3 +173,45 @@ def test_shard_from_dict_takes_only_the_rank_rows(compress):
         else:
             assert sh.nested is None
     assert covered == n
+
+
+def test_new_kernel_entries_reject_before_any_compute():
+    """The 8-bit GEMV, the fused backward and the one-launch double
+    quantization check shapes and dtypes on the host (no device needed)."""
+    from bnb_b200.kernels import GEMV8_MAX_M, GEMV_T_MAX_M, gemv_blockwise, gemv_t_nf4, quantize_nf4_dq
+    from bnb_b200.kernels.gemv import gemv_blockwise_applies, gemv_t_applies
+
+    assert gemv_blockwise_applies(1, 256, 64) and gemv_blockwise_applies(GEMV8_MAX_M, 128, 32)
+    assert not gemv_blockwise_applies(GEMV8_MAX_M + 1, 256, 64)
+    assert not gemv_blockwise_applies(1, 320, 64)           # K % 128 != 0
+    assert not gemv_blockwise_applies(1, 256, 16)           # blocks below 32
+    assert gemv_t_applies(GEMV_T_MAX_M, 512, 1000) and not gemv_t_applies(GEMV_T_MAX_M + 1, 512, 1000)
+    assert not gemv_t_applies(1, 320, 1000)                 # K % 256 != 0
+
+    codes = torch.zeros(64 * 256, dtype=torch.uint8)
+    absmax = torch.ones(64 * 256 // 64)
+    code = torch.linspace(-1, 1, 256)
+    with pytest.raises(ValueError):                         # more rows than the kernel takes
+        gemv_blockwise(torch.zeros(GEMV8_MAX_M + 1, 256, dtype=torch.bfloat16), codes, absmax, code, 64, 64)
+    with pytest.raises(NotImplementedError):                # float32 x
+        gemv_blockwise(torch.zeros(1, 256), codes, absmax, code, 64, 64)
+    with pytest.raises(ValueError):                         # K % 128 != 0
+        gemv_blockwise(torch.zeros(1, 192, dtype=torch.bfloat16), codes[:64 * 192], absmax, code, 64, 64)
+    with pytest.raises(ValueError):                         # host tensors
+        gemv_blockwise(torch.zeros(1, 256, dtype=torch.bfloat16), codes, absmax, code, 64, 64)
+
+    nf4 = torch.zeros(64 * 512 // 2, dtype=torch.uint8)
+    scales = torch.ones(64 * 512 // 64)
+    with pytest.raises(ValueError):                         # g must be (M, n_rows)
+        gemv_t_nf4(torch.zeros(1, 63, dtype=torch.bfloat16), nf4, scales, 64, 512, 64)
+    with pytest.raises(ValueError):                         # more rows of g than the kernel takes
+        gemv_t_nf4(torch.zeros(GEMV_T_MAX_M + 1, 64, dtype=torch.bfloat16), nf4, scales, 64, 512, 64)
+    with pytest.raises(NotImplementedError):                # float32 g
+        gemv_t_nf4(torch.zeros(1, 64), nf4, scales, 64, 512, 64)
+    with pytest.raises(ValueError):                         # blocks below 32
+        gemv_t_nf4(torch.zeros(1, 64, dtype=torch.bfloat16), nf4, scales, 64, 512, 16)
+    with pytest.raises(ValueError):                         # host tensors
+        gemv_t_nf4(torch.zeros(1, 64, dtype=torch.bfloat16), nf4, scales, 64, 512, 64)
+
+    with pytest.raises(ValueError):                         # nothing to quantize
+        quantize_nf4_dq(torch.zeros(0, dtype=torch.bfloat16), 64)
